@@ -1,0 +1,116 @@
+"""ctypes binding of ``libbayes_ssm_b200.so`` (the C ABI in include/bayes_ssm_b200.h).
+
+The library is built in-tree (``bayes_ssm/_build.py``) and loaded once.  A
+missing or unloadable library raises :class:`ExtensionUnavailable`; there is
+no fallback path for CUDA tensors.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional
+
+PKG_ROOT = Path(__file__).resolve().parents[1]
+LIB_PATH = Path(os.environ.get("BAYES_SSM_B200_LIB", PKG_ROOT / "lib" / "libbayes_ssm_b200.so"))
+
+BSSM_OK = 0
+BSSM_F32 = 0
+BSSM_BF16 = 1
+SUPPORTED = ((1, 8), (2, 8), (4, 8), (8, 8))
+
+_LIB: Optional[ctypes.CDLL] = None
+_LOAD_ERROR: Optional[BaseException] = None
+
+
+class ExtensionUnavailable(RuntimeError):
+    """The CUDA library could not be loaded."""
+
+
+class KernelError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+
+_vp, _l, _i, _d, _sz = ctypes.c_void_p, ctypes.c_long, ctypes.c_int, ctypes.c_double, ctypes.c_size_t
+
+_SIGNATURES = {
+    "bssm_last_error": ([], ctypes.c_char_p),
+    "bssm_version": ([], _i),
+    "bssm_forward_chunked_ex": ([_i, _i, _i, _i] + [_vp] * 13 + [_l, _l, _i, _d, _vp], _i),
+    "bssm_backward_workspace_bytes": ([_i, _i, _l, _l, _i], _sz),
+    "bssm_backward_chunked_ex": ([_i, _i, _i, _i, _i, _i] + [_vp] * 21 + [_vp, _sz, _l, _l, _i, _d, _vp], _i),
+    "bssm_assoc_scan_ex": ([_i, _i] + [_vp] * 10 + [_l, _l, _d, _vp], _i),
+}
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once) and declare the prototypes used here."""
+    global _LIB, _LOAD_ERROR
+    if _LIB is not None:
+        return _LIB
+    if _LOAD_ERROR is not None:
+        raise ExtensionUnavailable(str(_LOAD_ERROR)) from _LOAD_ERROR
+    try:
+        if not LIB_PATH.exists():
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing; build it with `python -c 'import __graft_entry__ as g; g.build()'` "
+                "or `python bayes-ssm_b200/bayes_ssm/_build.py`")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+    except BaseException as exc:  # remember the failure; every later call raises it
+        _LOAD_ERROR = exc
+        raise ExtensionUnavailable(f"cannot load {LIB_PATH}: {exc}") from exc
+    _LIB = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != BSSM_OK:
+        msg = load().bssm_last_error().decode(errors="replace")
+        raise KernelError(f"{what} failed (status {rc}): {msg}")
+
+
+def ptr(t) -> Optional[int]:
+    """Device pointer of a tensor (None passes NULL)."""
+    return None if t is None else t.data_ptr()
+
+
+def forward_chunked(key_dim, value_dim, io_dtype, fixed, keys, values, queries, decay, process,
+                    observation, mean0, cov0, out, mean_final, cov_final, bmean, bcov, n, t,
+                    chunks, floor, stream) -> None:
+    lib = load()
+    rc = lib.bssm_forward_chunked_ex(
+        key_dim, value_dim, io_dtype, int(fixed), ptr(keys), ptr(values), ptr(queries), ptr(decay),
+        ptr(process), ptr(observation), ptr(mean0), ptr(cov0), ptr(out), ptr(mean_final),
+        ptr(cov_final), ptr(bmean), ptr(bcov), n, t, chunks, float(floor), stream)
+    check(rc, "bssm_forward_chunked_ex")
+
+
+def workspace_bytes(key_dim, value_dim, n, t, chunks) -> int:
+    return int(load().bssm_backward_workspace_bytes(key_dim, value_dim, n, t, chunks))
+
+
+def backward_chunked(key_dim, value_dim, io_dtype, fixed, need_dynamics, need_initial, keys, values,
+                     queries, decay, process, observation, mean0, cov0, bmean, bcov, gy, gmf, gcf,
+                     gk, gv, gq, gd, gp, gr, gm0, gc0, workspace, workspace_nbytes, n, t, chunks,
+                     floor, stream) -> None:
+    lib = load()
+    rc = lib.bssm_backward_chunked_ex(
+        key_dim, value_dim, io_dtype, int(fixed), int(need_dynamics), int(need_initial), ptr(keys),
+        ptr(values), ptr(queries), ptr(decay), ptr(process), ptr(observation), ptr(mean0), ptr(cov0),
+        ptr(bmean), ptr(bcov), ptr(gy), ptr(gmf), ptr(gcf), ptr(gk), ptr(gv), ptr(gq), ptr(gd),
+        ptr(gp), ptr(gr), ptr(gm0), ptr(gc0), ptr(workspace), workspace_nbytes, n, t, chunks,
+        float(floor), stream)
+    check(rc, "bssm_backward_chunked_ex")
+
+
+def assoc_scan(key_dim, value_dim, keys, values, queries, observation, mean0, cov0, out, mean_final,
+               cov_final, status, n, t, floor, stream) -> None:
+    lib = load()
+    rc = lib.bssm_assoc_scan_ex(key_dim, value_dim, ptr(keys), ptr(values), ptr(queries),
+                                ptr(observation), ptr(mean0), ptr(cov0), ptr(out), ptr(mean_final),
+                                ptr(cov_final), ptr(status), n, t, float(floor), stream)
+    check(rc, "bssm_assoc_scan_ex")

@@ -1,0 +1,410 @@
+"""Benchmark: Bayes-mixer recurrence forward + backward at B256 T512 H64 D8 M8.
+
+One step = the chunked forward kernel + the single-launch replay backward
+(full dynamics gradients, no final-state gradients: the trainer's
+readout-only path) over N = B*H = 16384 chains of T = 512 tokens, chunk 64,
+with BF16 keys/values/queries (the mixer's projection outputs) and FP32
+decay / process / observation noise.  Inputs are seeded synthetic tensors with
+the mixer's distributions.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun: every rank owns its own 16384 chains (the layer
+shards over batch x heads with no exchange), so scaling is weak; the time is
+the max over ranks.  ``--impl reference`` times the CPU restatement of the
+reference algorithm (oracle/, FP32, all host threads) on a bounded sample of
+the same workload; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "bayes-ssm_b200"))
+
+B, T, H, D, M, CHUNK = 256, 512, 64, 8, 8, 64
+N_CHAINS = B * H
+TOKENS = B * T
+FLOOR = 1e-6
+METRIC = "Bayes mixer fwd+bwd tok/s/GPU (B256 T512 H64 D8 M8); % of FP32/HBM roofline"
+UNIT = "tok/s"
+
+# Algorithmic bytes per chain-step at the dtypes read/written here (BF16 k/q/v
+# and their gradients, FP32 everything else).  Forward: read k, q (2D bf16),
+# v (M bf16), decay (D f32), process + observation (2 f32); write y (M f32).
+# Backward: re-read the same plus gy (M f32); write gk, gq (2D bf16), gv (M
+# bf16), gdecay (D f32), gprocess + gobservation (2 f32).  Chunk-boundary
+# checkpoints are an implementation choice and are not counted.
+FWD_BYTES = 2 * D * 2 + M * 2 + D * 4 + 2 * 4 + M * 4
+BWD_BYTES = (2 * D * 2 + M * 2 + D * 4 + 2 * 4) + M * 4 + (2 * D * 2 + M * 2 + D * 4 + 2 * 4)
+# FLOPs per chain-step (FMA = 2): forward 4D^2+7DM+10D+M+1; backward =
+# recompute (forward - 2DM) + adjoint (18D^2+22DM+10D+M).
+FWD_FLOPS = 4 * D * D + 7 * D * M + 10 * D + M + 1
+BWD_FLOPS = (FWD_FLOPS - 2 * D * M) + (18 * D * D + 22 * D * M + 10 * D + M)
+# FP32 non-tensor peak: no measured figure exists on this pool, so the nominal
+# 148 SMs x 128 FP32 lanes x 2 flop x 1965 MHz is used and labelled as such.
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+# DRAM traffic per backward launch measured by ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum) on this exact workload; see
+# profiles/backward_d8m8_config3.md.  None until a capture exists.
+NCU_BWD_TRAFFIC_BYTES = None
+
+
+def _peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while the timed loop runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        reasons = []
+        for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                          ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+            if any(r[key].lower() == "active" for r in rows):
+                reasons.append(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in rows),
+                "sm_max_mhz": max(r["smax"] for r in rows),
+                "power_w_max": max(r["power"] for r in rows),
+                "samples": len(rows), "reasons": reasons}
+
+
+def make_inputs(n: int, seed: int, device):
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    k = F.normalize(torch.randn(n, T, D, generator=g), dim=-1).to(torch.bfloat16)
+    q = F.normalize(torch.randn(n, T, D, generator=g), dim=-1).to(torch.bfloat16)
+    v = (torch.randn(n, T, M, generator=g) / math.sqrt(M)).to(torch.bfloat16)
+    a = torch.sigmoid(2.0 + torch.randn(n, T, D, generator=g))
+    p = F.softplus(-4.0 + torch.randn(n, T, generator=g))
+    r = F.softplus(torch.randn(n, T, generator=g)) + 1e-4
+    gy = torch.randn(n, T, M, generator=g) / math.sqrt(M)
+    out = dict(k=k, q=q, v=v, a=a, p=p, r=r, gy=gy)
+    if device is not None:
+        out = {key: val.to(device) for key, val in out.items()}
+    return out
+
+
+def run_reference(args, rank: int) -> None:
+    """CPU arm: the oracle port (FP32, all host threads), bounded sample."""
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import oracle
+
+    line = cpu_baseline_measure(steps=args.steps, warmup=args.warmup)
+    value = line["value"]
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * TOKENS / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args.gpus),
+        "cpu_baseline": line,
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    del np
+
+
+def cpu_baseline_measure(steps: int = 1, warmup: int = 0, sample_chains: int | None = None) -> dict:
+    """Time oracle fwd+bwd (FP32) on a sample of chains; scale to tok/s."""
+    import numpy as np
+    from oracle import oracle
+
+    threads = oracle.num_threads()
+
+    def arrays(n):
+        return {k: v.float().numpy() for k, v in make_inputs(n, 1234, None).items()}
+
+    if sample_chains is None:
+        # calibrate on a few chains, then size the sample for ~10 s of work
+        # (capped at the full workload)
+        small = max(8, 2 * threads)
+        arr = arrays(small)
+        t0 = time.perf_counter()
+        oracle.forward(arr["k"], arr["v"], arr["q"], arr["a"], arr["p"], arr["r"], floor=FLOOR,
+                       precision="f32")
+        oracle.backward(arr["k"], arr["v"], arr["q"], arr["a"], arr["p"], arr["r"], None, None,
+                        arr["gy"], None, None, floor=FLOOR, precision="f32")
+        per_chain = (time.perf_counter() - t0) / small
+        sample_chains = int(min(N_CHAINS, max(small, 10.0 / max(per_chain, 1e-9))))
+    arr = arrays(sample_chains)
+
+    def one():
+        y, _, _ = oracle.forward(arr["k"], arr["v"], arr["q"], arr["a"], arr["p"], arr["r"],
+                                 floor=FLOOR, precision="f32")
+        oracle.backward(arr["k"], arr["v"], arr["q"], arr["a"], arr["p"], arr["r"], None, None,
+                        arr["gy"], None, None, floor=FLOOR, precision="f32")
+        return y
+
+    for _ in range(max(0, min(warmup, 1))):
+        one()
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    tokens = sample_chains * T / H  # a token of the workload carries H chains
+    del np
+    return {"value": tokens / sec, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{sample_chains} of {N_CHAINS} chains x T={T}, fwd+bwd, oracle FP32 "
+                      f"(oracle/bayes_oracle.c), median of {len(times)} run(s); "
+                      f"tok/s = chains*T/H / seconds"}
+
+
+def workload_config(n_gpus: int, chains: int = N_CHAINS) -> dict:
+    return {"workload": "Bayes mixer recurrence fwd + replay bwd (BASELINE config 3)"
+                        + ("" if chains == N_CHAINS else f" [profiling size: {chains} chains]"),
+            "B": chains // H, "T": T, "H": H, "D": D, "M": M, "chunk": CHUNK,
+            "chains_per_gpu": chains, "global_batch": chains // H * n_gpus, "seq_len": T,
+            "io_dtype": "bf16 k/q/v, fp32 decay/noise/state",
+            "gradients": "k, v, q, decay, process, observation (readout-only loss)",
+            "l2": "inputs larger than L2 (~0.74 GB read per step)",
+            "parallelism": f"dp{n_gpus} (chains sharded, no data-path collective)"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--chains", type=int, default=N_CHAINS,
+                    help="chains per GPU (default: the config's B*H = 16384; smaller for profiling)")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    import bayes_ssm
+    from bayes_ssm import _capi
+
+    n = args.chains
+    inp = make_inputs(n, 100 + rank, dev)
+    nb = (T + CHUNK - 1) // CHUNK
+    f32 = dict(device=dev, dtype=torch.float32)
+    out = torch.empty(n, T, M, **f32)
+    mt = torch.empty(n, D, M, **f32)
+    pt = torch.empty(n, D, D, **f32)
+    bm = torch.empty(n, nb + 1, D, M, **f32)
+    bc = torch.empty(n, nb + 1, D, D, **f32)
+    gk = torch.empty_like(inp["k"])
+    gq = torch.empty_like(inp["q"])
+    gv = torch.empty_like(inp["v"])
+    gd = torch.empty(n, T, D, **f32)
+    gp = torch.empty(n, T, **f32)
+    gr = torch.empty(n, T, **f32)
+    ws_bytes = _capi.workspace_bytes(D, M, n, T, CHUNK)
+    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    io = _capi.BSSM_BF16
+
+    def fwd():
+        _capi.forward_chunked(D, M, io, False, inp["k"], inp["v"], inp["q"], inp["a"], inp["p"],
+                              inp["r"], None, None, out, mt, pt, bm, bc, n, T, CHUNK, FLOOR, sp)
+
+    def bwd():
+        _capi.backward_chunked(D, M, io, False, True, False, inp["k"], inp["v"], inp["q"], inp["a"],
+                               inp["p"], inp["r"], None, None, bm, bc, inp["gy"], None, None, gk, gv,
+                               gq, gd, gp, gr, None, None, ws, ws_bytes, n, T, CHUNK, FLOOR, sp)
+
+    for _ in range(args.warmup):
+        fwd()
+        bwd()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            fwd()
+            ev[i][1].record(stream)
+            bwd()
+            ev[i][2].record(stream)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = start.elapsed_time(stop)
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    step_ms = total_ms / args.steps
+    t = torch.tensor([step_ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, fwd_ms, bwd_ms = (float(x) for x in t.tolist())
+    tokens = n * T // H  # a token of the workload carries H chains
+    value = tokens * world / (step_ms / 1e3)
+    clk = clocks.summary()
+
+    # ---- end to end through the public API, host buffers every step
+    e2e = None
+    if not args.no_e2e:
+        e2e = measure_e2e(args, dev, rank, world, bayes_ssm, n)
+
+    if rank == 0:
+        hbm_peak, peak_kind = _peaks()
+        chain_steps = n * T
+        bwd_gbs = chain_steps * BWD_BYTES / (bwd_ms / 1e3) / 1e9
+        bwd_tflops = chain_steps * BWD_FLOPS / (bwd_ms / 1e3) / 1e12
+        fwd_gbs = chain_steps * FWD_BYTES / (fwd_ms / 1e3) / 1e9
+        fwd_tflops = chain_steps * FWD_FLOPS / (fwd_ms / 1e3) / 1e12
+        traffic = NCU_BWD_TRAFFIC_BYTES
+        roofline = {
+            "kernel": "backward_kernel<8,8,...,bf16> (dominant: replay backward)",
+            "bound": "hbm", "achieved": round(bwd_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(bwd_gbs / hbm_peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": chain_steps * BWD_BYTES,
+            "fp32": {"achieved": round(bwd_tflops, 2), "peak": round(FP32_NOMINAL_TFLOPS, 1),
+                     "unit": "TFLOP/s", "frac": round(bwd_tflops / FP32_NOMINAL_TFLOPS, 4),
+                     "peak_source": "nominal 148 SM x 128 lanes x 2 x 1965 MHz (no measured FP32 figure)"},
+            "forward_kernel": {"ms": round(fwd_ms, 4), "GB/s": round(fwd_gbs, 1),
+                               "TFLOP/s": round(fwd_tflops, 2)},
+            "backward_kernel": {"ms": round(bwd_ms, 4), "GB/s": round(bwd_gbs, 1),
+                                "TFLOP/s": round(bwd_tflops, 2)},
+        }
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            cpu = cpu_baseline_measure(steps=1, warmup=0)
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(world, n), "roofline": roofline,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps * world,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def measure_e2e(args, dev, rank, world, bayes_ssm, n):
+    """Public API (bayesian_layer + autograd) with pinned host inputs each step."""
+    import torch
+
+    host = make_inputs(n, 100 + rank, None)
+    host = {k: v.pin_memory() for k, v in host.items() if k != "gy"}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    steps = max(3, min(args.steps, 10))
+
+    def one():
+        d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+        for key in ("k", "v", "q", "a", "p", "r"):
+            d[key].requires_grad_(True)
+        y, _, _ = bayes_ssm.bayesian_layer(d["k"], d["v"], d["q"], transition_diagonals=d["a"],
+                                           process_variances=d["p"], observation_variances=d["r"],
+                                           chunk_length=CHUNK, optimized=True)
+        loss = y.square().sum()
+        loss.backward()
+        return loss.detach().to("cpu", non_blocking=False)
+
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        one()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": round(n * T // H * world / (ms / 1e3), 1), "unit": UNIT,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "ms_per_step": round(ms, 3),
+            "steps": steps,
+            "path": "bayes_ssm.bayesian_layer(optimized=True) + loss.backward(); pinned host "
+                    "inputs copied H2D every step, loss read back"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,215 @@
+/*
+ * bayes_ssm_b200.h -- C ABI of the B200 (sm_100a) Bayesian-layer kernels.
+ *
+ * Plain pointers and sizes only.  Every entry point:
+ *   - takes device pointers (CUDA global memory of the current device) for
+ *     tensors and a cudaStream_t passed as void*; it only enqueues work on
+ *     that stream (no host synchronisation, no allocation);
+ *   - returns BSSM_OK (0) or a BSSM_ERR_* code; bssm_last_error() then
+ *     returns a message for the calling thread.
+ *
+ * Shapes (row-major, contiguous; N independent chains, T tokens):
+ *   keys, queries [N,T,D]; values [N,T,M]; decay [N,T,D]; process,
+ *   observation [N,T]; mean0 [N,D,M]; cov0 [N,D,D];
+ *   out [N,T,M]; mean_final [N,D,M]; cov_final [N,D,D];
+ *   boundary_mean [N,NB+1,D,M]; boundary_cov [N,NB+1,D,D], NB = ceil(T/chunks).
+ * Supported (D, M): (1,8), (2,8), (4,8), (8,8).
+ * io_dtype selects the element type of keys/values/queries and of their
+ * gradients: BSSM_F32 or BSSM_BF16.  Everything else is float32; the mean,
+ * covariance and every reduction are float32.
+ *
+ * Pointer alignment: keys/queries/values/decay and their gradients must be
+ * aligned to min(16, row bytes); BSSM_ERR_ALIGNMENT otherwise.
+ *
+ * Reference interface these replace (paths within catid/bayes-ssm): the
+ * per-key-dim pybind modules loaded by bayes_ssm/fused_cuda.py:23-55, whose
+ * exports are listed at bayes_ssm/persistent_bayes_chunked_d8.cu:653,
+ * _d4m8.cu:577, _d2m8.cu:602 and _d1m8.cu:673.
+ */
+#ifndef BAYES_SSM_B200_H
+#define BAYES_SSM_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BSSM_OK 0
+#define BSSM_ERR_INVALID 1     /* bad shape, size or null pointer */
+#define BSSM_ERR_UNSUPPORTED 2 /* (D, M) or dtype without a kernel */
+#define BSSM_ERR_ALIGNMENT 3   /* a vector-loaded pointer is misaligned */
+#define BSSM_ERR_CUDA 4        /* CUDA launch or runtime error */
+#define BSSM_ERR_WORKSPACE 5   /* workspace missing or too small */
+
+#define BSSM_F32 0
+#define BSSM_BF16 1
+
+/* Message for the last failing call on this thread ("" after success). */
+const char *bssm_last_error(void);
+
+/* ABI version: major * 10000 + minor * 100 + patch. */
+int bssm_version(void);
+
+/* ---------------------------------------------------------------------
+ * Generic entry points.
+ * ------------------------------------------------------------------- */
+
+/*
+ * Chunked forward: readouts, final state and the chunk-boundary states the
+ * backward replays from.  fixed != 0 ignores decay/process/observation (may
+ * be NULL) and uses A = 0.97 I, Q = 0.1 I, R = 1.  mean0 == NULL means zeros,
+ * cov0 == NULL means identity.  The covariance enters as (cov0 + cov0^T)/2.
+ * Replaces forward_chunked / forward_chunked_fixed,
+ * bayes_ssm/persistent_bayes_chunked_d8.cu:530-548.
+ */
+int bssm_forward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed,
+                            const void *keys, const void *values, const void *queries,
+                            const float *decay, const float *process, const float *observation,
+                            const float *mean0, const float *cov0,
+                            float *out, float *mean_final, float *cov_final,
+                            float *boundary_mean, float *boundary_cov,
+                            long n, long t, int chunks, double denominator_floor,
+                            void *stream);
+
+/* Bytes of device workspace bssm_backward_chunked_ex needs (0 allowed). */
+size_t bssm_backward_workspace_bytes(int key_dim, int value_dim, long n, long t, int chunks);
+
+/*
+ * Chunk-replay backward.  One launch: for every chain, chunks are replayed
+ * from boundary_mean/boundary_cov in reverse order and the adjoint runs over
+ * each replayed span in the same kernel.
+ *   grad_out [N,T,M] (NULL = zeros), grad_mean_final [N,D,M] (NULL = zeros),
+ *   grad_cov_final [N,D,D] (NULL = zeros).
+ * Outputs grad_keys/grad_values/grad_queries are always written.
+ * need_dynamics != 0 also writes grad_decay [N,T,D], grad_process and
+ * grad_observation [N,T] (zeros when fixed != 0).
+ * need_initial != 0 also writes grad_mean0 [N,D,M] and grad_cov0 [N,D,D]
+ * (symmetric: the covariance entered as (cov0 + cov0^T)/2).
+ * workspace: device memory of bssm_backward_workspace_bytes(...) bytes.
+ * Replaces backward_chunked and its lean / fixed / noinitial variants,
+ * bayes_ssm/persistent_bayes_chunked_d8.cu:550-651,
+ * bayes_ssm/persistent_bayes_chunked_d2m8.cu:576-600.
+ */
+int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed,
+                             int need_dynamics, int need_initial,
+                             const void *keys, const void *values, const void *queries,
+                             const float *decay, const float *process, const float *observation,
+                             const float *mean0, const float *cov0,
+                             const float *boundary_mean, const float *boundary_cov,
+                             const float *grad_out, const float *grad_mean_final,
+                             const float *grad_cov_final,
+                             void *grad_keys, void *grad_values, void *grad_queries,
+                             float *grad_decay, float *grad_process, float *grad_observation,
+                             float *grad_mean0, float *grad_cov0,
+                             void *workspace, size_t workspace_bytes,
+                             long n, long t, int chunks, double denominator_floor,
+                             void *stream);
+
+/*
+ * Static associative scan (A = I, Q = 0), forward only, float32.
+ *   keys/queries [N,T,D], values [N,T,M], observation [N,T] (every entry
+ *   finite and >= denominator_floor; the caller validates, the kernel also
+ *   flags), mean0 [N,D,M] (NULL = 0), cov0 [N,D,D] (NULL = I; must be
+ *   positive definite), out [N,T,M], mean_final [N,D,M], cov_final [N,D,D].
+ *   status: device int the caller zeroes; the kernel ORs 1 when a precision
+ *   matrix is not positive definite and 2 when an observation variance is
+ *   below the floor or not finite.
+ * Limits: 1 <= D <= 32, 1 <= M <= 256, N <= 65535 per call.
+ * Replaces associative_static_bayesian_cuda, bayes_ssm/replay_ssm.py:276-339
+ * (whose default path is the eager information-form scan :155-270).
+ */
+int bssm_assoc_scan_ex(int key_dim, int value_dim, const float *keys, const float *values,
+                       const float *queries, const float *observation, const float *mean0,
+                       const float *cov0, float *out, float *mean_final, float *cov_final,
+                       int *status, long n, long t, double denominator_floor, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Reference-named float32 entry points, one set per key dimension
+ * (M = 8).  Same arguments as the reference's pybind functions, with the
+ * output buffers and the backward workspace supplied by the caller.
+ * ------------------------------------------------------------------- */
+#define BSSM_DECLARE_DIM(DN)                                                                     \
+    /* forward_chunked: persistent_bayes_chunked_d8.cu:530 and its D4/D2/D1 twins */            \
+    int bssm_d##DN##_forward_chunked(const float *keys, const float *values, const float *queries, \
+                                     const float *decay, const float *process,                  \
+                                     const float *observation, const float *mean0,              \
+                                     const float *cov0, float *out, float *mean_final,          \
+                                     float *cov_final, float *boundary_mean,                    \
+                                     float *boundary_cov, long n, long t, int chunks,           \
+                                     double denominator_floor, void *stream);                   \
+    /* forward_chunked_fixed: persistent_bayes_chunked_d8.cu:539 */                              \
+    int bssm_d##DN##_forward_chunked_fixed(const float *keys, const float *values,               \
+                                           const float *queries, const float *decay,            \
+                                           const float *process, const float *observation,      \
+                                           const float *mean0, const float *cov0, float *out,   \
+                                           float *mean_final, float *cov_final,                 \
+                                           float *boundary_mean, float *boundary_cov, long n,   \
+                                           long t, int chunks, double denominator_floor,        \
+                                           void *stream);                                       \
+    /* backward_chunked (full: 8 gradients): persistent_bayes_chunked_d8.cu:632 */               \
+    int bssm_d##DN##_backward_chunked(                                                          \
+        const float *keys, const float *values, const float *queries, const float *decay,       \
+        const float *process, const float *observation, const float *mean0, const float *cov0,  \
+        const float *boundary_mean, const float *boundary_cov, const float *grad_out,           \
+        const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,            \
+        float *grad_values, float *grad_queries, float *grad_decay, float *grad_process,        \
+        float *grad_observation, float *grad_mean0, float *grad_cov0, void *workspace,          \
+        size_t workspace_bytes, long n, long t, int chunks, double denominator_floor,           \
+        void *stream);                                                                          \
+    /* backward_chunked_lean (k, v, q gradients): persistent_bayes_chunked_d8.cu:637 */          \
+    int bssm_d##DN##_backward_chunked_lean(                                                     \
+        const float *keys, const float *values, const float *queries, const float *decay,       \
+        const float *process, const float *observation, const float *mean0, const float *cov0,  \
+        const float *boundary_mean, const float *boundary_cov, const float *grad_out,           \
+        const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,            \
+        float *grad_values, float *grad_queries, void *workspace, size_t workspace_bytes,       \
+        long n, long t, int chunks, double denominator_floor, void *stream);                    \
+    /* backward_chunked_fixed: persistent_bayes_chunked_d8.cu:648 */                             \
+    int bssm_d##DN##_backward_chunked_fixed(                                                    \
+        const float *keys, const float *values, const float *queries, const float *decay,       \
+        const float *process, const float *observation, const float *mean0, const float *cov0,  \
+        const float *boundary_mean, const float *boundary_cov, const float *grad_out,           \
+        const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,            \
+        float *grad_values, float *grad_queries, float *grad_decay, float *grad_process,        \
+        float *grad_observation, float *grad_mean0, float *grad_cov0, void *workspace,          \
+        size_t workspace_bytes, long n, long t, int chunks, double denominator_floor,           \
+        void *stream);                                                                          \
+    /* backward_chunked_lean_fixed: persistent_bayes_chunked_d8.cu:642 */                        \
+    int bssm_d##DN##_backward_chunked_lean_fixed(                                               \
+        const float *keys, const float *values, const float *queries, const float *decay,       \
+        const float *process, const float *observation, const float *mean0, const float *cov0,  \
+        const float *boundary_mean, const float *boundary_cov, const float *grad_out,           \
+        const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,            \
+        float *grad_values, float *grad_queries, void *workspace, size_t workspace_bytes,       \
+        long n, long t, int chunks, double denominator_floor, void *stream);
+
+BSSM_DECLARE_DIM(1)
+BSSM_DECLARE_DIM(2)
+BSSM_DECLARE_DIM(4)
+BSSM_DECLARE_DIM(8)
+
+/* backward_chunked_noinitial[_fixed] (6 gradients: k, v, q, decay, process,
+ * observation): persistent_bayes_chunked_d2m8.cu:576-600. */
+int bssm_d2_backward_chunked_noinitial(
+    const float *keys, const float *values, const float *queries, const float *decay,
+    const float *process, const float *observation, const float *mean0, const float *cov0,
+    const float *boundary_mean, const float *boundary_cov, const float *grad_out,
+    const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,
+    float *grad_values, float *grad_queries, float *grad_decay, float *grad_process,
+    float *grad_observation, void *workspace, size_t workspace_bytes, long n, long t,
+    int chunks, double denominator_floor, void *stream);
+int bssm_d2_backward_chunked_noinitial_fixed(
+    const float *keys, const float *values, const float *queries, const float *decay,
+    const float *process, const float *observation, const float *mean0, const float *cov0,
+    const float *boundary_mean, const float *boundary_cov, const float *grad_out,
+    const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,
+    float *grad_values, float *grad_queries, float *grad_decay, float *grad_process,
+    float *grad_observation, void *workspace, size_t workspace_bytes, long n, long t,
+    int chunks, double denominator_floor, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BAYES_SSM_B200_H */

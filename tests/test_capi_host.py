@@ -1,0 +1,83 @@
+"""CPU-side checks of the C ABI: the library loads and exports every symbol
+the header declares; argument validation fails loudly without a GPU."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = ROOT / "include" / "bayes_ssm_b200.h"
+
+
+def _declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    names = set(re.findall(r"\b(bssm_[a-z0-9_]+)\s*\(", text))
+    # expand the per-dimension macro declarations
+    macro = re.search(r"#define BSSM_DECLARE_DIM\(DN\)(.*?)\n\n", text, re.S).group(1)
+    templ = set(re.findall(r"bssm_d##DN##_([a-z_]+)\s*\(", macro))
+    for dn in re.findall(r"BSSM_DECLARE_DIM\((\d+)\)", text):
+        names |= {f"bssm_d{dn}_{t}" for t in templ}
+    names.discard("bssm_d")
+    return {n for n in names if not n.startswith("bssm_d##")}
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from bayes_ssm import _build, _capi
+    _build.build()
+    return _capi.load()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    declared = _declared_symbols()
+    assert len(declared) >= 30
+    out = subprocess.run(["nm", "-D", "--defined-only", str(Path(lib._name))], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (bssm_\w+)", out))
+    missing = declared - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+
+
+def test_version_and_last_error(lib):
+    assert lib.bssm_version() >= 10000
+    assert isinstance(lib.bssm_last_error(), bytes)
+
+
+def test_unsupported_shape_rejected_without_gpu(lib):
+    from bayes_ssm import _capi
+    rc = lib.bssm_forward_chunked_ex(3, 8, 0, 0, *([None] * 13), 1, 1, 1, 1e-6, None)
+    assert rc == 2
+    assert b"no kernel" in lib.bssm_last_error()
+    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *([None] * 13), 1, 1, 0, 1e-6, None)
+    assert rc == 1 and b"chunks" in lib.bssm_last_error()
+    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *([None] * 13), 1, 1, 4, -1.0, None)
+    assert rc == 1 and b"floor" in lib.bssm_last_error()
+    rc = lib.bssm_forward_chunked_ex(8, 8, 7, 0, *([None] * 13), 1, 1, 4, 1e-6, None)
+    assert rc == 2
+    with pytest.raises(_capi.KernelError):
+        _capi.check(rc, "probe")
+
+
+def test_null_pointers_rejected_without_gpu(lib):
+    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *([None] * 13), 4, 10, 4, 1e-6, None)
+    assert rc == 1 and b"null" in lib.bssm_last_error()
+    rc = lib.bssm_backward_chunked_ex(8, 8, 0, 0, 1, 1, *([None] * 21), None, 0, 4, 10, 4, 1e-6, None)
+    assert rc == 1
+
+
+def test_workspace_size_formula(lib):
+    # chunks <= sub-chunk length: no phase-A workspace
+    assert lib.bssm_backward_workspace_bytes(8, 8, 100, 512, 4) == 0
+    # D8: 16 floats per lane, 8 lanes, (64/4 - 1) saved states per chain
+    assert lib.bssm_backward_workspace_bytes(8, 8, 10, 512, 64) == 10 * 15 * 8 * 16 * 4
+    assert lib.bssm_backward_workspace_bytes(3, 8, 10, 512, 64) == 0
+
+
+def test_assoc_scan_limits_without_gpu(lib):
+    rc = lib.bssm_assoc_scan_ex(33, 8, *([None] * 10), 1, 1, 1e-6, None)
+    assert rc == 2 and b"key_dim" in lib.bssm_last_error()

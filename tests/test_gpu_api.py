@@ -1,0 +1,156 @@
+"""GPU: the public ``bayes_ssm`` API (autograd boundary) on the kernels, and
+the static associative scan kernel, vs the FP64 oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from harness import assert_parity, make_inputs, to_np64
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _api(inp, **kw):
+    import bayes_ssm
+    return bayes_ssm.bayesian_layer(inp["k"], inp["v"], inp["q"], transition_diagonals=inp["a"],
+                                    process_variances=inp["p"], observation_variances=inp["r"],
+                                    **kw)
+
+
+def _leaf(inp, device="cuda"):
+    return {k: (None if v is None else v.detach().to(device).requires_grad_())
+            for k, v in inp.items()}
+
+
+@pytest.mark.parametrize("d", (1, 2, 4, 8))
+def test_api_autograd_matches_oracle(d):
+    inp = _leaf(make_inputs(12, 37, d, 8, seed=d, init="random"))
+    y, mt, pt = _api(inp, initial_mean=inp["M0"], initial_covariance=inp["P0"], chunk_length=8,
+                     optimized=True)
+    loss = y.square().mean() + mt.square().mean() + pt.square().mean()
+    names = ("k", "v", "q", "a", "p", "r", "M0", "P0")
+    grads = torch.autograd.grad(loss, [inp[x] for x in names])
+    ref = oracle.forward(*[to_np64(inp[x]) for x in names])
+    assert_parity(y, ref[0], what="y")
+    gy = 2 * ref[0] / ref[0].size
+    gmt = 2 * ref[1] / ref[1].size
+    gpt = 2 * ref[2] / ref[2].size
+    rg = oracle.backward(*[to_np64(inp[x]) for x in names], gy, gmt, gpt)
+    for x, g in zip(names, grads):
+        assert_parity(g, rg[x], what=f"grad {x}")
+
+
+def test_api_bf16_projection_path_equals_promoted_fp32():
+    """BF16 k/q/v enter the kernel directly; same values as promoting first."""
+    inp = make_inputs(16, 33, 8, 8, seed=3, io_dtype=torch.bfloat16)
+    a = _leaf(inp)
+    b = {k: (None if v is None else v.detach().clone().requires_grad_()) for k, v in a.items()}
+    ya, _, _ = _api(a, chunk_length=16, optimized=True)
+    yb, _, _ = _api({**b, "k": b["k"].float(), "v": b["v"].float(), "q": b["q"].float()},
+                    chunk_length=16, optimized=True)
+    assert torch.equal(ya, yb)
+    ga = torch.autograd.grad(ya.square().sum(), [a["k"], a["v"], a["q"], a["a"]])
+    gb = torch.autograd.grad(yb.square().sum(), [b["k"], b["v"], b["q"], b["a"]])
+    for x, y in zip(ga, gb):
+        assert x.dtype == y.dtype
+        assert torch.equal(x, y)
+
+
+def test_api_batch_shape_and_broadcast_noise():
+    import bayes_ssm
+    g = torch.Generator().manual_seed(0)
+    k = torch.nn.functional.normalize(torch.randn(2, 3, 20, 4, generator=g), dim=-1).cuda()
+    v = torch.randn(2, 3, 20, 8, generator=g).cuda()
+    q = torch.nn.functional.normalize(torch.randn(2, 3, 20, 4, generator=g), dim=-1).cuda()
+    a = torch.sigmoid(torch.randn(3, 20, 4, generator=g) + 2).cuda()
+    y, mt, pt = bayes_ssm.bayesian_layer(k, v, q, transition_diagonals=a, process_variances=0.01,
+                                         observation_variances=0.5, chunk_length=6, optimized=True)
+    assert y.shape == (2, 3, 20, 8) and mt.shape == (2, 3, 4, 8) and pt.shape == (2, 3, 4, 4)
+    ae = a.expand(2, 3, 20, 4).reshape(6, 20, 4)
+    ref = oracle.forward(to_np64(k.reshape(6, 20, 4)), to_np64(v.reshape(6, 20, 8)),
+                         to_np64(q.reshape(6, 20, 4)), to_np64(ae), np.full((6, 20), 0.01),
+                         np.full((6, 20), 0.5))
+    assert_parity(y.reshape(6, 20, 8), ref[0], what="y")
+
+
+def test_replay_ssm_module_uses_kernels():
+    import bayes_ssm
+    from bayes_ssm import _capi
+    mod = bayes_ssm.ReplaySSM(8, 8, chunk_length=16).cuda()
+    inp = make_inputs(4, 40, 8, 8, seed=11)
+    k, v, q, a = (inp[x].cuda().requires_grad_() for x in ("k", "v", "q", "a"))
+    y, _, _ = mod(k, v, q, transition_diagonals=a)
+    y.square().sum().backward()
+    assert _capi._LIB is not None  # the C library served the call
+    ref = oracle.forward(to_np64(k), to_np64(v), to_np64(q), to_np64(a), np.full((4, 40), 0.05),
+                         np.full((4, 40), 0.2))
+    assert_parity(y, ref[0], what="y")
+    rg = oracle.backward(to_np64(k), to_np64(v), to_np64(q), to_np64(a), np.full((4, 40), 0.05),
+                         np.full((4, 40), 0.2), None, None, 2 * ref[0])
+    assert_parity(k.grad, rg["k"], what="grad k")
+    assert_parity(a.grad, rg["a"], what="grad a")
+
+
+def test_kernel_failure_is_loud():
+    """An unsupported kernel call raises; nothing falls back silently."""
+    from bayes_ssm.fused_cuda import fused_diagonal_bayesian
+    k = torch.randn(2, 5, 3, device="cuda")
+    with pytest.raises(ValueError, match="no kernel"):
+        fused_diagonal_bayesian(k, torch.randn(2, 5, 8, device="cuda"), k, torch.ones(2, 5, 3, device="cuda"),
+                                torch.zeros(2, 5, device="cuda"), torch.ones(2, 5, device="cuda"), None, None,
+                                chunk_length=4, denominator_floor=1e-6)
+
+
+# ----------------------------------------------------------------- assoc scan
+
+def _scan_case(name):
+    with np.load(GOLDEN / f"{name}.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.mark.parametrize("name", ["assoc_config1", "assoc_random_init", "assoc_config2_slice"])
+def test_assoc_scan_kernel_vs_reference_fixture(name):
+    import bayes_ssm
+    g = _scan_case(name)
+    t = lambda x: torch.from_numpy(g[x]).float().cuda()
+    with torch.no_grad():
+        y, mt, pt = bayes_ssm.associative_static_bayesian_cuda(
+            t("in_k"), t("in_v"), t("in_q"), observation_variances=t("in_r"),
+            initial_mean=t("in_M0"), initial_covariance=t("in_P0"))
+    assert_parity(y, g["out_y"], what="y")
+    assert_parity(mt, g["out_MT"], what="M_T")
+    assert_parity(pt, g["out_PT"], what="P_T")
+
+
+def test_assoc_scan_config2_full_vs_oracle():
+    """Config 2: B4 T64 H8 (32 chains), D = M = 16."""
+    import bayes_ssm
+    g = torch.Generator().manual_seed(2)
+    n, t, d, m = 32, 64, 16, 16
+    k = torch.randn(n, t, d, generator=g) / 4
+    q = torch.randn(n, t, d, generator=g) / 4
+    v = torch.randn(n, t, m, generator=g)
+    r = torch.nn.functional.softplus(torch.randn(n, t, generator=g)) + 1e-2
+    with torch.no_grad():
+        y, mt, pt = bayes_ssm.associative_static_bayesian_cuda(k.cuda(), v.cuda(), q.cuda(),
+                                                               observation_variances=r.cuda())
+    ry, rmt, rpt = oracle.assoc_scan(to_np64(k), to_np64(v), to_np64(q), to_np64(r))
+    assert_parity(y, ry, what="y")
+    assert_parity(mt, rmt, what="M_T")
+    assert_parity(pt, rpt, what="P_T")
+    # and the scan equals the dense recurrence it replaces
+    dy = oracle.forward(to_np64(k), to_np64(v), to_np64(q), None, None, to_np64(r))[0]
+    assert_parity(y, dy, what="y vs dense")
+
+
+def test_assoc_scan_rejects_small_variance_on_gpu():
+    import bayes_ssm
+    k = torch.randn(2, 8, 4, device="cuda")
+    r = torch.full((2, 8), 0.5, device="cuda")
+    r[1, 3] = 1e-9
+    with pytest.raises(ValueError, match="denominator_floor"):
+        bayes_ssm.associative_static_bayesian_cuda(k, torch.randn(2, 8, 3, device="cuda"), k,
+                                                   observation_variances=r)
