@@ -628,7 +628,9 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
                 float gaP = 0.f, gpk = 0.f;
 #pragma unroll
                 for (int j = 0; j < D; ++j) {
-                    const float x = gu_own * k[j] + gu[j] * k_own;
+                    // rounded products and sum, never contracted to an FMA:
+                    // lane i and lane j then form bit-identical S_ij, S_ji
+                    const float x = __fadd_rn(__fmul_rn(gu_own, k[j]), __fmul_rn(gu[j], k_own));
                     const float Sj = fmaf(0.5f, x, R[j]);
                     if constexpr (NEED_DYN) {
                         gaP = fmaf(Sj, a[j] * Pp[j], gaP);
