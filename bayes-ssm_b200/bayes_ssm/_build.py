@@ -17,7 +17,7 @@ CSRC = PKG_ROOT / "csrc"
 INCLUDE = PKG_ROOT.parent / "include"
 LIB_DIR = PKG_ROOT / "lib"
 LIB = LIB_DIR / "libbayes_ssm_b200.so"
-SOURCES = ["bssm_recurrence.cu", "bssm_assoc_scan.cu"]
+SOURCES = ["bssm_recurrence.cu", "bssm_staged.cu", "bssm_assoc_scan.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -32,7 +32,7 @@ def _stale() -> bool:
     if not LIB.exists():
         return True
     mtime = LIB.stat().st_mtime
-    deps = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    deps = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
     return any(p.stat().st_mtime > mtime for p in deps)
 
 
@@ -43,14 +43,18 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objs = []
     obj_dir = PKG_ROOT / "_build"
     obj_dir.mkdir(exist_ok=True)
-    for src in SOURCES:
+    procs = []
+    for src in SOURCES:  # one nvcc per translation unit, in parallel
         obj = obj_dir / (Path(src).stem + ".o")
         cmd = [nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC",
                "-I", str(INCLUDE), "-c", str(CSRC / src), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
-        subprocess.run(cmd, check=True)
+        procs.append((src, subprocess.Popen(cmd)))
         objs.append(str(obj))
+    failed = [src for src, proc in procs if proc.wait() != 0]
+    if failed:
+        raise RuntimeError(f"nvcc failed for {failed}")
     tmp = LIB.with_suffix(".so.tmp")
     subprocess.run([nvcc(), "-shared", *ARCH, *objs, "-o", str(tmp)], check=True)
     os.replace(tmp, LIB)

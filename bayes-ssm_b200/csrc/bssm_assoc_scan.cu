@@ -21,6 +21,7 @@
 
 #include "../../include/bayes_ssm_b200.h"
 #include "bssm_common.cuh"
+#include "bssm_internal.h"
 
 namespace bssm {
 
@@ -256,8 +257,6 @@ __global__ void __launch_bounds__(kScanThreads) assoc_scan_kernel(const ScanArgs
     }
 }
 
-extern thread_local std::string g_last_error;
-int fail(int code, const char *fmt, ...);
 
 }  // namespace bssm
 

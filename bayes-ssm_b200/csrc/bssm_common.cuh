@@ -78,6 +78,43 @@ struct LaneGroup {
             for (int v = 0; v < NV; ++v) out[v] = vals[v][0];
         }
     }
+    // Row gather: lane `sub` owns RPL consecutive entries (rows sub*RPL ..);
+    // out receives all LPC*RPL entries in row order.
+    template <int RPL>
+    __device__ __forceinline__ void gather_rows(const float (&own)[RPL], float (&out)[LPC * RPL]) const {
+#pragma unroll
+        for (int src = 0; src < LPC; ++src)
+#pragma unroll
+            for (int r = 0; r < RPL; ++r) out[src * RPL + r] = bcast(own[r], src);
+    }
+    // Reduce-scatter of NV vectors of LPC*RPL partial sums: lane `sub` ends
+    // with the group totals of entries sub*RPL .. sub*RPL+RPL-1 of each vector.
+    // Recursive halving: at the stage with partner distance h the lanes with
+    // bit h set keep the upper half of their current window.
+    template <int NV, int RPL>
+    __device__ __forceinline__ void reduce_scatter_rows(float (&vals)[NV][LPC * RPL],
+                                                        float (&out)[NV][RPL]) const {
+        if constexpr (LPC > 1) {
+#pragma unroll
+            for (int h = LPC / 2; h >= 1; h >>= 1) {
+                const bool upper = (sub & h) != 0;
+#pragma unroll
+                for (int x = 0; x < h * RPL; ++x) {
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) {
+                        const float lo = vals[v][x], hi = vals[v][x + h * RPL];
+                        const float send = upper ? lo : hi;
+                        const float keep = upper ? hi : lo;
+                        vals[v][x] = keep + xor_(send, h);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int v = 0; v < NV; ++v)
+#pragma unroll
+            for (int r = 0; r < RPL; ++r) out[v][r] = vals[v][r];
+    }
 };
 
 // v[idx] for a runtime idx without dynamic register indexing.
@@ -160,5 +197,83 @@ __device__ __forceinline__ void store_vec(__nv_bfloat16 *__restrict__ p, const f
 
 __device__ __forceinline__ void store_one(float *p, float v) { *p = v; }
 __device__ __forceinline__ void store_one(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+}  // namespace bssm
+
+namespace bssm {
+
+// ---------------------------------------------------------------------------
+// Asynchronous global -> shared copies (cp.async, L2-only for 16-byte pieces).
+// ---------------------------------------------------------------------------
+template <int G>
+__device__ __forceinline__ void cp_async(uint32_t smem_addr, const void *gptr) {
+    static_assert(G == 4 || G == 8 || G == 16, "cp.async piece size");
+    if constexpr (G == 16) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr), "l"(gptr) : "memory");
+    } else {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(smem_addr), "l"(gptr), "n"(G)
+                     : "memory");
+    }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// N consecutive elements from shared memory, widened to float.
+template <int N>
+__device__ __forceinline__ void lds_vec(const float *p, float (&o)[N]) {
+    if constexpr (N % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < N; i += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(p + i);
+            o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
+        }
+    } else if constexpr (N == 2) {
+        const float2 v = *reinterpret_cast<const float2 *>(p);
+        o[0] = v.x; o[1] = v.y;
+    } else {
+        static_assert(N == 1, "width");
+        o[0] = p[0];
+    }
+}
+template <int N>
+__device__ __forceinline__ void lds_vec(const __nv_bfloat16 *p, float (&o)[N]) {
+    if constexpr (N % 8 == 0) {
+#pragma unroll
+        for (int i = 0; i < N; i += 8) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(p + i);
+            o[i] = bf16_lo(w.x); o[i + 1] = bf16_hi(w.x); o[i + 2] = bf16_lo(w.y); o[i + 3] = bf16_hi(w.y);
+            o[i + 4] = bf16_lo(w.z); o[i + 5] = bf16_hi(w.z); o[i + 6] = bf16_lo(w.w); o[i + 7] = bf16_hi(w.w);
+        }
+    } else if constexpr (N == 4) {
+        const uint2 w = *reinterpret_cast<const uint2 *>(p);
+        o[0] = bf16_lo(w.x); o[1] = bf16_hi(w.x); o[2] = bf16_lo(w.y); o[3] = bf16_hi(w.y);
+    } else if constexpr (N == 2) {
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(p);
+        o[0] = bf16_lo(w); o[1] = bf16_hi(w);
+    } else {
+        static_assert(N == 1, "width");
+        const unsigned short h = *reinterpret_cast<const unsigned short *>(p);
+        o[0] = __uint_as_float(static_cast<uint32_t>(h) << 16);
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void sts_vec(float *p, const float (&v)[N]) {
+    if constexpr (N % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < N; i += 4)
+            *reinterpret_cast<float4 *>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else if constexpr (N == 2) {
+        *reinterpret_cast<float2 *>(p) = make_float2(v[0], v[1]);
+    } else {
+        static_assert(N == 1, "width");
+        p[0] = v[0];
+    }
+}
 
 }  // namespace bssm

@@ -1,0 +1,94 @@
+// bssm_internal.h -- declarations shared by the kernel translation units.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "../../include/bayes_ssm_b200.h"
+#include "bssm_common.cuh"
+
+namespace bssm {
+
+// Fixed-dynamics constants (A = 0.97 I, Q = 0.1 I, R = 1), as in catid/bayes-ssm
+// bayes_ssm/bayesian_layer.py:360-400.
+constexpr float kFixedDecay = 0.97f;
+constexpr float kFixedProcess = 0.1f;
+constexpr float kFixedObservation = 1.0f;
+
+template <typename TIn>
+struct FwdArgs {
+    const TIn *keys, *values, *queries;
+    const float *decay, *process, *observation, *mean0, *cov0;
+    float *out, *mean_final, *cov_final, *bmean, *bcov;
+    long n, t;
+    int chunks;
+    float floor;
+};
+
+template <typename TIn>
+struct BwdArgs {
+    const TIn *keys, *values, *queries;
+    const float *decay, *process, *observation, *mean0, *cov0;
+    const float *bmean, *bcov, *gy, *gmf, *gcf;
+    TIn *gk, *gv, *gq;
+    float *ga, *gp, *gr, *gm0, *gc0;
+    float *ws;
+    long n, t;
+    int chunks;
+    float floor;
+};
+
+// Error reporting (thread-local message behind bssm_last_error()).
+extern thread_local std::string g_last_error;
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+
+inline int check_launch(const char *what) {
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return fail(BSSM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+    g_last_error.clear();
+    return BSSM_OK;
+}
+
+// Lane's CPL columns (col0 ..) of a row-major [D, M] mean in global memory.
+template <int D, int M, int CPL>
+__device__ __forceinline__ void load_mean_cols_g(const float *base, int col0, float (&Mc)[CPL][D]) {
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+        float row[CPL];
+        load_vec<CPL>(base + i * M + col0, row);
+#pragma unroll
+        for (int l = 0; l < CPL; ++l) Mc[l][i] = row[l];
+    }
+}
+template <int D, int M, int CPL>
+__device__ __forceinline__ void store_mean_cols_g(float *base, int col0, const float (&Mc)[CPL][D]) {
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+        float row[CPL];
+#pragma unroll
+        for (int l = 0; l < CPL; ++l) row[l] = Mc[l][i];
+        store_vec<CPL>(base + i * M + col0, row);
+    }
+}
+
+// Coherent vector load, for data the same kernel wrote earlier (the phase-A
+// workspace): ld.global, never the read-only path.
+template <int N>
+__device__ __forceinline__ void load_vec_coherent(const float *p, float (&o)[N]) {
+    static_assert(N % 4 == 0, "width");
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(p + i);
+        o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
+    }
+}
+
+// Shared-memory-staged kernels (bssm_staged.cu).
+template <typename TIn> bool staged_supported(int d);
+template <typename TIn> int staged_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st);
+template <typename TIn>
+int staged_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st);
+
+}  // namespace bssm

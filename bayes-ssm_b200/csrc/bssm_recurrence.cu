@@ -30,12 +30,9 @@
 
 #include "../../include/bayes_ssm_b200.h"
 #include "bssm_common.cuh"
+#include "bssm_internal.h"
 
 namespace bssm {
-
-constexpr float kFixedDecay = 0.97f;
-constexpr float kFixedProcess = 0.1f;
-constexpr float kFixedObservation = 1.0f;
 
 // Threads per CTA for a key dimension (chains per CTA = threads / D).
 template <int D>
@@ -56,29 +53,6 @@ template <int D, int M>
 struct Slot {
     static constexpr int kLane = ((M + D) + 3) / 4 * 4;
     static constexpr int kChain = kLane * D;
-};
-
-template <typename TIn>
-struct FwdArgs {
-    const TIn *keys, *values, *queries;
-    const float *decay, *process, *observation, *mean0, *cov0;
-    float *out, *mean_final, *cov_final, *bmean, *bcov;
-    long n, t;
-    int chunks;
-    float floor;
-};
-
-template <typename TIn>
-struct BwdArgs {
-    const TIn *keys, *values, *queries;
-    const float *decay, *process, *observation, *mean0, *cov0;
-    const float *bmean, *bcov, *gy, *gmf, *gcf;
-    TIn *gk, *gv, *gq;
-    float *ga, *gp, *gr, *gm0, *gc0;
-    float *ws;
-    long n, t;
-    int chunks;
-    float floor;
 };
 
 // Per-token inputs of one lane.
@@ -461,10 +435,16 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
                 load_vec<D>(bc + ci * D * D + own * D, P);
             } else {
                 const float *slot = ws + static_cast<long>(j - 1) * SL::kChain + own * SL::kLane;
+                // written earlier by this kernel: coherent loads, not the read-only path
                 float flat[M];
-                load_vec<M>(slot, flat);
+                load_vec_coherent<M>(slot, flat);
                 unflatten_mean<D, M>(flat, Mc);
-                load_vec<D>(slot + M, P);
+                if constexpr (D % 4 == 0) {
+                    load_vec_coherent<D>(slot + M, P);
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < D; ++jj) P[jj] = slot[M + jj];
+                }
             }
             float Mstart[CPL][D];
 #pragma unroll
@@ -676,7 +656,6 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
 // ===========================================================================
 thread_local std::string g_last_error;
 
-int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char *fmt, ...) {
     char buf[512];
     va_list ap;
@@ -699,13 +678,6 @@ inline size_t vec_align(int elems, size_t elem_bytes) {
 template <int D, int M, int S>
 constexpr size_t backward_smem_bytes() {
     return static_cast<size_t>(Launch<D>::kChains) * History<D, M, S>::kFloats * sizeof(float);
-}
-
-inline int check_launch(const char *what) {
-    cudaError_t err = cudaGetLastError();
-    if (err != cudaSuccess) return fail(BSSM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
-    g_last_error.clear();
-    return BSSM_OK;
 }
 
 template <int D, int M, bool FIXED, typename TIn>
@@ -769,8 +741,21 @@ inline size_t workspace_bytes(int d, int m, long n, long t, int chunks) {
 
 inline bool supported(int d, int m) { return m == 8 && (d == 1 || d == 2 || d == 4 || d == 8); }
 
+// Kernel family: the shared-memory-staged kernels (bssm_staged.cu) serve
+// every shape they support; BSSM_KERNELS=v1 selects the per-lane-load kernels
+// of this file instead (kept as a second, independently written path that the
+// tests cross-check).
+inline bool use_v1() {
+    static const bool v1 = [] {
+        const char *e = std::getenv("BSSM_KERNELS");
+        return e != nullptr && std::strcmp(e, "v1") == 0;
+    }();
+    return v1;
+}
+
 template <typename TIn>
 int forward_dispatch(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
+    if (!use_v1() && staged_supported<TIn>(d)) return staged_forward<TIn>(d, fixed, a, st);
     switch (d) {
         case 1: return fixed ? launch_forward<1, 8, true>(a, st) : launch_forward<1, 8, false>(a, st);
         case 2: return fixed ? launch_forward<2, 8, true>(a, st) : launch_forward<2, 8, false>(a, st);
@@ -782,6 +767,7 @@ int forward_dispatch(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
 
 template <typename TIn>
 int backward_dispatch(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
+    if (!use_v1() && a.t > 0 && staged_supported<TIn>(d)) return staged_backward<TIn>(d, fixed, dyn, init, a, st);
     switch (d) {
         case 1: return fixed ? launch_backward<1, 8, true>(a, dyn, init, st)
                              : launch_backward<1, 8, false>(a, dyn, init, st);
