@@ -36,9 +36,11 @@ _vp, _l, _i, _d, _sz = ctypes.c_void_p, ctypes.c_long, ctypes.c_int, ctypes.c_do
 _SIGNATURES = {
     "bssm_last_error": ([], ctypes.c_char_p),
     "bssm_version": ([], _i),
-    "bssm_forward_chunked_ex": ([_i, _i, _i, _i] + [_vp] * 13 + [_l, _l, _i, _d, _vp], _i),
+    "bssm_forward_chunked_ex": ([_i, _i, _i, _i] + [_vp] * 13 + [_vp, _sz, _l, _l, _i, _d, _vp], _i),
+    "bssm_replay_states_bytes": ([_i, _i, _l, _l, _i], _sz),
     "bssm_backward_workspace_bytes": ([_i, _i, _l, _l, _i], _sz),
-    "bssm_backward_chunked_ex": ([_i, _i, _i, _i, _i, _i] + [_vp] * 21 + [_vp, _sz, _l, _l, _i, _d, _vp], _i),
+    "bssm_backward_chunked_ex": ([_i, _i, _i, _i, _i, _i] + [_vp] * 10 + [_vp, _sz] + [_vp] * 11
+                                 + [_vp, _sz, _l, _l, _i, _d, _vp], _i),
     "bssm_assoc_scan_ex": ([_i, _i] + [_vp] * 10 + [_l, _l, _d, _vp], _i),
 }
 
@@ -80,13 +82,19 @@ def ptr(t) -> Optional[int]:
 
 def forward_chunked(key_dim, value_dim, io_dtype, fixed, keys, values, queries, decay, process,
                     observation, mean0, cov0, out, mean_final, cov_final, bmean, bcov, n, t,
-                    chunks, floor, stream) -> None:
+                    chunks, floor, stream, replay_states=None) -> None:
     lib = load()
+    rs_bytes = 0 if replay_states is None else replay_states.numel() * replay_states.element_size()
     rc = lib.bssm_forward_chunked_ex(
         key_dim, value_dim, io_dtype, int(fixed), ptr(keys), ptr(values), ptr(queries), ptr(decay),
         ptr(process), ptr(observation), ptr(mean0), ptr(cov0), ptr(out), ptr(mean_final),
-        ptr(cov_final), ptr(bmean), ptr(bcov), n, t, chunks, float(floor), stream)
+        ptr(cov_final), ptr(bmean), ptr(bcov), ptr(replay_states), rs_bytes, n, t, chunks,
+        float(floor), stream)
     check(rc, "bssm_forward_chunked_ex")
+
+
+def replay_states_bytes(key_dim, value_dim, n, t, chunks) -> int:
+    return int(load().bssm_replay_states_bytes(key_dim, value_dim, n, t, chunks))
 
 
 def workspace_bytes(key_dim, value_dim, n, t, chunks) -> int:
@@ -96,14 +104,15 @@ def workspace_bytes(key_dim, value_dim, n, t, chunks) -> int:
 def backward_chunked(key_dim, value_dim, io_dtype, fixed, need_dynamics, need_initial, keys, values,
                      queries, decay, process, observation, mean0, cov0, bmean, bcov, gy, gmf, gcf,
                      gk, gv, gq, gd, gp, gr, gm0, gc0, workspace, workspace_nbytes, n, t, chunks,
-                     floor, stream) -> None:
+                     floor, stream, replay_states=None) -> None:
     lib = load()
+    rs_bytes = 0 if replay_states is None else replay_states.numel() * replay_states.element_size()
     rc = lib.bssm_backward_chunked_ex(
         key_dim, value_dim, io_dtype, int(fixed), int(need_dynamics), int(need_initial), ptr(keys),
         ptr(values), ptr(queries), ptr(decay), ptr(process), ptr(observation), ptr(mean0), ptr(cov0),
-        ptr(bmean), ptr(bcov), ptr(gy), ptr(gmf), ptr(gcf), ptr(gk), ptr(gv), ptr(gq), ptr(gd),
-        ptr(gp), ptr(gr), ptr(gm0), ptr(gc0), ptr(workspace), workspace_nbytes, n, t, chunks,
-        float(floor), stream)
+        ptr(bmean), ptr(bcov), ptr(replay_states), rs_bytes, ptr(gy), ptr(gmf), ptr(gcf), ptr(gk),
+        ptr(gv), ptr(gq), ptr(gd), ptr(gp), ptr(gr), ptr(gm0), ptr(gc0), ptr(workspace),
+        workspace_nbytes, n, t, chunks, float(floor), stream)
     check(rc, "bssm_backward_chunked_ex")
 
 

@@ -17,6 +17,7 @@ Differences from the reference boundary, all deliberate:
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -33,6 +34,10 @@ def _io_dtype(dtype: torch.dtype) -> int:
     if dtype == torch.bfloat16:
         return _capi.BSSM_BF16
     raise TypeError(f"fused Bayesian kernels take float32 or bfloat16 keys/values/queries, got {dtype}")
+
+
+def _save_replay_states() -> bool:
+    return os.environ.get("BAYES_SSM_SAVE_REPLAY_STATES", "1") != "0"
 
 
 def _stream(device: torch.device) -> int:
@@ -56,6 +61,15 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
         cov_final = torch.empty(n, d, d, **f32)
         bmean = torch.empty(n, nb + 1, d, m, **f32)
         bcov = torch.empty(n, nb + 1, d, d, **f32)
+        # Replay states: the forward also saves the state every 4 tokens inside
+        # each chunk so the backward replays 4-token spans without first
+        # recomputing the chunk (memory N*T/4*(D*M+D*D)*4 bytes; set
+        # BAYES_SSM_SAVE_REPLAY_STATES=0 to trade it for that recomputation).
+        rs = None
+        if _save_replay_states() and any(ctx.needs_input_grad[:8]):
+            rs_bytes = _capi.replay_states_bytes(d, m, n, t, int(chunk_length))
+            if rs_bytes:
+                rs = torch.empty(rs_bytes // 4, **f32)
         with torch.cuda.device(dev):
             _capi.forward_chunked(d, m, _io_dtype(keys.dtype), fixed_dynamics, keys, values, queries,
                                   None if fixed_dynamics else decay,
@@ -63,8 +77,8 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
                                   None if fixed_dynamics else observation,
                                   initial_mean, initial_covariance, out, mean_final, cov_final,
                                   bmean, bcov, n, t, int(chunk_length), denominator_floor,
-                                  _stream(dev))
-        ctx.save_for_backward(keys, values, queries, decay, process, observation, bmean, bcov)
+                                  _stream(dev), replay_states=rs)
+        ctx.save_for_backward(keys, values, queries, decay, process, observation, bmean, bcov, rs)
         ctx.chunk_length = int(chunk_length)
         ctx.denominator_floor = float(denominator_floor)
         ctx.fixed_dynamics = bool(fixed_dynamics)
@@ -73,7 +87,7 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out, grad_mean, grad_cov):
-        keys, values, queries, decay, process, observation, bmean, bcov = ctx.saved_tensors
+        keys, values, queries, decay, process, observation, bmean, bcov, rs = ctx.saved_tensors
         n, t, d = keys.shape
         m = values.shape[-1]
         dev = keys.device
@@ -92,7 +106,7 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
         gr = torch.empty(n, t, **f32) if need_dyn else None
         gm0 = torch.empty(n, d, m, **f32) if need_init else None
         gc0 = torch.empty(n, d, d, **f32) if need_init else None
-        ws_bytes = _capi.workspace_bytes(d, m, n, t, ctx.chunk_length)
+        ws_bytes = 0 if rs is not None else _capi.workspace_bytes(d, m, n, t, ctx.chunk_length)
         ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
         fixed = ctx.fixed_dynamics
         with torch.cuda.device(dev):
@@ -101,7 +115,7 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
                                    None if fixed else process, None if fixed else observation,
                                    None, None, bmean, bcov, gy, gmf, gcf, gk, gv, gq, gd, gp, gr,
                                    gm0, gc0, ws, ws_bytes, n, t, ctx.chunk_length,
-                                   ctx.denominator_floor, _stream(dev))
+                                   ctx.denominator_floor, _stream(dev), replay_states=rs)
         return (gk if needs[0] else None, gv if needs[1] else None, gq if needs[2] else None,
                 gd if needs[3] else None, gp if needs[4] else None, gr if needs[5] else None,
                 gm0 if needs[6] else None, gc0 if needs[7] else None, None, None, None)

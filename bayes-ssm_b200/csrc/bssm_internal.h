@@ -22,6 +22,7 @@ struct FwdArgs {
     const TIn *keys, *values, *queries;
     const float *decay, *process, *observation, *mean0, *cov0;
     float *out, *mean_final, *cov_final, *bmean, *bcov;
+    float *rs;  // replay states (nullptr: not saved)
     long n, t;
     int chunks;
     float floor;
@@ -35,10 +36,25 @@ struct BwdArgs {
     TIn *gk, *gv, *gq;
     float *ga, *gp, *gr, *gm0, *gc0;
     float *ws;
+    const float *rs;  // replay states saved by the forward (nullptr: phase A recomputes them)
     long n, t;
     int chunks;
     float floor;
 };
+
+// Replay states: the state at every kReplaySpan-token boundary inside each
+// chunk (not at the chunk start, which is the boundary checkpoint).  Layout
+// per chain: [chunk][slot][mean D*M row-major | covariance D*D row-major].
+constexpr int kReplaySpan = 4;
+__host__ __device__ inline long replay_slots_per_chunk(long t, int chunks) {
+    const long span = chunks < t ? chunks : t;
+    const long nsub = (span + kReplaySpan - 1) / kReplaySpan;
+    return nsub > 1 ? nsub - 1 : 0;
+}
+__host__ __device__ inline float *replay_slot(const float *rs, long chain, long nb, long slots, long ci,
+                                              long j, int d, int m) {
+    return const_cast<float *>(rs) + ((chain * nb + ci) * slots + (j - 1)) * static_cast<long>(d * m + d * d);
+}
 
 // Error reporting (thread-local message behind bssm_last_error()).
 extern thread_local std::string g_last_error;

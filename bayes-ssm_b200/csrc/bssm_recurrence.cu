@@ -229,11 +229,16 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
                                              A.observation, nullptr, chain * T, col0);
     int in_chunk = 0;
     long c = 0;
+    const long rs_slots = replay_slots_per_chunk(T, L);
     for (long ti = 0; ti < T; ++ti) {
         if (in_chunk == 0) {
             store_mean_cols<D, M>(bm + c * D * M, col0, Mc);
             store_vec<D>(bc + c * D * D + own * D, P);
             ++c;
+        } else if (A.rs != nullptr && in_chunk % kReplaySpan == 0) {
+            float *slot = replay_slot(A.rs, chain, nb, rs_slots, c - 1, in_chunk / kReplaySpan, D, M);
+            store_mean_cols<D, M>(slot, col0, Mc);
+            store_vec<D>(slot + D * M + own * D, P);
         }
         if (++in_chunk == L) in_chunk = 0;
         const long row = chain * T + ti;
@@ -397,7 +402,8 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
         const int nsub = (len + S - 1) / S;
 
         // ---- phase A: states at sub-chunk starts 1 .. nsub-1 -> workspace
-        if (nsub > 1) {
+        // (skipped when the forward saved them)
+        if (nsub > 1 && A.rs == nullptr) {
             float Mc[CPL][D], P[D];
             load_mean_cols<D, M>(bm + ci * D * M, col0, Mc);
             load_vec<D>(bc + ci * D * D + own * D, P);
@@ -433,6 +439,10 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
             if (j == 0) {
                 load_mean_cols<D, M>(bm + ci * D * M, col0, Mc);
                 load_vec<D>(bc + ci * D * D + own * D, P);
+            } else if (A.rs != nullptr) {
+                const float *slot = replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j, D, M);
+                load_mean_cols<D, M>(slot, col0, Mc);
+                load_vec<D>(slot + D * M + own * D, P);
             } else {
                 const float *slot = ws + static_cast<long>(j - 1) * SL::kChain + own * SL::kLane;
                 // written earlier by this kernel: coherent loads, not the read-only path
@@ -741,6 +751,14 @@ inline size_t workspace_bytes(int d, int m, long n, long t, int chunks) {
 
 inline bool supported(int d, int m) { return m == 8 && (d == 1 || d == 2 || d == 4 || d == 8); }
 
+inline size_t replay_bytes(int d, int m, long n, long t, int chunks) {
+    if (n <= 0 || t <= 0 || chunks <= 0) return 0;
+    const long nb = (t + chunks - 1) / chunks;
+    return static_cast<size_t>(n) * static_cast<size_t>(nb) *
+           static_cast<size_t>(replay_slots_per_chunk(t, chunks)) * static_cast<size_t>(d * m + d * d) *
+           sizeof(float);
+}
+
 // Kernel family: the shared-memory-staged kernels (bssm_staged.cu) serve
 // every shape they support; BSSM_KERNELS=v1 selects the per-lane-load kernels
 // of this file instead (kept as a second, independently written path that the
@@ -808,7 +826,8 @@ int bssm_forward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed,
                             const void *values, const void *queries, const float *decay,
                             const float *process, const float *observation, const float *mean0,
                             const float *cov0, float *out, float *mean_final, float *cov_final,
-                            float *boundary_mean, float *boundary_cov, long n, long t, int chunks,
+                            float *boundary_mean, float *boundary_cov, float *replay_states,
+                            size_t replay_states_bytes, long n, long t, int chunks,
                             double denominator_floor, void *stream) {
     int rc = validate_common(key_dim, value_dim, io_dtype, n, t, chunks, denominator_floor);
     if (rc) return rc;
@@ -818,6 +837,11 @@ int bssm_forward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed,
     }
     if (!mean_final || !cov_final || !boundary_mean || !boundary_cov)
         return fail(BSSM_ERR_INVALID, "forward: null output pointer");
+    const size_t rs_need = replay_bytes(key_dim, value_dim, n, t, chunks);
+    if (rs_need == 0) replay_states = nullptr;  // nothing to save (chunks <= the replay span)
+    if (replay_states != nullptr && replay_states_bytes < rs_need)
+        return fail(BSSM_ERR_WORKSPACE, "forward: replay_states of %zu bytes required (got %zu)", rs_need,
+                    replay_states_bytes);
     if (t > 0 && (!keys || !values || !queries || !out))
         return fail(BSSM_ERR_INVALID, "forward: null keys/values/queries/out");
     if (!fixed && t > 0 && (!decay || !process || !observation))
@@ -828,22 +852,28 @@ int bssm_forward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed,
         !aligned(values, vec_align(cpl, esz)) || !aligned(decay, vec_align(key_dim, 4)) ||
         !aligned(out, vec_align(cpl, 4)) || !aligned(mean_final, 16) || !aligned(boundary_mean, 16) ||
         !aligned(cov_final, vec_align(key_dim, 4)) || !aligned(boundary_cov, vec_align(key_dim, 4)) ||
-        !aligned(mean0, vec_align(cpl, 4)))
+        !aligned(mean0, vec_align(cpl, 4)) || !aligned(replay_states, 16))
         return fail(BSSM_ERR_ALIGNMENT, "forward: misaligned pointer");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const float fl = static_cast<float>(denominator_floor);
     if (io_dtype == BSSM_F32) {
         FwdArgs<float> a{static_cast<const float *>(keys), static_cast<const float *>(values),
                          static_cast<const float *>(queries), decay, process, observation, mean0, cov0,
-                         out, mean_final, cov_final, boundary_mean, boundary_cov, n, t, chunks, fl};
+                         out, mean_final, cov_final, boundary_mean, boundary_cov, replay_states, n, t,
+                         chunks, fl};
         return forward_dispatch(key_dim, fixed, a, st);
     }
     FwdArgs<__nv_bfloat16> a{static_cast<const __nv_bfloat16 *>(keys),
                              static_cast<const __nv_bfloat16 *>(values),
                              static_cast<const __nv_bfloat16 *>(queries), decay, process, observation,
-                             mean0, cov0, out, mean_final, cov_final, boundary_mean, boundary_cov, n, t,
-                             chunks, fl};
+                             mean0, cov0, out, mean_final, cov_final, boundary_mean, boundary_cov,
+                             replay_states, n, t, chunks, fl};
     return forward_dispatch(key_dim, fixed, a, st);
+}
+
+size_t bssm_replay_states_bytes(int key_dim, int value_dim, long n, long t, int chunks) {
+    if (!supported(key_dim, value_dim)) return 0;
+    return replay_bytes(key_dim, value_dim, n, t, chunks);
 }
 
 size_t bssm_backward_workspace_bytes(int key_dim, int value_dim, long n, long t, int chunks) {
@@ -856,6 +886,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                              const void *queries, const float *decay, const float *process,
                              const float *observation, const float *mean0, const float *cov0,
                              const float *boundary_mean, const float *boundary_cov,
+                             const float *replay_states, size_t replay_states_bytes,
                              const float *grad_out, const float *grad_mean_final,
                              const float *grad_cov_final, void *grad_keys, void *grad_values,
                              void *grad_queries, float *grad_decay, float *grad_process,
@@ -886,7 +917,13 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         return fail(BSSM_ERR_INVALID, "backward: decay/process/observation required unless fixed");
     if (dyn && t > 0 && (!grad_decay || !grad_process || !grad_observation))
         return fail(BSSM_ERR_INVALID, "backward: need_dynamics requires grad_decay/process/observation");
-    const size_t need = workspace_bytes(key_dim, value_dim, n, t, chunks);
+    const size_t rs_need = replay_bytes(key_dim, value_dim, n, t, chunks);
+    if (rs_need == 0) replay_states = nullptr;
+    if (replay_states != nullptr && replay_states_bytes < rs_need)
+        return fail(BSSM_ERR_WORKSPACE, "backward: replay_states of %zu bytes required (got %zu)", rs_need,
+                    replay_states_bytes);
+    // the phase-A workspace is needed only when the replay states were not saved
+    const size_t need = replay_states ? 0 : workspace_bytes(key_dim, value_dim, n, t, chunks);
     if (need > 0 && (workspace == nullptr || workspace_bytes_ < need))
         return fail(BSSM_ERR_WORKSPACE, "backward: workspace of %zu bytes required (got %zu)", need,
                     workspace_bytes_);
@@ -897,7 +934,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         !aligned(grad_out, vec_align(cpl, 4)) || !aligned(grad_values, vec_align(cpl, esz)) ||
         !aligned(boundary_mean, 16) || !aligned(boundary_cov, vec_align(key_dim, 4)) ||
         !aligned(grad_mean_final, vec_align(cpl, 4)) || !aligned(grad_mean0, vec_align(cpl, 4)) ||
-        !aligned(grad_cov0, vec_align(key_dim, 4)) || !aligned(workspace, 16))
+        !aligned(grad_cov0, vec_align(key_dim, 4)) || !aligned(workspace, 16) || !aligned(replay_states, 16))
         return fail(BSSM_ERR_ALIGNMENT, "backward: misaligned pointer");
     const float fl = static_cast<float>(denominator_floor);
     float *ws = static_cast<float *>(workspace);
@@ -907,7 +944,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                          boundary_mean, boundary_cov, grad_out, grad_mean_final, grad_cov_final,
                          static_cast<float *>(grad_keys), static_cast<float *>(grad_values),
                          static_cast<float *>(grad_queries), grad_decay, grad_process, grad_observation,
-                         grad_mean0, grad_cov0, ws, n, t, chunks, fl};
+                         grad_mean0, grad_cov0, ws, replay_states, n, t, chunks, fl};
         return backward_dispatch(key_dim, fixed, dyn, init, a, st);
     }
     BwdArgs<__nv_bfloat16> a{static_cast<const __nv_bfloat16 *>(keys),
@@ -917,7 +954,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                              grad_cov_final, static_cast<__nv_bfloat16 *>(grad_keys),
                              static_cast<__nv_bfloat16 *>(grad_values),
                              static_cast<__nv_bfloat16 *>(grad_queries), grad_decay, grad_process,
-                             grad_observation, grad_mean0, grad_cov0, ws, n, t, chunks, fl};
+                             grad_observation, grad_mean0, grad_cov0, ws, replay_states, n, t, chunks, fl};
     return backward_dispatch(key_dim, fixed, dyn, init, a, st);
 }
 
@@ -932,7 +969,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                                      void *stream) {                                               \
         return bssm_forward_chunked_ex(DN, 8, BSSM_F32, 0, keys, values, queries, decay, process,  \
                                        observation, mean0, cov0, out, mean_final, cov_final,       \
-                                       boundary_mean, boundary_cov, n, t, chunks,                  \
+                                       boundary_mean, boundary_cov, nullptr, 0, n, t, chunks,      \
                                        denominator_floor, stream);                                 \
     }                                                                                              \
     int bssm_d##DN##_forward_chunked_fixed(const float *keys, const float *values,                 \
@@ -945,7 +982,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                                            void *stream) {                                         \
         return bssm_forward_chunked_ex(DN, 8, BSSM_F32, 1, keys, values, queries, decay, process,  \
                                        observation, mean0, cov0, out, mean_final, cov_final,       \
-                                       boundary_mean, boundary_cov, n, t, chunks,                  \
+                                       boundary_mean, boundary_cov, nullptr, 0, n, t, chunks,      \
                                        denominator_floor, stream);                                 \
     }                                                                                              \
     int bssm_d##DN##_backward_chunked(                                                             \
@@ -959,7 +996,8 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         void *stream) {                                                                            \
         return bssm_backward_chunked_ex(DN, 8, BSSM_F32, 0, 1, 1, keys, values, queries, decay,    \
                                         process, observation, mean0, cov0, boundary_mean,          \
-                                        boundary_cov, grad_out, grad_mean_final, grad_cov_final,   \
+                                        boundary_cov, nullptr, 0, grad_out, grad_mean_final,       \
+                                        grad_cov_final,                                            \
                                         grad_keys, grad_values, grad_queries, grad_decay,          \
                                         grad_process, grad_observation, grad_mean0, grad_cov0,     \
                                         workspace, workspace_bytes, n, t, chunks,                  \
@@ -974,7 +1012,8 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         long t, int chunks, double denominator_floor, void *stream) {                              \
         return bssm_backward_chunked_ex(DN, 8, BSSM_F32, 0, 0, 0, keys, values, queries, decay,    \
                                         process, observation, mean0, cov0, boundary_mean,          \
-                                        boundary_cov, grad_out, grad_mean_final, grad_cov_final,   \
+                                        boundary_cov, nullptr, 0, grad_out, grad_mean_final,       \
+                                        grad_cov_final,                                            \
                                         grad_keys, grad_values, grad_queries, nullptr, nullptr,    \
                                         nullptr, nullptr, nullptr, workspace, workspace_bytes, n,  \
                                         t, chunks, denominator_floor, stream);                     \
@@ -990,7 +1029,8 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         void *stream) {                                                                            \
         return bssm_backward_chunked_ex(DN, 8, BSSM_F32, 1, 1, 1, keys, values, queries, decay,    \
                                         process, observation, mean0, cov0, boundary_mean,          \
-                                        boundary_cov, grad_out, grad_mean_final, grad_cov_final,   \
+                                        boundary_cov, nullptr, 0, grad_out, grad_mean_final,       \
+                                        grad_cov_final,                                            \
                                         grad_keys, grad_values, grad_queries, grad_decay,          \
                                         grad_process, grad_observation, grad_mean0, grad_cov0,     \
                                         workspace, workspace_bytes, n, t, chunks,                  \
@@ -1005,7 +1045,8 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         long t, int chunks, double denominator_floor, void *stream) {                              \
         return bssm_backward_chunked_ex(DN, 8, BSSM_F32, 1, 0, 0, keys, values, queries, decay,    \
                                         process, observation, mean0, cov0, boundary_mean,          \
-                                        boundary_cov, grad_out, grad_mean_final, grad_cov_final,   \
+                                        boundary_cov, nullptr, 0, grad_out, grad_mean_final,       \
+                                        grad_cov_final,                                            \
                                         grad_keys, grad_values, grad_queries, nullptr, nullptr,    \
                                         nullptr, nullptr, nullptr, workspace, workspace_bytes, n,  \
                                         t, chunks, denominator_floor, stream);                     \
@@ -1025,8 +1066,8 @@ int bssm_d2_backward_chunked_noinitial(
     void *workspace, size_t workspace_bytes, long n, long t, int chunks, double denominator_floor,
     void *stream) {
     return bssm_backward_chunked_ex(2, 8, BSSM_F32, 0, 1, 0, keys, values, queries, decay, process,
-                                    observation, mean0, cov0, boundary_mean, boundary_cov, grad_out,
-                                    grad_mean_final, grad_cov_final, grad_keys, grad_values,
+                                    observation, mean0, cov0, boundary_mean, boundary_cov, nullptr, 0,
+                                    grad_out, grad_mean_final, grad_cov_final, grad_keys, grad_values,
                                     grad_queries, grad_decay, grad_process, grad_observation,
                                     nullptr, nullptr, workspace, workspace_bytes, n, t, chunks,
                                     denominator_floor, stream);
@@ -1041,8 +1082,8 @@ int bssm_d2_backward_chunked_noinitial_fixed(
     void *workspace, size_t workspace_bytes, long n, long t, int chunks, double denominator_floor,
     void *stream) {
     return bssm_backward_chunked_ex(2, 8, BSSM_F32, 1, 1, 0, keys, values, queries, decay, process,
-                                    observation, mean0, cov0, boundary_mean, boundary_cov, grad_out,
-                                    grad_mean_final, grad_cov_final, grad_keys, grad_values,
+                                    observation, mean0, cov0, boundary_mean, boundary_cov, nullptr, 0,
+                                    grad_out, grad_mean_final, grad_cov_final, grad_keys, grad_values,
                                     grad_queries, grad_decay, grad_process, grad_observation,
                                     nullptr, nullptr, workspace, workspace_bytes, n, t, chunks,
                                     denominator_floor, stream);

@@ -270,6 +270,7 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
         cp_async_commit();
     }
     long ckpt = 0;
+    const long rs_slots = replay_slots_per_chunk(T, L);
     for (long q = 0; q < ntile; ++q) {
         const long qn = q + kStages - 1;
         if (qn < ntile)
@@ -291,6 +292,14 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
                     for (int r = 0; r < RPL; ++r) store_vec<D>(bc + ckpt * D * D + (row0 + r) * D, P[r]);
                 }
                 ++ckpt;
+            } else if (A.rs != nullptr && (t - (ckpt - 1) * L) % kReplaySpan == 0) {
+                if (active) {
+                    float *slot = replay_slot(A.rs, chain, nb, rs_slots, ckpt - 1,
+                                              (t - (ckpt - 1) * L) / kReplaySpan, D, M);
+                    store_mean_cols_g<D, M, CPL>(slot, col0, Mc);
+#pragma unroll
+                    for (int r = 0; r < RPL; ++r) store_vec<D>(slot + D * M + (row0 + r) * D, P[r]);
+                }
             }
             Tok<D, M, LPC> tk;
             read_tok<D, M, LPC, FIXED, TIn>(stage, c, tau, sub, tk);
@@ -332,14 +341,14 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
 struct Schedule {
     long ci;
     int phase, j, nsub, len;
-    bool done;
+    bool done, skipA;
     long T;
     int L;
     __device__ __forceinline__ void enter_chunk() {
         const long t0 = ci * L;
         len = static_cast<int>((T - t0) < L ? (T - t0) : L);
         nsub = (len + kS - 1) / kS;
-        if (nsub > 1) {
+        if (nsub > 1 && !skipA) {
             phase = kPhaseA;
             j = 0;
         } else {
@@ -347,9 +356,10 @@ struct Schedule {
             j = nsub - 1;
         }
     }
-    __device__ __forceinline__ void init(long T_, int L_) {
+    __device__ __forceinline__ void init(long T_, int L_, bool skipA_) {
         T = T_;
         L = L_;
+        skipA = skipA_;
         ci = (T + L - 1) / L - 1;
         done = ci < 0;
         if (!done) enter_chunk();
@@ -417,8 +427,9 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
             for (int j = 0; j < D; ++j) R[r][j] = 0.5f * (gc[(row0 + r) * D + j] + gc[j * D + row0 + r]);
     }
 
+    const bool have_rs = A.rs != nullptr;
     Schedule prod;
-    prod.init(T, L);
+    prod.init(T, L, have_rs);
 #pragma unroll
     for (int s = 0; s < kStages - 1; ++s) {
         if (!prod.done) {
@@ -446,8 +457,8 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
         const int len = static_cast<int>((T - t0c) < L ? (T - t0c) : L);
         const int nsub = (len + kS - 1) / kS;
 
-        // ---- phase A
-        if (nsub > 1) {
+        // ---- phase A (skipped when the forward saved the replay states)
+        if (nsub > 1 && !have_rs) {
             float Mc[CPL][D], P[RPL][D];
             if (active) {
                 load_mean_cols_g<D, M, CPL>(bm + ci * D * M, col0, Mc);
@@ -509,6 +520,11 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                 load_mean_cols_g<D, M, CPL>(bm + ci * D * M, col0, Mc);
 #pragma unroll
                 for (int r = 0; r < RPL; ++r) load_vec<D>(bc + ci * D * D + (row0 + r) * D, P[r]);
+            } else if (have_rs) {
+                const float *slot = replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j, D, M);
+                load_mean_cols_g<D, M, CPL>(slot, col0, Mc);
+#pragma unroll
+                for (int r = 0; r < RPL; ++r) load_vec<D>(slot + D * M + (row0 + r) * D, P[r]);
             } else {
                 // written by this kernel in phase A: coherent loads
                 float flat[G::kWsLane];
@@ -547,7 +563,13 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                 if (sub == 0) *reinterpret_cast<float2 *>(hist + G::hB + tau * 4) = make_float2(beta, s);
             }
             __syncwarp();
-            // Mc now holds the post-update mean of the sub-chunk's last token
+            // Mc holds the post-update mean of the sub-chunk's last token; after
+            // each reverse step Mn takes that step's pre-update mean
+            float Mn[CPL][D];
+#pragma unroll
+            for (int l = 0; l < CPL; ++l)
+#pragma unroll
+                for (int i = 0; i < D; ++i) Mn[l][i] = Mc[l][i];
             for (int tau = slen - 1; tau >= 0; --tau) {
                 const long row = chain * T + ci * L + static_cast<long>(j) * kS + tau;
                 float k[D], a[D], q[D], u[D], k_own[RPL], a_own[RPL], u_own[RPL];
@@ -581,7 +603,7 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 #pragma unroll
                     for (int l = 0; l < CPL; ++l) gyv[l] = 0.f;
                 }
-                float Mp[CPL][D], Mn[CPL][D], Pp[RPL][D];
+                float Mp[CPL][D], Pp[RPL][D];
                 {
                     float flat[G::hMB];
                     get_block<G::hMB, LPC>(hist + G::hM + tau * M * D, sub, flat);
@@ -589,18 +611,6 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                     for (int l = 0; l < CPL; ++l)
 #pragma unroll
                         for (int i = 0; i < D; ++i) Mp[l][i] = flat[l * D + i];
-                    if (tau + 1 < slen) {
-                        get_block<G::hMB, LPC>(hist + G::hM + (tau + 1) * M * D, sub, flat);
-#pragma unroll
-                        for (int l = 0; l < CPL; ++l)
-#pragma unroll
-                            for (int i = 0; i < D; ++i) Mn[l][i] = flat[l * D + i];
-                    } else {
-#pragma unroll
-                        for (int l = 0; l < CPL; ++l)
-#pragma unroll
-                            for (int i = 0; i < D; ++i) Mn[l][i] = Mc[l][i];
-                    }
                     float pf[G::hPB];
                     get_block<G::hPB, LPC>(hist + G::hP + tau * D * D, sub, pf);
 #pragma unroll
@@ -748,6 +758,10 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                         }
                     }
                 }
+#pragma unroll
+                for (int l = 0; l < CPL; ++l)
+#pragma unroll
+                    for (int i = 0; i < D; ++i) Mn[l][i] = Mp[l][i];
             }
             __syncwarp();
             ++qc;

@@ -271,20 +271,24 @@ def main() -> None:
     gd = torch.empty(n, T, D, **f32)
     gp = torch.empty(n, T, **f32)
     gr = torch.empty(n, T, **f32)
-    ws_bytes = _capi.workspace_bytes(D, M, n, T, CHUNK)
-    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+    # replay states: saved by the forward every 4 tokens inside each chunk, so
+    # the backward needs no phase-A recomputation and no workspace
+    rs_bytes = _capi.replay_states_bytes(D, M, n, T, CHUNK)
+    rs = torch.empty(max(rs_bytes // 4, 1), device=dev, dtype=torch.float32)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     io = _capi.BSSM_BF16
 
     def fwd():
         _capi.forward_chunked(D, M, io, False, inp["k"], inp["v"], inp["q"], inp["a"], inp["p"],
-                              inp["r"], None, None, out, mt, pt, bm, bc, n, T, CHUNK, FLOOR, sp)
+                              inp["r"], None, None, out, mt, pt, bm, bc, n, T, CHUNK, FLOOR, sp,
+                              replay_states=rs)
 
     def bwd():
         _capi.backward_chunked(D, M, io, False, True, False, inp["k"], inp["v"], inp["q"], inp["a"],
                                inp["p"], inp["r"], None, None, bm, bc, inp["gy"], None, None, gk, gv,
-                               gq, gd, gp, gr, None, None, ws, ws_bytes, n, T, CHUNK, FLOOR, sp)
+                               gq, gd, gp, gr, None, None, None, 0, n, T, CHUNK, FLOOR, sp,
+                               replay_states=rs)
 
     for _ in range(args.warmup):
         fwd()

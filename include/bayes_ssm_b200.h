@@ -60,6 +60,10 @@ int bssm_version(void);
  * backward replays from.  fixed != 0 ignores decay/process/observation (may
  * be NULL) and uses A = 0.97 I, Q = 0.1 I, R = 1.  mean0 == NULL means zeros,
  * cov0 == NULL means identity.  The covariance enters as (cov0 + cov0^T)/2.
+ * replay_states (optional, may be NULL): when given, the forward also saves
+ * the state at every 4-token boundary inside each chunk
+ * (bssm_replay_states_bytes(...) bytes); a backward given the same buffer
+ * skips recomputing them.
  * Replaces forward_chunked / forward_chunked_fixed,
  * bayes_ssm/persistent_bayes_chunked_d8.cu:530-548.
  */
@@ -69,8 +73,12 @@ int bssm_forward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed,
                             const float *mean0, const float *cov0,
                             float *out, float *mean_final, float *cov_final,
                             float *boundary_mean, float *boundary_cov,
+                            float *replay_states, size_t replay_states_bytes,
                             long n, long t, int chunks, double denominator_floor,
                             void *stream);
+
+/* Bytes of the optional replay-state buffer (0 when chunks <= 4: nothing to save). */
+size_t bssm_replay_states_bytes(int key_dim, int value_dim, long n, long t, int chunks);
 
 /* Bytes of device workspace bssm_backward_chunked_ex needs (0 allowed). */
 size_t bssm_backward_workspace_bytes(int key_dim, int value_dim, long n, long t, int chunks);
@@ -86,7 +94,10 @@ size_t bssm_backward_workspace_bytes(int key_dim, int value_dim, long n, long t,
  * grad_observation [N,T] (zeros when fixed != 0).
  * need_initial != 0 also writes grad_mean0 [N,D,M] and grad_cov0 [N,D,D]
  * (symmetric: the covariance entered as (cov0 + cov0^T)/2).
- * workspace: device memory of bssm_backward_workspace_bytes(...) bytes.
+ * replay_states: the buffer the forward filled (then no workspace is
+ * needed), or NULL.
+ * workspace: device memory of bssm_backward_workspace_bytes(...) bytes when
+ * replay_states is NULL (NULL allowed when that size is 0).
  * Replaces backward_chunked and its lean / fixed / noinitial variants,
  * bayes_ssm/persistent_bayes_chunked_d8.cu:550-651,
  * bayes_ssm/persistent_bayes_chunked_d2m8.cu:576-600.
@@ -97,6 +108,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                              const float *decay, const float *process, const float *observation,
                              const float *mean0, const float *cov0,
                              const float *boundary_mean, const float *boundary_cov,
+                             const float *replay_states, size_t replay_states_bytes,
                              const float *grad_out, const float *grad_mean_final,
                              const float *grad_cov_final,
                              void *grad_keys, void *grad_values, void *grad_queries,

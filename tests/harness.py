@@ -57,8 +57,9 @@ def cuda(x):
     return None if x is None else x.cuda().contiguous()
 
 
-def capi_forward(inp, *, chunks, floor=1e-6, fixed=False):
-    """Forward through bssm_forward_chunked_ex; returns CPU float tensors."""
+def capi_forward(inp, *, chunks, floor=1e-6, fixed=False, replay_states=True):
+    """Forward through bssm_forward_chunked_ex (optionally saving the replay
+    states the backward then reuses); returns device tensors."""
     k, v, q = cuda(inp["k"]), cuda(inp["v"]), cuda(inp["q"])
     a, p, r = cuda(inp["a"]), cuda(inp["p"]), cuda(inp["r"])
     m0, p0 = cuda(inp["M0"]), cuda(inp["P0"])
@@ -71,11 +72,16 @@ def capi_forward(inp, *, chunks, floor=1e-6, fixed=False):
     pt = torch.empty(n, d, d, device=dev)
     bm = torch.empty(n, nb + 1, d, m, device=dev)
     bc = torch.empty(n, nb + 1, d, d, device=dev)
+    rs = None
+    if replay_states:
+        nbytes = _capi.replay_states_bytes(d, m, n, t, chunks)
+        rs = torch.full((nbytes // 4,), float("nan"), device=dev) if nbytes else None
     _capi.forward_chunked(d, m, io_code(k.dtype), fixed, k, v, q, None if fixed else a,
                           None if fixed else p, None if fixed else r, m0, p0, out, mt, pt, bm, bc,
-                          n, t, chunks, floor, torch.cuda.current_stream().cuda_stream)
+                          n, t, chunks, floor, torch.cuda.current_stream().cuda_stream,
+                          replay_states=rs)
     torch.cuda.synchronize()
-    return dict(y=out, MT=mt, PT=pt, bm=bm, bc=bc)
+    return dict(y=out, MT=mt, PT=pt, bm=bm, bc=bc, rs=rs)
 
 
 def capi_backward(inp, fwd, gy, gmt, gpt, *, chunks, floor=1e-6, fixed=False, need_dyn=True,
@@ -91,13 +97,14 @@ def capi_backward(inp, fwd, gy, gmt, gpt, *, chunks, floor=1e-6, fixed=False, ne
     gr = torch.full((n, t), float("nan"), device=dev) if need_dyn else None
     gm0 = torch.full((n, d, m), float("nan"), device=dev) if need_init else None
     gc0 = torch.full((n, d, d), float("nan"), device=dev) if need_init else None
-    nbytes = _capi.workspace_bytes(d, m, n, t, chunks)
+    rs = fwd.get("rs")
+    nbytes = 0 if rs is not None else _capi.workspace_bytes(d, m, n, t, chunks)
     ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
     _capi.backward_chunked(d, m, io_code(k.dtype), fixed, need_dyn, need_init, k, v, q,
                            None if fixed else a, None if fixed else p, None if fixed else r, None,
                            None, fwd["bm"], fwd["bc"], cuda(gy), cuda(gmt), cuda(gpt), gk, gv, gq,
                            gd, gp, gr, gm0, gc0, ws, nbytes, n, t, chunks, floor,
-                           torch.cuda.current_stream().cuda_stream)
+                           torch.cuda.current_stream().cuda_stream, replay_states=rs)
     torch.cuda.synchronize()
     return dict(k=gk, v=gv, q=gq, a=gd, p=gp, r=gr, M0=gm0, P0=gc0)
 

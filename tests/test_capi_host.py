@@ -50,24 +50,35 @@ def test_version_and_last_error(lib):
 
 def test_unsupported_shape_rejected_without_gpu(lib):
     from bayes_ssm import _capi
-    rc = lib.bssm_forward_chunked_ex(3, 8, 0, 0, *([None] * 13), 1, 1, 1, 1e-6, None)
+    fwd_nulls = [None] * 13 + [None, 0]
+    rc = lib.bssm_forward_chunked_ex(3, 8, 0, 0, *fwd_nulls, 1, 1, 1, 1e-6, None)
     assert rc == 2
     assert b"no kernel" in lib.bssm_last_error()
-    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *([None] * 13), 1, 1, 0, 1e-6, None)
+    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *fwd_nulls, 1, 1, 0, 1e-6, None)
     assert rc == 1 and b"chunks" in lib.bssm_last_error()
-    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *([None] * 13), 1, 1, 4, -1.0, None)
+    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *fwd_nulls, 1, 1, 4, -1.0, None)
     assert rc == 1 and b"floor" in lib.bssm_last_error()
-    rc = lib.bssm_forward_chunked_ex(8, 8, 7, 0, *([None] * 13), 1, 1, 4, 1e-6, None)
+    rc = lib.bssm_forward_chunked_ex(8, 8, 7, 0, *fwd_nulls, 1, 1, 4, 1e-6, None)
     assert rc == 2
     with pytest.raises(_capi.KernelError):
         _capi.check(rc, "probe")
 
 
 def test_null_pointers_rejected_without_gpu(lib):
-    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *([None] * 13), 4, 10, 4, 1e-6, None)
+    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *([None] * 13), None, 0, 4, 10, 4, 1e-6, None)
     assert rc == 1 and b"null" in lib.bssm_last_error()
-    rc = lib.bssm_backward_chunked_ex(8, 8, 0, 0, 1, 1, *([None] * 21), None, 0, 4, 10, 4, 1e-6, None)
+    bwd_nulls = [None] * 10 + [None, 0] + [None] * 11
+    rc = lib.bssm_backward_chunked_ex(8, 8, 0, 0, 1, 1, *bwd_nulls, None, 0, 4, 10, 4, 1e-6, None)
     assert rc == 1
+
+
+def test_replay_states_size_formula(lib):
+    # chunks <= 4: nothing between boundary checkpoints to save
+    assert lib.bssm_replay_states_bytes(8, 8, 100, 512, 4) == 0
+    # D8M8, chunk 64: 15 states per chunk, 8 chunks, 128 floats each
+    assert lib.bssm_replay_states_bytes(8, 8, 10, 512, 64) == 10 * 8 * 15 * 128 * 4
+    # partial last chunk: slots are sized by the full chunk length
+    assert lib.bssm_replay_states_bytes(2, 8, 3, 70, 32) == 3 * 3 * 7 * (16 + 4) * 4
 
 
 def test_workspace_size_formula(lib):

@@ -44,10 +44,10 @@ def _grads_out(n, t, d, m, seed):
 
 
 def _check_all(inp, *, chunks, fixed=False, need_dyn=True, need_init=True, gy_none=False,
-               final_grads=True, seed=0, bf16_tol=4e-3):
+               final_grads=True, seed=0, bf16_tol=4e-3, replay_states=True):
     n, t, d = inp["k"].shape
     m = inp["v"].shape[-1]
-    fwd = capi_forward(inp, chunks=chunks, fixed=fixed)
+    fwd = capi_forward(inp, chunks=chunks, fixed=fixed, replay_states=replay_states)
     y, mt, pt = _oracle_fwd(inp, fixed=fixed)
     assert_parity(fwd["y"], y, what="y")
     assert_parity(fwd["MT"], mt, what="M_T")
@@ -81,6 +81,24 @@ def _check_all(inp, *, chunks, fixed=False, need_dyn=True, need_init=True, gy_no
 def test_dynamic_fp32_all_gradients(d, chunks):
     inp = make_inputs(37, 61, d, 8, seed=d * 10 + chunks, dist="paper", init="random")
     _check_all(inp, chunks=chunks, seed=d)
+
+
+@pytest.mark.parametrize("d", DIMS)
+@pytest.mark.parametrize("chunks", [7, 64])
+def test_backward_recomputes_replay_states(d, chunks):
+    """Without the forward's replay states the backward recomputes them (phase A)."""
+    inp = make_inputs(29, 70, d, 8, seed=d * 3 + chunks, dist="paper", init="random")
+    _check_all(inp, chunks=chunks, seed=d, replay_states=False)
+
+
+def test_replay_states_match_recomputed_states():
+    """Both backward modes give bit-identical gradients."""
+    inp = make_inputs(24, 90, 8, 8, seed=77, init="random")
+    gy, gmt, gpt = _grads_out(24, 90, 8, 8, 0)
+    a = capi_backward(inp, capi_forward(inp, chunks=32, replay_states=True), gy, gmt, gpt, chunks=32)
+    b = capi_backward(inp, capi_forward(inp, chunks=32, replay_states=False), gy, gmt, gpt, chunks=32)
+    for key in a:
+        assert torch.equal(a[key], b[key]), key
 
 
 @pytest.mark.parametrize("d", DIMS)
@@ -176,6 +194,7 @@ def test_workspace_too_small_is_rejected():
     assert need > 0
     ws = torch.empty(need - 16, device="cuda", dtype=torch.uint8)
     with pytest.raises(_capi.KernelError, match="workspace"):
+        # no replay states: the phase-A workspace is required
         _capi.backward_chunked(8, 8, 0, 0, 0, 0, k, inp["v"].cuda(), inp["q"].cuda(), inp["a"].cuda(),
                                inp["p"].cuda(), inp["r"].cuda(), None, None, fwd["bm"], fwd["bc"],
                                torch.zeros(4, 40, 8, device="cuda"), None, None, torch.empty_like(k),
