@@ -94,9 +94,9 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
         needs = ctx.needs_input_grad
         need_dyn = bool(needs[3] or needs[4] or needs[5])
         need_init = bool(needs[6] or needs[7])
-        gy = None if grad_out is None else grad_out.contiguous().float()
-        gmf = None if grad_mean is None else grad_mean.contiguous().float()
-        gcf = None if grad_cov is None else grad_cov.contiguous().float()
+        gy = None if grad_out is None else _aligned(grad_out.contiguous().float())
+        gmf = None if grad_mean is None else _aligned(grad_mean.contiguous().float())
+        gcf = None if grad_cov is None else _aligned(grad_cov.contiguous().float())
         gk = torch.empty_like(keys)
         gv = torch.empty_like(values)
         gq = torch.empty_like(queries)
@@ -122,8 +122,8 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
 
 
 def _aligned(x: Tensor) -> Tensor:
-    """Vector loads need 16-byte aligned rows; re-home an offset view."""
-    return x if x.data_ptr() % 16 == 0 else x.clone()
+    """The kernels need 16-byte aligned tensors; re-home an offset view."""
+    return x if x.data_ptr() % 16 == 0 else x.clone(memory_format=torch.contiguous_format)
 
 
 def kernel_supports(key_dim: int, value_dim: int) -> bool:
@@ -175,7 +175,7 @@ def fused_diagonal_bayesian(
     def prep(x, shape):
         if x is None:
             return None
-        return x.to(device=dev, dtype=f32).expand(shape).contiguous()
+        return _aligned(x.to(device=dev, dtype=f32).expand(shape).contiguous())
 
     decay = prep(decay, (n, t, d))
     process = prep(process, (n, t))
@@ -192,7 +192,6 @@ def fused_diagonal_bayesian(
     keys = _aligned(keys.contiguous())
     values = _aligned(values.contiguous())
     queries = _aligned(queries.contiguous())
-    decay = _aligned(decay)
     return _ChunkedBayesianFunction.apply(
         keys, values, queries, decay, process, observation, initial_mean, initial_covariance,
         int(chunk_length), float(denominator_floor), bool(fixed_dynamics))

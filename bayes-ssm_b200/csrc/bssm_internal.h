@@ -44,16 +44,19 @@ struct BwdArgs {
 
 // Replay states: the state at every kReplaySpan-token boundary inside each
 // chunk (not at the chunk start, which is the boundary checkpoint).  Layout
-// per chain: [chunk][slot][mean D*M row-major | covariance D*D row-major].
+// per chain: [chunk][slot][mean D*M row-major | covariance D*D row-major | pad].
 constexpr int kReplaySpan = 4;
 __host__ __device__ inline long replay_slots_per_chunk(long t, int chunks) {
     const long span = chunks < t ? chunks : t;
     const long nsub = (span + kReplaySpan - 1) / kReplaySpan;
     return nsub > 1 ? nsub - 1 : 0;
 }
+// Floats per saved state, padded to a 16-byte multiple so that every slot
+// starts 16-byte aligned (the lanes move it with 128-bit accesses).
+__host__ __device__ constexpr int replay_state_floats(int d, int m) { return (d * m + d * d + 3) / 4 * 4; }
 __host__ __device__ inline float *replay_slot(const float *rs, long chain, long nb, long slots, long ci,
                                               long j, int d, int m) {
-    return const_cast<float *>(rs) + ((chain * nb + ci) * slots + (j - 1)) * static_cast<long>(d * m + d * d);
+    return const_cast<float *>(rs) + ((chain * nb + ci) * slots + (j - 1)) * static_cast<long>(replay_state_floats(d, m));
 }
 
 // Error reporting (thread-local message behind bssm_last_error()).

@@ -680,11 +680,6 @@ inline bool aligned(const void *p, size_t bytes) {
     return p == nullptr || (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
 }
 
-inline size_t vec_align(int elems, size_t elem_bytes) {
-    size_t b = static_cast<size_t>(elems) * elem_bytes;
-    return b >= 16 ? 16 : b;
-}
-
 template <int D, int M, int S>
 constexpr size_t backward_smem_bytes() {
     return static_cast<size_t>(Launch<D>::kChains) * History<D, M, S>::kFloats * sizeof(float);
@@ -755,8 +750,8 @@ inline size_t replay_bytes(int d, int m, long n, long t, int chunks) {
     if (n <= 0 || t <= 0 || chunks <= 0) return 0;
     const long nb = (t + chunks - 1) / chunks;
     return static_cast<size_t>(n) * static_cast<size_t>(nb) *
-           static_cast<size_t>(replay_slots_per_chunk(t, chunks)) * static_cast<size_t>(d * m + d * d) *
-           sizeof(float);
+           static_cast<size_t>(replay_slots_per_chunk(t, chunks)) *
+           static_cast<size_t>(replay_state_floats(d, m)) * sizeof(float);
 }
 
 // Kernel family: the shared-memory-staged kernels (bssm_staged.cu) serve
@@ -846,14 +841,12 @@ int bssm_forward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed,
         return fail(BSSM_ERR_INVALID, "forward: null keys/values/queries/out");
     if (!fixed && t > 0 && (!decay || !process || !observation))
         return fail(BSSM_ERR_INVALID, "forward: decay/process/observation required unless fixed");
-    const size_t esz = io_dtype == BSSM_BF16 ? 2 : 4;
-    const int cpl = value_dim / key_dim;
-    if (!aligned(keys, vec_align(key_dim, esz)) || !aligned(queries, vec_align(key_dim, esz)) ||
-        !aligned(values, vec_align(cpl, esz)) || !aligned(decay, vec_align(key_dim, 4)) ||
-        !aligned(out, vec_align(cpl, 4)) || !aligned(mean_final, 16) || !aligned(boundary_mean, 16) ||
-        !aligned(cov_final, vec_align(key_dim, 4)) || !aligned(boundary_cov, vec_align(key_dim, 4)) ||
-        !aligned(mean0, vec_align(cpl, 4)) || !aligned(replay_states, 16))
-        return fail(BSSM_ERR_ALIGNMENT, "forward: misaligned pointer");
+    // every tensor is moved with up-to-16-byte vector accesses and cp.async:
+    // require 16-byte aligned base pointers (any fresh CUDA allocation is)
+    const void *ptrs[] = {keys, values, queries, decay, process, observation, mean0, cov0, out,
+                          mean_final, cov_final, boundary_mean, boundary_cov, replay_states};
+    for (const void *p : ptrs)
+        if (!aligned(p, 16)) return fail(BSSM_ERR_ALIGNMENT, "forward: pointer %p is not 16-byte aligned", p);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const float fl = static_cast<float>(denominator_floor);
     if (io_dtype == BSSM_F32) {
@@ -927,15 +920,12 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
     if (need > 0 && (workspace == nullptr || workspace_bytes_ < need))
         return fail(BSSM_ERR_WORKSPACE, "backward: workspace of %zu bytes required (got %zu)", need,
                     workspace_bytes_);
-    const size_t esz = io_dtype == BSSM_BF16 ? 2 : 4;
-    const int cpl = value_dim / key_dim;
-    if (!aligned(keys, vec_align(key_dim, esz)) || !aligned(queries, vec_align(key_dim, esz)) ||
-        !aligned(values, vec_align(cpl, esz)) || !aligned(decay, vec_align(key_dim, 4)) ||
-        !aligned(grad_out, vec_align(cpl, 4)) || !aligned(grad_values, vec_align(cpl, esz)) ||
-        !aligned(boundary_mean, 16) || !aligned(boundary_cov, vec_align(key_dim, 4)) ||
-        !aligned(grad_mean_final, vec_align(cpl, 4)) || !aligned(grad_mean0, vec_align(cpl, 4)) ||
-        !aligned(grad_cov0, vec_align(key_dim, 4)) || !aligned(workspace, 16) || !aligned(replay_states, 16))
-        return fail(BSSM_ERR_ALIGNMENT, "backward: misaligned pointer");
+    const void *ptrs[] = {keys, values, queries, decay, process, observation, boundary_mean,
+                          boundary_cov, replay_states, grad_out, grad_mean_final, grad_cov_final,
+                          grad_keys, grad_values, grad_queries, grad_decay, grad_process,
+                          grad_observation, grad_mean0, grad_cov0, workspace};
+    for (const void *p : ptrs)
+        if (!aligned(p, 16)) return fail(BSSM_ERR_ALIGNMENT, "backward: pointer %p is not 16-byte aligned", p);
     const float fl = static_cast<float>(denominator_floor);
     float *ws = static_cast<float *>(workspace);
     if (io_dtype == BSSM_F32) {

@@ -18,8 +18,9 @@
  * gradients: BSSM_F32 or BSSM_BF16.  Everything else is float32; the mean,
  * covariance and every reduction are float32.
  *
- * Pointer alignment: keys/queries/values/decay and their gradients must be
- * aligned to min(16, row bytes); BSSM_ERR_ALIGNMENT otherwise.
+ * Pointer alignment: every tensor pointer of the recurrence entry points must
+ * be 16-byte aligned (any fresh CUDA allocation is); BSSM_ERR_ALIGNMENT
+ * otherwise.
  *
  * Reference interface these replace (paths within catid/bayes-ssm): the
  * per-key-dim pybind modules loaded by bayes_ssm/fused_cuda.py:23-55, whose

@@ -79,6 +79,8 @@ def test_replay_states_size_formula(lib):
     assert lib.bssm_replay_states_bytes(8, 8, 10, 512, 64) == 10 * 8 * 15 * 128 * 4
     # partial last chunk: slots are sized by the full chunk length
     assert lib.bssm_replay_states_bytes(2, 8, 3, 70, 32) == 3 * 3 * 7 * (16 + 4) * 4
+    # D1: 9 floats per state, padded to 12 so every slot is 16-byte aligned
+    assert lib.bssm_replay_states_bytes(1, 8, 5, 64, 64) == 5 * 1 * 15 * 12 * 4
 
 
 def test_workspace_size_formula(lib):
@@ -92,3 +94,13 @@ def test_workspace_size_formula(lib):
 def test_assoc_scan_limits_without_gpu(lib):
     rc = lib.bssm_assoc_scan_ex(33, 8, *([None] * 10), 1, 1, 1e-6, None)
     assert rc == 2 and b"key_dim" in lib.bssm_last_error()
+
+
+def test_misaligned_pointer_rejected_before_launch(lib):
+    """A 4-byte-offset pointer is refused on the host; no kernel is launched
+    (fake addresses are never dereferenced)."""
+    good = 0x10000
+    ptrs = [good + 0x1000 * i for i in range(13)]
+    ptrs[0] += 4  # keys: misaligned
+    rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *ptrs, None, 0, 2, 16, 8, 1e-6, None)
+    assert rc == 3 and b"16-byte" in lib.bssm_last_error()
