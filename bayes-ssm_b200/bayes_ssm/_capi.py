@@ -42,6 +42,8 @@ _SIGNATURES = {
     "bssm_backward_chunked_ex": ([_i, _i, _i, _i, _i, _i] + [_vp] * 10 + [_vp, _sz] + [_vp] * 11
                                  + [_vp, _sz, _l, _l, _i, _d, _vp], _i),
     "bssm_assoc_scan_ex": ([_i, _i] + [_vp] * 10 + [_l, _l, _d, _vp], _i),
+    "bssm_backward_noalloc_max_scratch_bytes": ([], _sz),
+    "bssm_backward_chunked_noalloc": ([_i, _i, _i, _i, _i, _i] + [_vp] * 21 + [_l, _l, _i, _d, _vp], _i),
 }
 
 
@@ -123,3 +125,17 @@ def assoc_scan(key_dim, value_dim, keys, values, queries, observation, mean0, co
                                 ptr(observation), ptr(mean0), ptr(cov0), ptr(out), ptr(mean_final),
                                 ptr(cov_final), ptr(status), n, t, float(floor), stream)
     check(rc, "bssm_assoc_scan_ex")
+
+
+def backward_chunked_noalloc(key_dim, value_dim, io_dtype, fixed, need_dynamics, need_initial, keys,
+                             values, queries, decay, process, observation, mean0, cov0, bmean, bcov,
+                             gy, gmf, gcf, gk, gv, gq, gd, gp, gr, gm0, gc0, n, t, chunks, floor,
+                             stream) -> None:
+    """The allocation-free backward (static device scratch; see the header)."""
+    lib = load()
+    rc = lib.bssm_backward_chunked_noalloc(
+        key_dim, value_dim, io_dtype, int(fixed), int(need_dynamics), int(need_initial), ptr(keys),
+        ptr(values), ptr(queries), ptr(decay), ptr(process), ptr(observation), ptr(mean0), ptr(cov0),
+        ptr(bmean), ptr(bcov), ptr(gy), ptr(gmf), ptr(gcf), ptr(gk), ptr(gv), ptr(gq), ptr(gd),
+        ptr(gp), ptr(gr), ptr(gm0), ptr(gc0), n, t, chunks, float(floor), stream)
+    check(rc, "bssm_backward_chunked_noalloc")

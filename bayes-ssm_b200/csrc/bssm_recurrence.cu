@@ -26,7 +26,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "../../include/bayes_ssm_b200.h"
 #include "bssm_common.cuh"
@@ -809,6 +811,52 @@ int validate_common(int d, int m, int io_dtype, long n, long t, int chunks, doub
 
 }  // namespace bssm
 
+// ---------------------------------------------------------------------------
+// Allocation-free backward: phase-A scratch in a static device array.
+//
+// Some callers cannot allocate device memory when they call the backward: a
+// host whose allocator owns the whole device budget (a raw allocation would
+// bypass it and can fail), a serving loop that cannot take the device-wide
+// synchronisation an allocation implies, or a C/FFI host (cgo, JNI, ctypes)
+// with no device allocator of its own.  bssm_backward_chunked_noalloc() lets
+// them run the recompute-mode backward without passing a workspace: the
+// phase-A scratch lives in g_noalloc_scratch, a file-scope array of
+// kNoAllocScratchBytes that every GPU loading this library holds until exit.
+// ---------------------------------------------------------------------------
+namespace bssm {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of g_noalloc_scratch for the current device.  The symbol's
+// name in host code is only a host-side stand-in, so the address is looked up
+// with cudaGetSymbolAddress once per device (with that device current) and
+// cached.  Returns nullptr after recording an error.
+static void *noalloc_scratch_current_device() {
+    static std::mutex mu;
+    static std::unordered_map<int, void *> cache;
+    int dev = -1;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) {
+        fail(BSSM_ERR_CUDA, "noalloc backward: cudaGetDevice: %s", cudaGetErrorString(err));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(dev);
+    if (it != cache.end()) return it->second;
+    void *ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess || ptr == nullptr) {
+        fail(BSSM_ERR_CUDA, "noalloc backward: cudaGetSymbolAddress on device %d: %s", dev,
+             cudaGetErrorString(err));
+        return nullptr;
+    }
+    cache.emplace(dev, ptr);
+    return ptr;
+}
+
+}  // namespace bssm
+
 using namespace bssm;
 
 extern "C" {
@@ -1077,6 +1125,43 @@ int bssm_d2_backward_chunked_noinitial_fixed(
                                     grad_queries, grad_decay, grad_process, grad_observation,
                                     nullptr, nullptr, workspace, workspace_bytes, n, t, chunks,
                                     denominator_floor, stream);
+}
+
+size_t bssm_backward_noalloc_max_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int bssm_backward_chunked_noalloc(int key_dim, int value_dim, int io_dtype, int fixed,
+                                  int need_dynamics, int need_initial, const void *keys,
+                                  const void *values, const void *queries, const float *decay,
+                                  const float *process, const float *observation,
+                                  const float *mean0, const float *cov0,
+                                  const float *boundary_mean, const float *boundary_cov,
+                                  const float *grad_out, const float *grad_mean_final,
+                                  const float *grad_cov_final, void *grad_keys, void *grad_values,
+                                  void *grad_queries, float *grad_decay, float *grad_process,
+                                  float *grad_observation, float *grad_mean0, float *grad_cov0,
+                                  long n, long t, int chunks, double denominator_floor, void *stream) {
+    int rc = validate_common(key_dim, value_dim, io_dtype, n, t, chunks, denominator_floor);
+    if (rc) return rc;
+    const size_t need = workspace_bytes(key_dim, value_dim, n, t, chunks);
+    if (need > kNoAllocScratchBytes)
+        return fail(BSSM_ERR_WORKSPACE,
+                    "noalloc backward: this problem needs %zu bytes of scratch but the static scratch "
+                    "holds %zu (n=%ld, t=%ld, chunks=%d); use bssm_backward_chunked_ex with a "
+                    "caller-provided workspace or the forward's replay states",
+                    need, kNoAllocScratchBytes, n, t, chunks);
+    void *scratch = nullptr;
+    if (need > 0) {
+        scratch = noalloc_scratch_current_device();
+        if (scratch == nullptr) return BSSM_ERR_CUDA;
+    }
+    // the scratch is written before it is read inside one launch: no clearing
+    return bssm_backward_chunked_ex(key_dim, value_dim, io_dtype, fixed, need_dynamics, need_initial, keys,
+                                    values, queries, decay, process, observation, mean0, cov0,
+                                    boundary_mean, boundary_cov, nullptr, 0, grad_out, grad_mean_final,
+                                    grad_cov_final, grad_keys, grad_values, grad_queries, grad_decay,
+                                    grad_process, grad_observation, grad_mean0, grad_cov0, scratch,
+                                    need > 0 ? kNoAllocScratchBytes : 0, n, t, chunks, denominator_floor,
+                                    stream);
 }
 
 }  // extern "C"

@@ -221,6 +221,44 @@ int bssm_d2_backward_chunked_noinitial_fixed(
     float *grad_observation, void *workspace, size_t workspace_bytes, long n, long t,
     int chunks, double denominator_floor, void *stream);
 
+/*
+ * Allocation-free backward (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory at call time -- a host whose
+ * allocator owns the device memory budget, a serving loop that cannot take the
+ * device-wide synchronisation an allocation implies, or an FFI host with no
+ * device allocator -- this runs the same backward as bssm_backward_chunked_ex
+ * (recompute mode: no replay states) with its phase-A scratch in a static
+ * device array of bssm_backward_noalloc_max_scratch_bytes() bytes (32 MiB),
+ * which every GPU that loads the library holds until the process exits.
+ *   - Arguments are those of bssm_backward_chunked_ex without replay_states
+ *     and workspace.  Inputs and outputs are still the caller's.
+ *   - A problem whose scratch (bssm_backward_workspace_bytes) exceeds the
+ *     static size is rejected with BSSM_ERR_WORKSPACE and a message.
+ *   - Nothing is allocated or freed (no cudaMalloc / cudaFree).
+ *   - The first call on a device looks up the array's device address with
+ *     cudaGetSymbolAddress (with that device current); make that first call
+ *     before any stream capture on that device.
+ *   - All calls on a device share the one array and it keeps the last call's
+ *     contents; nothing in it needs to start at zero.  Calls that overlap on
+ *     the GPU (concurrent streams, or several host threads on one device)
+ *     race on it: serialise them.
+ */
+size_t bssm_backward_noalloc_max_scratch_bytes(void);
+int bssm_backward_chunked_noalloc(int key_dim, int value_dim, int io_dtype, int fixed,
+                                  int need_dynamics, int need_initial,
+                                  const void *keys, const void *values, const void *queries,
+                                  const float *decay, const float *process, const float *observation,
+                                  const float *mean0, const float *cov0,
+                                  const float *boundary_mean, const float *boundary_cov,
+                                  const float *grad_out, const float *grad_mean_final,
+                                  const float *grad_cov_final,
+                                  void *grad_keys, void *grad_values, void *grad_queries,
+                                  float *grad_decay, float *grad_process, float *grad_observation,
+                                  float *grad_mean0, float *grad_cov0,
+                                  long n, long t, int chunks, double denominator_floor,
+                                  void *stream);
+
 #ifdef __cplusplus
 }
 #endif
