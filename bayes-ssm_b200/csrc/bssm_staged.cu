@@ -8,7 +8,7 @@
 //   lanes, lane `sub` owning covariance rows sub*RPL.. (RPL = D/LPC) and mean
 //   columns sub*CPL.. (CPL = M/LPC).
 // * Token inputs arrive in shared memory as tiles of kS tokens x C chains,
-//   copied with cp.async by all lanes, kStages tiles in flight; the compute
+//   copied with cp.async by all lanes, several tiles in flight; the compute
 //   lanes never wait on a global load inside the recurrence.
 // * Backward: per chunk (last to first) phase A replays the chunk from its
 //   boundary checkpoint and saves the state at every kS-token boundary into
@@ -26,13 +26,49 @@
 namespace bssm {
 namespace staged {
 
-constexpr int kS = 4;       // tokens per tile = history sub-chunk
-constexpr int kStages = 3;  // tiles in flight
+constexpr int kS = 4;          // tokens per tile = history sub-chunk
+constexpr int kStagesFwd = 3;  // forward: tiles in flight
+constexpr int kStagesBwd = 2;  // backward: one tile is consumed over a replay and a reverse pass
 
 constexpr int al16(int x) { return (x + 15) / 16 * 16; }
-// chain stride in a tile: avoid a multiple of 128 bytes so that the chains
-// read by one 8-lane phase of a 128-bit shared load fall on distinct banks
-constexpr int padcs(int x) { return (x % 128 == 0) ? x + 16 : x; }
+
+// Bank check for one tile region: C chains of LPC lanes; chain c's data starts
+// at byte c*cs.  Two access patterns are checked: every lane reading its own
+// `lane_bytes`-wide slice (lane_bytes 0: all lanes of a chain read the same
+// word), and the chain's lanes reading one shared 16-byte chunk.  Shared
+// memory serves 128 bytes of distinct lanes per wavefront; within a wavefront
+// two different words in the same bank conflict.
+constexpr bool region_conflict_free(int cs, int lane_bytes, int C, int LPC) {
+    const int patterns[2] = {lane_bytes, 16};
+    for (int pi = 0; pi < 2; ++pi) {
+        const int w = patterns[pi];
+        const bool bcast = (w == 0 || w == 16);  // one address per chain
+        const int access = (w == 0) ? 4 : w;
+        const int lanes_per_wave = 128 / access < 32 ? 128 / access : 32;
+        const int chains_per_wave = lanes_per_wave / LPC > 0 ? lanes_per_wave / LPC : 1;
+        for (int c0 = 0; c0 < C; c0 += chains_per_wave) {
+            int owner[32] = {};
+            for (int b = 0; b < 32; ++b) owner[b] = -1;
+            for (int c = c0; c < c0 + chains_per_wave && c < C; ++c) {
+                for (int sub = 0; sub < (bcast ? 1 : LPC); ++sub) {
+                    const int word0 = (c * cs + (bcast ? 0 : sub * access)) / 4;
+                    for (int x = 0; x < access / 4; ++x) {
+                        const int word = word0 + x, bank = word % 32;
+                        if (owner[bank] >= 0 && owner[bank] != word) return false;
+                        owner[bank] = word;
+                    }
+                }
+            }
+        }
+    }
+    return true;
+}
+// Smallest 16-byte-padded chain stride >= bytes that is conflict free.
+constexpr int chain_stride(int bytes, int lane_bytes, int C, int LPC) {
+    for (int pad = 0; pad <= 128; pad += 16)
+        if (region_conflict_free(al16(bytes) + pad, lane_bytes, C, LPC)) return al16(bytes) + pad;
+    return al16(bytes);
+}
 
 template <int D, int M, int LPC, typename TIn>
 struct Geo {
@@ -41,15 +77,24 @@ struct Geo {
     // tile (bytes)
     static constexpr int rbK = D * static_cast<int>(sizeof(TIn)), rbV = M * static_cast<int>(sizeof(TIn));
     static constexpr int rbA = D * 4, rbG = M * 4, rbP = 4;
-    static constexpr int csK = padcs(al16(kS * rbK)), csV = padcs(al16(kS * rbV));
-    static constexpr int csA = padcs(al16(kS * rbA)), csG = padcs(al16(kS * rbG)), csP = al16(kS * rbP);
+    // each lane reads its own RPL keys / decays and CPL values / gy entries
+    static constexpr int csK = chain_stride(kS * rbK, RPL * static_cast<int>(sizeof(TIn)), C, LPC);
+    static constexpr int csV = chain_stride(kS * rbV, CPL * static_cast<int>(sizeof(TIn)), C, LPC);
+    static constexpr int csA = chain_stride(kS * rbA, RPL * 4, C, LPC);
+    static constexpr int csG = chain_stride(kS * rbG, CPL * 4, C, LPC);
+    static constexpr int csP = chain_stride(kS * rbP, 0, C, LPC);
     static constexpr int oK = 0, oQ = oK + C * csK, oV = oQ + C * csK, oA = oV + C * csV;
     static constexpr int oG = oA + C * csA, oP = oG + C * csG, oR = oP + C * csP, kTile = oR + C * csP;
-    // history (floats per chain)
+    // history (floats).  Per chain, the lane-private blocks of the pre-token
+    // mean and covariance: [token][lane-interleaved 4-float chunks], chain
+    // stride == 16 (mod 32) so the two chains of a 128-bit wavefront use
+    // different banks.  Then, shared by the CTA and indexed [token][chain][.],
+    // the small vectors u (D), e (M) and (beta, s).
     static constexpr int hMB = CPL * D, hPB = RPL * D;  // lane blocks per token
-    static constexpr int hM = 0, hP = hM + kS * M * D, hU = hP + kS * D * D, hE = hU + kS * D;
-    static constexpr int hB = hE + kS * M, kHistRaw = hB + kS * 4;
-    static constexpr int kHist = kHistRaw + ((16 - kHistRaw % 32) + 32) % 32;  // == 16 mod 32
+    static constexpr int hM = 0, hP = hM + kS * M * D, kMPRaw = hP + kS * D * D;
+    static constexpr int kHistMP = kMPRaw + ((16 - kMPRaw % 32) + 32) % 32;
+    static constexpr int hU = C * kHistMP, hE = hU + kS * C * D, hB = hE + kS * C * M;
+    static constexpr int kHistAll = hB + kS * C * 2;
     // phase-A workspace (floats per chain per saved state)
     static constexpr int kWsLane = (hMB + hPB + 3) / 4 * 4, kWsChain = kWsLane * LPC;
 };
@@ -137,6 +182,15 @@ __device__ __forceinline__ void issue_tile(char *stage, const Inputs<D, M, LPC, 
     }
     if (kind == kPhaseB && in.gy != nullptr)
         issue_rows<G::rbG, G::csG, G::C>(s + G::oG, in.gy, T, n0, nvalid, t0, ntok, lane);
+}
+
+// Ask L2 to start fetching a saved state (mean + covariance, `floats` floats)
+// that this chain will load at its next sub-chunk; the lanes split the lines.
+template <int LPC>
+__device__ __forceinline__ void prefetch_state_l2(const float *p, int floats, int sub) {
+    const int lines = (floats * 4 + 127) / 128;
+    for (int l = sub; l < lines; l += LPC)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p + l * 32));
 }
 
 // One token's inputs for this lane, read from a staged tile.
@@ -263,7 +317,7 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
 
     const long ntile = (T + kS - 1) / kS;
 #pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
+    for (int s = 0; s < kStagesFwd - 1; ++s) {
         if (s < ntile)
             issue_tile<D, M, LPC, FIXED, TIn>(smem + s * G::kTile, in, kForward, T, n0, nvalid, s * kS,
                                               static_cast<int>((T - s * kS) < kS ? (T - s * kS) : kS), lane);
@@ -272,15 +326,15 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
     long ckpt = 0;
     const long rs_slots = replay_slots_per_chunk(T, L);
     for (long q = 0; q < ntile; ++q) {
-        const long qn = q + kStages - 1;
+        const long qn = q + kStagesFwd - 1;
         if (qn < ntile)
-            issue_tile<D, M, LPC, FIXED, TIn>(smem + (qn % kStages) * G::kTile, in, kForward, T, n0, nvalid,
+            issue_tile<D, M, LPC, FIXED, TIn>(smem + (qn % kStagesFwd) * G::kTile, in, kForward, T, n0, nvalid,
                                               qn * kS, static_cast<int>((T - qn * kS) < kS ? (T - qn * kS) : kS),
                                               lane);
         cp_async_commit();
-        cp_async_wait<kStages - 1>();
+        cp_async_wait<kStagesFwd - 1>();
         __syncwarp();
-        const char *stage = smem + (q % kStages) * G::kTile;
+        const char *stage = smem + (q % kStagesFwd) * G::kTile;
         const long t0 = q * kS;
         const int ntok = static_cast<int>((T - t0) < kS ? (T - t0) : kS);
         for (int tau = 0; tau < ntok; ++tau) {
@@ -403,7 +457,11 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
     const float floor_ = A.floor;
     const bool has_gy = A.gy != nullptr;
     const Inputs<D, M, LPC, FIXED, TIn> in{A.keys, A.values, A.queries, A.decay, A.process, A.observation, A.gy};
-    float *hist = reinterpret_cast<float *>(smem + kStages * G::kTile) + c * G::kHist;
+    float *const hist_all = reinterpret_cast<float *>(smem + kStagesBwd * G::kTile);
+    float *const hist = hist_all + c * G::kHistMP;  // this chain's mean/covariance blocks
+    auto hU_at = [&](int tau) { return hist_all + G::hU + (tau * C + c) * D; };
+    auto hE_at = [&](int tau) { return hist_all + G::hE + (tau * C + c) * M; };
+    auto hB_at = [&](int tau) { return hist_all + G::hB + (tau * C + c) * 2; };
     const float *bm = A.bmean + chain * (nb + 1) * D * M;
     const float *bc = A.bcov + chain * (nb + 1) * D * D;
     float *ws = A.ws + chain * static_cast<long>(nsub_max > 1 ? nsub_max - 1 : 0) * G::kWsChain + sub * G::kWsLane;
@@ -431,7 +489,7 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
     Schedule prod;
     prod.init(T, L, have_rs);
 #pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
+    for (int s = 0; s < kStagesBwd - 1; ++s) {
         if (!prod.done) {
             issue_tile<D, M, LPC, FIXED, TIn>(smem + s * G::kTile, in, prod.phase, T, n0, nvalid, prod.t0(),
                                               prod.ntok(), lane);
@@ -442,14 +500,14 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
     long qc = 0;  // tiles consumed
     auto acquire = [&]() -> const char * {
         if (!prod.done) {
-            issue_tile<D, M, LPC, FIXED, TIn>(smem + ((qc + kStages - 1) % kStages) * G::kTile, in, prod.phase,
+            issue_tile<D, M, LPC, FIXED, TIn>(smem + ((qc + kStagesBwd - 1) % kStagesBwd) * G::kTile, in, prod.phase,
                                               T, n0, nvalid, prod.t0(), prod.ntok(), lane);
             prod.advance();
         }
         cp_async_commit();
-        cp_async_wait<kStages - 1>();
+        cp_async_wait<kStagesBwd - 1>();
         __syncwarp();
-        return smem + (qc % kStages) * G::kTile;
+        return smem + (qc % kStagesBwd) * G::kTile;
     };
 
     for (long ci = nb - 1; ci >= 0; --ci) {
@@ -538,6 +596,26 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 #pragma unroll
                     for (int jj = 0; jj < D; ++jj) P[r][jj] = flat[G::hMB + r * D + jj];
             }
+            // the state of the next sub-chunk to be processed: start its fetch now
+            if (active && have_rs) {
+                if (j > 1) {
+                    prefetch_state_l2<LPC>(replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j - 1, D, M),
+                                           replay_state_floats(D, M), sub);
+                } else if (j == 1) {
+                    prefetch_state_l2<LPC>(bm + ci * D * M, D * M, sub);
+                    prefetch_state_l2<LPC>(bc + ci * D * D, D * D, sub);
+                } else if (ci > 0) {
+                    const int len_prev = L;  // chunks before the last are full
+                    const int nsub_prev = (len_prev + kS - 1) / kS;
+                    if (nsub_prev > 1) {
+                        prefetch_state_l2<LPC>(replay_slot(A.rs, chain, nb, nsub_max - 1, ci - 1, nsub_prev - 1, D, M),
+                                               replay_state_floats(D, M), sub);
+                    } else {
+                        prefetch_state_l2<LPC>(bm + (ci - 1) * D * M, D * M, sub);
+                        prefetch_state_l2<LPC>(bc + (ci - 1) * D * D, D * D, sub);
+                    }
+                }
+            }
             // replay into history
             for (int tau = 0; tau < slen; ++tau) {
                 {
@@ -558,9 +636,9 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                 read_tok<D, M, LPC, FIXED, TIn>(stage, c, tau, sub, tk);
                 float u[D], u_own[RPL], e[CPL], beta, s;
                 forward_step<D, M, LPC>(g, tk, floor_, Mc, P, u, u_own, e, beta, s);
-                sts_vec<RPL>(hist + G::hU + tau * D + row0, u_own);
-                sts_vec<CPL>(hist + G::hE + tau * M + col0, e);
-                if (sub == 0) *reinterpret_cast<float2 *>(hist + G::hB + tau * 4) = make_float2(beta, s);
+                sts_vec<RPL>(hU_at(tau) + row0, u_own);
+                sts_vec<CPL>(hE_at(tau) + col0, e);
+                if (sub == 0) *reinterpret_cast<float2 *>(hB_at(tau)) = make_float2(beta, s);
             }
             __syncwarp();
             // Mc holds the post-update mean of the sub-chunk's last token; after
@@ -590,12 +668,12 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                     lds_vec<RPL>(ar + row0, a_own);
                     p = reinterpret_cast<const float *>(stage + G::oP + c * G::csP)[tau];
                 }
-                lds_vec<D>(hist + G::hU + tau * D, u);
-                lds_vec<RPL>(hist + G::hU + tau * D + row0, u_own);
-                const float2 bs = *reinterpret_cast<const float2 *>(hist + G::hB + tau * 4);
+                lds_vec<D>(hU_at(tau), u);
+                lds_vec<RPL>(hU_at(tau) + row0, u_own);
+                const float2 bs = *reinterpret_cast<const float2 *>(hB_at(tau));
                 const float beta = bs.x, s = bs.y;
                 float e[CPL], gyv[CPL];
-                lds_vec<CPL>(hist + G::hE + tau * M + col0, e);
+                lds_vec<CPL>(hE_at(tau) + col0, e);
                 if (has_gy) {
                     lds_vec<CPL>(reinterpret_cast<const float *>(stage + G::oG + c * G::csG + tau * G::rbG) + col0,
                                  gyv);
@@ -782,12 +860,12 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 // ===========================================================================
 template <int D, int M, int LPC, typename TIn>
 constexpr size_t fwd_smem() {
-    return static_cast<size_t>(kStages) * Geo<D, M, LPC, TIn>::kTile;
+    return static_cast<size_t>(kStagesFwd) * Geo<D, M, LPC, TIn>::kTile;
 }
 template <int D, int M, int LPC, typename TIn>
 constexpr size_t bwd_smem() {
     using G = Geo<D, M, LPC, TIn>;
-    return static_cast<size_t>(kStages) * G::kTile + static_cast<size_t>(G::C) * G::kHist * sizeof(float);
+    return static_cast<size_t>(kStagesBwd) * G::kTile + static_cast<size_t>(G::kHistAll) * sizeof(float);
 }
 
 template <int D, int M, int LPC, bool FIXED, typename TIn>
