@@ -19,7 +19,7 @@
 #include <cstdio>
 #include <string>
 
-#include "../../include/bayes_ssm_b200.h"
+#include "bayes_ssm_b200.h"
 #include "bssm_common.cuh"
 #include "bssm_internal.h"
 

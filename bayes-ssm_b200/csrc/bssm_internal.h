@@ -6,7 +6,7 @@
 
 #include <string>
 
-#include "../../include/bayes_ssm_b200.h"
+#include "bayes_ssm_b200.h"
 #include "bssm_common.cuh"
 
 namespace bssm {

@@ -30,7 +30,7 @@
 #include <string>
 #include <unordered_map>
 
-#include "../../include/bayes_ssm_b200.h"
+#include "bayes_ssm_b200.h"
 #include "bssm_common.cuh"
 #include "bssm_internal.h"
 

@@ -19,7 +19,7 @@
 //   adjoints (dL/dM columns and R = sym(dL/dP) rows).
 #include <cstdint>
 
-#include "../../include/bayes_ssm_b200.h"
+#include "bayes_ssm_b200.h"
 #include "bssm_common.cuh"
 #include "bssm_internal.h"
 
