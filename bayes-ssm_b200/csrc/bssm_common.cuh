@@ -87,6 +87,32 @@ struct LaneGroup {
 #pragma unroll
             for (int r = 0; r < RPL; ++r) out[src * RPL + r] = bcast(own[r], src);
     }
+    // Gather into lane-relative row order (see bssm_staged.cu): position x
+    // receives row x ^ (sub*RPL), owned by rank (x/RPL) ^ sub at its slot x%RPL.
+    template <int RPL>
+    __device__ __forceinline__ void gather_lane(const float (&own)[RPL], float (&out)[LPC * RPL]) const {
+#pragma unroll
+        for (int x = 0; x < LPC * RPL; ++x) out[x] = bcast(own[x % RPL], (x / RPL) ^ sub);
+    }
+    // Reduce-scatter of NV vectors held in lane-relative row order: at the
+    // stage with partner distance h a lane keeps positions [0, h*RPL) and its
+    // partner's positions [h*RPL, 2h*RPL) hold the same rows, so no selects
+    // are needed.  Lane `sub` ends with the totals of its own rows in
+    // positions 0 .. RPL-1.
+    template <int NV, int RPL>
+    __device__ __forceinline__ void reduce_scatter_lane(float (&vals)[NV][LPC * RPL],
+                                                        float (&out)[NV][RPL]) const {
+#pragma unroll
+        for (int h = LPC / 2; h >= 1; h >>= 1)
+#pragma unroll
+            for (int x = 0; x < h * RPL; ++x)
+#pragma unroll
+                for (int v = 0; v < NV; ++v) vals[v][x] += xor_(vals[v][x + h * RPL], h);
+#pragma unroll
+        for (int v = 0; v < NV; ++v)
+#pragma unroll
+            for (int r = 0; r < RPL; ++r) out[v][r] = vals[v][r];
+    }
     // Reduce-scatter of NV vectors of LPC*RPL partial sums: lane `sub` ends
     // with the group totals of entries sub*RPL .. sub*RPL+RPL-1 of each vector.
     // Recursive halving: at the stage with partner distance h the lanes with

@@ -193,82 +193,153 @@ __device__ __forceinline__ void prefetch_state_l2(const float *p, int floats, in
         asm volatile("prefetch.global.L2 [%0];" ::"l"(p + l * 32));
 }
 
-// One token's inputs for this lane, read from a staged tile.
+// ---------------------------------------------------------------------------
+// Lane-relative row order.
+//
+// Lane `sub` owns rows sub*RPL .. sub*RPL+RPL-1.  It keeps every row-indexed
+// vector -- keys, decays, queries, gains, its mean columns, the columns of its
+// covariance rows and the matching adjoints -- in the order
+//     position x  <->  row x ^ (sub*RPL).
+// Its own rows then sit at the fixed positions 0 .. RPL-1 (so the diagonal of
+// its covariance rows is at a compile-time position), and the reduce-scatter
+// of per-row partial sums needs no selects (LaneGroup::reduce_scatter_lane).
+// Global and shared-memory copies of the state stay in plain row order; the
+// helpers below translate.
+// ---------------------------------------------------------------------------
+template <int D, int LPC>
+__device__ __forceinline__ int lane_row(int x, int sub) { return x ^ (sub * (D / LPC)); }
+
+// D row-indexed elements at `base` (plain order) -> lane order.
+template <int D, int LPC, typename T>
+__device__ __forceinline__ void lds_rows(const T *base, int sub, float (&out)[D]) {
+    constexpr int RPL = D / LPC;
+#pragma unroll
+    for (int m = 0; m < LPC; ++m) {
+        float chunk[RPL];
+        lds_vec<RPL>(base + (m ^ sub) * RPL, chunk);
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) out[m * RPL + i] = chunk[i];
+    }
+}
+// Global row (D floats, plain order) <-> lane order.
+template <int D, int LPC>
+__device__ __forceinline__ void ldg_row(const float *rowp, int sub, float (&out)[D]) {
+    constexpr int RPL = D / LPC;
+#pragma unroll
+    for (int m = 0; m < LPC; ++m) {
+        float chunk[RPL];
+        load_vec<RPL>(rowp + (m ^ sub) * RPL, chunk);
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) out[m * RPL + i] = chunk[i];
+    }
+}
+template <int D, int LPC>
+__device__ __forceinline__ void stg_row(float *rowp, int sub, const float (&v)[D]) {
+    constexpr int RPL = D / LPC;
+#pragma unroll
+    for (int m = 0; m < LPC; ++m) {
+        float chunk[RPL];
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) chunk[i] = v[m * RPL + i];
+        store_vec<RPL>(rowp + (m ^ sub) * RPL, chunk);
+    }
+}
+// The lane's CPL columns (col0 ..) of a row-major [D, M] mean, rows in lane order.
+template <int D, int M, int LPC>
+__device__ __forceinline__ void ldg_mean_cols(const float *base, int col0, int sub, float (&Mc)[M / LPC][D]) {
+    constexpr int CPL = M / LPC;
+#pragma unroll
+    for (int x = 0; x < D; ++x) {
+        float row[CPL];
+        load_vec<CPL>(base + lane_row<D, LPC>(x, sub) * M + col0, row);
+#pragma unroll
+        for (int l = 0; l < CPL; ++l) Mc[l][x] = row[l];
+    }
+}
+template <int D, int M, int LPC>
+__device__ __forceinline__ void stg_mean_cols(float *base, int col0, int sub, const float (&Mc)[M / LPC][D]) {
+    constexpr int CPL = M / LPC;
+#pragma unroll
+    for (int x = 0; x < D; ++x) {
+        float row[CPL];
+#pragma unroll
+        for (int l = 0; l < CPL; ++l) row[l] = Mc[l][x];
+        store_vec<CPL>(base + lane_row<D, LPC>(x, sub) * M + col0, row);
+    }
+}
+
+// One token's inputs for this lane, read from a staged tile (keys and decays
+// in lane order: the lane's own rows at positions 0 .. RPL-1).
 template <int D, int M, int LPC>
 struct Tok {
     float k[D], a[D], v[M / LPC];
     float p, r;
-    float k_own[D / LPC], a_own[D / LPC];
 };
 
 template <int D, int M, int LPC, bool FIXED, typename TIn>
 __device__ __forceinline__ void read_tok(const char *stage, int c, int tau, int sub, Tok<D, M, LPC> &tk) {
     using G = Geo<D, M, LPC, TIn>;
-    constexpr int RPL = G::RPL, CPL = G::CPL;
-    const TIn *kr = reinterpret_cast<const TIn *>(stage + G::oK + c * G::csK + tau * G::rbK);
-    lds_vec<D>(kr, tk.k);
+    constexpr int CPL = G::CPL;
+    lds_rows<D, LPC>(reinterpret_cast<const TIn *>(stage + G::oK + c * G::csK + tau * G::rbK), sub, tk.k);
     lds_vec<CPL>(reinterpret_cast<const TIn *>(stage + G::oV + c * G::csV + tau * G::rbV) + sub * CPL, tk.v);
     if constexpr (FIXED) {
 #pragma unroll
         for (int j = 0; j < D; ++j) tk.a[j] = kFixedDecay;
         tk.p = kFixedProcess;
         tk.r = kFixedObservation;
-#pragma unroll
-        for (int r = 0; r < RPL; ++r) tk.a_own[r] = kFixedDecay;
     } else {
-        const float *ar = reinterpret_cast<const float *>(stage + G::oA + c * G::csA + tau * G::rbA);
-        lds_vec<D>(ar, tk.a);
-        lds_vec<RPL>(ar + sub * RPL, tk.a_own);
+        lds_rows<D, LPC>(reinterpret_cast<const float *>(stage + G::oA + c * G::csA + tau * G::rbA), sub, tk.a);
         tk.p = reinterpret_cast<const float *>(stage + G::oP + c * G::csP)[tau];
         tk.r = reinterpret_cast<const float *>(stage + G::oR + c * G::csP)[tau];
     }
-    lds_vec<RPL>(kr + sub * RPL, tk.k_own);
 }
 
-// One predict/update step on the lane's slice (rows row0.., columns col0..).
+// One predict/update step on the lane's slice (own rows, own columns), all
+// row-indexed arrays in lane order.
 template <int D, int M, int LPC>
 __device__ __forceinline__ void forward_step(const LaneGroup<LPC> &g, const Tok<D, M, LPC> &tk, float floor_,
                                              float (&Mc)[M / LPC][D], float (&P)[D / LPC][D], float (&u)[D],
                                              float (&u_own)[D / LPC], float (&e)[M / LPC], float &beta,
                                              float &s) {
     constexpr int RPL = D / LPC, CPL = M / LPC;
-    const int row0 = g.sub * RPL;
     float wk[D];
 #pragma unroll
-    for (int j = 0; j < D; ++j) wk[j] = tk.a[j] * tk.k[j];
+    for (int x = 0; x < D; ++x) wk[x] = tk.a[x] * tk.k[x];
+    float sp = 0.f;
 #pragma unroll
     for (int r = 0; r < RPL; ++r) {
         float z = 0.f;
 #pragma unroll
-        for (int j = 0; j < D; ++j) z = fmaf(P[r][j], wk[j], z);
-        u_own[r] = fmaf(tk.a_own[r], z, tk.p * tk.k_own[r]);
+        for (int x = 0; x < D; ++x) z = fmaf(P[r][x], wk[x], z);
+        u_own[r] = fmaf(tk.a[r], z, tk.p * tk.k[r]);
+        sp = fmaf(tk.k[r], u_own[r], sp);
     }
 #pragma unroll
     for (int l = 0; l < CPL; ++l) {
         float acc = 0.f;
 #pragma unroll
-        for (int i = 0; i < D; ++i) acc = fmaf(Mc[l][i], wk[i], acc);
+        for (int x = 0; x < D; ++x) acc = fmaf(Mc[l][x], wk[x], acc);
         e[l] = tk.v[l] - acc;
     }
-    g.template gather_rows<RPL>(u_own, u);
-    s = tk.r;
-#pragma unroll
-    for (int j = 0; j < D; ++j) s = fmaf(tk.k[j], u[j], s);
+    g.template gather_lane<RPL>(u_own, u);
+    // s = r + k.u as a butterfly sum: bit-identical in every lane of the chain
+    s = tk.r + g.allsum(sp);
     beta = 1.0f / (s < floor_ ? floor_ : s);  // clamp_min: NaN stays NaN
 #pragma unroll
     for (int l = 0; l < CPL; ++l) {
         const float be = beta * e[l];
 #pragma unroll
-        for (int i = 0; i < D; ++i) Mc[l][i] = fmaf(tk.a[i], Mc[l][i], be * u[i]);
+        for (int x = 0; x < D; ++x) Mc[l][x] = fmaf(tk.a[x], Mc[l][x], be * u[x]);
     }
-    // rows of P' = A P A + p I - beta u u^T from commutative products only,
-    // so the rows of different lanes stay bit-for-bit symmetric
+    // rows of P' = A P A + p I - beta u u^T from commutative products and a
+    // chain-wide beta, so the rows of different lanes stay bit-for-bit
+    // symmetric; the diagonal entry of own row r is at position r
 #pragma unroll
     for (int r = 0; r < RPL; ++r) {
 #pragma unroll
-        for (int j = 0; j < D; ++j) {
-            const float upd = fmaf(-beta, u_own[r] * u[j], (tk.a_own[r] * tk.a[j]) * P[r][j]);
-            P[r][j] = (j == row0 + r) ? upd + tk.p : upd;
+        for (int x = 0; x < D; ++x) {
+            const float upd = fmaf(-beta, u_own[r] * u[x], (tk.a[r] * tk.a[x]) * P[r][x]);
+            P[r][x] = (x == r) ? upd + tk.p : upd;
         }
     }
 }
@@ -303,14 +374,17 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
 #pragma unroll
     for (int r = 0; r < RPL; ++r)
 #pragma unroll
-        for (int j = 0; j < D; ++j) P[r][j] = (j == row0 + r) ? 1.f : 0.f;
-    if (active && A.mean0 != nullptr) load_mean_cols_g<D, M, CPL>(A.mean0 + chain * D * M, col0, Mc);
+        for (int x = 0; x < D; ++x) P[r][x] = (x == r) ? 1.f : 0.f;
+    if (active && A.mean0 != nullptr) ldg_mean_cols<D, M, LPC>(A.mean0 + chain * D * M, col0, sub, Mc);
     if (active && A.cov0 != nullptr) {
         const float *c0 = A.cov0 + chain * D * D;
 #pragma unroll
         for (int r = 0; r < RPL; ++r)
 #pragma unroll
-            for (int j = 0; j < D; ++j) P[r][j] = 0.5f * (c0[(row0 + r) * D + j] + c0[j * D + row0 + r]);
+            for (int x = 0; x < D; ++x) {
+                const int j = lane_row<D, LPC>(x, sub);
+                P[r][x] = 0.5f * (c0[(row0 + r) * D + j] + c0[j * D + row0 + r]);
+            }
     }
     float *bm = A.bmean + chain * (nb + 1) * D * M;
     float *bc = A.bcov + chain * (nb + 1) * D * D;
@@ -341,18 +415,18 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
             const long t = t0 + tau;
             if (t == ckpt * L) {
                 if (active) {
-                    store_mean_cols_g<D, M, CPL>(bm + ckpt * D * M, col0, Mc);
+                    stg_mean_cols<D, M, LPC>(bm + ckpt * D * M, col0, sub, Mc);
 #pragma unroll
-                    for (int r = 0; r < RPL; ++r) store_vec<D>(bc + ckpt * D * D + (row0 + r) * D, P[r]);
+                    for (int r = 0; r < RPL; ++r) stg_row<D, LPC>(bc + ckpt * D * D + (row0 + r) * D, sub, P[r]);
                 }
                 ++ckpt;
             } else if (A.rs != nullptr && (t - (ckpt - 1) * L) % kReplaySpan == 0) {
                 if (active) {
                     float *slot = replay_slot(A.rs, chain, nb, rs_slots, ckpt - 1,
                                               (t - (ckpt - 1) * L) / kReplaySpan, D, M);
-                    store_mean_cols_g<D, M, CPL>(slot, col0, Mc);
+                    stg_mean_cols<D, M, LPC>(slot, col0, sub, Mc);
 #pragma unroll
-                    for (int r = 0; r < RPL; ++r) store_vec<D>(slot + D * M + (row0 + r) * D, P[r]);
+                    for (int r = 0; r < RPL; ++r) stg_row<D, LPC>(slot + D * M + (row0 + r) * D, sub, P[r]);
                 }
             }
             Tok<D, M, LPC> tk;
@@ -360,7 +434,7 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
             float u[D], u_own[RPL], e[CPL], beta, s;
             forward_step<D, M, LPC>(g, tk, A.floor, Mc, P, u, u_own, e, beta, s);
             float qv[D];
-            lds_vec<D>(reinterpret_cast<const TIn *>(stage + G::oQ + c * G::csK + tau * G::rbK), qv);
+            lds_rows<D, LPC>(reinterpret_cast<const TIn *>(stage + G::oQ + c * G::csK + tau * G::rbK), sub, qv);
             float y[CPL];
 #pragma unroll
             for (int l = 0; l < CPL; ++l) {
@@ -375,12 +449,12 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
     }
     cp_async_wait<0>();
     if (active) {
-        store_mean_cols_g<D, M, CPL>(bm + nb * D * M, col0, Mc);
-        store_mean_cols_g<D, M, CPL>(A.mean_final + chain * D * M, col0, Mc);
+        stg_mean_cols<D, M, LPC>(bm + nb * D * M, col0, sub, Mc);
+        stg_mean_cols<D, M, LPC>(A.mean_final + chain * D * M, col0, sub, Mc);
 #pragma unroll
         for (int r = 0; r < RPL; ++r) {
-            store_vec<D>(bc + nb * D * D + (row0 + r) * D, P[r]);
-            store_vec<D>(A.cov_final + chain * D * D + (row0 + r) * D, P[r]);
+            stg_row<D, LPC>(bc + nb * D * D + (row0 + r) * D, sub, P[r]);
+            stg_row<D, LPC>(A.cov_final + chain * D * D + (row0 + r) * D, sub, P[r]);
         }
     }
 }
@@ -476,13 +550,16 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
     for (int r = 0; r < RPL; ++r)
 #pragma unroll
         for (int j = 0; j < D; ++j) R[r][j] = 0.f;
-    if (active && A.gmf != nullptr) load_mean_cols_g<D, M, CPL>(A.gmf + chain * D * M, col0, gM);
+    if (active && A.gmf != nullptr) ldg_mean_cols<D, M, LPC>(A.gmf + chain * D * M, col0, sub, gM);
     if (active && A.gcf != nullptr) {
         const float *gc = A.gcf + chain * D * D;
 #pragma unroll
         for (int r = 0; r < RPL; ++r)
 #pragma unroll
-            for (int j = 0; j < D; ++j) R[r][j] = 0.5f * (gc[(row0 + r) * D + j] + gc[j * D + row0 + r]);
+            for (int x = 0; x < D; ++x) {
+                const int j = lane_row<D, LPC>(x, sub);
+                R[r][x] = 0.5f * (gc[(row0 + r) * D + j] + gc[j * D + row0 + r]);
+            }
     }
 
     const bool have_rs = A.rs != nullptr;
@@ -519,9 +596,9 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
         if (nsub > 1 && !have_rs) {
             float Mc[CPL][D], P[RPL][D];
             if (active) {
-                load_mean_cols_g<D, M, CPL>(bm + ci * D * M, col0, Mc);
+                ldg_mean_cols<D, M, LPC>(bm + ci * D * M, col0, sub, Mc);
 #pragma unroll
-                for (int r = 0; r < RPL; ++r) load_vec<D>(bc + ci * D * D + (row0 + r) * D, P[r]);
+                for (int r = 0; r < RPL; ++r) ldg_row<D, LPC>(bc + ci * D * D + (row0 + r) * D, sub, P[r]);
             } else {
 #pragma unroll
                 for (int l = 0; l < CPL; ++l)
@@ -530,7 +607,7 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 #pragma unroll
                 for (int r = 0; r < RPL; ++r)
 #pragma unroll
-                    for (int j = 0; j < D; ++j) P[r][j] = (j == row0 + r) ? 1.f : 0.f;
+                    for (int x = 0; x < D; ++x) P[r][x] = (x == r) ? 1.f : 0.f;
             }
             for (int j = 0; j + 1 < nsub; ++j) {
                 const char *stage = acquire();
@@ -573,16 +650,16 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 #pragma unroll
                 for (int r = 0; r < RPL; ++r)
 #pragma unroll
-                    for (int jj = 0; jj < D; ++jj) P[r][jj] = (jj == row0 + r) ? 1.f : 0.f;
+                    for (int x = 0; x < D; ++x) P[r][x] = (x == r) ? 1.f : 0.f;
             } else if (j == 0) {
-                load_mean_cols_g<D, M, CPL>(bm + ci * D * M, col0, Mc);
+                ldg_mean_cols<D, M, LPC>(bm + ci * D * M, col0, sub, Mc);
 #pragma unroll
-                for (int r = 0; r < RPL; ++r) load_vec<D>(bc + ci * D * D + (row0 + r) * D, P[r]);
+                for (int r = 0; r < RPL; ++r) ldg_row<D, LPC>(bc + ci * D * D + (row0 + r) * D, sub, P[r]);
             } else if (have_rs) {
                 const float *slot = replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j, D, M);
-                load_mean_cols_g<D, M, CPL>(slot, col0, Mc);
+                ldg_mean_cols<D, M, LPC>(slot, col0, sub, Mc);
 #pragma unroll
-                for (int r = 0; r < RPL; ++r) load_vec<D>(slot + D * M + (row0 + r) * D, P[r]);
+                for (int r = 0; r < RPL; ++r) ldg_row<D, LPC>(slot + D * M + (row0 + r) * D, sub, P[r]);
             } else {
                 // written by this kernel in phase A: coherent loads
                 float flat[G::kWsLane];
@@ -650,26 +727,20 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                 for (int i = 0; i < D; ++i) Mn[l][i] = Mc[l][i];
             for (int tau = slen - 1; tau >= 0; --tau) {
                 const long row = chain * T + ci * L + static_cast<long>(j) * kS + tau;
-                float k[D], a[D], q[D], u[D], k_own[RPL], a_own[RPL], u_own[RPL];
-                const TIn *kr = reinterpret_cast<const TIn *>(stage + G::oK + c * G::csK + tau * G::rbK);
-                lds_vec<D>(kr, k);
-                lds_vec<RPL>(kr + row0, k_own);
-                lds_vec<D>(reinterpret_cast<const TIn *>(stage + G::oQ + c * G::csK + tau * G::rbK), q);
+                // row-indexed vectors in lane order: own rows at positions 0 .. RPL-1
+                float k[D], a[D], q[D], u[D];
+                lds_rows<D, LPC>(reinterpret_cast<const TIn *>(stage + G::oK + c * G::csK + tau * G::rbK), sub, k);
+                lds_rows<D, LPC>(reinterpret_cast<const TIn *>(stage + G::oQ + c * G::csK + tau * G::rbK), sub, q);
                 float p;
                 if constexpr (FIXED) {
 #pragma unroll
                     for (int jj = 0; jj < D; ++jj) a[jj] = kFixedDecay;
-#pragma unroll
-                    for (int r = 0; r < RPL; ++r) a_own[r] = kFixedDecay;
                     p = kFixedProcess;
                 } else {
-                    const float *ar = reinterpret_cast<const float *>(stage + G::oA + c * G::csA + tau * G::rbA);
-                    lds_vec<D>(ar, a);
-                    lds_vec<RPL>(ar + row0, a_own);
+                    lds_rows<D, LPC>(reinterpret_cast<const float *>(stage + G::oA + c * G::csA + tau * G::rbA), sub, a);
                     p = reinterpret_cast<const float *>(stage + G::oP + c * G::csP)[tau];
                 }
-                lds_vec<D>(hU_at(tau), u);
-                lds_vec<RPL>(hU_at(tau) + row0, u_own);
+                lds_rows<D, LPC>(hU_at(tau), sub, u);
                 const float2 bs = *reinterpret_cast<const float2 *>(hB_at(tau));
                 const float beta = bs.x, s = bs.y;
                 float e[CPL], gyv[CPL];
@@ -737,7 +808,7 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                     }
                 float tot[4][RPL];
                 if constexpr (NEED_DYN) {
-                    g.template reduce_scatter_rows<4, RPL>(part, tot);
+                    g.template reduce_scatter_lane<4, RPL>(part, tot);
                 } else {
                     float part3[3][D];
 #pragma unroll
@@ -745,7 +816,7 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 #pragma unroll
                         for (int i = 0; i < D; ++i) part3[v][i] = part[v][i];
                     float tot3[3][RPL];
-                    g.template reduce_scatter_rows<3, RPL>(part3, tot3);
+                    g.template reduce_scatter_lane<3, RPL>(part3, tot3);
 #pragma unroll
                     for (int r = 0; r < RPL; ++r) {
                         tot[0][r] = tot3[0][r];
@@ -763,8 +834,8 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 #pragma unroll
                     for (int jj = 0; jj < D; ++jj) acc = fmaf(R[r][jj], u[jj], acc);
                     Ru[r] = acc;
-                    gb = fmaf(-u_own[r], acc, gb);
-                    if constexpr (NEED_DYN) trR += pick(R[r], row0 + r);
+                    gb = fmaf(-u[r], acc, gb);
+                    if constexpr (NEED_DYN) trR += R[r][r];
                 }
                 if constexpr (NEED_DYN) {
 #pragma unroll
@@ -778,9 +849,9 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                 const float gs = (s >= floor_) ? -beta * beta * gb : 0.f;
                 float gu_own[RPL];
 #pragma unroll
-                for (int r = 0; r < RPL; ++r) gu_own[r] = beta * tot[1][r] - 2.f * beta * Ru[r] + gs * k_own[r];
+                for (int r = 0; r < RPL; ++r) gu_own[r] = beta * tot[1][r] - 2.f * beta * Ru[r] + gs * k[r];
                 float gu[D];
-                g.template gather_rows<RPL>(gu_own, gu);
+                g.template gather_lane<RPL>(gu_own, gu);
 
                 float ag[D];
 #pragma unroll
@@ -791,17 +862,17 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                     float z = 0.f;
 #pragma unroll
                     for (int jj = 0; jj < D; ++jj) z = fmaf(Pp[r][jj], ag[jj], z);
-                    const float gk3 = fmaf(a_own[r], z, p * gu_own[r]);
-                    gk_own[r] = fmaf(-a_own[r], tot[2][r], fmaf(gs, u_own[r], gk3));
+                    const float gk3 = fmaf(a[r], z, p * gu_own[r]);
+                    gk_own[r] = fmaf(-a[r], tot[2][r], fmaf(gs, u[r], gk3));
                     float gaP = 0.f;
 #pragma unroll
                     for (int jj = 0; jj < D; ++jj) {
                         // rounded products and sum, never contracted: lanes
                         // owning rows i and j form bit-identical S_ij, S_ji
-                        const float x = __fadd_rn(__fmul_rn(gu_own[r], k[jj]), __fmul_rn(gu[jj], k_own[r]));
+                        const float x = __fadd_rn(__fmul_rn(gu_own[r], k[jj]), __fmul_rn(gu[jj], k[r]));
                         const float Sj = fmaf(0.5f, x, R[r][jj]);
                         if constexpr (NEED_DYN) gaP = fmaf(Sj, a[jj] * Pp[r][jj], gaP);
-                        R[r][jj] = (a_own[r] * a[jj]) * Sj;
+                        R[r][jj] = (a[r] * a[jj]) * Sj;
                     }
                     ga_own[r] = fmaf(2.f, gaP, tot[3][r]);
                 }
@@ -848,9 +919,9 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
     cp_async_wait<0>();
     if constexpr (NEED_INIT) {
         if (active) {
-            store_mean_cols_g<D, M, CPL>(A.gm0 + chain * D * M, col0, gM);
+            stg_mean_cols<D, M, LPC>(A.gm0 + chain * D * M, col0, sub, gM);
 #pragma unroll
-            for (int r = 0; r < RPL; ++r) store_vec<D>(A.gc0 + chain * D * D + (row0 + r) * D, R[r]);
+            for (int r = 0; r < RPL; ++r) stg_row<D, LPC>(A.gc0 + chain * D * D + (row0 + r) * D, sub, R[r]);
         }
     }
 }
