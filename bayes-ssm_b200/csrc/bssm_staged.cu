@@ -344,6 +344,89 @@ __device__ __forceinline__ void forward_step(const LaneGroup<LPC> &g, const Tok<
     }
 }
 
+// Plain-order token inputs and step, used by the forward kernel: the own
+// rows' values are separate loads and the diagonal update is a select.  For
+// the latency-bound forward this measured faster than the lane-relative
+// order, which trades them for more, narrower shared-memory loads.
+template <int D, int M, int LPC>
+struct TokPlain {
+    float k[D], a[D], v[M / LPC];
+    float p, r;
+    float k_own[D / LPC], a_own[D / LPC];
+};
+
+template <int D, int M, int LPC, bool FIXED, typename TIn>
+__device__ __forceinline__ void read_tok_plain(const char *stage, int c, int tau, int sub, TokPlain<D, M, LPC> &tk) {
+    using G = Geo<D, M, LPC, TIn>;
+    constexpr int RPL = G::RPL, CPL = G::CPL;
+    const TIn *kr = reinterpret_cast<const TIn *>(stage + G::oK + c * G::csK + tau * G::rbK);
+    lds_vec<D>(kr, tk.k);
+    lds_vec<CPL>(reinterpret_cast<const TIn *>(stage + G::oV + c * G::csV + tau * G::rbV) + sub * CPL, tk.v);
+    if constexpr (FIXED) {
+#pragma unroll
+        for (int j = 0; j < D; ++j) tk.a[j] = kFixedDecay;
+        tk.p = kFixedProcess;
+        tk.r = kFixedObservation;
+#pragma unroll
+        for (int r = 0; r < RPL; ++r) tk.a_own[r] = kFixedDecay;
+    } else {
+        const float *ar = reinterpret_cast<const float *>(stage + G::oA + c * G::csA + tau * G::rbA);
+        lds_vec<D>(ar, tk.a);
+        lds_vec<RPL>(ar + sub * RPL, tk.a_own);
+        tk.p = reinterpret_cast<const float *>(stage + G::oP + c * G::csP)[tau];
+        tk.r = reinterpret_cast<const float *>(stage + G::oR + c * G::csP)[tau];
+    }
+    lds_vec<RPL>(kr + sub * RPL, tk.k_own);
+}
+
+// One predict/update step on the lane's slice (rows row0.., columns col0..).
+template <int D, int M, int LPC>
+__device__ __forceinline__ void forward_step_plain(const LaneGroup<LPC> &g, const TokPlain<D, M, LPC> &tk, float floor_,
+                                             float (&Mc)[M / LPC][D], float (&P)[D / LPC][D], float (&u)[D],
+                                             float (&u_own)[D / LPC], float (&e)[M / LPC], float &beta,
+                                             float &s) {
+    constexpr int RPL = D / LPC, CPL = M / LPC;
+    const int row0 = g.sub * RPL;
+    float wk[D];
+#pragma unroll
+    for (int j = 0; j < D; ++j) wk[j] = tk.a[j] * tk.k[j];
+#pragma unroll
+    for (int r = 0; r < RPL; ++r) {
+        float z = 0.f;
+#pragma unroll
+        for (int j = 0; j < D; ++j) z = fmaf(P[r][j], wk[j], z);
+        u_own[r] = fmaf(tk.a_own[r], z, tk.p * tk.k_own[r]);
+    }
+#pragma unroll
+    for (int l = 0; l < CPL; ++l) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < D; ++i) acc = fmaf(Mc[l][i], wk[i], acc);
+        e[l] = tk.v[l] - acc;
+    }
+    g.template gather_rows<RPL>(u_own, u);
+    s = tk.r;
+#pragma unroll
+    for (int j = 0; j < D; ++j) s = fmaf(tk.k[j], u[j], s);
+    beta = 1.0f / (s < floor_ ? floor_ : s);  // clamp_min: NaN stays NaN
+#pragma unroll
+    for (int l = 0; l < CPL; ++l) {
+        const float be = beta * e[l];
+#pragma unroll
+        for (int i = 0; i < D; ++i) Mc[l][i] = fmaf(tk.a[i], Mc[l][i], be * u[i]);
+    }
+    // rows of P' = A P A + p I - beta u u^T from commutative products only,
+    // so the rows of different lanes stay bit-for-bit symmetric
+#pragma unroll
+    for (int r = 0; r < RPL; ++r) {
+#pragma unroll
+        for (int j = 0; j < D; ++j) {
+            const float upd = fmaf(-beta, u_own[r] * u[j], (tk.a_own[r] * tk.a[j]) * P[r][j]);
+            P[r][j] = (j == row0 + r) ? upd + tk.p : upd;
+        }
+    }
+}
+
 // ===========================================================================
 // Forward
 // ===========================================================================
@@ -374,17 +457,14 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
 #pragma unroll
     for (int r = 0; r < RPL; ++r)
 #pragma unroll
-        for (int x = 0; x < D; ++x) P[r][x] = (x == r) ? 1.f : 0.f;
-    if (active && A.mean0 != nullptr) ldg_mean_cols<D, M, LPC>(A.mean0 + chain * D * M, col0, sub, Mc);
+        for (int j = 0; j < D; ++j) P[r][j] = (j == row0 + r) ? 1.f : 0.f;
+    if (active && A.mean0 != nullptr) load_mean_cols_g<D, M, CPL>(A.mean0 + chain * D * M, col0, Mc);
     if (active && A.cov0 != nullptr) {
         const float *c0 = A.cov0 + chain * D * D;
 #pragma unroll
         for (int r = 0; r < RPL; ++r)
 #pragma unroll
-            for (int x = 0; x < D; ++x) {
-                const int j = lane_row<D, LPC>(x, sub);
-                P[r][x] = 0.5f * (c0[(row0 + r) * D + j] + c0[j * D + row0 + r]);
-            }
+            for (int j = 0; j < D; ++j) P[r][j] = 0.5f * (c0[(row0 + r) * D + j] + c0[j * D + row0 + r]);
     }
     float *bm = A.bmean + chain * (nb + 1) * D * M;
     float *bc = A.bcov + chain * (nb + 1) * D * D;
@@ -415,26 +495,26 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
             const long t = t0 + tau;
             if (t == ckpt * L) {
                 if (active) {
-                    stg_mean_cols<D, M, LPC>(bm + ckpt * D * M, col0, sub, Mc);
+                    store_mean_cols_g<D, M, CPL>(bm + ckpt * D * M, col0, Mc);
 #pragma unroll
-                    for (int r = 0; r < RPL; ++r) stg_row<D, LPC>(bc + ckpt * D * D + (row0 + r) * D, sub, P[r]);
+                    for (int r = 0; r < RPL; ++r) store_vec<D>(bc + ckpt * D * D + (row0 + r) * D, P[r]);
                 }
                 ++ckpt;
             } else if (A.rs != nullptr && (t - (ckpt - 1) * L) % kReplaySpan == 0) {
                 if (active) {
                     float *slot = replay_slot(A.rs, chain, nb, rs_slots, ckpt - 1,
                                               (t - (ckpt - 1) * L) / kReplaySpan, D, M);
-                    stg_mean_cols<D, M, LPC>(slot, col0, sub, Mc);
+                    store_mean_cols_g<D, M, CPL>(slot, col0, Mc);
 #pragma unroll
-                    for (int r = 0; r < RPL; ++r) stg_row<D, LPC>(slot + D * M + (row0 + r) * D, sub, P[r]);
+                    for (int r = 0; r < RPL; ++r) store_vec<D>(slot + D * M + (row0 + r) * D, P[r]);
                 }
             }
-            Tok<D, M, LPC> tk;
-            read_tok<D, M, LPC, FIXED, TIn>(stage, c, tau, sub, tk);
+            TokPlain<D, M, LPC> tk;
+            read_tok_plain<D, M, LPC, FIXED, TIn>(stage, c, tau, sub, tk);
             float u[D], u_own[RPL], e[CPL], beta, s;
-            forward_step<D, M, LPC>(g, tk, A.floor, Mc, P, u, u_own, e, beta, s);
+            forward_step_plain<D, M, LPC>(g, tk, A.floor, Mc, P, u, u_own, e, beta, s);
             float qv[D];
-            lds_rows<D, LPC>(reinterpret_cast<const TIn *>(stage + G::oQ + c * G::csK + tau * G::rbK), sub, qv);
+            lds_vec<D>(reinterpret_cast<const TIn *>(stage + G::oQ + c * G::csK + tau * G::rbK), qv);
             float y[CPL];
 #pragma unroll
             for (int l = 0; l < CPL; ++l) {
@@ -449,12 +529,12 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
     }
     cp_async_wait<0>();
     if (active) {
-        stg_mean_cols<D, M, LPC>(bm + nb * D * M, col0, sub, Mc);
-        stg_mean_cols<D, M, LPC>(A.mean_final + chain * D * M, col0, sub, Mc);
+        store_mean_cols_g<D, M, CPL>(bm + nb * D * M, col0, Mc);
+        store_mean_cols_g<D, M, CPL>(A.mean_final + chain * D * M, col0, Mc);
 #pragma unroll
         for (int r = 0; r < RPL; ++r) {
-            stg_row<D, LPC>(bc + nb * D * D + (row0 + r) * D, sub, P[r]);
-            stg_row<D, LPC>(A.cov_final + chain * D * D + (row0 + r) * D, sub, P[r]);
+            store_vec<D>(bc + nb * D * D + (row0 + r) * D, P[r]);
+            store_vec<D>(A.cov_final + chain * D * D + (row0 + r) * D, P[r]);
         }
     }
 }

@@ -92,13 +92,16 @@ def test_backward_recomputes_replay_states(d, chunks):
 
 
 def test_replay_states_match_recomputed_states():
-    """Both backward modes give bit-identical gradients."""
+    """Both backward modes agree: states saved by the forward kernel vs states
+    the backward recomputes itself.  The forward kernel and the backward's
+    replay evaluate the same recurrence with different summation orders, so
+    the two agree to rounding, within the FP32 parity bar."""
     inp = make_inputs(24, 90, 8, 8, seed=77, init="random")
     gy, gmt, gpt = _grads_out(24, 90, 8, 8, 0)
     a = capi_backward(inp, capi_forward(inp, chunks=32, replay_states=True), gy, gmt, gpt, chunks=32)
     b = capi_backward(inp, capi_forward(inp, chunks=32, replay_states=False), gy, gmt, gpt, chunks=32)
     for key in a:
-        assert torch.equal(a[key], b[key]), key
+        assert_parity(a[key], b[key].cpu().numpy(), rel=1e-6, cos=0.999999, what=f"grad {key}")
 
 
 @pytest.mark.parametrize("d", DIMS)
