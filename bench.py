@@ -54,10 +54,11 @@ BWD_FLOPS = (FWD_FLOPS - 2 * D * M) + (18 * D * D + 22 * D * M + 10 * D + M)
 # FP32 non-tensor peak: no measured figure exists on this pool, so the nominal
 # 148 SMs x 128 FP32 lanes x 2 flop x 1965 MHz is used and labelled as such.
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
-# DRAM traffic per backward launch measured by ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum) on this exact workload; see
-# profiles/backward_d8m8_config3.md.  None until a capture exists.
-NCU_BWD_TRAFFIC_BYTES = None
+# DRAM traffic per backward launch (dram__bytes_read.sum + dram__bytes_write.sum)
+# from one ncu capture of the half-size case (8,192 chains, one full wave at
+# the same per-SM occupancy), scaled by chains to the 16,384-chain launch: every
+# chain moves the same bytes.  See profiles/backward_staged_d8m8_bf16.md.
+NCU_BWD_TRAFFIC_BYTES = 2 * (1043.770e6 + 348.490e6)
 
 
 def _peaks():
@@ -335,9 +336,9 @@ def main() -> None:
         bwd_tflops = chain_steps * BWD_FLOPS / (bwd_ms / 1e3) / 1e12
         fwd_gbs = chain_steps * FWD_BYTES / (fwd_ms / 1e3) / 1e9
         fwd_tflops = chain_steps * FWD_FLOPS / (fwd_ms / 1e3) / 1e12
-        traffic = NCU_BWD_TRAFFIC_BYTES
+        traffic = NCU_BWD_TRAFFIC_BYTES if n == N_CHAINS else None
         roofline = {
-            "kernel": "backward_kernel<8,8,...,bf16> (dominant: replay backward)",
+            "kernel": "backward_staged<8,8,4,0,1,0,bf16> (dominant: replay backward)",
             "bound": "hbm", "achieved": round(bwd_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(bwd_gbs / hbm_peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
             "traffic": traffic,
