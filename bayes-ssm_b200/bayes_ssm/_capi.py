@@ -44,6 +44,8 @@ _SIGNATURES = {
     "bssm_assoc_scan_ex": ([_i, _i] + [_vp] * 10 + [_l, _l, _d, _vp], _i),
     "bssm_backward_noalloc_max_scratch_bytes": ([], _sz),
     "bssm_backward_chunked_noalloc": ([_i, _i, _i, _i, _i, _i] + [_vp] * 21 + [_l, _l, _i, _d, _vp], _i),
+    "bssm_debug_wait_timeouts": ([], ctypes.c_uint),
+    "bssm_debug_last_family": ([], _i),
 }
 
 
@@ -139,3 +141,16 @@ def backward_chunked_noalloc(key_dim, value_dim, io_dtype, fixed, need_dynamics,
         ptr(bmean), ptr(bcov), ptr(gy), ptr(gmf), ptr(gcf), ptr(gk), ptr(gv), ptr(gq), ptr(gd),
         ptr(gp), ptr(gr), ptr(gm0), ptr(gc0), n, t, chunks, float(floor), stream)
     check(rc, "bssm_backward_chunked_noalloc")
+
+
+def wait_timeouts() -> int:
+    """Bounded in-kernel waits that gave up since load (0 in a healthy run)."""
+    return int(load().bssm_debug_wait_timeouts())
+
+
+FAMILIES = {0: None, 1: "chain", 2: "staged", 3: "v1"}
+
+
+def last_family() -> str | None:
+    """Kernel family of this thread's last forward/backward call."""
+    return FAMILIES[int(load().bssm_debug_last_family())]

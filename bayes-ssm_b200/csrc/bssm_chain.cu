@@ -1,0 +1,1271 @@
+// bssm_chain.cu -- thread-per-chain forward and replay backward for sm_100a.
+//
+// Same recurrence and adjoint as the other kernel families (catid/bayes-ssm
+// bayes_ssm/bayesian_layer.py:153-181 and :207-251; adjoint formula sheet
+// bayes_ssm/persistent_bayes_chunked_d8.cu:358-419), organised so that one
+// thread owns one chain:
+//
+// * The thread keeps the chain's covariance as its upper triangle (D(D+1)/2
+//   registers) and its mean as D x M registers.  The predict / update /
+//   readout and the whole reverse step are thread-local: no shuffle, no
+//   partial sums to exchange, and every symmetric covariance entry (and its
+//   adjoint) is computed once.
+// * A CTA is 4 warps = 128 chains; a warp's 32 chains are consecutive.  Token
+//   inputs move by TMA: per tile of kS tokens, one lane issues one tensor copy
+//   per input field for the warp's 32 chains.  The tensor maps traverse
+//   (row, chain, token), so a tile lands token-major in shared memory and
+//   thread c reads its row of token tau at [tau][c][.]: consecutive threads,
+//   consecutive rows, no bank conflict and no per-thread address arithmetic.
+//   Outputs leave the same way (staged rows, then TMA tensor stores).
+// * Backward (one launch): for each kS-token sub-chunk, last to first, the
+//   thread reloads the sub-chunk's start state (saved by the forward every kS
+//   tokens, or the boundary checkpoint), replays the sub-chunk -- a
+//   covariance pass, then a mean pass -- and runs the reverse step over it.
+//   The per-token history (pre-step mean and covariance, gain, innovation,
+//   beta, s) lives in tensor memory: lane = chain, ~120 columns per token at
+//   D8M8.  Registers hold only the adjoint state (dL/dM, R = sym dL/dP) and
+//   the working set of one token.
+//
+// The TMA path needs tile starts and rows aligned to 16 bytes: T and the
+// chunk length multiples of kS, key rows of 16 bytes (D8 in BF16, D4/D8 in
+// FP32).  chain_eligible() checks this; other shapes use the other families.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "bayes_ssm_b200.h"
+#include "bssm_common.cuh"
+#include "bssm_internal.h"
+#include "bssm_tmem.cuh"
+
+namespace bssm {
+namespace chain {
+
+constexpr int kS = kReplaySpan;  // tokens per tile = replay sub-chunk
+constexpr int kWarps = 4;        // one warp per TMEM lane quarter
+constexpr int kThreads = 32 * kWarps;
+constexpr int kSmemMax = 227 * 1024;
+
+constexpr int al128(int x) { return (x + 127) / 128 * 128; }
+
+// N consecutive floats from 16-byte aligned shared memory.
+template <int N>
+__device__ __forceinline__ void lds_n(const float *p, float (&o)[N]) {
+#pragma unroll
+    for (int i = 0; i + 4 <= N; i += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(p + i);
+        o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
+    }
+    constexpr int b = N / 4 * 4;
+    if constexpr (N % 4 >= 2) {
+        const float2 v = *reinterpret_cast<const float2 *>(p + b);
+        o[b] = v.x; o[b + 1] = v.y;
+    }
+    if constexpr (N % 2 == 1) o[N - 1] = p[N - 1];
+}
+__device__ __forceinline__ float sel4(const float (&x)[4], int i) {
+    return i == 0 ? x[0] : i == 1 ? x[1] : i == 2 ? x[2] : x[3];
+}
+
+
+__device__ __forceinline__ float sel4v(const float4 &x, int i) {
+    return i == 0 ? x.x : i == 1 ? x.y : i == 2 ? x.z : x.w;
+}
+
+// ---- mbarriers ---------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, int bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// Bounded wait for the phase of the given parity.  A wait that gives up is
+// counted (the results are then wrong, never a hang); the host reads the
+// count through bssm_debug_wait_timeouts().
+__device__ unsigned int g_wait_timeouts = 0;
+constexpr int kWaitLimit = 1 << 22;
+__device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity) {
+    const uint32_t addr = smem_u32(bar);
+    for (int it = 0; it < kWaitLimit; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return;
+    }
+    atomicAdd(&g_wait_timeouts, 1u);
+}
+
+// ---- TMA tensor copies (no multicast) ------------------------------------------
+__device__ __forceinline__ void tma_load_3d(void *sdst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(sdst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void *sdst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(sdst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, int x, int y, int z, const void *ssrc) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z), "r"(smem_u32(ssrc))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *ssrc) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_u32(ssrc))
+                 : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most N of the issuing thread's committed groups may still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Tensor maps of one launch.  Token maps traverse (row, chain, token) with a
+// box of (row, 32 chains, kS tokens); noise maps (token, chain) with a box of
+// (kS tokens, 32 chains); the replay-state map (float, chain) with a box of
+// (one state, 32 chains).
+struct FwdMaps {
+    CUtensorMap k, q, v, a, p, r, y, rs;
+};
+struct BwdMaps {
+    CUtensorMap k, q, v, a, p, r, gy, rs, gk, gv, gq, ga, gp, gr;
+};
+
+// Shared-memory geometry of one warp's tile (one stage), box layouts.
+template <int D, int M, bool FIXED, bool BWD, typename TIn>
+struct Tile {
+    static constexpr int rbK = D * static_cast<int>(sizeof(TIn)), rbV = M * static_cast<int>(sizeof(TIn));
+    static constexpr int szK = kS * 32 * rbK, szV = kS * 32 * rbV, szA = FIXED ? 0 : kS * 32 * D * 4;
+    static constexpr int szP = FIXED ? 0 : 32 * kS * 4, szG = BWD ? kS * 32 * M * 4 : 0;
+    static constexpr int oK = 0, oQ = al128(oK + szK), oV = al128(oQ + szK), oA = al128(oV + szV);
+    static constexpr int oP = al128(oA + szA), oR = al128(oP + szP), oG = al128(oR + szP);
+    static constexpr int kBytes = al128(oG + szG);
+    static constexpr int kTx = 2 * szK + szV + szA + 2 * szP;  // bytes the token maps deliver, without gy
+};
+
+// The warp's copies of tokens [t0, t0+kS) of chains [chain0, chain0+32),
+// issued by one lane; the stage is complete when `bytes` have landed.
+template <int D, int M, bool FIXED, bool BWD, typename TIn, typename Maps>
+__device__ __forceinline__ void issue_tile(char *tile, const Maps &mp, int chain0, int t0, bool with_gy,
+                                           uint64_t *bar, int extra_bytes) {
+    using Tl = Tile<D, M, FIXED, BWD, TIn>;
+    mbar_arrive_tx(bar, Tl::kTx + (with_gy ? Tl::szG : 0) + extra_bytes);
+    tma_load_3d(tile + Tl::oK, &mp.k, 0, chain0, t0, bar);
+    tma_load_3d(tile + Tl::oQ, &mp.q, 0, chain0, t0, bar);
+    tma_load_3d(tile + Tl::oV, &mp.v, 0, chain0, t0, bar);
+    if constexpr (!FIXED) {
+        tma_load_3d(tile + Tl::oA, &mp.a, 0, chain0, t0, bar);
+        tma_load_2d(tile + Tl::oP, &mp.p, t0, chain0, bar);
+        tma_load_2d(tile + Tl::oR, &mp.r, t0, chain0, bar);
+    }
+    if constexpr (BWD) {
+        if (with_gy) tma_load_3d(tile + Tl::oG, &mp.gy, 0, chain0, t0, bar);
+    }
+}
+
+// Reads of token tau's rows for lane c from a tile.
+template <int D, int M, bool FIXED, bool BWD, typename TIn>
+struct TileRead {
+    using Tl = Tile<D, M, FIXED, BWD, TIn>;
+    const char *t;
+    int c;
+    __device__ __forceinline__ void keys(int tau, float (&k)[D]) const {
+        lds_vec<D>(reinterpret_cast<const TIn *>(t + Tl::oK) + (tau * 32 + c) * D, k);
+    }
+    __device__ __forceinline__ void queries(int tau, float (&q)[D]) const {
+        lds_vec<D>(reinterpret_cast<const TIn *>(t + Tl::oQ) + (tau * 32 + c) * D, q);
+    }
+    __device__ __forceinline__ void values(int tau, float (&v)[M]) const {
+        lds_vec<M>(reinterpret_cast<const TIn *>(t + Tl::oV) + (tau * 32 + c) * M, v);
+    }
+    __device__ __forceinline__ void decay(int tau, float (&a)[D]) const {
+        if constexpr (FIXED) {
+#pragma unroll
+            for (int j = 0; j < D; ++j) a[j] = kFixedDecay;
+        } else {
+            lds_vec<D>(reinterpret_cast<const float *>(t + Tl::oA) + (tau * 32 + c) * D, a);
+        }
+    }
+    __device__ __forceinline__ void noise(float4 &p4, float4 &r4) const {
+        if constexpr (FIXED) {
+            p4 = make_float4(kFixedProcess, kFixedProcess, kFixedProcess, kFixedProcess);
+            r4 = make_float4(kFixedObservation, kFixedObservation, kFixedObservation, kFixedObservation);
+        } else {
+            p4 = reinterpret_cast<const float4 *>(t + Tl::oP)[c];
+            r4 = reinterpret_cast<const float4 *>(t + Tl::oR)[c];
+        }
+    }
+    __device__ __forceinline__ void gy(int tau, float (&g)[M]) const {
+        lds_vec<M>(reinterpret_cast<const float *>(t + Tl::oG) + (tau * 32 + c) * M, g);
+    }
+};
+
+// ---------------------------------------------------------------------------
+// The recurrence on one thread's registers.  P is the packed upper triangle.
+// Products are the same commutative pairs, in the same order, as the other
+// kernel families use.
+// ---------------------------------------------------------------------------
+template <int D>
+__device__ __forceinline__ void cov_step(float (&P)[tri_size(D)], const float (&k)[D], const float (&a)[D],
+                                         float p, float r, float floor_, float (&u)[D], float &beta, float &s) {
+    float wk[D];
+#pragma unroll
+    for (int j = 0; j < D; ++j) wk[j] = a[j] * k[j];
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+        float z = 0.f;
+#pragma unroll
+        for (int j = 0; j < D; ++j) z = fmaf(P[tri_index(D, i, j)], wk[j], z);
+        u[i] = fmaf(a[i], z, p * k[i]);
+    }
+    s = r;
+#pragma unroll
+    for (int j = 0; j < D; ++j) s = fmaf(k[j], u[j], s);
+    beta = 1.0f / (s < floor_ ? floor_ : s);  // clamp_min: NaN stays NaN
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int j = i; j < D; ++j) {
+            const int t = tri_index(D, i, j);
+            const float upd = fmaf(-beta, u[i] * u[j], (a[i] * a[j]) * P[t]);
+            P[t] = (i == j) ? upd + p : upd;
+        }
+}
+
+template <int D, int M>
+__device__ __forceinline__ void mean_step(float (&Mm)[D][M], const float (&k)[D], const float (&a)[D],
+                                          const float (&v)[M], const float (&u)[D], float beta, float (&e)[M]) {
+    float wk[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) wk[i] = a[i] * k[i];
+#pragma unroll
+    for (int c = 0; c < M; ++c) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < D; ++i) acc = fmaf(Mm[i][c], wk[i], acc);
+        e[c] = v[c] - acc;
+    }
+#pragma unroll
+    for (int c = 0; c < M; ++c) {
+        const float be = beta * e[c];
+#pragma unroll
+        for (int i = 0; i < D; ++i) Mm[i][c] = fmaf(a[i], Mm[i][c], be * u[i]);
+    }
+}
+
+// State <-> global memory (row-major mean, full covariance).
+template <int D, int M>
+__device__ __forceinline__ void store_mean(float *dst, const float (&Mm)[D][M]) {
+#pragma unroll
+    for (int i = 0; i < D; ++i) store_vec<M>(dst + i * M, Mm[i]);
+}
+template <int D>
+__device__ __forceinline__ void store_cov_full(float *dst, const float (&P)[tri_size(D)]) {
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+        float row[D];
+#pragma unroll
+        for (int j = 0; j < D; ++j) row[j] = P[tri_index(D, i, j)];
+        store_vec<D>(dst + i * D, row);
+    }
+}
+// Packed replay state: [mean D*M | covariance upper triangle | pad], into
+// 16-byte aligned shared memory (staging for a bulk store).
+template <int D, int M>
+__device__ __forceinline__ void stage_packed_state(float *dst, const float (&Mm)[D][M],
+                                                   const float (&P)[tri_size(D)]) {
+    constexpr int SF = replay_state_floats(D, M);
+    float flat[SF];
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int c = 0; c < M; ++c) flat[i * M + c] = Mm[i][c];
+#pragma unroll
+    for (int t = 0; t < tri_size(D); ++t) flat[D * M + t] = P[t];
+#pragma unroll
+    for (int x = D * M + tri_size(D); x < SF; ++x) flat[x] = 0.f;
+    sts_vec<SF>(dst, flat);
+}
+
+// Order in which a chain's tiles are consumed by the forward: chunk by chunk,
+// kS-token sub-chunks in order (sub-chunks restart at every chunk boundary,
+// so the replay states sit at tile starts).
+struct FwdItems {
+    long T, ci, nb;
+    int L, j, nsub, len;
+    bool done;
+    __device__ __forceinline__ void enter() {
+        const long t0 = ci * L;
+        len = static_cast<int>((T - t0) < L ? (T - t0) : L);
+        nsub = (len + kS - 1) / kS;
+        j = 0;
+    }
+    __device__ __forceinline__ void init(long T_, int L_) {
+        T = T_;
+        L = L_;
+        nb = (T + L - 1) / L;
+        ci = 0;
+        done = nb <= 0;
+        if (!done) enter();
+    }
+    __device__ __forceinline__ void advance() {
+        if (++j >= nsub) {
+            if (++ci >= nb) {
+                done = true;
+            } else {
+                enter();
+            }
+        }
+    }
+    __device__ __forceinline__ long t0() const { return ci * L + static_cast<long>(j) * kS; }
+    __device__ __forceinline__ int ntok() const { return (len - j * kS) < kS ? (len - j * kS) : kS; }
+};
+
+template <int D, int M, bool FIXED, typename TIn>
+struct FwdGeo {
+    using Tl = Tile<D, M, FIXED, false, TIn>;
+    static constexpr int SF = replay_state_floats(D, M);
+    static constexpr int kYB = kS * 32 * M * 4;  // a warp's readout rows, box layout [tau][chain][M]
+    static constexpr int kSB = 32 * SF * 4;      // a warp's states, box layout [chain][SF]
+    static constexpr int kPerStage = kWarps * Tl::kBytes;
+    static constexpr int kFixed = kWarps * (2 * kYB + kSB) + 128 + kWarps * 4 * 8;
+    static constexpr int kFit = (kSmemMax - kFixed) / kPerStage;
+    static constexpr int kStages = kFit < 4 ? kFit : 4;
+    static_assert(kStages >= 2, "forward tile too large");
+    static constexpr int oY = 0;                            // [warp][2][kYB]
+    static constexpr int oS = oY + kWarps * 2 * kYB;        // [warp][kSB]
+    static constexpr int oT = al128(oS + kWarps * kSB);     // [stage][warp][tile]
+    static constexpr int oBar = oT + kStages * kPerStage;   // [warp][stage]
+    static constexpr int kSmem = oBar + kWarps * kStages * 8 + 128;  // + alignment slack
+    static_assert(kSmem <= kSmemMax, "forward shared memory");
+};
+
+// 128-byte aligned start of dynamic shared memory.
+__device__ __forceinline__ char *smem_base(char *raw) {
+    const uint32_t a = smem_u32(raw);
+    return raw + ((128 - (a & 127)) & 127);
+}
+
+// ===========================================================================
+// Forward
+// ===========================================================================
+template <int D, int M, bool FIXED, typename TIn>
+__global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> A, const __grid_constant__ FwdMaps mp) {
+    using G = FwdGeo<D, M, FIXED, TIn>;
+    using Tl = typename G::Tl;
+    constexpr int NS = G::kStages, TRI = tri_size(D), SF = G::SF;
+    extern __shared__ __align__(128) char smem_raw[];
+    char *const smem = smem_base(smem_raw);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int chain0 = static_cast<int>(blockIdx.x) * kThreads + warp * 32;
+    const long chain = chain0 + lane;
+    const bool active = chain < A.n;
+    const long T = A.t;
+    const int L = A.chunks;
+    const long nb = (T + L - 1) / L;
+    const long rs_slots = replay_slots_per_chunk(T, L);
+    char *const tiles = smem + G::oT + warp * Tl::kBytes;  // + stage * G::kPerStage
+    char *const ybuf = smem + G::oY + warp * 2 * G::kYB;
+    float *const sbuf = reinterpret_cast<float *>(smem + G::oS + warp * G::kSB);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + warp * NS;
+    if (lane == 0) {
+        for (int s = 0; s < NS; ++s) mbar_init(bars + s, 1);
+        mbar_init_fence();
+    }
+    __syncwarp();
+
+    float Mm[D][M], P[TRI];
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int c = 0; c < M; ++c) Mm[i][c] = 0.f;
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int j = i; j < D; ++j) P[tri_index(D, i, j)] = (i == j) ? 1.f : 0.f;
+    if (active && A.mean0 != nullptr) {
+#pragma unroll
+        for (int i = 0; i < D; ++i) load_vec<M>(A.mean0 + chain * D * M + i * M, Mm[i]);
+    }
+    if (active && A.cov0 != nullptr) {
+        const float *c0 = A.cov0 + chain * D * D;
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+#pragma unroll
+            for (int j = i; j < D; ++j) P[tri_index(D, i, j)] = 0.5f * (c0[i * D + j] + c0[j * D + i]);
+    }
+    float *const bm = A.bmean + chain * (nb + 1) * D * M;
+    float *const bc = A.bcov + chain * (nb + 1) * D * D;
+
+    FwdItems prod, cons;
+    prod.init(T, L);
+    cons.init(T, L);
+    if (lane == 0) {
+        for (int s = 0; s < NS - 1 && !prod.done; ++s) {
+            issue_tile<D, M, FIXED, false, TIn>(tiles + s * G::kPerStage, mp, chain0, static_cast<int>(prod.t0()),
+                                                false, bars + s, 0);
+            prod.advance();
+        }
+    } else {
+        for (int s = 0; s < NS - 1 && !prod.done; ++s) prod.advance();
+    }
+    long q = 0;
+    while (!cons.done) {
+        // every lane is done with the stage about to be refilled (it held tile q-1)
+        __syncwarp();
+        if (!prod.done) {
+            const int st = static_cast<int>((q + NS - 1) % NS);
+            if (lane == 0)
+                issue_tile<D, M, FIXED, false, TIn>(tiles + st * G::kPerStage, mp, chain0,
+                                                    static_cast<int>(prod.t0()), false, bars + st, 0);
+            prod.advance();
+        }
+        // staging: the state buffer (last read by tile q-1's state store) and
+        // readout buffer q&1 (tile q-2's store) are free once every store but
+        // the newest (tile q-1's readout) has read its source
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        mbar_wait(bars + q % NS, static_cast<uint32_t>((q / NS) & 1));
+        const TileRead<D, M, FIXED, false, TIn> rd{tiles + (q % NS) * G::kPerStage, lane};
+        const long ci = cons.ci;
+        const int t0 = static_cast<int>(cons.t0());
+        if (cons.j == 0) {
+            if (active) {
+                store_mean<D, M>(bm + ci * D * M, Mm);
+                store_cov_full<D>(bc + ci * D * D, P);
+            }
+        } else if (A.rs != nullptr) {
+            stage_packed_state<D, M>(sbuf + lane * SF, Mm, P);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&mp.rs, static_cast<int>((ci * rs_slots + cons.j - 1) * SF), chain0, sbuf);
+                bulk_commit();
+            }
+        }
+        float *const yb = reinterpret_cast<float *>(ybuf + (q & 1) * G::kYB);
+        float4 p4, r4;
+        rd.noise(p4, r4);
+        auto step = [&](int tau) {
+            float k[D], a[D], v[M], qv[D];
+            const float p = sel4v(p4, tau), r = sel4v(r4, tau);
+            rd.keys(tau, k);
+            rd.decay(tau, a);
+            rd.values(tau, v);
+            float u[D], e[M], beta, s;
+            cov_step<D>(P, k, a, p, r, A.floor, u, beta, s);
+            mean_step<D, M>(Mm, k, a, v, u, beta, e);
+            rd.queries(tau, qv);
+            float y[M];
+#pragma unroll
+            for (int c = 0; c < M; ++c) {
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < D; ++i) acc = fmaf(Mm[i][c], qv[i], acc);
+                y[c] = acc;
+            }
+            sts_vec<M>(yb + (tau * 32 + lane) * M, y);
+        };
+#pragma unroll 1
+        for (int tau = 0; tau < kS; ++tau) step(tau);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_3d(&mp.y, 0, chain0, t0, yb);
+            bulk_commit();
+        }
+        cons.advance();
+        ++q;
+    }
+    if (active) {
+        store_mean<D, M>(bm + nb * D * M, Mm);
+        store_cov_full<D>(bc + nb * D * D, P);
+        store_mean<D, M>(A.mean_final + chain * D * M, Mm);
+        store_cov_full<D>(A.cov_final + chain * D * D, P);
+    }
+    if (lane == 0) bulk_wait_all();
+}
+
+// ===========================================================================
+// Backward
+// ===========================================================================
+
+// TMEM columns of one lane (= one chain).  Fields, each kept for the kS
+// tokens of the current sub-chunk:
+// (kRp, one copy: the covariance adjoint, parked while the sub-chunk is
+// replayed so that its registers serve the replay.)
+enum Field { kMp = 0, kPp = 1, kU = 2, kE = 3, kBS = 4, kRp = 5, kNumFields = 6 };
+// Every field is split into power-of-two pieces of at most 32 columns
+// (binary expansion, largest first); all pieces of one width are placed
+// together, widest first, so every piece starts at a multiple of its width.
+template <int D, int M>
+struct TLayout {
+    __host__ __device__ static constexpr int size(int f) {
+        return f == kMp ? D * M : f == kPp ? tri_size(D) : f == kU ? D : f == kE ? M : f == kBS ? 2 : tri_size(D);
+    }
+    __host__ __device__ static constexpr int copies(int f) { return f == kRp ? 1 : kS; }
+    __host__ __device__ static constexpr int npieces(int n, int w) { return w == 32 ? n / 32 : (((n % 32) & w) ? 1 : 0); }
+    // position inside the field of the first piece of width w
+    __host__ __device__ static constexpr int piece_pos(int n, int w) {
+        int p = (n / 32) * 32;
+        if (w == 32) return 0;
+        for (int x = 16; x > w; x >>= 1)
+            if ((n % 32) & x) p += x;
+        return p;
+    }
+    // column of the first piece of width w of field f, token 0
+    __host__ __device__ static constexpr int col0(int f, int w) {
+        int c = 0;
+        for (int x = 32; x > w; x >>= 1)
+            for (int g = 0; g < kNumFields; ++g) c += copies(g) * npieces(size(g), x) * x;
+        for (int g = 0; g < f; ++g) c += copies(g) * npieces(size(g), w) * w;
+        return c;
+    }
+    __host__ __device__ static constexpr int total() {
+        int c = 0;
+        for (int x = 32; x >= 1; x >>= 1)
+            for (int g = 0; g < kNumFields; ++g) c += copies(g) * npieces(size(g), x) * x;
+        return c;
+    }
+    __host__ __device__ static constexpr int alloc() {
+        int a = 32;
+        while (a < total()) a *= 2;
+        return a;
+    }
+    static_assert(total() <= 512, "history does not fit in tensor memory");
+};
+
+template <int D, int M, int F, int W = 32>
+__device__ __forceinline__ void field_st(uint32_t base, int tau, const uint32_t *r) {
+    using TL = TLayout<D, M>;
+    constexpr int n = TL::size(F), np = TL::npieces(n, W);
+    if constexpr (np > 0) {
+        constexpr int c0 = TL::col0(F, W), pos = TL::piece_pos(n, W);
+#pragma unroll
+        for (int idx = 0; idx < np; ++idx) tmem::st_cols<W>(base + c0 + (tau * np + idx) * W, r + pos + idx * W);
+    }
+    if constexpr (W > 1) field_st<D, M, F, W / 2>(base, tau, r);
+}
+template <int D, int M, int F, int W = 32>
+__device__ __forceinline__ void field_ld(uint32_t base, int tau, uint32_t *r) {
+    using TL = TLayout<D, M>;
+    constexpr int n = TL::size(F), np = TL::npieces(n, W);
+    if constexpr (np > 0) {
+        constexpr int c0 = TL::col0(F, W), pos = TL::piece_pos(n, W);
+#pragma unroll
+        for (int idx = 0; idx < np; ++idx) tmem::ld_cols<W>(base + c0 + (tau * np + idx) * W, r + pos + idx * W);
+    }
+    if constexpr (W > 1) field_ld<D, M, F, W / 2>(base, tau, r);
+}
+// Store N floats as field F of token tau.
+template <int D, int M, int F, int N>
+__device__ __forceinline__ void put(uint32_t base, int tau, const float *v) {
+    static_assert(N == TLayout<D, M>::size(F), "field size");
+    uint32_t r[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) r[i] = __float_as_uint(v[i]);
+    field_st<D, M, F>(base, tau, r);
+}
+// Load field F of token tau (waits for the load).
+template <int D, int M, int F, int N>
+__device__ __forceinline__ void get(uint32_t base, int tau, float *v) {
+    static_assert(N == TLayout<D, M>::size(F), "field size");
+    uint32_t r[N];
+    field_ld<D, M, F>(base, tau, r);
+    tmem::wait_ld_bind<N>(r);
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Load rows [R0, R0+NR) of the pre-step mean of token tau.  The mean field
+// is row-major, so for M = 8 a 32-column piece is 4 whole rows.
+template <int D, int M, int R0, int NR>
+__device__ __forceinline__ void get_mean_rows(uint32_t base, int tau, float (&out)[NR][M]) {
+    using TL = TLayout<D, M>;
+    constexpr int n = D * M;
+    uint32_t r[NR * M];
+    if constexpr (n >= 32) {
+        static_assert((R0 * M) % 32 == 0 && (NR * M) % 32 == 0, "row block = whole pieces");
+        constexpr int np = TL::npieces(n, 32), c0 = TL::col0(kMp, 32);
+#pragma unroll
+        for (int b = 0; b < NR * M / 32; ++b)
+            tmem::ld_cols<32>(base + c0 + (tau * np + R0 * M / 32 + b) * 32, r + 32 * b);
+    } else {
+        static_assert(R0 == 0 && NR == D, "small means load whole");
+        field_ld<D, M, kMp>(base, tau, r);
+    }
+    tmem::wait_ld_bind<NR * M>(r);
+#pragma unroll
+    for (int i = 0; i < NR; ++i)
+#pragma unroll
+        for (int c = 0; c < M; ++c) out[i][c] = __uint_as_float(r[i * M + c]);
+}
+
+// Consumption order of the backward: chunks from the last, kS-token
+// sub-chunks from the last.
+struct BwdItems {
+    long T, ci;
+    int L, j, nsub, len;
+    bool done;
+    __device__ __forceinline__ void enter() {
+        const long t0 = ci * L;
+        len = static_cast<int>((T - t0) < L ? (T - t0) : L);
+        nsub = (len + kS - 1) / kS;
+        j = nsub - 1;
+    }
+    __device__ __forceinline__ void init(long T_, int L_) {
+        T = T_;
+        L = L_;
+        ci = (T + L - 1) / L - 1;
+        done = ci < 0;
+        if (!done) enter();
+    }
+    __device__ __forceinline__ void advance() {
+        if (--j < 0) {
+            if (--ci < 0) {
+                done = true;
+            } else {
+                enter();
+            }
+        }
+    }
+    __device__ __forceinline__ long t0() const { return ci * L + static_cast<long>(j) * kS; }
+    __device__ __forceinline__ int ntok() const { return (len - j * kS) < kS ? (len - j * kS) : kS; }
+};
+
+
+template <int D, int M, bool FIXED, typename TIn>
+struct BwdGeo {
+    using Tl = Tile<D, M, FIXED, true, TIn>;
+    static constexpr int SF = replay_state_floats(D, M);
+    static constexpr int kSB = 32 * SF * 4;  // a warp's start states, box layout [chain][SF]
+    // a warp's gradient rows of one sub-chunk, box layouts: keys, values,
+    // queries, decay [tau][chain][row]; process, observation [chain][tau]
+    static constexpr int rbK = Tl::rbK, rbV = Tl::rbV;
+    static constexpr int gK = 0, gV = al128(gK + kS * 32 * rbK), gQ = al128(gV + kS * 32 * rbV);
+    static constexpr int gA = al128(gQ + kS * 32 * rbK), gP = al128(gA + kS * 32 * D * 4);
+    static constexpr int gR = al128(gP + 32 * kS * 4), kOB = al128(gR + 32 * kS * 4);
+    static constexpr int kPerStage = kWarps * Tl::kBytes;
+    static constexpr int oT = 0;                              // [stage][warp][tile]
+    static constexpr int oS = oT + 2 * kPerStage;             // [warp][kSB]
+    static constexpr int oO = al128(oS + kWarps * kSB);       // [warp][kOB]
+    static constexpr bool kStageOut = oO + kWarps * kOB + kWarps * 2 * 8 + 16 + 128 <= kSmemMax;
+    static constexpr int oBar = kStageOut ? oO + kWarps * kOB : oO;  // [warp][stage]
+    static constexpr int oSlot = oBar + kWarps * 2 * 8;
+    static constexpr int kSmem = oSlot + 16 + 128;  // + alignment slack
+    static_assert(kSmem <= kSmemMax, "backward shared memory");
+};
+
+// One gradient row of token tau: into the staging box (written back at the
+// sub-chunk's end), or straight to global memory.
+template <bool STAGE, int N, typename T>
+__device__ __forceinline__ void put_row(T *stage_row, T *gdst, const float (&v)[N], bool active) {
+    if constexpr (STAGE) {
+        store_vec<N>(stage_row, v);
+    } else if (active) {
+        store_vec<N>(gdst, v);
+    }
+}
+
+// Copy a sub-chunk's start state from a boundary checkpoint (full
+// covariance, by its upper triangle) into this thread's state row.
+template <int D, int M>
+__device__ __forceinline__ void issue_checkpoint(uint32_t sdst, const float *ck_mean, const float *ck_cov) {
+    static_assert((D * M) % 4 == 0, "mean rows");
+#pragma unroll
+    for (int x = 0; x < D * M / 4; ++x) cp_async<16>(sdst + 16 * x, ck_mean + 4 * x);
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int j = i; j < D; ++j) cp_async<4>(sdst + 4 * (D * M + tri_index(D, i, j)), ck_cov + i * D + j);
+}
+
+template <int D, int M, bool FIXED, bool NEED_DYN, bool NEED_INIT, typename TIn>
+__global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn> A, const __grid_constant__ BwdMaps mp) {
+    using G = BwdGeo<D, M, FIXED, TIn>;
+    using Tl = typename G::Tl;
+    using TL = TLayout<D, M>;
+    constexpr int TRI = tri_size(D), SF = G::SF;
+    extern __shared__ __align__(128) char smem_raw[];
+    char *const smem = smem_base(smem_raw);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int chain0 = static_cast<int>(blockIdx.x) * kThreads + warp * 32;
+    const long chain = chain0 + lane;
+    const bool active = chain < A.n;
+    const long T = A.t;
+    const int L = A.chunks;
+    const long nb = (T + L - 1) / L;
+    const long rs_slots = replay_slots_per_chunk(T, L);
+    const float floor_ = A.floor;
+    const bool has_gy = A.gy != nullptr;
+    char *const tiles = smem + G::oT + warp * Tl::kBytes;  // + stage * G::kPerStage
+    float *const sbox = reinterpret_cast<float *>(smem + G::oS + warp * G::kSB);
+    float *const state = sbox + lane * SF;
+    char *const out = smem + G::oO + warp * G::kOB;
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + warp * 2;
+    uint32_t *const slot = reinterpret_cast<uint32_t *>(smem + G::oSlot);
+    const float *const bm = A.bmean + chain * (nb + 1) * D * M;
+    const float *const bc = A.bcov + chain * (nb + 1) * D * D;
+
+    for (int x = 0; x < SF; ++x) state[x] = 0.f;  // idle lanes replay finite zeros
+    if (lane == 0) {
+        mbar_init(bars, 1);
+        mbar_init(bars + 1, 1);
+        mbar_init_fence();
+    }
+    if (warp == 0) {
+        tmem::alloc(slot, TL::alloc());
+        tmem::relinquish();
+    }
+    tmem::fence_before_sync();
+    __syncthreads();
+    tmem::fence_after_sync();
+    // this warp's lane quarter; the thread's own lane is implicit
+    const uint32_t tb = *slot + (static_cast<uint32_t>(warp * 32) << 16);
+
+    // adjoint state: dL/d(mean) and R = sym(dL/d(covariance)), packed
+    float gM[D][M], Rp[TRI];
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int c = 0; c < M; ++c) gM[i][c] = 0.f;
+#pragma unroll
+    for (int t = 0; t < TRI; ++t) Rp[t] = 0.f;
+    if (active && A.gmf != nullptr) {
+#pragma unroll
+        for (int i = 0; i < D; ++i) load_vec<M>(A.gmf + chain * D * M + i * M, gM[i]);
+    }
+    if (active && A.gcf != nullptr) {
+        const float *gc = A.gcf + chain * D * D;
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+#pragma unroll
+            for (int j = i; j < D; ++j) Rp[tri_index(D, i, j)] = 0.5f * (gc[i * D + j] + gc[j * D + i]);
+    }
+
+    // one item: the sub-chunk's input tile and its start state (a saved
+    // replay state in the same TMA transaction, or a boundary checkpoint by
+    // per-thread copies)
+    auto issue_item = [&](const BwdItems &it, int stage) {
+        const bool saved = it.j > 0;
+        if (lane == 0) {
+            uint64_t *bar = bars + stage;
+            issue_tile<D, M, FIXED, true, TIn>(tiles + stage * G::kPerStage, mp, chain0, static_cast<int>(it.t0()),
+                                               has_gy, bar, saved ? G::kSB : 0);
+            if (saved) tma_load_2d(sbox, &mp.rs, static_cast<int>((it.ci * rs_slots + it.j - 1) * SF), chain0, bar);
+        }
+        if (!saved && active) issue_checkpoint<D, M>(smem_u32(state), bm + it.ci * D * M, bc + it.ci * D * D);
+        cp_async_commit();
+    };
+
+    BwdItems prod, cons;
+    prod.init(T, L);
+    cons.init(T, L);
+    if (!prod.done) {
+        issue_item(prod, 0);
+        prod.advance();
+    }
+    long q = 0;
+    while (!cons.done) {
+        cp_async_wait<0>();
+        mbar_wait(bars + (q & 1), static_cast<uint32_t>((q >> 1) & 1));
+        const TileRead<D, M, FIXED, true, TIn> rd{tiles + (q & 1) * G::kPerStage, lane};
+        const int t0 = static_cast<int>(cons.t0());
+        const long row0 = chain * T + t0;
+        float4 p4, r4;
+        rd.noise(p4, r4);
+        put<D, M, kRp, TRI>(tb, 0, Rp);  // parked during the replay
+
+        // ---- covariance pass: pre-step covariance, gain, beta and s per token
+        {
+            float P[TRI];
+            lds_n<TRI>(state + D * M, P);
+            auto cstep = [&](int tau) {
+                float k[D], a[D], u[D], bs[2];
+                rd.keys(tau, k);
+                rd.decay(tau, a);
+                put<D, M, kPp, TRI>(tb, tau, P);
+                cov_step<D>(P, k, a, sel4v(p4, tau), sel4v(r4, tau), floor_, u, bs[0], bs[1]);
+                put<D, M, kU, D>(tb, tau, u);
+                put<D, M, kBS, 2>(tb, tau, bs);
+            };
+#pragma unroll 1
+            for (int tau = 0; tau < kS; ++tau) cstep(tau);
+        }
+        tmem::wait_st();
+        // ---- mean pass: pre-step mean and innovation per token; gq = M' gy
+        {
+            float Mm[D][M];
+#pragma unroll
+            for (int i = 0; i < D; ++i) lds_n<M>(state + i * M, Mm[i]);
+            // every lane has read its start state and is done with the other
+            // stage: fetch the next sub-chunk while this one is processed
+            __syncwarp();
+            if (!prod.done) {
+                issue_item(prod, static_cast<int>((q + 1) & 1));
+                prod.advance();
+            }
+            if constexpr (G::kStageOut) {
+                if (lane == 0) bulk_wait_read<0>();  // the previous sub-chunk's gradient stores
+                __syncwarp();
+            }
+            auto mstep = [&](int tau) {
+                float k[D], a[D], v[M], u[D], bs[2], e[M];
+                rd.keys(tau, k);
+                rd.decay(tau, a);
+                rd.values(tau, v);
+                get<D, M, kU, D>(tb, tau, u);
+                get<D, M, kBS, 2>(tb, tau, bs);
+                {
+                    float flat[D * M];
+#pragma unroll
+                    for (int i = 0; i < D; ++i)
+#pragma unroll
+                        for (int c = 0; c < M; ++c) flat[i * M + c] = Mm[i][c];
+                    put<D, M, kMp, D * M>(tb, tau, flat);
+                }
+                mean_step<D, M>(Mm, k, a, v, u, bs[0], e);
+                put<D, M, kE, M>(tb, tau, e);
+                float gq[D];
+                if (has_gy) {
+                    float gy[M];
+                    rd.gy(tau, gy);
+#pragma unroll
+                    for (int i = 0; i < D; ++i) {
+                        float acc = 0.f;
+#pragma unroll
+                        for (int c = 0; c < M; ++c) acc = fmaf(Mm[i][c], gy[c], acc);
+                        gq[i] = acc;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < D; ++i) gq[i] = 0.f;
+                }
+                put_row<G::kStageOut, D>(reinterpret_cast<TIn *>(out + G::gQ) + (tau * 32 + lane) * D,
+                                         A.gq + (row0 + tau) * D, gq, active);
+            };
+#pragma unroll 1
+            for (int tau = 0; tau < kS; ++tau) mstep(tau);
+        }
+        tmem::wait_st();
+        get<D, M, kRp, TRI>(tb, 0, Rp);
+
+        // ---- reverse step over the sub-chunk
+        float4 gp4 = make_float4(0.f, 0.f, 0.f, 0.f), gr4 = gp4;
+        auto rstep = [&](int tau) {
+            const long row = row0 + tau;
+            float k[D], a[D];
+            const float p = sel4v(p4, tau);
+            rd.keys(tau, k);
+            rd.decay(tau, a);
+            float u[D], e[M], bs[2];
+            get<D, M, kU, D>(tb, tau, u);
+            get<D, M, kE, M>(tb, tau, e);
+            get<D, M, kBS, 2>(tb, tau, bs);
+            const float beta = bs[0], s = bs[1];
+            // dL/d(post-update mean)
+            if (has_gy) {
+                float qv[D], gy[M];
+                rd.queries(tau, qv);
+                rd.gy(tau, gy);
+#pragma unroll
+                for (int i = 0; i < D; ++i)
+#pragma unroll
+                    for (int c = 0; c < M; ++c) gM[i][c] = fmaf(qv[i], gy[c], gM[i][c]);
+            }
+            float ge[M], h[D], gb = 0.f;
+#pragma unroll
+            for (int c = 0; c < M; ++c) {
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < D; ++i) acc = fmaf(gM[i][c], u[i], acc);
+                ge[c] = beta * acc;
+                gb = fmaf(e[c], acc, gb);  // u^T gM' e
+            }
+#pragma unroll
+            for (int i = 0; i < D; ++i) {
+                float acc = 0.f;
+#pragma unroll
+                for (int c = 0; c < M; ++c) acc = fmaf(gM[i][c], e[c], acc);
+                h[i] = acc;
+            }
+            // pre-step mean: -A M ge (keys), decay gradient, dL/d(pre-step mean)
+            float pk[D], gam[D];
+            constexpr int RB = (D * M >= 32) ? 32 / M : D;  // rows per TMEM load
+#pragma unroll
+            for (int r0 = 0; r0 < D; r0 += RB) {
+                float Mp[RB][M];
+                if constexpr (RB == D) {
+                    get_mean_rows<D, M, 0, D>(tb, tau, Mp);
+                } else {
+                    if (r0 == 0) {
+                        get_mean_rows<D, M, 0, RB>(tb, tau, Mp);
+                    } else {
+                        get_mean_rows<D, M, RB, RB>(tb, tau, Mp);
+                    }
+                }
+#pragma unroll
+                for (int ii = 0; ii < RB; ++ii) {
+                    const int i = r0 + ii;
+                    float pki = 0.f, gai = 0.f;
+#pragma unroll
+                    for (int c = 0; c < M; ++c) {
+                        pki = fmaf(Mp[ii][c], ge[c], pki);
+                        const float gmb = fmaf(-k[i], ge[c], gM[i][c]);
+                        if constexpr (NEED_DYN) gai = fmaf(gmb, Mp[ii][c], gai);
+                        gM[i][c] = a[i] * gmb;
+                    }
+                    pk[i] = pki;
+                    gam[i] = gai;
+                }
+            }
+            // covariance adjoint
+            float Ru[D], trR = 0.f;
+#pragma unroll
+            for (int i = 0; i < D; ++i) {
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < D; ++j) acc = fmaf(Rp[tri_index(D, i, j)], u[j], acc);
+                Ru[i] = acc;
+                gb = fmaf(-u[i], acc, gb);
+                if constexpr (NEED_DYN) trR += Rp[tri_index(D, i, i)];
+            }
+            const float gs = (s >= floor_) ? -beta * beta * gb : 0.f;
+            float gu[D], ag[D];
+#pragma unroll
+            for (int i = 0; i < D; ++i) {
+                gu[i] = beta * h[i] - 2.f * beta * Ru[i] + gs * k[i];
+                ag[i] = a[i] * gu[i];
+            }
+            float Pp[TRI];
+            get<D, M, kPp, TRI>(tb, tau, Pp);
+            float gk[D];
+#pragma unroll
+            for (int i = 0; i < D; ++i) {
+                float z = 0.f;
+#pragma unroll
+                for (int j = 0; j < D; ++j) z = fmaf(Pp[tri_index(D, i, j)], ag[j], z);
+                const float gk3 = fmaf(a[i], z, p * gu[i]);
+                gk[i] = fmaf(-a[i], pk[i], fmaf(gs, u[i], gk3));
+            }
+            float gaP[D];
+#pragma unroll
+            for (int i = 0; i < D; ++i) gaP[i] = 0.f;
+#pragma unroll
+            for (int i = 0; i < D; ++i)
+#pragma unroll
+                for (int j = i; j < D; ++j) {
+                    const int t = tri_index(D, i, j);
+                    // S = R + sym(gu k^T): rounded products and sum, never contracted
+                    const float x = __fadd_rn(__fmul_rn(gu[i], k[j]), __fmul_rn(gu[j], k[i]));
+                    const float S = fmaf(0.5f, x, Rp[t]);
+                    if constexpr (NEED_DYN) {
+                        const float w = S * Pp[t];
+                        gaP[i] = fmaf(w, a[j], gaP[i]);
+                        if (i != j) gaP[j] = fmaf(w, a[i], gaP[j]);
+                    }
+                    Rp[t] = (a[i] * a[j]) * S;
+                }
+            put_row<G::kStageOut, D>(reinterpret_cast<TIn *>(out + G::gK) + (tau * 32 + lane) * D, A.gk + row * D, gk,
+                                     active);
+            put_row<G::kStageOut, M>(reinterpret_cast<TIn *>(out + G::gV) + (tau * 32 + lane) * M, A.gv + row * M, ge,
+                                     active);
+            if constexpr (NEED_DYN) {
+                float ga[D], gpv, grv;
+                if constexpr (FIXED) {
+#pragma unroll
+                    for (int i = 0; i < D; ++i) ga[i] = 0.f;
+                    gpv = 0.f;
+                    grv = 0.f;
+                } else {
+                    float gpk = 0.f;
+#pragma unroll
+                    for (int i = 0; i < D; ++i) {
+                        ga[i] = fmaf(2.f, gaP[i], gam[i]);
+                        gpk = fmaf(gu[i], k[i], gpk);
+                    }
+                    gpv = trR + gpk;
+                    grv = gs;
+                }
+                put_row<G::kStageOut, D>(reinterpret_cast<float *>(out + G::gA) + (tau * 32 + lane) * D,
+                                         A.ga + row * D, ga, active);
+                if constexpr (G::kStageOut) {
+                    gp4.x = tau == 0 ? gpv : gp4.x;
+                    gp4.y = tau == 1 ? gpv : gp4.y;
+                    gp4.z = tau == 2 ? gpv : gp4.z;
+                    gp4.w = tau == 3 ? gpv : gp4.w;
+                    gr4.x = tau == 0 ? grv : gr4.x;
+                    gr4.y = tau == 1 ? grv : gr4.y;
+                    gr4.z = tau == 2 ? grv : gr4.z;
+                    gr4.w = tau == 3 ? grv : gr4.w;
+                } else if (active) {
+                    A.gp[row] = gpv;
+                    A.gr[row] = grv;
+                }
+            }
+        };
+#pragma unroll 1
+        for (int tau = kS - 1; tau >= 0; --tau) rstep(tau);
+        if constexpr (G::kStageOut) {
+            if constexpr (NEED_DYN) {
+                reinterpret_cast<float4 *>(out + G::gP)[lane] = gp4;
+                reinterpret_cast<float4 *>(out + G::gR)[lane] = gr4;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_3d(&mp.gk, 0, chain0, t0, out + G::gK);
+                tma_store_3d(&mp.gv, 0, chain0, t0, out + G::gV);
+                tma_store_3d(&mp.gq, 0, chain0, t0, out + G::gQ);
+                if constexpr (NEED_DYN) {
+                    tma_store_3d(&mp.ga, 0, chain0, t0, out + G::gA);
+                    tma_store_2d(&mp.gp, t0, chain0, out + G::gP);
+                    tma_store_2d(&mp.gr, t0, chain0, out + G::gR);
+                }
+                bulk_commit();
+            }
+        }
+        cons.advance();
+        ++q;
+    }
+    cp_async_wait<0>();
+    if constexpr (NEED_INIT) {
+        if (active) {
+            store_mean<D, M>(A.gm0 + chain * D * M, gM);
+            store_cov_full<D>(A.gc0 + chain * D * D, Rp);
+        }
+    }
+    if constexpr (G::kStageOut) {
+        if (lane == 0) bulk_wait_all();
+    }
+    tmem::fence_before_sync();
+    __syncthreads();
+    tmem::fence_after_sync();
+    if (warp == 0) tmem::dealloc(*slot, TL::alloc());
+}
+
+// ===========================================================================
+// Host side: tensor maps and launchers
+// ===========================================================================
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeFn encode_fn() {
+    static EncodeFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeFn>(nullptr);
+        return reinterpret_cast<EncodeFn>(p);
+    }();
+    return fn;
+}
+
+template <typename T>
+constexpr CUtensorMapDataType dtype_of() {
+    return sizeof(T) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+}
+
+// Token-major map of a [N, T, rowelems] tensor: dims (row, chain, token),
+// box (row, 32 chains, kS tokens).
+template <typename T>
+bool map_tok(CUtensorMap *m, const T *base, int rowelems, long n, long t) {
+    if (base == nullptr) return true;
+    const cuuint64_t es = sizeof(T);
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(rowelems), static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(t)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(t) * rowelems * es, rowelems * es};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(rowelems), 32, kS};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return encode_fn()(m, dtype_of<T>(), 3, const_cast<T *>(base), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// Map of a [N, W] float tensor: dims (column, chain), box (bw, 32 chains).
+inline bool map_rows(CUtensorMap *m, const float *base, long w, long n, int bw) {
+    if (base == nullptr) return true;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(bw), 32};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Shapes the TMA path serves: 16-byte rows everywhere, every tile start on a
+// 16-byte boundary of the noise rows, coordinates within int32.
+template <typename TIn>
+bool eligible(int d, int m, long n, long t, int chunks) {
+    const int es = static_cast<int>(sizeof(TIn));
+    return (d == 4 || d == 8) && m == 8 && (d * es) % 16 == 0 && (m * es) % 16 == 0 && t > 0 && t % kS == 0 &&
+           chunks % kS == 0 && n < (1L << 30) && t < (1L << 30) && encode_fn() != nullptr;
+}
+
+template <int D, int M, bool FIXED, typename TIn>
+int launch_fwd(const FwdArgs<TIn> &a, cudaStream_t st) {
+    using G = FwdGeo<D, M, FIXED, TIn>;
+    auto k = forward_chain<D, M, FIXED, TIn>;
+    static bool attr = [&] {
+        return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem) == cudaSuccess;
+    }();
+    if (!attr) return fail(BSSM_ERR_CUDA, "forward_chain: shared-memory attribute refused");
+    if (a.out == nullptr) return fail(BSSM_ERR_INVALID, "forward_chain: null output");
+    FwdMaps mp;
+    std::memset(&mp, 0, sizeof(mp));
+    const long nb = (a.t + a.chunks - 1) / a.chunks;
+    const long W = nb * replay_slots_per_chunk(a.t, a.chunks) * replay_state_floats(D, M);
+    bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
+              map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.y, a.out, M, a.n, a.t);
+    if (!FIXED)
+        ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
+             map_rows(&mp.r, a.observation, a.t, a.n, kS);
+    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, W, a.n, replay_state_floats(D, M));
+    if (!ok) return fail(BSSM_ERR_CUDA, "forward_chain: tensor-map encoding failed");
+    const long grid = (a.n + kThreads - 1) / kThreads;
+    k<<<static_cast<unsigned>(grid), kThreads, G::kSmem, st>>>(a, mp);
+    return check_launch("forward_chain");
+}
+
+// The backward allocates TMEM columns per CTA; co-resident CTAs on one SM
+// must fit in the SM's 512 columns, or an allocation would wait for another
+// CTA to finish.  Shared memory is raised until the occupancy guarantees it.
+template <int D, int M, bool FIXED, bool NEED_DYN, bool NEED_INIT, typename TIn>
+int launch_bwd(const BwdArgs<TIn> &a, cudaStream_t st) {
+    using G = BwdGeo<D, M, FIXED, TIn>;
+    using TL = TLayout<D, M>;
+    auto k = backward_chain<D, M, FIXED, NEED_DYN, NEED_INIT, TIn>;
+    static int smem = [&] {
+        int bytes = G::kSmem;
+        const int max_ctas = 512 / TL::alloc();
+        for (;;) {
+            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return -1;
+            int per_sm = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, bytes) != cudaSuccess) return -1;
+            if (per_sm <= max_ctas) return per_sm >= 1 ? bytes : -1;
+            bytes += 8 * 1024;
+            if (bytes > kSmemMax) return -1;
+        }
+    }();
+    if (smem < 0) return fail(BSSM_ERR_CUDA, "backward_chain: no launch configuration fits tensor memory");
+    if (a.gk == nullptr || a.gv == nullptr || a.gq == nullptr ||
+        (NEED_DYN && (a.ga == nullptr || a.gp == nullptr || a.gr == nullptr)) ||
+        (NEED_INIT && (a.gm0 == nullptr || a.gc0 == nullptr)))
+        return fail(BSSM_ERR_INVALID, "backward_chain: null gradient output");
+    BwdMaps mp;
+    std::memset(&mp, 0, sizeof(mp));
+    const long nb = (a.t + a.chunks - 1) / a.chunks;
+    const long W = nb * replay_slots_per_chunk(a.t, a.chunks) * replay_state_floats(D, M);
+    bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
+              map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.gy, a.gy, M, a.n, a.t);
+    if (!FIXED)
+        ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
+             map_rows(&mp.r, a.observation, a.t, a.n, kS);
+    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, W, a.n, replay_state_floats(D, M));
+    if (G::kStageOut) {
+        ok = ok && map_tok(&mp.gk, a.gk, D, a.n, a.t) && map_tok(&mp.gv, a.gv, M, a.n, a.t) &&
+             map_tok(&mp.gq, a.gq, D, a.n, a.t);
+        if (NEED_DYN)
+            ok = ok && map_tok(&mp.ga, a.ga, D, a.n, a.t) && map_rows(&mp.gp, a.gp, a.t, a.n, kS) &&
+                 map_rows(&mp.gr, a.gr, a.t, a.n, kS);
+    }
+    if (!ok) return fail(BSSM_ERR_CUDA, "backward_chain: tensor-map encoding failed");
+    const long grid = (a.n + kThreads - 1) / kThreads;
+    k<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(a, mp);
+    return check_launch("backward_chain");
+}
+
+template <int D, typename TIn>
+int fwd_d(int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
+    if constexpr ((D * static_cast<int>(sizeof(TIn))) % 16 != 0) {
+        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels need 16-byte key rows");
+    } else {
+        return fixed ? launch_fwd<D, 8, true, TIn>(a, st) : launch_fwd<D, 8, false, TIn>(a, st);
+    }
+}
+
+template <int D, bool FIXED, typename TIn>
+int bwd_f(bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
+    if (dyn && init) return launch_bwd<D, 8, FIXED, true, true, TIn>(a, st);
+    if (dyn) return launch_bwd<D, 8, FIXED, true, false, TIn>(a, st);
+    if (init) return launch_bwd<D, 8, FIXED, false, true, TIn>(a, st);
+    return launch_bwd<D, 8, FIXED, false, false, TIn>(a, st);
+}
+
+template <int D, typename TIn>
+int bwd_d(int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
+    if constexpr ((D * static_cast<int>(sizeof(TIn))) % 16 != 0) {
+        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels need 16-byte key rows");
+    } else {
+        return fixed ? bwd_f<D, true, TIn>(dyn, init, a, st) : bwd_f<D, false, TIn>(dyn, init, a, st);
+    }
+}
+
+}  // namespace chain
+
+template <typename TIn>
+bool chain_eligible(int d, long n, long t, int chunks) {
+    return chain::eligible<TIn>(d, 8, n, t, chunks);
+}
+
+template <typename TIn>
+int chain_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
+    if (a.n == 0) return BSSM_OK;
+    if (!chain_eligible<TIn>(d, a.n, a.t, a.chunks))
+        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels: shape not supported");
+    switch (d) {
+        case 4: return chain::fwd_d<4, TIn>(fixed, a, st);
+        case 8: return chain::fwd_d<8, TIn>(fixed, a, st);
+    }
+    return fail(BSSM_ERR_UNSUPPORTED, "key_dim %d", d);
+}
+
+template <typename TIn>
+int chain_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
+    if (a.n == 0 || (a.t == 0 && !init)) return BSSM_OK;
+    if (!chain_eligible<TIn>(d, a.n, a.t, a.chunks))
+        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels: shape not supported");
+    if (a.rs == nullptr && replay_slots_per_chunk(a.t, a.chunks) > 0)
+        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain backward needs the forward's replay states");
+    switch (d) {
+        case 4: return chain::bwd_d<4, TIn>(fixed, dyn, init, a, st);
+        case 8: return chain::bwd_d<8, TIn>(fixed, dyn, init, a, st);
+    }
+    return fail(BSSM_ERR_UNSUPPORTED, "key_dim %d", d);
+}
+
+}  // namespace bssm
+
+extern "C" unsigned int bssm_debug_wait_timeouts(void) {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, bssm::chain::g_wait_timeouts, sizeof(v)) != cudaSuccess) return ~0u;
+    return v;
+}
+
+namespace bssm {
+template bool chain_eligible<float>(int, long, long, int);
+template bool chain_eligible<__nv_bfloat16>(int, long, long, int);
+template int chain_forward<float>(int, int, const FwdArgs<float> &, cudaStream_t);
+template int chain_forward<__nv_bfloat16>(int, int, const FwdArgs<__nv_bfloat16> &, cudaStream_t);
+template int chain_backward<float>(int, int, bool, bool, const BwdArgs<float> &, cudaStream_t);
+template int chain_backward<__nv_bfloat16>(int, int, bool, bool, const BwdArgs<__nv_bfloat16> &, cudaStream_t);
+
+}  // namespace bssm

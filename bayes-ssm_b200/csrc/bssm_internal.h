@@ -44,8 +44,29 @@ struct BwdArgs {
 
 // Replay states: the state at every kReplaySpan-token boundary inside each
 // chunk (not at the chunk start, which is the boundary checkpoint).  Layout
-// per chain: [chunk][slot][mean D*M row-major | covariance D*D row-major | pad].
+// per chain: [chunk][slot][mean D*M row-major | covariance upper triangle,
+// row by row (tri_index) | pad].  The covariance is exactly symmetric in every
+// kernel family, so its upper triangle is the whole state.
 constexpr int kReplaySpan = 4;
+
+// Position of covariance entry (i, j) in the row-by-row upper triangle.
+__host__ __device__ constexpr int tri_index(int d, int i, int j) {
+    return i <= j ? i * d - i * (i - 1) / 2 + (j - i) : j * d - j * (j - 1) / 2 + (i - j);
+}
+__host__ __device__ constexpr int tri_size(int d) { return d * (d + 1) / 2; }
+
+// Row `row` of a covariance (D floats) to / from the packed upper triangle.
+template <int D>
+__device__ __forceinline__ void store_row_packed(float *packed, int row, const float (&v)[D]) {
+#pragma unroll
+    for (int j = 0; j < D; ++j)
+        if (j >= row) packed[tri_index(D, row, j)] = v[j];
+}
+template <int D>
+__device__ __forceinline__ void load_row_packed(const float *packed, int row, float (&v)[D]) {
+#pragma unroll
+    for (int j = 0; j < D; ++j) v[j] = packed[tri_index(D, row, j)];
+}
 __host__ __device__ inline long replay_slots_per_chunk(long t, int chunks) {
     const long span = chunks < t ? chunks : t;
     const long nsub = (span + kReplaySpan - 1) / kReplaySpan;
@@ -53,7 +74,7 @@ __host__ __device__ inline long replay_slots_per_chunk(long t, int chunks) {
 }
 // Floats per saved state, padded to a 16-byte multiple so that every slot
 // starts 16-byte aligned (the lanes move it with 128-bit accesses).
-__host__ __device__ constexpr int replay_state_floats(int d, int m) { return (d * m + d * d + 3) / 4 * 4; }
+__host__ __device__ constexpr int replay_state_floats(int d, int m) { return (d * m + tri_size(d) + 3) / 4 * 4; }
 __host__ __device__ inline float *replay_slot(const float *rs, long chain, long nb, long slots, long ci,
                                               long j, int d, int m) {
     return const_cast<float *>(rs) + ((chain * nb + ci) * slots + (j - 1)) * static_cast<long>(replay_state_floats(d, m));
@@ -109,5 +130,13 @@ template <typename TIn> bool staged_supported(int d);
 template <typename TIn> int staged_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st);
 template <typename TIn>
 int staged_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st);
+
+// Thread-per-chain kernels (bssm_chain.cu): shapes with 16-byte rows and
+// T, chunk length multiples of kReplaySpan.  The backward needs the forward's
+// replay states whenever a chunk is longer than kReplaySpan tokens.
+template <typename TIn> bool chain_eligible(int d, long n, long t, int chunks);
+template <typename TIn> int chain_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st);
+template <typename TIn>
+int chain_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st);
 
 }  // namespace bssm

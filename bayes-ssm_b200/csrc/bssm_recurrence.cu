@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
         } else if (A.rs != nullptr && in_chunk % kReplaySpan == 0) {
             float *slot = replay_slot(A.rs, chain, nb, rs_slots, c - 1, in_chunk / kReplaySpan, D, M);
             store_mean_cols<D, M>(slot, col0, Mc);
-            store_vec<D>(slot + D * M + own * D, P);
+            store_row_packed<D>(slot + D * M, own, P);
         }
         if (++in_chunk == L) in_chunk = 0;
         const long row = chain * T + ti;
@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
             } else if (A.rs != nullptr) {
                 const float *slot = replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j, D, M);
                 load_mean_cols<D, M>(slot, col0, Mc);
-                load_vec<D>(slot + D * M + own * D, P);
+                load_row_packed<D>(slot + D * M, own, P);
             } else {
                 const float *slot = ws + static_cast<long>(j - 1) * SL::kChain + own * SL::kLane;
                 // written earlier by this kernel: coherent loads, not the read-only path
@@ -756,21 +756,48 @@ inline size_t replay_bytes(int d, int m, long n, long t, int chunks) {
            static_cast<size_t>(replay_state_floats(d, m)) * sizeof(float);
 }
 
-// Kernel family: the shared-memory-staged kernels (bssm_staged.cu) serve
-// every shape they support; BSSM_KERNELS=v1 selects the per-lane-load kernels
-// of this file instead (kept as a second, independently written path that the
-// tests cross-check).
-inline bool use_v1() {
-    static const bool v1 = [] {
-        const char *e = std::getenv("BSSM_KERNELS");
-        return e != nullptr && std::strcmp(e, "v1") == 0;
-    }();
-    return v1;
+// Kernel families.  Three independently written implementations of the same
+// recurrence:
+//   chain  -- one thread per chain, history in tensor memory (bssm_chain.cu);
+//             needs many chains to fill the GPU (a CTA is 128 chains);
+//   staged -- a few lanes per chain, cp.async-staged tiles (bssm_staged.cu);
+//   v1     -- D lanes per chain, direct loads (this file).
+// Default: chain for large batches, staged below that, v1 where neither
+// supports the shape.  BSSM_KERNELS=chain|staged|v1 forces a family (the
+// tests run every family against the oracle).
+enum Family { kAuto = 0, kChain = 1, kStaged = 2, kV1 = 3 };
+constexpr long kChainMinChains = 4096;
+
+// Read at every call (a getenv per launch), so one process can switch.
+inline Family forced_family() {
+    const char *e = std::getenv("BSSM_KERNELS");
+    if (e == nullptr) return kAuto;
+    if (std::strcmp(e, "chain") == 0) return kChain;
+    if (std::strcmp(e, "staged") == 0) return kStaged;
+    if (std::strcmp(e, "v1") == 0) return kV1;
+    return kAuto;
 }
 
 template <typename TIn>
+Family pick_family(int d, long n, long t, int chunks, bool chain_ok) {
+    const Family f = forced_family();
+    chain_ok = chain_ok && chain_eligible<TIn>(d, n, t, chunks);
+    if (f == kV1) return kV1;
+    if (f == kChain && chain_ok) return kChain;
+    if (f == kAuto && chain_ok && n >= kChainMinChains) return kChain;
+    if (staged_supported<TIn>(d)) return kStaged;
+    return kV1;
+}
+
+// The family the calling thread's last forward / backward launch used.
+thread_local int g_last_family = 0;
+
+template <typename TIn>
 int forward_dispatch(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
-    if (!use_v1() && staged_supported<TIn>(d)) return staged_forward<TIn>(d, fixed, a, st);
+    const Family f = pick_family<TIn>(d, a.n, a.t, a.chunks, true);
+    g_last_family = f;
+    if (f == kChain) return chain_forward<TIn>(d, fixed, a, st);
+    if (f == kStaged) return staged_forward<TIn>(d, fixed, a, st);
     switch (d) {
         case 1: return fixed ? launch_forward<1, 8, true>(a, st) : launch_forward<1, 8, false>(a, st);
         case 2: return fixed ? launch_forward<2, 8, true>(a, st) : launch_forward<2, 8, false>(a, st);
@@ -782,7 +809,11 @@ int forward_dispatch(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
 
 template <typename TIn>
 int backward_dispatch(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
-    if (!use_v1() && a.t > 0 && staged_supported<TIn>(d)) return staged_backward<TIn>(d, fixed, dyn, init, a, st);
+    const bool chain_ok = a.rs != nullptr || replay_slots_per_chunk(a.t, a.chunks) == 0;
+    const Family f = pick_family<TIn>(d, a.n, a.t, a.chunks, chain_ok);
+    g_last_family = (f == kStaged && a.t == 0) ? kV1 : f;
+    if (f == kChain) return chain_backward<TIn>(d, fixed, dyn, init, a, st);
+    if (f == kStaged && a.t > 0) return staged_backward<TIn>(d, fixed, dyn, init, a, st);
     switch (d) {
         case 1: return fixed ? launch_backward<1, 8, true>(a, dyn, init, st)
                              : launch_backward<1, 8, false>(a, dyn, init, st);
@@ -862,6 +893,8 @@ using namespace bssm;
 extern "C" {
 
 const char *bssm_last_error(void) { return g_last_error.c_str(); }
+
+int bssm_debug_last_family(void) { return bssm::g_last_family; }
 
 int bssm_version(void) { return 10000; }
 

@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
                                               (t - (ckpt - 1) * L) / kReplaySpan, D, M);
                     store_mean_cols_g<D, M, CPL>(slot, col0, Mc);
 #pragma unroll
-                    for (int r = 0; r < RPL; ++r) store_vec<D>(slot + D * M + (row0 + r) * D, P[r]);
+                    for (int r = 0; r < RPL; ++r) store_row_packed<D>(slot + D * M, row0 + r, P[r]);
                 }
             }
             TokPlain<D, M, LPC> tk;
@@ -739,7 +739,10 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                 const float *slot = replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j, D, M);
                 ldg_mean_cols<D, M, LPC>(slot, col0, sub, Mc);
 #pragma unroll
-                for (int r = 0; r < RPL; ++r) ldg_row<D, LPC>(slot + D * M + (row0 + r) * D, sub, P[r]);
+                for (int r = 0; r < RPL; ++r)
+#pragma unroll
+                    for (int x = 0; x < D; ++x)
+                        P[r][x] = slot[D * M + tri_index(D, row0 + r, lane_row<D, LPC>(x, sub))];
             } else {
                 // written by this kernel in phase A: coherent loads
                 float flat[G::kWsLane];

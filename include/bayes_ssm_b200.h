@@ -259,6 +259,27 @@ int bssm_backward_chunked_noalloc(int key_dim, int value_dim, int io_dtype, int 
                                   long n, long t, int chunks, double denominator_floor,
                                   void *stream);
 
+/*
+ * Diagnostics (no counterpart in the reference).
+ *
+ * The thread-per-chain kernels wait on shared-memory barriers for their own
+ * asynchronous copies.  Every such wait is bounded: one that gives up is
+ * counted in a device word and the kernel runs on (its results are then
+ * wrong) instead of hanging the GPU.  This returns that count on the current
+ * device since the library was loaded -- 0 in a healthy process.  It
+ * synchronises the device.
+ */
+unsigned int bssm_debug_wait_timeouts(void);
+
+/*
+ * Kernel family that served the calling thread's last forward or backward
+ * call: 1 thread-per-chain, 2 staged, 3 per-lane; 0 before any call.  The
+ * library picks by shape and batch size; the environment variable
+ * BSSM_KERNELS=chain|staged|v1, read at every call, forces a family where it
+ * supports the shape.
+ */
+int bssm_debug_last_family(void);
+
 #ifdef __cplusplus
 }
 #endif

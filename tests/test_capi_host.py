@@ -75,11 +75,14 @@ def test_null_pointers_rejected_without_gpu(lib):
 def test_replay_states_size_formula(lib):
     # chunks <= 4: nothing between boundary checkpoints to save
     assert lib.bssm_replay_states_bytes(8, 8, 100, 512, 4) == 0
-    # D8M8, chunk 64: 15 states per chunk, 8 chunks, 128 floats each
-    assert lib.bssm_replay_states_bytes(8, 8, 10, 512, 64) == 10 * 8 * 15 * 128 * 4
-    # partial last chunk: slots are sized by the full chunk length
-    assert lib.bssm_replay_states_bytes(2, 8, 3, 70, 32) == 3 * 3 * 7 * (16 + 4) * 4
-    # D1: 9 floats per state, padded to 12 so every slot is 16-byte aligned
+    # D8M8, chunk 64: 15 states per chunk, 8 chunks; 64 mean + 36 packed
+    # covariance floats each
+    assert lib.bssm_replay_states_bytes(8, 8, 10, 512, 64) == 10 * 8 * 15 * (64 + 36) * 4
+    # D4M8: 32 + 10 floats, padded to 44
+    assert lib.bssm_replay_states_bytes(4, 8, 2, 64, 64) == 2 * 1 * 15 * 44 * 4
+    # partial last chunk: slots are sized by the full chunk length; D2: 16 + 3 -> 20
+    assert lib.bssm_replay_states_bytes(2, 8, 3, 70, 32) == 3 * 3 * 7 * 20 * 4
+    # D1: 8 + 1 floats per state, padded to 12 so every slot is 16-byte aligned
     assert lib.bssm_replay_states_bytes(1, 8, 5, 64, 64) == 5 * 1 * 15 * 12 * 4
 
 

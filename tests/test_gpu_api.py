@@ -43,6 +43,23 @@ def test_api_autograd_matches_oracle(d):
         assert_parity(g, rg[x], what=f"grad {x}")
 
 
+def test_api_large_batch_default_kernels(monkeypatch):
+    """At 4,096+ chains the default dispatch picks the thread-per-chain family
+    (forward saving replay states, backward consuming them)."""
+    monkeypatch.delenv("BSSM_KERNELS", raising=False)
+    inp = make_inputs(4096, 24, 8, 8, seed=11, io_dtype=torch.bfloat16)
+    leaf = _leaf(inp)
+    y, _, _ = _api(leaf, chunk_length=16, optimized=True)
+    names = ("k", "v", "q", "a", "p", "r")
+    grads = torch.autograd.grad(y.square().mean(), [leaf[x] for x in names])
+    ref = oracle.forward(*[to_np64(inp[x]) for x in names], None, None)
+    assert_parity(y, ref[0], what="y")
+    gy = 2 * ref[0] / ref[0].size
+    rg = oracle.backward(*[to_np64(inp[x]) for x in names], None, None, gy, None, None)
+    for x, g in zip(names, grads):
+        assert_parity(g, rg[x], rel=4e-3 if x in ("k", "v", "q") else 1e-5, what=f"grad {x}")
+
+
 def test_api_bf16_projection_path_equals_promoted_fp32():
     """BF16 k/q/v enter the kernel directly; same values as promoting first."""
     inp = make_inputs(16, 33, 8, 8, seed=3, io_dtype=torch.bfloat16)

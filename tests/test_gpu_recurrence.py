@@ -22,6 +22,15 @@ pytestmark = pytest.mark.gpu
 DIMS = (1, 2, 4, 8)
 
 
+@pytest.fixture(autouse=True, params=["chain", "staged", "v1"])
+def family(request, monkeypatch):
+    """Run every case on each kernel family (the library reads BSSM_KERNELS at
+    every call).  A family that does not support a shape hands it to the next
+    one (chain -> staged -> v1), so every case runs on some family."""
+    monkeypatch.setenv("BSSM_KERNELS", request.param)
+    return request.param
+
+
 def _oracle_fwd(inp, fixed=False, floor=1e-6):
     return oracle.forward(to_np64(inp["k"]), to_np64(inp["v"]), to_np64(inp["q"]),
                           None if fixed else to_np64(inp["a"]), None if fixed else to_np64(inp["p"]),
@@ -102,6 +111,48 @@ def test_replay_states_match_recomputed_states():
     b = capi_backward(inp, capi_forward(inp, chunks=32, replay_states=False), gy, gmt, gpt, chunks=32)
     for key in a:
         assert_parity(a[key], b[key].cpu().numpy(), rel=1e-6, cos=0.999999, what=f"grad {key}")
+
+
+@pytest.mark.parametrize("d,io", [(8, "bf16"), (8, "f32"), (4, "f32")])
+@pytest.mark.parametrize("chunks", [4, 16, 48])
+def test_tma_eligible_shapes(d, io, chunks, family):
+    """Shapes the thread-per-chain family serves (T and chunk multiples of 4,
+    16-byte rows): a partial warp, several warps, full and ragged chunks."""
+    from bayes_ssm import _capi
+    dt = torch.bfloat16 if io == "bf16" else torch.float32
+    inp = make_inputs(70, 48, d, 8, seed=100 + d + chunks, init="random", io_dtype=dt)
+    _check_all(inp, chunks=chunks, seed=d)
+    if family == "chain":
+        assert _capi.last_family() == "chain"
+
+
+@pytest.mark.parametrize("fixed,need_dyn,need_init,gy_none,final_grads",
+                         [(False, False, False, False, False), (True, True, True, False, True),
+                          (False, True, False, True, True), (False, False, True, False, True)])
+def test_tma_eligible_variants(fixed, need_dyn, need_init, gy_none, final_grads, family):
+    from bayes_ssm import _capi
+    inp = make_inputs(40, 32, 8, 8, seed=7, init="random", io_dtype=torch.bfloat16)
+    _check_all(inp, chunks=16, fixed=fixed, need_dyn=need_dyn, need_init=need_init, gy_none=gy_none,
+               final_grads=final_grads, seed=2)
+    if family == "chain":
+        assert _capi.last_family() == "chain"
+
+
+@pytest.mark.parametrize("fwd_family,bwd_family", [("chain", "staged"), ("staged", "chain"),
+                                                    ("v1", "chain"), ("chain", "v1")])
+def test_replay_states_shared_across_families(fwd_family, bwd_family, monkeypatch):
+    """All families write and read one replay-state format (mean, then the
+    covariance's upper triangle): a backward of one family consumes the
+    states another family's forward saved."""
+    inp = make_inputs(40, 56, 8, 8, seed=91, init="random")
+    monkeypatch.setenv("BSSM_KERNELS", fwd_family)
+    fwd = capi_forward(inp, chunks=16)
+    monkeypatch.setenv("BSSM_KERNELS", bwd_family)
+    gy, gmt, gpt = _grads_out(40, 56, 8, 8, 5)
+    got = capi_backward(inp, fwd, gy, gmt, gpt, chunks=16)
+    ref = _oracle_bwd(inp, gy, gmt, gpt)
+    for key in ("k", "v", "q", "a", "p", "r", "M0", "P0"):
+        assert_parity(got[key], ref[key], what=f"grad {key}")
 
 
 @pytest.mark.parametrize("d", DIMS)
@@ -204,3 +255,9 @@ def test_workspace_too_small_is_rejected():
                                torch.empty(4, 40, 8, device="cuda"), torch.empty_like(k), None, None,
                                None, None, None, ws, need - 16, 4, 40, 32, 1e-6,
                                torch.cuda.current_stream().cuda_stream)
+
+
+def test_zz_no_bounded_wait_gave_up():
+    """Every barrier wait inside the kernels of this module's runs completed."""
+    from bayes_ssm import _capi
+    assert _capi.wait_timeouts() == 0
