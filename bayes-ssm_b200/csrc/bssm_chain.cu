@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
             stage_packed_state<D, M>(sbuf + lane * SF, Mm, P);
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0) {
+            if (lane == 0 && chain0 < A.n) {
                 tma_store_2d(&mp.rs, static_cast<int>((ci * rs_slots + cons.j - 1) * SF), chain0, sbuf);
                 bulk_commit();
             }
@@ -491,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-            tma_store_3d(&mp.y, 0, chain0, t0, yb);
+            if (chain0 < A.n) tma_store_3d(&mp.y, 0, chain0, t0, yb);
             bulk_commit();
         }
         cons.advance();
@@ -1032,7 +1032,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
             }
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0) {
+            if (lane == 0 && chain0 < A.n) {
                 tma_store_3d(&mp.gk, 0, chain0, t0, out + G::gK);
                 tma_store_3d(&mp.gv, 0, chain0, t0, out + G::gV);
                 tma_store_3d(&mp.gq, 0, chain0, t0, out + G::gQ);
@@ -1057,6 +1057,487 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
     if constexpr (G::kStageOut) {
         if (lane == 0) bulk_wait_all();
     }
+    tmem::fence_before_sync();
+    __syncthreads();
+    tmem::fence_after_sync();
+    if (warp == 0) tmem::dealloc(*slot, TL::alloc());
+}
+
+// ===========================================================================
+// Backward with two warps per chain group (D = M, BF16 inputs, dynamic
+// noise): the headline configuration.
+//
+// Group g (32 chains) has a covariance warp (warp g) and a mean warp (warp
+// g + 4).  Both sit on SM sub-partition g and reach TMEM lane quarter g, so
+// they share the chains' tensor-memory history; the sub-partition interleaves
+// two instruction streams instead of one.
+//   covariance warp: replays the covariance (history: pre-step covariance,
+//     gain, beta, s), then runs the R-adjoint of the reverse step;
+//   mean warp: replays the mean from the gains (history: pre-step mean,
+//     innovation, gq), then runs the dL/dM adjoint and hands the covariance
+//     warp h = gM' e, pk = M ge, the decay term and u.gM'.e per token.
+// Synchronisation is by mbarriers: tile stage full / free, start state read,
+// replay token ready (covariance -> mean), exchange slot full / free.  The
+// gradient rows are staged in the tile's own input slots once those inputs
+// are dead (gk in keys, gv in queries, gq in values, ga in decay, gp / gr in
+// process / observation) and leave by TMA stores.
+// ===========================================================================
+constexpr int kSplitWarps = 8;
+constexpr int kSplitThreads = 32 * kSplitWarps;
+
+template <int D, int M, typename TIn>
+struct SplitGeo {
+    using Tl = Tile<D, M, false, true, TIn>;
+    static_assert(D == M, "in-place gradient staging needs D == M");
+    static_assert(sizeof(TIn) == 2, "tile budget assumes BF16 inputs");
+    static constexpr int SF = replay_state_floats(D, M);
+    static constexpr int kSB = 32 * SF * 4;   // a group's start states [chain][SF]
+    static constexpr int kXF = 3 * D + 1;     // exchanged floats per chain and token: h, pk, gam, gb
+    static constexpr int kXB = kXF * 32 * 4;  // one exchange slot, [float][chain]
+    static constexpr int kPerStage = 4 * Tl::kBytes;
+    static constexpr int oT = 0;                             // [stage][group][tile]
+    static constexpr int oS = oT + 2 * kPerStage;            // [group][kSB]
+    static constexpr int oX = al128(oS + 4 * kSB);           // [group][slot][kXB]
+    static constexpr int oBar = al128(oX + 4 * 2 * kXB);     // [group][13]
+    static constexpr int kBars = 13;  // full[2] empty[2] sfree rt[4] xfull[2] xempty[2]
+    static constexpr int oSlot = oBar + 4 * kBars * 8;
+    static constexpr int kSmem = oSlot + 16 + 128;
+    static_assert(kSmem <= kSmemMax, "split backward shared memory");
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int D, int M, bool NEED_DYN, bool NEED_INIT, typename TIn>
+__global__ void __launch_bounds__(kSplitThreads, 1)
+    backward_split(const BwdArgs<TIn> A, const __grid_constant__ BwdMaps mp) {
+    using G = SplitGeo<D, M, TIn>;
+    using Tl = typename G::Tl;
+    using TL = TLayout<D, M>;
+    constexpr int TRI = tri_size(D), SF = G::SF, XF = G::kXF;
+    extern __shared__ __align__(128) char smem_raw[];
+    char *const smem = smem_base(smem_raw);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int grp = warp & 3;
+    const bool cov_warp = warp < 4;
+    const int chain0 = static_cast<int>(blockIdx.x) * 128 + grp * 32;
+    const long chain = chain0 + lane;
+    const bool active = chain < A.n;
+    const long T = A.t;
+    const int L = A.chunks;
+    const long nb = (T + L - 1) / L;
+    const long rs_slots = replay_slots_per_chunk(T, L);
+    const float floor_ = A.floor;
+    const bool has_gy = A.gy != nullptr;
+    char *const tiles = smem + G::oT + grp * Tl::kBytes;  // + stage * G::kPerStage
+    float *const sbox = reinterpret_cast<float *>(smem + G::oS + grp * G::kSB);
+    float *const state = sbox + lane * SF;
+    float *const xch = reinterpret_cast<float *>(smem + G::oX + grp * 2 * G::kXB);  // + slot * XF * 32
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + grp * G::kBars;
+    uint64_t *const full = bars, *const empty = bars + 2, *const sfree = bars + 4, *const rt = bars + 5;
+    uint64_t *const xfull = bars + 9, *const xempty = bars + 11;
+    uint32_t *const slot = reinterpret_cast<uint32_t *>(smem + G::oSlot);
+    const float *const bm = A.bmean + chain * (nb + 1) * D * M;
+    const float *const bc = A.bcov + chain * (nb + 1) * D * D;
+
+    if (cov_warp) {
+        for (int x = 0; x < SF; ++x) state[x] = 0.f;  // idle lanes replay finite zeros
+        if (lane == 0) {
+            mbar_init(full, 1);
+            mbar_init(full + 1, 1);
+            mbar_init(empty, 2);
+            mbar_init(empty + 1, 2);
+            mbar_init(sfree, 2);
+            for (int x = 0; x < kS; ++x) mbar_init(rt + x, 32);
+            mbar_init(xfull, 32);
+            mbar_init(xfull + 1, 32);
+            mbar_init(xempty, 32);
+            mbar_init(xempty + 1, 32);
+            mbar_init_fence();
+        }
+    }
+    if (warp == 0) {
+        tmem::alloc(slot, TL::alloc());
+        tmem::relinquish();
+    }
+    tmem::fence_before_sync();
+    __syncthreads();
+    tmem::fence_after_sync();
+    const uint32_t tb = *slot + (static_cast<uint32_t>(grp * 32) << 16);
+
+    // the tile of an item (and its saved start state) by the covariance
+    // warp's lane 0; a checkpoint start state by each warp for its own part
+    auto issue_tile_state = [&](const BwdItems &it, int stage) {
+        const bool saved = it.j > 0;
+        issue_tile<D, M, false, true, TIn>(tiles + stage * G::kPerStage, mp, chain0, static_cast<int>(it.t0()),
+                                           has_gy, full + stage, saved ? G::kSB : 0);
+        if (saved) tma_load_2d(sbox, &mp.rs, static_cast<int>((it.ci * rs_slots + it.j - 1) * SF), chain0, full + stage);
+    };
+    auto issue_checkpoint_part = [&](const BwdItems &it) {
+        if (it.j > 0 || !active) return;
+        const uint32_t s = smem_u32(state);
+        if (cov_warp) {
+            const float *ck = bc + it.ci * D * D;
+#pragma unroll
+            for (int i = 0; i < D; ++i)
+#pragma unroll
+                for (int j = i; j < D; ++j) cp_async<4>(s + 4 * (D * M + tri_index(D, i, j)), ck + i * D + j);
+        } else {
+            const float *ck = bm + it.ci * D * M;
+#pragma unroll
+            for (int x = 0; x < D * M / 4; ++x) cp_async<16>(s + 16 * x, ck + 4 * x);
+        }
+    };
+
+    BwdItems cur, nxt;
+    cur.init(T, L);
+    nxt.init(T, L);
+    if (!nxt.done) {
+        if (cov_warp && lane == 0) issue_tile_state(nxt, 0);
+        issue_checkpoint_part(nxt);
+        cp_async_commit();
+        nxt.advance();
+    }
+
+    if (cov_warp) {
+        // ------------------------------------------------------------------
+        // covariance warp
+        // ------------------------------------------------------------------
+        float Rp[TRI];
+#pragma unroll
+        for (int t = 0; t < TRI; ++t) Rp[t] = 0.f;
+        if (active && A.gcf != nullptr) {
+            const float *gc = A.gcf + chain * D * D;
+#pragma unroll
+            for (int i = 0; i < D; ++i)
+#pragma unroll
+                for (int j = i; j < D; ++j) Rp[tri_index(D, i, j)] = 0.5f * (gc[i * D + j] + gc[j * D + i]);
+        }
+        long q = 0;
+        while (!cur.done) {
+            cp_async_wait<0>();
+            mbar_wait(full + (q & 1), static_cast<uint32_t>((q >> 1) & 1));
+            char *const tile = tiles + (q & 1) * G::kPerStage;
+            const TileRead<D, M, false, true, TIn> rd{tile, lane};
+            const int t0 = static_cast<int>(cur.t0());
+            float4 p4, r4;
+            rd.noise(p4, r4);
+            float P[TRI];
+            lds_n<TRI>(state + D * M, P);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sfree);
+            if (!nxt.done) issue_checkpoint_part(nxt);  // this warp's part of the row is read
+            cp_async_commit();
+            // replay: pre-step covariance, gain, beta, s; hand each token's
+            // gain to the mean warp
+#pragma unroll 1
+            for (int tau = 0; tau < kS; ++tau) {
+                float k[D], a[D], u[D], bs[2];
+                rd.keys(tau, k);
+                rd.decay(tau, a);
+                put<D, M, kPp, TRI>(tb, tau, P);
+                cov_step<D>(P, k, a, sel4v(p4, tau), sel4v(r4, tau), floor_, u, bs[0], bs[1]);
+                put<D, M, kU, D>(tb, tau, u);
+                put<D, M, kBS, 2>(tb, tau, bs);
+                tmem::wait_st();
+                tmem::fence_before_sync();
+                mbar_arrive(rt + tau);
+            }
+            // next sub-chunk: once the mean warp has read its start state
+            // and both warps released the stage the next tile goes to
+            if (!nxt.done) {
+                if (lane == 0) {
+                    if (q >= 1) mbar_wait(empty + ((q + 1) & 1), static_cast<uint32_t>(((q - 1) >> 1) & 1));
+                    mbar_wait(sfree, static_cast<uint32_t>(q & 1));
+                    issue_tile_state(nxt, static_cast<int>((q + 1) & 1));
+                }
+                nxt.advance();
+            } else if (lane == 0) {
+                mbar_wait(sfree, static_cast<uint32_t>(q & 1));
+            }
+            // reverse: covariance adjoint
+            float4 gp4 = make_float4(0.f, 0.f, 0.f, 0.f), gr4 = gp4;
+#pragma unroll 1
+            for (int tau = kS - 1; tau >= 0; --tau) {
+                const int xs = tau & 1;
+                mbar_wait(xfull + xs, tau < 2 ? 1u : 0u);
+                tmem::fence_after_sync();
+                const float *xp = xch + xs * XF * 32 + lane;
+                float h[D], pk[D], gam[D];
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    h[i] = xp[i * 32];
+                    pk[i] = xp[(D + i) * 32];
+                    gam[i] = xp[(2 * D + i) * 32];
+                }
+                float gb = xp[3 * D * 32];
+                mbar_arrive(xempty + xs);
+                float k[D], a[D], u[D], bs[2];
+                rd.keys(tau, k);
+                rd.decay(tau, a);
+                const float p = sel4v(p4, tau);
+                get<D, M, kU, D>(tb, tau, u);
+                get<D, M, kBS, 2>(tb, tau, bs);
+                const float beta = bs[0], s = bs[1];
+                float Ru[D], trR = 0.f;
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int j = 0; j < D; ++j) acc = fmaf(Rp[tri_index(D, i, j)], u[j], acc);
+                    Ru[i] = acc;
+                    gb = fmaf(-u[i], acc, gb);
+                    if constexpr (NEED_DYN) trR += Rp[tri_index(D, i, i)];
+                }
+                const float gs = (s >= floor_) ? -beta * beta * gb : 0.f;
+                float gu[D], ag[D];
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    gu[i] = beta * h[i] - 2.f * beta * Ru[i] + gs * k[i];
+                    ag[i] = a[i] * gu[i];
+                }
+                float Pp[TRI];
+                get<D, M, kPp, TRI>(tb, tau, Pp);
+                float gk[D];
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    float z = 0.f;
+#pragma unroll
+                    for (int j = 0; j < D; ++j) z = fmaf(Pp[tri_index(D, i, j)], ag[j], z);
+                    const float gk3 = fmaf(a[i], z, p * gu[i]);
+                    gk[i] = fmaf(-a[i], pk[i], fmaf(gs, u[i], gk3));
+                }
+                float gaP[D];
+#pragma unroll
+                for (int i = 0; i < D; ++i) gaP[i] = 0.f;
+#pragma unroll
+                for (int i = 0; i < D; ++i)
+#pragma unroll
+                    for (int j = i; j < D; ++j) {
+                        const int t = tri_index(D, i, j);
+                        const float x = __fadd_rn(__fmul_rn(gu[i], k[j]), __fmul_rn(gu[j], k[i]));
+                        const float S = fmaf(0.5f, x, Rp[t]);
+                        if constexpr (NEED_DYN) {
+                            const float w = S * Pp[t];
+                            gaP[i] = fmaf(w, a[j], gaP[i]);
+                            if (i != j) gaP[j] = fmaf(w, a[i], gaP[j]);
+                        }
+                        Rp[t] = (a[i] * a[j]) * S;
+                    }
+                // keys and decay of this token are dead: their slots take gk, ga
+                store_vec<D>(reinterpret_cast<TIn *>(tile + Tl::oK) + (tau * 32 + lane) * D, gk);
+                if constexpr (NEED_DYN) {
+                    float ga[D], gpk = 0.f;
+#pragma unroll
+                    for (int i = 0; i < D; ++i) {
+                        ga[i] = fmaf(2.f, gaP[i], gam[i]);
+                        gpk = fmaf(gu[i], k[i], gpk);
+                    }
+                    store_vec<D>(reinterpret_cast<float *>(tile + Tl::oA) + (tau * 32 + lane) * D, ga);
+                    const float gpv = trR + gpk;
+                    gp4.x = tau == 0 ? gpv : gp4.x;
+                    gp4.y = tau == 1 ? gpv : gp4.y;
+                    gp4.z = tau == 2 ? gpv : gp4.z;
+                    gp4.w = tau == 3 ? gpv : gp4.w;
+                    gr4.x = tau == 0 ? gs : gr4.x;
+                    gr4.y = tau == 1 ? gs : gr4.y;
+                    gr4.z = tau == 2 ? gs : gr4.z;
+                    gr4.w = tau == 3 ? gs : gr4.w;
+                }
+            }
+            if constexpr (NEED_DYN) {
+                reinterpret_cast<float4 *>(tile + Tl::oP)[lane] = gp4;
+                reinterpret_cast<float4 *>(tile + Tl::oR)[lane] = gr4;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                if (chain0 < A.n) {
+                    tma_store_3d(&mp.gk, 0, chain0, t0, tile + Tl::oK);
+                    if constexpr (NEED_DYN) {
+                        tma_store_3d(&mp.ga, 0, chain0, t0, tile + Tl::oA);
+                        tma_store_2d(&mp.gp, t0, chain0, tile + Tl::oP);
+                        tma_store_2d(&mp.gr, t0, chain0, tile + Tl::oR);
+                    }
+                }
+                bulk_commit();
+                bulk_wait_read<0>();
+                mbar_arrive(empty + (q & 1));
+            }
+            cur.advance();
+            ++q;
+        }
+        cp_async_wait<0>();
+        if constexpr (NEED_INIT) {
+            if (active) store_cov_full<D>(A.gc0 + chain * D * D, Rp);
+        }
+    } else {
+        // ------------------------------------------------------------------
+        // mean warp
+        // ------------------------------------------------------------------
+        float gM[D][M];
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+#pragma unroll
+            for (int c = 0; c < M; ++c) gM[i][c] = 0.f;
+        if (active && A.gmf != nullptr) {
+#pragma unroll
+            for (int i = 0; i < D; ++i) load_vec<M>(A.gmf + chain * D * M + i * M, gM[i]);
+        }
+        long q = 0;
+        while (!cur.done) {
+            cp_async_wait<0>();
+            mbar_wait(full + (q & 1), static_cast<uint32_t>((q >> 1) & 1));
+            char *const tile = tiles + (q & 1) * G::kPerStage;
+            const TileRead<D, M, false, true, TIn> rd{tile, lane};
+            const int t0 = static_cast<int>(cur.t0());
+            float Mm[D][M];
+#pragma unroll
+            for (int i = 0; i < D; ++i) lds_n<M>(state + i * M, Mm[i]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sfree);
+            if (!nxt.done) {
+                issue_checkpoint_part(nxt);
+                nxt.advance();
+            }
+            cp_async_commit();
+            // replay: pre-step mean and innovation; gq = M' gy into the
+            // token's (dead) value slot
+#pragma unroll 1
+            for (int tau = 0; tau < kS; ++tau) {
+                float k[D], a[D], v[M], u[D], bs[2], e[M];
+                rd.keys(tau, k);
+                rd.decay(tau, a);
+                rd.values(tau, v);
+                mbar_wait(rt + tau, static_cast<uint32_t>(q & 1));
+                tmem::fence_after_sync();
+                get<D, M, kU, D>(tb, tau, u);
+                get<D, M, kBS, 2>(tb, tau, bs);
+                {
+                    float flat[D * M];
+#pragma unroll
+                    for (int i = 0; i < D; ++i)
+#pragma unroll
+                        for (int c = 0; c < M; ++c) flat[i * M + c] = Mm[i][c];
+                    put<D, M, kMp, D * M>(tb, tau, flat);
+                }
+                mean_step<D, M>(Mm, k, a, v, u, bs[0], e);
+                put<D, M, kE, M>(tb, tau, e);
+                float gq[D];
+                if (has_gy) {
+                    float gy[M];
+                    rd.gy(tau, gy);
+#pragma unroll
+                    for (int i = 0; i < D; ++i) {
+                        float acc = 0.f;
+#pragma unroll
+                        for (int c = 0; c < M; ++c) acc = fmaf(Mm[i][c], gy[c], acc);
+                        gq[i] = acc;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < D; ++i) gq[i] = 0.f;
+                }
+                store_vec<D>(reinterpret_cast<TIn *>(tile + Tl::oV) + (tau * 32 + lane) * D, gq);
+            }
+            tmem::wait_st();
+            // reverse: mean adjoint, the covariance warp's inputs via the
+            // exchange slots
+#pragma unroll 1
+            for (int tau = kS - 1; tau >= 0; --tau) {
+                float k[D], a[D], u[D], e[M], bs[2];
+                rd.keys(tau, k);
+                rd.decay(tau, a);
+                get<D, M, kU, D>(tb, tau, u);
+                get<D, M, kE, M>(tb, tau, e);
+                get<D, M, kBS, 2>(tb, tau, bs);
+                const float beta = bs[0];
+                if (has_gy) {
+                    float qv[D], gy[M];
+                    rd.queries(tau, qv);
+                    rd.gy(tau, gy);
+#pragma unroll
+                    for (int i = 0; i < D; ++i)
+#pragma unroll
+                        for (int c = 0; c < M; ++c) gM[i][c] = fmaf(qv[i], gy[c], gM[i][c]);
+                }
+                float ge[M], h[D], gb = 0.f;
+#pragma unroll
+                for (int c = 0; c < M; ++c) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int i = 0; i < D; ++i) acc = fmaf(gM[i][c], u[i], acc);
+                    ge[c] = beta * acc;
+                    gb = fmaf(e[c], acc, gb);
+                }
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int c = 0; c < M; ++c) acc = fmaf(gM[i][c], e[c], acc);
+                    h[i] = acc;
+                }
+                float pk[D], gam[D];
+                constexpr int RB = 32 / M;  // rows per TMEM load
+#pragma unroll
+                for (int r0 = 0; r0 < D; r0 += RB) {
+                    float Mp[RB][M];
+                    if (r0 == 0) {
+                        get_mean_rows<D, M, 0, RB>(tb, tau, Mp);
+                    } else {
+                        get_mean_rows<D, M, RB, RB>(tb, tau, Mp);
+                    }
+#pragma unroll
+                    for (int ii = 0; ii < RB; ++ii) {
+                        const int i = r0 + ii;
+                        float pki = 0.f, gai = 0.f;
+#pragma unroll
+                        for (int c = 0; c < M; ++c) {
+                            pki = fmaf(Mp[ii][c], ge[c], pki);
+                            const float gmb = fmaf(-k[i], ge[c], gM[i][c]);
+                            if constexpr (NEED_DYN) gai = fmaf(gmb, Mp[ii][c], gai);
+                            gM[i][c] = a[i] * gmb;
+                        }
+                        pk[i] = pki;
+                        gam[i] = gai;
+                    }
+                }
+                // the token's query slot is dead: it takes gv
+                store_vec<M>(reinterpret_cast<TIn *>(tile + Tl::oQ) + (tau * 32 + lane) * M, ge);
+                const int xs = tau & 1;
+                if (q > 0 || tau < 2) mbar_wait(xempty + xs, tau < 2 ? 0u : 1u);
+                float *const xp = xch + xs * XF * 32 + lane;
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    xp[i * 32] = h[i];
+                    xp[(D + i) * 32] = pk[i];
+                    xp[(2 * D + i) * 32] = gam[i];
+                }
+                xp[3 * D * 32] = gb;
+                tmem::fence_before_sync();  // this token's TMEM reads are done
+                mbar_arrive(xfull + xs);
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                if (chain0 < A.n) {
+                    tma_store_3d(&mp.gq, 0, chain0, t0, tile + Tl::oV);
+                    tma_store_3d(&mp.gv, 0, chain0, t0, tile + Tl::oQ);
+                }
+                bulk_commit();
+                bulk_wait_read<0>();
+                mbar_arrive(empty + (q & 1));
+            }
+            cur.advance();
+            ++q;
+        }
+        cp_async_wait<0>();
+        if constexpr (NEED_INIT) {
+            if (active) store_mean<D, M>(A.gm0 + chain * D * M, gM);
+        }
+    }
+    if (lane == 0) bulk_wait_all();
     tmem::fence_before_sync();
     __syncthreads();
     tmem::fence_after_sync();
@@ -1193,6 +1674,48 @@ int launch_bwd(const BwdArgs<TIn> &a, cudaStream_t st) {
     return check_launch("backward_chain");
 }
 
+template <int D, int M, bool NEED_DYN, bool NEED_INIT, typename TIn>
+int launch_split(const BwdArgs<TIn> &a, cudaStream_t st) {
+    using G = SplitGeo<D, M, TIn>;
+    auto k = backward_split<D, M, NEED_DYN, NEED_INIT, TIn>;
+    static int smem = [&] {
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem) != cudaSuccess) return -1;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kSplitThreads, G::kSmem) != cudaSuccess)
+            return -1;
+        return per_sm == 1 ? G::kSmem : -1;  // one CTA per SM: it holds all 512 TMEM columns
+    }();
+    if (smem < 0) return fail(BSSM_ERR_CUDA, "backward_split: no launch configuration fits tensor memory");
+    if (a.gk == nullptr || a.gv == nullptr || a.gq == nullptr ||
+        (NEED_DYN && (a.ga == nullptr || a.gp == nullptr || a.gr == nullptr)) ||
+        (NEED_INIT && (a.gm0 == nullptr || a.gc0 == nullptr)))
+        return fail(BSSM_ERR_INVALID, "backward_split: null gradient output");
+    BwdMaps mp;
+    std::memset(&mp, 0, sizeof(mp));
+    const long nb = (a.t + a.chunks - 1) / a.chunks;
+    const long W = nb * replay_slots_per_chunk(a.t, a.chunks) * replay_state_floats(D, M);
+    bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
+              map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.gy, a.gy, M, a.n, a.t) &&
+              map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
+              map_rows(&mp.r, a.observation, a.t, a.n, kS) && map_tok(&mp.gk, a.gk, D, a.n, a.t) &&
+              map_tok(&mp.gv, a.gv, M, a.n, a.t) && map_tok(&mp.gq, a.gq, D, a.n, a.t);
+    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, W, a.n, replay_state_floats(D, M));
+    if (NEED_DYN)
+        ok = ok && map_tok(&mp.ga, a.ga, D, a.n, a.t) && map_rows(&mp.gp, a.gp, a.t, a.n, kS) &&
+             map_rows(&mp.gr, a.gr, a.t, a.n, kS);
+    if (!ok) return fail(BSSM_ERR_CUDA, "backward_split: tensor-map encoding failed");
+    const long grid = (a.n + 127) / 128;
+    k<<<static_cast<unsigned>(grid), kSplitThreads, smem, st>>>(a, mp);
+    return check_launch("backward_split");
+}
+
+// BSSM_KERNELS=chain1: the one-warp-per-group backward even where the split
+// one applies (both are tested).
+inline bool split_allowed() {
+    const char *e = std::getenv("BSSM_KERNELS");
+    return e == nullptr || std::strcmp(e, "chain1") != 0;
+}
+
 template <int D, typename TIn>
 int fwd_d(int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
     if constexpr ((D * static_cast<int>(sizeof(TIn))) % 16 != 0) {
@@ -1204,6 +1727,14 @@ int fwd_d(int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
 
 template <int D, bool FIXED, typename TIn>
 int bwd_f(bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
+    if constexpr (D == 8 && !FIXED && sizeof(TIn) == 2) {
+        if (split_allowed()) {
+            if (dyn && init) return launch_split<D, 8, true, true, TIn>(a, st);
+            if (dyn) return launch_split<D, 8, true, false, TIn>(a, st);
+            if (init) return launch_split<D, 8, false, true, TIn>(a, st);
+            return launch_split<D, 8, false, false, TIn>(a, st);
+        }
+    }
     if (dyn && init) return launch_bwd<D, 8, FIXED, true, true, TIn>(a, st);
     if (dyn) return launch_bwd<D, 8, FIXED, true, false, TIn>(a, st);
     if (init) return launch_bwd<D, 8, FIXED, false, true, TIn>(a, st);

@@ -772,7 +772,7 @@ constexpr long kChainMinChains = 4096;
 inline Family forced_family() {
     const char *e = std::getenv("BSSM_KERNELS");
     if (e == nullptr) return kAuto;
-    if (std::strcmp(e, "chain") == 0) return kChain;
+    if (std::strcmp(e, "chain") == 0 || std::strcmp(e, "chain1") == 0) return kChain;
     if (std::strcmp(e, "staged") == 0) return kStaged;
     if (std::strcmp(e, "v1") == 0) return kV1;
     return kAuto;

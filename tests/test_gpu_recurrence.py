@@ -22,11 +22,13 @@ pytestmark = pytest.mark.gpu
 DIMS = (1, 2, 4, 8)
 
 
-@pytest.fixture(autouse=True, params=["chain", "staged", "v1"])
+@pytest.fixture(autouse=True, params=["chain", "chain1", "staged", "v1"])
 def family(request, monkeypatch):
     """Run every case on each kernel family (the library reads BSSM_KERNELS at
     every call).  A family that does not support a shape hands it to the next
-    one (chain -> staged -> v1), so every case runs on some family."""
+    one (chain -> staged -> v1), so every case runs on some family.  "chain1"
+    is the thread-per-chain family with its one-warp backward where the
+    two-warp backward would apply."""
     monkeypatch.setenv("BSSM_KERNELS", request.param)
     return request.param
 
@@ -122,7 +124,7 @@ def test_tma_eligible_shapes(d, io, chunks, family):
     dt = torch.bfloat16 if io == "bf16" else torch.float32
     inp = make_inputs(70, 48, d, 8, seed=100 + d + chunks, init="random", io_dtype=dt)
     _check_all(inp, chunks=chunks, seed=d)
-    if family == "chain":
+    if family in ("chain", "chain1"):
         assert _capi.last_family() == "chain"
 
 
@@ -134,7 +136,7 @@ def test_tma_eligible_variants(fixed, need_dyn, need_init, gy_none, final_grads,
     inp = make_inputs(40, 32, 8, 8, seed=7, init="random", io_dtype=torch.bfloat16)
     _check_all(inp, chunks=16, fixed=fixed, need_dyn=need_dyn, need_init=need_init, gy_none=gy_none,
                final_grads=final_grads, seed=2)
-    if family == "chain":
+    if family in ("chain", "chain1"):
         assert _capi.last_family() == "chain"
 
 
