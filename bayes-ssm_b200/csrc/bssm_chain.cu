@@ -145,10 +145,10 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // (kS tokens, 32 chains); the replay-state map (float, chain) with a box of
 // (one state, 32 chains).
 struct FwdMaps {
-    CUtensorMap k, q, v, a, p, r, y, rs;
+    CUtensorMap k, q, v, a, p, r, y, rs, gu, gb, gs;
 };
 struct BwdMaps {
-    CUtensorMap k, q, v, a, p, r, gy, rs, gk, gv, gq, ga, gp, gr;
+    CUtensorMap k, q, v, a, p, r, gy, rs, gk, gv, gq, ga, gp, gr, gu, gb, gs;
 };
 
 // Shared-memory geometry of one warp's tile (one stage), box layouts.
@@ -289,24 +289,6 @@ __device__ __forceinline__ void store_cov_full(float *dst, const float (&P)[tri_
         store_vec<D>(dst + i * D, row);
     }
 }
-// Packed replay state: [mean D*M | covariance upper triangle | pad], into
-// 16-byte aligned shared memory (staging for a bulk store).
-template <int D, int M>
-__device__ __forceinline__ void stage_packed_state(float *dst, const float (&Mm)[D][M],
-                                                   const float (&P)[tri_size(D)]) {
-    constexpr int SF = replay_state_floats(D, M);
-    float flat[SF];
-#pragma unroll
-    for (int i = 0; i < D; ++i)
-#pragma unroll
-        for (int c = 0; c < M; ++c) flat[i * M + c] = Mm[i][c];
-#pragma unroll
-    for (int t = 0; t < tri_size(D); ++t) flat[D * M + t] = P[t];
-#pragma unroll
-    for (int x = D * M + tri_size(D); x < SF; ++x) flat[x] = 0.f;
-    sts_vec<SF>(dst, flat);
-}
-
 // Order in which a chain's tiles are consumed by the forward: chunk by chunk,
 // kS-token sub-chunks in order (sub-chunks restart at every chunk boundary,
 // so the replay states sit at tile starts).
@@ -345,19 +327,20 @@ template <int D, int M, bool FIXED, typename TIn>
 struct FwdGeo {
     using Tl = Tile<D, M, FIXED, false, TIn>;
     static constexpr int SF = replay_state_floats(D, M);
-    static constexpr int kYB = kS * 32 * M * 4;  // a warp's readout rows, box layout [tau][chain][M]
-    static constexpr int kSB = 32 * SF * 4;      // a warp's states, box layout [chain][SF]
+    // a warp's outputs of one tile, box layouts: readout [tau][chain][M],
+    // gains [tau][chain][D], beta and s [chain][tau]
+    static constexpr int yY = 0, yU = kS * 32 * M * 4, yB = yU + kS * 32 * D * 4, yS = yB + 32 * kS * 4;
+    static constexpr int kYB = yS + 32 * kS * 4;
     static constexpr int kPerStage = kWarps * Tl::kBytes;
-    static constexpr int kFixed = kWarps * (2 * kYB + kSB) + 128 + kWarps * 4 * 8;
+    static constexpr int kFixed = kWarps * kYB + 128 + kWarps * 4 * 8;
     static constexpr int kFit = (kSmemMax - kFixed) / kPerStage;
-    static constexpr int kStages = kFit < 4 ? kFit : 4;
-    static_assert(kStages >= 2, "forward tile too large");
-    static constexpr int oY = 0;                            // [warp][2][kYB]
-    static constexpr int oS = oY + kWarps * 2 * kYB;        // [warp][kSB]
-    static constexpr int oT = al128(oS + kWarps * kSB);     // [stage][warp][tile]
+    static constexpr bool kFits = kFit >= 2;  // else the shape goes to another family
+    static constexpr int kStages = kFit < 2 ? 2 : (kFit < 4 ? kFit : 4);
+    static constexpr int oY = 0;                            // [warp][kYB]
+    static constexpr int oT = al128(oY + kWarps * kYB);     // [stage][warp][tile]
     static constexpr int oBar = oT + kStages * kPerStage;   // [warp][stage]
     static constexpr int kSmem = oBar + kWarps * kStages * 8 + 128;  // + alignment slack
-    static_assert(kSmem <= kSmemMax, "forward shared memory");
+    static_assert(!kFits || kSmem <= kSmemMax, "forward shared memory");
 };
 
 // 128-byte aligned start of dynamic shared memory.
@@ -385,8 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
     const long nb = (T + L - 1) / L;
     const long rs_slots = replay_slots_per_chunk(T, L);
     char *const tiles = smem + G::oT + warp * Tl::kBytes;  // + stage * G::kPerStage
-    char *const ybuf = smem + G::oY + warp * 2 * G::kYB;
-    float *const sbuf = reinterpret_cast<float *>(smem + G::oS + warp * G::kSB);
+    char *const ob = smem + G::oY + warp * G::kYB;
     uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + warp * NS;
     if (lane == 0) {
         for (int s = 0; s < NS; ++s) mbar_init(bars + s, 1);
@@ -440,11 +422,6 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
                                                     static_cast<int>(prod.t0()), false, bars + st, 0);
             prod.advance();
         }
-        // staging: the state buffer (last read by tile q-1's state store) and
-        // readout buffer q&1 (tile q-2's store) are free once every store but
-        // the newest (tile q-1's readout) has read its source
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
         mbar_wait(bars + q % NS, static_cast<uint32_t>((q / NS) & 1));
         const TileRead<D, M, FIXED, false, TIn> rd{tiles + (q % NS) * G::kPerStage, lane};
         const long ci = cons.ci;
@@ -454,17 +431,21 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
                 store_mean<D, M>(bm + ci * D * M, Mm);
                 store_cov_full<D>(bc + ci * D * D, P);
             }
-        } else if (A.rs != nullptr) {
-            stage_packed_state<D, M>(sbuf + lane * SF, Mm, P);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0 && chain0 < A.n) {
-                tma_store_2d(&mp.rs, static_cast<int>((ci * rs_slots + cons.j - 1) * SF), chain0, sbuf);
-                bulk_commit();
-            }
         }
-        float *const yb = reinterpret_cast<float *>(ybuf + (q & 1) * G::kYB);
-        float4 p4, r4;
+        if (cons.j != 0 && A.rs != nullptr && active) {
+            // the state, float by float: each store of the warp is one
+            // contiguous line of the structure-of-arrays layout
+            const long base = replay_state_base(chain, nb, rs_slots, ci, cons.j, SF);
+#pragma unroll
+            for (int i = 0; i < D; ++i)
+#pragma unroll
+                for (int c = 0; c < M; ++c) A.rs[base + static_cast<long>(i * M + c) * 32] = Mm[i][c];
+#pragma unroll
+            for (int t = 0; t < TRI; ++t) A.rs[base + static_cast<long>(D * M + t) * 32] = P[t];
+        }
+        float *const yb = reinterpret_cast<float *>(ob + G::yY);
+        const bool gains = A.rs != nullptr;
+        float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = b4;
         rd.noise(p4, r4);
         auto step = [&](int tau) {
             float k[D], a[D], v[M], qv[D];
@@ -484,14 +465,41 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
                 for (int i = 0; i < D; ++i) acc = fmaf(Mm[i][c], qv[i], acc);
                 y[c] = acc;
             }
+            if (tau == 0) {
+                // the output staging was last read by tile q-1's output stores
+                if (lane == 0) bulk_wait_read<0>();
+                __syncwarp();
+            }
             sts_vec<M>(yb + (tau * 32 + lane) * M, y);
+            if (gains) {
+                sts_vec<D>(reinterpret_cast<float *>(ob + G::yU) + (tau * 32 + lane) * D, u);
+                b4.x = tau == 0 ? beta : b4.x;
+                b4.y = tau == 1 ? beta : b4.y;
+                b4.z = tau == 2 ? beta : b4.z;
+                b4.w = tau == 3 ? beta : b4.w;
+                s4.x = tau == 0 ? s : s4.x;
+                s4.y = tau == 1 ? s : s4.y;
+                s4.z = tau == 2 ? s : s4.z;
+                s4.w = tau == 3 ? s : s4.w;
+            }
         };
 #pragma unroll 1
         for (int tau = 0; tau < kS; ++tau) step(tau);
+        if (gains) {
+            reinterpret_cast<float4 *>(ob + G::yB)[lane] = b4;
+            reinterpret_cast<float4 *>(ob + G::yS)[lane] = s4;
+        }
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-            if (chain0 < A.n) tma_store_3d(&mp.y, 0, chain0, t0, yb);
+            if (chain0 < A.n) {
+                tma_store_3d(&mp.y, 0, chain0, t0, yb);
+                if (gains) {
+                    tma_store_3d(&mp.gu, 0, chain0, t0, ob + G::yU);
+                    tma_store_2d(&mp.gb, t0, chain0, ob + G::yB);
+                    tma_store_2d(&mp.gs, t0, chain0, ob + G::yS);
+                }
+            }
             bulk_commit();
         }
         cons.advance();
@@ -555,63 +563,60 @@ struct TLayout {
     static_assert(total() <= 512, "history does not fit in tensor memory");
 };
 
-template <int D, int M, int F, int W = 32>
+template <class TL, int F, int W = 32>
 __device__ __forceinline__ void field_st(uint32_t base, int tau, const uint32_t *r) {
-    using TL = TLayout<D, M>;
     constexpr int n = TL::size(F), np = TL::npieces(n, W);
     if constexpr (np > 0) {
         constexpr int c0 = TL::col0(F, W), pos = TL::piece_pos(n, W);
 #pragma unroll
         for (int idx = 0; idx < np; ++idx) tmem::st_cols<W>(base + c0 + (tau * np + idx) * W, r + pos + idx * W);
     }
-    if constexpr (W > 1) field_st<D, M, F, W / 2>(base, tau, r);
+    if constexpr (W > 1) field_st<TL, F, W / 2>(base, tau, r);
 }
-template <int D, int M, int F, int W = 32>
+template <class TL, int F, int W = 32>
 __device__ __forceinline__ void field_ld(uint32_t base, int tau, uint32_t *r) {
-    using TL = TLayout<D, M>;
     constexpr int n = TL::size(F), np = TL::npieces(n, W);
     if constexpr (np > 0) {
         constexpr int c0 = TL::col0(F, W), pos = TL::piece_pos(n, W);
 #pragma unroll
         for (int idx = 0; idx < np; ++idx) tmem::ld_cols<W>(base + c0 + (tau * np + idx) * W, r + pos + idx * W);
     }
-    if constexpr (W > 1) field_ld<D, M, F, W / 2>(base, tau, r);
+    if constexpr (W > 1) field_ld<TL, F, W / 2>(base, tau, r);
 }
-// Store N floats as field F of token tau.
-template <int D, int M, int F, int N>
+// Store N floats as field F of token (or slot) tau.
+template <class TL, int F, int N>
 __device__ __forceinline__ void put(uint32_t base, int tau, const float *v) {
-    static_assert(N == TLayout<D, M>::size(F), "field size");
+    static_assert(N == TL::size(F), "field size");
     uint32_t r[N];
 #pragma unroll
     for (int i = 0; i < N; ++i) r[i] = __float_as_uint(v[i]);
-    field_st<D, M, F>(base, tau, r);
+    field_st<TL, F>(base, tau, r);
 }
-// Load field F of token tau (waits for the load).
-template <int D, int M, int F, int N>
+// Load field F of token (or slot) tau (waits for the load).
+template <class TL, int F, int N>
 __device__ __forceinline__ void get(uint32_t base, int tau, float *v) {
-    static_assert(N == TLayout<D, M>::size(F), "field size");
+    static_assert(N == TL::size(F), "field size");
     uint32_t r[N];
-    field_ld<D, M, F>(base, tau, r);
+    field_ld<TL, F>(base, tau, r);
     tmem::wait_ld_bind<N>(r);
 #pragma unroll
     for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
 }
-// Load rows [R0, R0+NR) of the pre-step mean of token tau.  The mean field
-// is row-major, so for M = 8 a 32-column piece is 4 whole rows.
-template <int D, int M, int R0, int NR>
+// Load rows [R0, R0+NR) of the pre-step mean (field FM) of token tau.  The
+// mean field is row-major, so for M = 8 a 32-column piece is 4 whole rows.
+template <class TL, int FM, int D, int M, int R0, int NR>
 __device__ __forceinline__ void get_mean_rows(uint32_t base, int tau, float (&out)[NR][M]) {
-    using TL = TLayout<D, M>;
     constexpr int n = D * M;
     uint32_t r[NR * M];
     if constexpr (n >= 32) {
         static_assert((R0 * M) % 32 == 0 && (NR * M) % 32 == 0, "row block = whole pieces");
-        constexpr int np = TL::npieces(n, 32), c0 = TL::col0(kMp, 32);
+        constexpr int np = TL::npieces(n, 32), c0 = TL::col0(FM, 32);
 #pragma unroll
         for (int b = 0; b < NR * M / 32; ++b)
             tmem::ld_cols<32>(base + c0 + (tau * np + R0 * M / 32 + b) * 32, r + 32 * b);
     } else {
         static_assert(R0 == 0 && NR == D, "small means load whole");
-        field_ld<D, M, kMp>(base, tau, r);
+        field_ld<TL, FM>(base, tau, r);
     }
     tmem::wait_ld_bind<NR * M>(r);
 #pragma unroll
@@ -688,15 +693,21 @@ __device__ __forceinline__ void put_row(T *stage_row, T *gdst, const float (&v)[
 
 // Copy a sub-chunk's start state from a boundary checkpoint (full
 // covariance, by its upper triangle) into this thread's state row.
+// (The state box is [float][32 chains]: this thread's float f at sdst + 128 f.)
 template <int D, int M>
 __device__ __forceinline__ void issue_checkpoint(uint32_t sdst, const float *ck_mean, const float *ck_cov) {
-    static_assert((D * M) % 4 == 0, "mean rows");
 #pragma unroll
-    for (int x = 0; x < D * M / 4; ++x) cp_async<16>(sdst + 16 * x, ck_mean + 4 * x);
+    for (int x = 0; x < D * M; ++x) cp_async<4>(sdst + 128 * x, ck_mean + x);
 #pragma unroll
     for (int i = 0; i < D; ++i)
 #pragma unroll
-        for (int j = i; j < D; ++j) cp_async<4>(sdst + 4 * (D * M + tri_index(D, i, j)), ck_cov + i * D + j);
+        for (int j = i; j < D; ++j) cp_async<4>(sdst + 128 * (D * M + tri_index(D, i, j)), ck_cov + i * D + j);
+}
+
+// First row of a group's state (ci, j) in the [rows][32 chains] view of the
+// structure-of-arrays state part.
+__device__ __forceinline__ int state_row(int chain0, long nb, long slots, long ci, long j, int sf) {
+    return static_cast<int>((((static_cast<long>(chain0) >> 5) * nb + ci) * slots + (j - 1)) * sf);
 }
 
 template <int D, int M, bool FIXED, bool NEED_DYN, bool NEED_INIT, typename TIn>
@@ -718,15 +729,15 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
     const float floor_ = A.floor;
     const bool has_gy = A.gy != nullptr;
     char *const tiles = smem + G::oT + warp * Tl::kBytes;  // + stage * G::kPerStage
-    float *const sbox = reinterpret_cast<float *>(smem + G::oS + warp * G::kSB);
-    float *const state = sbox + lane * SF;
+    float *const sbox = reinterpret_cast<float *>(smem + G::oS + warp * G::kSB);  // [SF][32 chains]
+    float *const state = sbox + lane;                                             // float f at [32 f]
     char *const out = smem + G::oO + warp * G::kOB;
     uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + warp * 2;
     uint32_t *const slot = reinterpret_cast<uint32_t *>(smem + G::oSlot);
     const float *const bm = A.bmean + chain * (nb + 1) * D * M;
     const float *const bc = A.bcov + chain * (nb + 1) * D * D;
 
-    for (int x = 0; x < SF; ++x) state[x] = 0.f;  // idle lanes replay finite zeros
+    for (int x = 0; x < SF; ++x) state[x * 32] = 0.f;  // idle lanes replay finite zeros
     if (lane == 0) {
         mbar_init(bars, 1);
         mbar_init(bars + 1, 1);
@@ -771,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
             uint64_t *bar = bars + stage;
             issue_tile<D, M, FIXED, true, TIn>(tiles + stage * G::kPerStage, mp, chain0, static_cast<int>(it.t0()),
                                                has_gy, bar, saved ? G::kSB : 0);
-            if (saved) tma_load_2d(sbox, &mp.rs, static_cast<int>((it.ci * rs_slots + it.j - 1) * SF), chain0, bar);
+            if (saved) tma_load_2d(sbox, &mp.rs, 0, state_row(chain0, nb, rs_slots, it.ci, it.j, SF), bar);
         }
         if (!saved && active) issue_checkpoint<D, M>(smem_u32(state), bm + it.ci * D * M, bc + it.ci * D * D);
         cp_async_commit();
@@ -793,20 +804,21 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
         const long row0 = chain * T + t0;
         float4 p4, r4;
         rd.noise(p4, r4);
-        put<D, M, kRp, TRI>(tb, 0, Rp);  // parked during the replay
+        put<TLayout<D, M>, kRp, TRI>(tb, 0, Rp);  // parked during the replay
 
         // ---- covariance pass: pre-step covariance, gain, beta and s per token
         {
             float P[TRI];
-            lds_n<TRI>(state + D * M, P);
+#pragma unroll
+            for (int t = 0; t < TRI; ++t) P[t] = state[(D * M + t) * 32];
             auto cstep = [&](int tau) {
                 float k[D], a[D], u[D], bs[2];
                 rd.keys(tau, k);
                 rd.decay(tau, a);
-                put<D, M, kPp, TRI>(tb, tau, P);
+                put<TLayout<D, M>, kPp, TRI>(tb, tau, P);
                 cov_step<D>(P, k, a, sel4v(p4, tau), sel4v(r4, tau), floor_, u, bs[0], bs[1]);
-                put<D, M, kU, D>(tb, tau, u);
-                put<D, M, kBS, 2>(tb, tau, bs);
+                put<TLayout<D, M>, kU, D>(tb, tau, u);
+                put<TLayout<D, M>, kBS, 2>(tb, tau, bs);
             };
 #pragma unroll 1
             for (int tau = 0; tau < kS; ++tau) cstep(tau);
@@ -816,7 +828,9 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
         {
             float Mm[D][M];
 #pragma unroll
-            for (int i = 0; i < D; ++i) lds_n<M>(state + i * M, Mm[i]);
+            for (int i = 0; i < D; ++i)
+#pragma unroll
+                for (int c = 0; c < M; ++c) Mm[i][c] = state[(i * M + c) * 32];
             // every lane has read its start state and is done with the other
             // stage: fetch the next sub-chunk while this one is processed
             __syncwarp();
@@ -833,18 +847,18 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
                 rd.keys(tau, k);
                 rd.decay(tau, a);
                 rd.values(tau, v);
-                get<D, M, kU, D>(tb, tau, u);
-                get<D, M, kBS, 2>(tb, tau, bs);
+                get<TLayout<D, M>, kU, D>(tb, tau, u);
+                get<TLayout<D, M>, kBS, 2>(tb, tau, bs);
                 {
                     float flat[D * M];
 #pragma unroll
                     for (int i = 0; i < D; ++i)
 #pragma unroll
                         for (int c = 0; c < M; ++c) flat[i * M + c] = Mm[i][c];
-                    put<D, M, kMp, D * M>(tb, tau, flat);
+                    put<TLayout<D, M>, kMp, D * M>(tb, tau, flat);
                 }
                 mean_step<D, M>(Mm, k, a, v, u, bs[0], e);
-                put<D, M, kE, M>(tb, tau, e);
+                put<TLayout<D, M>, kE, M>(tb, tau, e);
                 float gq[D];
                 if (has_gy) {
                     float gy[M];
@@ -867,7 +881,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
             for (int tau = 0; tau < kS; ++tau) mstep(tau);
         }
         tmem::wait_st();
-        get<D, M, kRp, TRI>(tb, 0, Rp);
+        get<TLayout<D, M>, kRp, TRI>(tb, 0, Rp);
 
         // ---- reverse step over the sub-chunk
         float4 gp4 = make_float4(0.f, 0.f, 0.f, 0.f), gr4 = gp4;
@@ -878,9 +892,9 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
             rd.keys(tau, k);
             rd.decay(tau, a);
             float u[D], e[M], bs[2];
-            get<D, M, kU, D>(tb, tau, u);
-            get<D, M, kE, M>(tb, tau, e);
-            get<D, M, kBS, 2>(tb, tau, bs);
+            get<TLayout<D, M>, kU, D>(tb, tau, u);
+            get<TLayout<D, M>, kE, M>(tb, tau, e);
+            get<TLayout<D, M>, kBS, 2>(tb, tau, bs);
             const float beta = bs[0], s = bs[1];
             // dL/d(post-update mean)
             if (has_gy) {
@@ -915,12 +929,12 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
             for (int r0 = 0; r0 < D; r0 += RB) {
                 float Mp[RB][M];
                 if constexpr (RB == D) {
-                    get_mean_rows<D, M, 0, D>(tb, tau, Mp);
+                    get_mean_rows<TLayout<D, M>, kMp, D, M, 0, D>(tb, tau, Mp);
                 } else {
                     if (r0 == 0) {
-                        get_mean_rows<D, M, 0, RB>(tb, tau, Mp);
+                        get_mean_rows<TLayout<D, M>, kMp, D, M, 0, RB>(tb, tau, Mp);
                     } else {
-                        get_mean_rows<D, M, RB, RB>(tb, tau, Mp);
+                        get_mean_rows<TLayout<D, M>, kMp, D, M, RB, RB>(tb, tau, Mp);
                     }
                 }
 #pragma unroll
@@ -957,7 +971,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
                 ag[i] = a[i] * gu[i];
             }
             float Pp[TRI];
-            get<D, M, kPp, TRI>(tb, tau, Pp);
+            get<TLayout<D, M>, kPp, TRI>(tb, tau, Pp);
             float gk[D];
 #pragma unroll
             for (int i = 0; i < D; ++i) {
@@ -1069,44 +1083,101 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
 //
 // Group g (32 chains) has a covariance warp (warp g) and a mean warp (warp
 // g + 4).  Both sit on SM sub-partition g and reach TMEM lane quarter g, so
-// they share the chains' tensor-memory history; the sub-partition interleaves
+// they share the chains' tensor-memory lanes; the sub-partition interleaves
 // two instruction streams instead of one.
-//   covariance warp: replays the covariance (history: pre-step covariance,
-//     gain, beta, s), then runs the R-adjoint of the reverse step;
-//   mean warp: replays the mean from the gains (history: pre-step mean,
-//     innovation, gq), then runs the dL/dM adjoint and hands the covariance
-//     warp h = gM' e, pk = M ge, the decay term and u.gM'.e per token.
-// Synchronisation is by mbarriers: tile stage full / free, start state read,
-// replay token ready (covariance -> mean), exchange slot full / free.  The
-// gradient rows are staged in the tile's own input slots once those inputs
-// are dead (gk in keys, gv in queries, gq in values, ga in decay, gp / gr in
-// process / observation) and leave by TMA stores.
+//   covariance warp: replays the covariance from the gains the forward saved
+//     (history: pre-step covariance), then runs the R-adjoint of the reverse
+//     step;
+//   mean warp: replays the mean from the same gains (history: pre-step mean,
+//     innovation), writes gq, then runs the dL/dM adjoint and hands the
+//     covariance warp, per token, h = gM' e, pk = M ge, the decay term of the
+//     mean and u.gM'.e through a ring of three TMEM slots.
+// With the gains saved the two replays are independent; the warps meet only
+// at the exchange ring and at the tile stages.  Synchronisation is by
+// mbarriers (tile stage full / free, start state read, exchange slot full /
+// free).  The gradient rows are staged in the tile's own input slots once
+// those inputs are dead (gk in keys, gv in queries, gq in values, ga in
+// decay, gp in process, gr in observation) and leave by TMA stores.
 // ===========================================================================
 constexpr int kSplitWarps = 8;
 constexpr int kSplitThreads = 32 * kSplitWarps;
+constexpr int kXSlots = 3;
+
+// TMEM columns of one lane in the two-warp backward.
+enum SplitField { kSMp = 0, kSPp = 1, kSE = 2, kSX = 3, kSNumFields = 4 };
+template <int D, int M>
+struct TLayoutSplit {
+    __host__ __device__ static constexpr int size(int f) {
+        return f == kSMp ? D * M : f == kSPp ? tri_size(D) : f == kSE ? M : 3 * D + 1;
+    }
+    __host__ __device__ static constexpr int copies(int f) { return f == kSX ? kXSlots : kS; }
+    __host__ __device__ static constexpr int npieces(int n, int w) { return w == 32 ? n / 32 : (((n % 32) & w) ? 1 : 0); }
+    __host__ __device__ static constexpr int piece_pos(int n, int w) {
+        int p = (n / 32) * 32;
+        if (w == 32) return 0;
+        for (int x = 16; x > w; x >>= 1)
+            if ((n % 32) & x) p += x;
+        return p;
+    }
+    __host__ __device__ static constexpr int col0(int f, int w) {
+        int c = 0;
+        for (int x = 32; x > w; x >>= 1)
+            for (int g = 0; g < kSNumFields; ++g) c += copies(g) * npieces(size(g), x) * x;
+        for (int g = 0; g < f; ++g) c += copies(g) * npieces(size(g), w) * w;
+        return c;
+    }
+    __host__ __device__ static constexpr int total() {
+        int c = 0;
+        for (int x = 32; x >= 1; x >>= 1)
+            for (int g = 0; g < kSNumFields; ++g) c += copies(g) * npieces(size(g), x) * x;
+        return c;
+    }
+    __host__ __device__ static constexpr int alloc() {
+        int a = 32;
+        while (a < total()) a *= 2;
+        return a;
+    }
+    static_assert(total() <= 512, "history does not fit in tensor memory");
+};
 
 template <int D, int M, typename TIn>
 struct SplitGeo {
     using Tl = Tile<D, M, false, true, TIn>;
     static_assert(D == M, "in-place gradient staging needs D == M");
-    static_assert(sizeof(TIn) == 2, "tile budget assumes BF16 inputs");
     static constexpr int SF = replay_state_floats(D, M);
-    static constexpr int kSB = 32 * SF * 4;   // a group's start states [chain][SF]
-    static constexpr int kXF = 3 * D + 1;     // exchanged floats per chain and token: h, pk, gam, gb
-    static constexpr int kXB = kXF * 32 * 4;  // one exchange slot, [float][chain]
-    static constexpr int kPerStage = 4 * Tl::kBytes;
-    static constexpr int oT = 0;                             // [stage][group][tile]
-    static constexpr int oS = oT + 2 * kPerStage;            // [group][kSB]
-    static constexpr int oX = al128(oS + 4 * kSB);           // [group][slot][kXB]
-    static constexpr int oBar = al128(oX + 4 * 2 * kXB);     // [group][13]
-    static constexpr int kBars = 13;  // full[2] empty[2] sfree rt[4] xfull[2] xempty[2]
+    // per group and stage: the token tile, then the gains [tau][chain][D],
+    // beta and s [chain][tau]
+    static constexpr int oU = Tl::kBytes, oB = oU + kS * 32 * D * 4, oS = oB + 32 * kS * 4;
+    static constexpr int kTileBytes = al128(oS + 32 * kS * 4);
+    static constexpr int kTx = Tl::kTx + kS * 32 * D * 4 + 2 * 32 * kS * 4;  // without gy, without state
+    static constexpr int kSB = 32 * SF * 4;  // a group's start states [chain][SF]
+    static constexpr int kPerStage = 4 * kTileBytes;
+    static constexpr int oT = 0;                        // [stage][group][tile]
+    static constexpr int oSt = oT + 2 * kPerStage;      // [group][kSB]
+    static constexpr int oBar = al128(oSt + 4 * kSB);   // [group][kBars]
+    static constexpr int kBars = 5 + 2 * kXSlots;      // full[2] empty[2] sfree xfull[3] xempty[3]
     static constexpr int oSlot = oBar + 4 * kBars * 8;
     static constexpr int kSmem = oSlot + 16 + 128;
-    static_assert(kSmem <= kSmemMax, "split backward shared memory");
+    static constexpr bool kFits = kSmem <= kSmemMax;
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// The covariance update of one token from its saved gain: P' = A P A + p I
+// - beta u u^T (the arithmetic of cov_step).
+template <int D>
+__device__ __forceinline__ void cov_update(float (&P)[tri_size(D)], const float (&a)[D], float p,
+                                           const float (&u)[D], float beta) {
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int j = i; j < D; ++j) {
+            const int t = tri_index(D, i, j);
+            const float upd = fmaf(-beta, u[i] * u[j], (a[i] * a[j]) * P[t]);
+            P[t] = (i == j) ? upd + p : upd;
+        }
 }
 
 template <int D, int M, bool NEED_DYN, bool NEED_INIT, typename TIn>
@@ -1114,8 +1185,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     backward_split(const BwdArgs<TIn> A, const __grid_constant__ BwdMaps mp) {
     using G = SplitGeo<D, M, TIn>;
     using Tl = typename G::Tl;
-    using TL = TLayout<D, M>;
-    constexpr int TRI = tri_size(D), SF = G::SF, XF = G::kXF;
+    using TL = TLayoutSplit<D, M>;
+    constexpr int TRI = tri_size(D), SF = G::SF, XF = 3 * D + 1;
     extern __shared__ __align__(128) char smem_raw[];
     char *const smem = smem_base(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1130,30 +1201,28 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     const long rs_slots = replay_slots_per_chunk(T, L);
     const float floor_ = A.floor;
     const bool has_gy = A.gy != nullptr;
-    char *const tiles = smem + G::oT + grp * Tl::kBytes;  // + stage * G::kPerStage
-    float *const sbox = reinterpret_cast<float *>(smem + G::oS + grp * G::kSB);
-    float *const state = sbox + lane * SF;
-    float *const xch = reinterpret_cast<float *>(smem + G::oX + grp * 2 * G::kXB);  // + slot * XF * 32
+    char *const tiles = smem + G::oT + grp * G::kTileBytes;  // + stage * G::kPerStage
+    float *const sbox = reinterpret_cast<float *>(smem + G::oSt + grp * G::kSB);  // [SF][32 chains]
+    float *const state = sbox + lane;                                              // float f at [32 f]
     uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + grp * G::kBars;
-    uint64_t *const full = bars, *const empty = bars + 2, *const sfree = bars + 4, *const rt = bars + 5;
-    uint64_t *const xfull = bars + 9, *const xempty = bars + 11;
+    uint64_t *const full = bars, *const empty = bars + 2, *const sfree = bars + 4;
+    uint64_t *const xfull = bars + 5, *const xempty = bars + 5 + kXSlots;
     uint32_t *const slot = reinterpret_cast<uint32_t *>(smem + G::oSlot);
     const float *const bm = A.bmean + chain * (nb + 1) * D * M;
     const float *const bc = A.bcov + chain * (nb + 1) * D * D;
 
     if (cov_warp) {
-        for (int x = 0; x < SF; ++x) state[x] = 0.f;  // idle lanes replay finite zeros
+        for (int x = 0; x < SF; ++x) state[x * 32] = 0.f;  // idle lanes replay finite zeros
         if (lane == 0) {
             mbar_init(full, 1);
             mbar_init(full + 1, 1);
             mbar_init(empty, 2);
             mbar_init(empty + 1, 2);
             mbar_init(sfree, 2);
-            for (int x = 0; x < kS; ++x) mbar_init(rt + x, 32);
-            mbar_init(xfull, 32);
-            mbar_init(xfull + 1, 32);
-            mbar_init(xempty, 32);
-            mbar_init(xempty + 1, 32);
+            for (int x = 0; x < kXSlots; ++x) {
+                mbar_init(xfull + x, 32);
+                mbar_init(xempty + x, 32);
+            }
             mbar_init_fence();
         }
     }
@@ -1166,28 +1235,43 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     tmem::fence_after_sync();
     const uint32_t tb = *slot + (static_cast<uint32_t>(grp * 32) << 16);
 
-    // the tile of an item (and its saved start state) by the covariance
-    // warp's lane 0; a checkpoint start state by each warp for its own part
+    // An item's tile, gains (and saved start state) by the covariance warp's
+    // lane 0; a checkpoint start state by each warp for its own part.
     auto issue_tile_state = [&](const BwdItems &it, int stage) {
         const bool saved = it.j > 0;
-        issue_tile<D, M, false, true, TIn>(tiles + stage * G::kPerStage, mp, chain0, static_cast<int>(it.t0()),
-                                           has_gy, full + stage, saved ? G::kSB : 0);
-        if (saved) tma_load_2d(sbox, &mp.rs, static_cast<int>((it.ci * rs_slots + it.j - 1) * SF), chain0, full + stage);
+        char *const t = tiles + stage * G::kPerStage;
+        const int t0 = static_cast<int>(it.t0());
+        mbar_arrive_tx(full + stage, G::kTx + (has_gy ? Tl::szG : 0) + (saved ? G::kSB : 0));
+        tma_load_3d(t + Tl::oK, &mp.k, 0, chain0, t0, full + stage);
+        tma_load_3d(t + Tl::oQ, &mp.q, 0, chain0, t0, full + stage);
+        tma_load_3d(t + Tl::oV, &mp.v, 0, chain0, t0, full + stage);
+        tma_load_3d(t + Tl::oA, &mp.a, 0, chain0, t0, full + stage);
+        tma_load_2d(t + Tl::oP, &mp.p, t0, chain0, full + stage);
+        tma_load_2d(t + Tl::oR, &mp.r, t0, chain0, full + stage);
+        if (has_gy) tma_load_3d(t + Tl::oG, &mp.gy, 0, chain0, t0, full + stage);
+        tma_load_3d(t + G::oU, &mp.gu, 0, chain0, t0, full + stage);
+        tma_load_2d(t + G::oB, &mp.gb, t0, chain0, full + stage);
+        tma_load_2d(t + G::oS, &mp.gs, t0, chain0, full + stage);
+        if (saved) tma_load_2d(sbox, &mp.rs, 0, state_row(chain0, nb, rs_slots, it.ci, it.j, SF), full + stage);
     };
     auto issue_checkpoint_part = [&](const BwdItems &it) {
         if (it.j > 0 || !active) return;
-        const uint32_t s = smem_u32(state);
+        const uint32_t s = smem_u32(state);  // float f at s + 128 f
         if (cov_warp) {
             const float *ck = bc + it.ci * D * D;
 #pragma unroll
             for (int i = 0; i < D; ++i)
 #pragma unroll
-                for (int j = i; j < D; ++j) cp_async<4>(s + 4 * (D * M + tri_index(D, i, j)), ck + i * D + j);
+                for (int j = i; j < D; ++j) cp_async<4>(s + 128 * (D * M + tri_index(D, i, j)), ck + i * D + j);
         } else {
             const float *ck = bm + it.ci * D * M;
 #pragma unroll
-            for (int x = 0; x < D * M / 4; ++x) cp_async<16>(s + 16 * x, ck + 4 * x);
+            for (int x = 0; x < D * M; ++x) cp_async<4>(s + 128 * x, ck + x);
         }
+    };
+    // token tau's gain and scalars from the tile
+    auto gains = [&](const char *t, int tau, float (&u)[D]) {
+        lds_vec<D>(reinterpret_cast<const float *>(t + G::oU) + (tau * 32 + lane) * D, u);
     };
 
     BwdItems cur, nxt;
@@ -1199,6 +1283,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         cp_async_commit();
         nxt.advance();
     }
+    long ntok = 0;  // exchange tokens so far (ring position)
 
     if (cov_warp) {
         // ------------------------------------------------------------------
@@ -1223,27 +1308,15 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             const int t0 = static_cast<int>(cur.t0());
             float4 p4, r4;
             rd.noise(p4, r4);
+            const float4 b4 = reinterpret_cast<const float4 *>(tile + G::oB)[lane];
+            const float4 s4 = reinterpret_cast<const float4 *>(tile + G::oS)[lane];
             float P[TRI];
-            lds_n<TRI>(state + D * M, P);
+#pragma unroll
+            for (int t = 0; t < TRI; ++t) P[t] = state[(D * M + t) * 32];
             __syncwarp();
             if (lane == 0) mbar_arrive(sfree);
             if (!nxt.done) issue_checkpoint_part(nxt);  // this warp's part of the row is read
             cp_async_commit();
-            // replay: pre-step covariance, gain, beta, s; hand each token's
-            // gain to the mean warp
-#pragma unroll 1
-            for (int tau = 0; tau < kS; ++tau) {
-                float k[D], a[D], u[D], bs[2];
-                rd.keys(tau, k);
-                rd.decay(tau, a);
-                put<D, M, kPp, TRI>(tb, tau, P);
-                cov_step<D>(P, k, a, sel4v(p4, tau), sel4v(r4, tau), floor_, u, bs[0], bs[1]);
-                put<D, M, kU, D>(tb, tau, u);
-                put<D, M, kBS, 2>(tb, tau, bs);
-                tmem::wait_st();
-                tmem::fence_before_sync();
-                mbar_arrive(rt + tau);
-            }
             // next sub-chunk: once the mean warp has read its start state
             // and both warps released the stage the next tile goes to
             if (!nxt.done) {
@@ -1253,33 +1326,34 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                     issue_tile_state(nxt, static_cast<int>((q + 1) & 1));
                 }
                 nxt.advance();
-            } else if (lane == 0) {
-                mbar_wait(sfree, static_cast<uint32_t>(q & 1));
             }
+            // replay: pre-step covariance per token, updated with the saved gains
+#pragma unroll 1
+            for (int tau = 0; tau < kS; ++tau) {
+                float a[D], u[D];
+                rd.decay(tau, a);
+                gains(tile, tau, u);
+                put<TL, kSPp, TRI>(tb, tau, P);
+                cov_update<D>(P, a, sel4v(p4, tau), u, sel4v(b4, tau));
+            }
+            tmem::wait_st();
             // reverse: covariance adjoint
             float4 gp4 = make_float4(0.f, 0.f, 0.f, 0.f), gr4 = gp4;
 #pragma unroll 1
-            for (int tau = kS - 1; tau >= 0; --tau) {
-                const int xs = tau & 1;
-                mbar_wait(xfull + xs, tau < 2 ? 1u : 0u);
+            for (int tau = kS - 1; tau >= 0; --tau, ++ntok) {
+                const int xs = static_cast<int>(ntok % kXSlots);
+                mbar_wait(xfull + xs, static_cast<uint32_t>((ntok / kXSlots) & 1));
                 tmem::fence_after_sync();
-                const float *xp = xch + xs * XF * 32 + lane;
-                float h[D], pk[D], gam[D];
-#pragma unroll
-                for (int i = 0; i < D; ++i) {
-                    h[i] = xp[i * 32];
-                    pk[i] = xp[(D + i) * 32];
-                    gam[i] = xp[(2 * D + i) * 32];
-                }
-                float gb = xp[3 * D * 32];
+                float xv[XF];
+                get<TL, kSX, XF>(tb, xs, xv);
+                tmem::fence_before_sync();
                 mbar_arrive(xempty + xs);
-                float k[D], a[D], u[D], bs[2];
+                float k[D], a[D], u[D];
                 rd.keys(tau, k);
                 rd.decay(tau, a);
-                const float p = sel4v(p4, tau);
-                get<D, M, kU, D>(tb, tau, u);
-                get<D, M, kBS, 2>(tb, tau, bs);
-                const float beta = bs[0], s = bs[1];
+                gains(tile, tau, u);
+                const float p = sel4v(p4, tau), beta = sel4v(b4, tau), s = sel4v(s4, tau);
+                float gb = xv[3 * D];
                 float Ru[D], trR = 0.f;
 #pragma unroll
                 for (int i = 0; i < D; ++i) {
@@ -1294,11 +1368,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 float gu[D], ag[D];
 #pragma unroll
                 for (int i = 0; i < D; ++i) {
-                    gu[i] = beta * h[i] - 2.f * beta * Ru[i] + gs * k[i];
+                    gu[i] = beta * xv[i] - 2.f * beta * Ru[i] + gs * k[i];
                     ag[i] = a[i] * gu[i];
                 }
                 float Pp[TRI];
-                get<D, M, kPp, TRI>(tb, tau, Pp);
+                get<TL, kSPp, TRI>(tb, tau, Pp);
                 float gk[D];
 #pragma unroll
                 for (int i = 0; i < D; ++i) {
@@ -1306,7 +1380,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 #pragma unroll
                     for (int j = 0; j < D; ++j) z = fmaf(Pp[tri_index(D, i, j)], ag[j], z);
                     const float gk3 = fmaf(a[i], z, p * gu[i]);
-                    gk[i] = fmaf(-a[i], pk[i], fmaf(gs, u[i], gk3));
+                    gk[i] = fmaf(-a[i], xv[D + i], fmaf(gs, u[i], gk3));
                 }
                 float gaP[D];
 #pragma unroll
@@ -1331,7 +1405,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                     float ga[D], gpk = 0.f;
 #pragma unroll
                     for (int i = 0; i < D; ++i) {
-                        ga[i] = fmaf(2.f, gaP[i], gam[i]);
+                        ga[i] = fmaf(2.f, gaP[i], xv[2 * D + i]);
                         gpk = fmaf(gu[i], k[i], gpk);
                     }
                     store_vec<D>(reinterpret_cast<float *>(tile + Tl::oA) + (tau * 32 + lane) * D, ga);
@@ -1392,9 +1466,12 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             char *const tile = tiles + (q & 1) * G::kPerStage;
             const TileRead<D, M, false, true, TIn> rd{tile, lane};
             const int t0 = static_cast<int>(cur.t0());
+            const float4 b4 = reinterpret_cast<const float4 *>(tile + G::oB)[lane];
             float Mm[D][M];
 #pragma unroll
-            for (int i = 0; i < D; ++i) lds_n<M>(state + i * M, Mm[i]);
+            for (int i = 0; i < D; ++i)
+#pragma unroll
+                for (int c = 0; c < M; ++c) Mm[i][c] = state[(i * M + c) * 32];
             __syncwarp();
             if (lane == 0) mbar_arrive(sfree);
             if (!nxt.done) {
@@ -1406,24 +1483,21 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             // token's (dead) value slot
 #pragma unroll 1
             for (int tau = 0; tau < kS; ++tau) {
-                float k[D], a[D], v[M], u[D], bs[2], e[M];
+                float k[D], a[D], v[M], u[D], e[M];
                 rd.keys(tau, k);
                 rd.decay(tau, a);
                 rd.values(tau, v);
-                mbar_wait(rt + tau, static_cast<uint32_t>(q & 1));
-                tmem::fence_after_sync();
-                get<D, M, kU, D>(tb, tau, u);
-                get<D, M, kBS, 2>(tb, tau, bs);
+                gains(tile, tau, u);
                 {
                     float flat[D * M];
 #pragma unroll
                     for (int i = 0; i < D; ++i)
 #pragma unroll
                         for (int c = 0; c < M; ++c) flat[i * M + c] = Mm[i][c];
-                    put<D, M, kMp, D * M>(tb, tau, flat);
+                    put<TL, kSMp, D * M>(tb, tau, flat);
                 }
-                mean_step<D, M>(Mm, k, a, v, u, bs[0], e);
-                put<D, M, kE, M>(tb, tau, e);
+                mean_step<D, M>(Mm, k, a, v, u, sel4v(b4, tau), e);
+                put<TL, kSE, M>(tb, tau, e);
                 float gq[D];
                 if (has_gy) {
                     float gy[M];
@@ -1442,17 +1516,16 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 store_vec<D>(reinterpret_cast<TIn *>(tile + Tl::oV) + (tau * 32 + lane) * D, gq);
             }
             tmem::wait_st();
-            // reverse: mean adjoint, the covariance warp's inputs via the
-            // exchange slots
+            // reverse: mean adjoint; the covariance warp's inputs go through
+            // the exchange ring
 #pragma unroll 1
-            for (int tau = kS - 1; tau >= 0; --tau) {
-                float k[D], a[D], u[D], e[M], bs[2];
+            for (int tau = kS - 1; tau >= 0; --tau, ++ntok) {
+                float k[D], a[D], u[D], e[M];
                 rd.keys(tau, k);
                 rd.decay(tau, a);
-                get<D, M, kU, D>(tb, tau, u);
-                get<D, M, kE, M>(tb, tau, e);
-                get<D, M, kBS, 2>(tb, tau, bs);
-                const float beta = bs[0];
+                gains(tile, tau, u);
+                get<TL, kSE, M>(tb, tau, e);
+                const float beta = sel4v(b4, tau);
                 if (has_gy) {
                     float qv[D], gy[M];
                     rd.queries(tau, qv);
@@ -1462,7 +1535,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 #pragma unroll
                         for (int c = 0; c < M; ++c) gM[i][c] = fmaf(qv[i], gy[c], gM[i][c]);
                 }
-                float ge[M], h[D], gb = 0.f;
+                float xv[XF];  // h, pk, gam, u.gM'.e
+                float ge[M], gb = 0.f;
 #pragma unroll
                 for (int c = 0; c < M; ++c) {
                     float acc = 0.f;
@@ -1476,17 +1550,16 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                     float acc = 0.f;
 #pragma unroll
                     for (int c = 0; c < M; ++c) acc = fmaf(gM[i][c], e[c], acc);
-                    h[i] = acc;
+                    xv[i] = acc;
                 }
-                float pk[D], gam[D];
                 constexpr int RB = 32 / M;  // rows per TMEM load
 #pragma unroll
                 for (int r0 = 0; r0 < D; r0 += RB) {
                     float Mp[RB][M];
                     if (r0 == 0) {
-                        get_mean_rows<D, M, 0, RB>(tb, tau, Mp);
+                        get_mean_rows<TL, kSMp, D, M, 0, RB>(tb, tau, Mp);
                     } else {
-                        get_mean_rows<D, M, RB, RB>(tb, tau, Mp);
+                        get_mean_rows<TL, kSMp, D, M, RB, RB>(tb, tau, Mp);
                     }
 #pragma unroll
                     for (int ii = 0; ii < RB; ++ii) {
@@ -1499,23 +1572,21 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                             if constexpr (NEED_DYN) gai = fmaf(gmb, Mp[ii][c], gai);
                             gM[i][c] = a[i] * gmb;
                         }
-                        pk[i] = pki;
-                        gam[i] = gai;
+                        xv[D + i] = pki;
+                        xv[2 * D + i] = gai;
                     }
                 }
+                xv[3 * D] = gb;
                 // the token's query slot is dead: it takes gv
                 store_vec<M>(reinterpret_cast<TIn *>(tile + Tl::oQ) + (tau * 32 + lane) * M, ge);
-                const int xs = tau & 1;
-                if (q > 0 || tau < 2) mbar_wait(xempty + xs, tau < 2 ? 0u : 1u);
-                float *const xp = xch + xs * XF * 32 + lane;
-#pragma unroll
-                for (int i = 0; i < D; ++i) {
-                    xp[i * 32] = h[i];
-                    xp[(D + i) * 32] = pk[i];
-                    xp[(2 * D + i) * 32] = gam[i];
+                const int xs = static_cast<int>(ntok % kXSlots);
+                if (ntok >= kXSlots) {
+                    mbar_wait(xempty + xs, static_cast<uint32_t>(((ntok - kXSlots) / kXSlots) & 1));
+                    tmem::fence_after_sync();
                 }
-                xp[3 * D * 32] = gb;
-                tmem::fence_before_sync();  // this token's TMEM reads are done
+                put<TL, kSX, XF>(tb, xs, xv);
+                tmem::wait_st();
+                tmem::fence_before_sync();
                 mbar_arrive(xfull + xs);
             }
             fence_proxy_async();
@@ -1580,12 +1651,12 @@ bool map_tok(CUtensorMap *m, const T *base, int rowelems, long n, long t) {
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-// Map of a [N, W] float tensor: dims (column, chain), box (bw, 32 chains).
-inline bool map_rows(CUtensorMap *m, const float *base, long w, long n, int bw) {
+// Map of a [n, w] float tensor: dims (column, row), box (bw columns, bh rows).
+inline bool map_rows(CUtensorMap *m, const float *base, long w, long n, int bw, int bh = 32) {
     if (base == nullptr) return true;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(n)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w) * 4};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(bw), 32};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh)};
     const cuuint32_t estr[2] = {1, 1};
     return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -1613,13 +1684,16 @@ int launch_fwd(const FwdArgs<TIn> &a, cudaStream_t st) {
     FwdMaps mp;
     std::memset(&mp, 0, sizeof(mp));
     const long nb = (a.t + a.chunks - 1) / a.chunks;
-    const long W = nb * replay_slots_per_chunk(a.t, a.chunks) * replay_state_floats(D, M);
     bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
               map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.y, a.out, M, a.n, a.t);
     if (!FIXED)
         ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
              map_rows(&mp.r, a.observation, a.t, a.n, kS);
-    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, W, a.n, replay_state_floats(D, M));
+    if (a.rs != nullptr) {
+        const Gains gn = replay_gains(a.rs, a.n, a.t, a.chunks, D, M);
+        ok = ok && map_tok(&mp.gu, static_cast<const float *>(gn.u), D, a.n, a.t) &&
+             map_rows(&mp.gb, gn.beta, a.t, a.n, kS) && map_rows(&mp.gs, gn.s, a.t, a.n, kS);
+    }
     if (!ok) return fail(BSSM_ERR_CUDA, "forward_chain: tensor-map encoding failed");
     const long grid = (a.n + kThreads - 1) / kThreads;
     k<<<static_cast<unsigned>(grid), kThreads, G::kSmem, st>>>(a, mp);
@@ -1654,13 +1728,13 @@ int launch_bwd(const BwdArgs<TIn> &a, cudaStream_t st) {
     BwdMaps mp;
     std::memset(&mp, 0, sizeof(mp));
     const long nb = (a.t + a.chunks - 1) / a.chunks;
-    const long W = nb * replay_slots_per_chunk(a.t, a.chunks) * replay_state_floats(D, M);
+    const long W = replay_state_part(a.n, a.t, a.chunks, D, M) / 32;  // rows of 32 chains
     bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
               map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.gy, a.gy, M, a.n, a.t);
     if (!FIXED)
         ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
              map_rows(&mp.r, a.observation, a.t, a.n, kS);
-    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, W, a.n, replay_state_floats(D, M));
+    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, 32, W, 32, replay_state_floats(D, M));
     if (G::kStageOut) {
         ok = ok && map_tok(&mp.gk, a.gk, D, a.n, a.t) && map_tok(&mp.gv, a.gv, M, a.n, a.t) &&
              map_tok(&mp.gq, a.gq, D, a.n, a.t);
@@ -1693,16 +1767,19 @@ int launch_split(const BwdArgs<TIn> &a, cudaStream_t st) {
     BwdMaps mp;
     std::memset(&mp, 0, sizeof(mp));
     const long nb = (a.t + a.chunks - 1) / a.chunks;
-    const long W = nb * replay_slots_per_chunk(a.t, a.chunks) * replay_state_floats(D, M);
+    const long W = replay_state_part(a.n, a.t, a.chunks, D, M) / 32;  // rows of 32 chains
     bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
               map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.gy, a.gy, M, a.n, a.t) &&
               map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
               map_rows(&mp.r, a.observation, a.t, a.n, kS) && map_tok(&mp.gk, a.gk, D, a.n, a.t) &&
               map_tok(&mp.gv, a.gv, M, a.n, a.t) && map_tok(&mp.gq, a.gq, D, a.n, a.t);
-    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, W, a.n, replay_state_floats(D, M));
+    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, 32, W, 32, replay_state_floats(D, M));
     if (NEED_DYN)
         ok = ok && map_tok(&mp.ga, a.ga, D, a.n, a.t) && map_rows(&mp.gp, a.gp, a.t, a.n, kS) &&
              map_rows(&mp.gr, a.gr, a.t, a.n, kS);
+    const Gains gn = replay_gains(a.rs, a.n, a.t, a.chunks, D, M);
+    ok = ok && map_tok(&mp.gu, static_cast<const float *>(gn.u), D, a.n, a.t) &&
+         map_rows(&mp.gb, gn.beta, a.t, a.n, kS) && map_rows(&mp.gs, gn.s, a.t, a.n, kS);
     if (!ok) return fail(BSSM_ERR_CUDA, "backward_split: tensor-map encoding failed");
     const long grid = (a.n + 127) / 128;
     k<<<static_cast<unsigned>(grid), kSplitThreads, smem, st>>>(a, mp);
@@ -1717,9 +1794,18 @@ inline bool split_allowed() {
 }
 
 template <int D, typename TIn>
-int fwd_d(int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
+constexpr bool fwd_fits() {
     if constexpr ((D * static_cast<int>(sizeof(TIn))) % 16 != 0) {
-        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels need 16-byte key rows");
+        return false;
+    } else {
+        return FwdGeo<D, 8, false, TIn>::kFits && FwdGeo<D, 8, true, TIn>::kFits;
+    }
+}
+
+template <int D, typename TIn>
+int fwd_d(int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
+    if constexpr (!fwd_fits<D, TIn>()) {
+        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain forward: shape does not fit");
     } else {
         return fixed ? launch_fwd<D, 8, true, TIn>(a, st) : launch_fwd<D, 8, false, TIn>(a, st);
     }
@@ -1727,12 +1813,14 @@ int fwd_d(int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
 
 template <int D, bool FIXED, typename TIn>
 int bwd_f(bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
-    if constexpr (D == 8 && !FIXED && sizeof(TIn) == 2) {
-        if (split_allowed()) {
-            if (dyn && init) return launch_split<D, 8, true, true, TIn>(a, st);
-            if (dyn) return launch_split<D, 8, true, false, TIn>(a, st);
-            if (init) return launch_split<D, 8, false, true, TIn>(a, st);
-            return launch_split<D, 8, false, false, TIn>(a, st);
+    if constexpr (D == 8 && !FIXED) {
+        if constexpr (SplitGeo<D, 8, TIn>::kFits) {
+            if (split_allowed() && a.rs != nullptr) {  // the replay buffer carries the gains
+                if (dyn && init) return launch_split<D, 8, true, true, TIn>(a, st);
+                if (dyn) return launch_split<D, 8, true, false, TIn>(a, st);
+                if (init) return launch_split<D, 8, false, true, TIn>(a, st);
+                return launch_split<D, 8, false, false, TIn>(a, st);
+            }
         }
     }
     if (dyn && init) return launch_bwd<D, 8, FIXED, true, true, TIn>(a, st);
@@ -1753,14 +1841,16 @@ int bwd_d(int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st
 }  // namespace chain
 
 template <typename TIn>
-bool chain_eligible(int d, long n, long t, int chunks) {
-    return chain::eligible<TIn>(d, 8, n, t, chunks);
+bool chain_eligible(int d, long n, long t, int chunks, bool forward) {
+    if (!chain::eligible<TIn>(d, 8, n, t, chunks)) return false;
+    if (!forward) return true;
+    return d == 8 ? chain::fwd_fits<8, TIn>() : chain::fwd_fits<4, TIn>();
 }
 
 template <typename TIn>
 int chain_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
     if (a.n == 0) return BSSM_OK;
-    if (!chain_eligible<TIn>(d, a.n, a.t, a.chunks))
+    if (!chain_eligible<TIn>(d, a.n, a.t, a.chunks, true))
         return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels: shape not supported");
     switch (d) {
         case 4: return chain::fwd_d<4, TIn>(fixed, a, st);
@@ -1772,7 +1862,7 @@ int chain_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
 template <typename TIn>
 int chain_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
     if (a.n == 0 || (a.t == 0 && !init)) return BSSM_OK;
-    if (!chain_eligible<TIn>(d, a.n, a.t, a.chunks))
+    if (!chain_eligible<TIn>(d, a.n, a.t, a.chunks, false))
         return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels: shape not supported");
     if (a.rs == nullptr && replay_slots_per_chunk(a.t, a.chunks) > 0)
         return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain backward needs the forward's replay states");
@@ -1792,8 +1882,8 @@ extern "C" unsigned int bssm_debug_wait_timeouts(void) {
 }
 
 namespace bssm {
-template bool chain_eligible<float>(int, long, long, int);
-template bool chain_eligible<__nv_bfloat16>(int, long, long, int);
+template bool chain_eligible<float>(int, long, long, int, bool);
+template bool chain_eligible<__nv_bfloat16>(int, long, long, int, bool);
 template int chain_forward<float>(int, int, const FwdArgs<float> &, cudaStream_t);
 template int chain_forward<__nv_bfloat16>(int, int, const FwdArgs<__nv_bfloat16> &, cudaStream_t);
 template int chain_backward<float>(int, int, bool, bool, const BwdArgs<float> &, cudaStream_t);

@@ -42,11 +42,15 @@ struct BwdArgs {
     float floor;
 };
 
-// Replay states: the state at every kReplaySpan-token boundary inside each
-// chunk (not at the chunk start, which is the boundary checkpoint).  Layout
-// per chain: [chunk][slot][mean D*M row-major | covariance upper triangle,
-// row by row (tri_index) | pad].  The covariance is exactly symmetric in every
-// kernel family, so its upper triangle is the whole state.
+// Replay buffer, part one -- replay states: the state at every
+// kReplaySpan-token boundary inside each chunk (not at the chunk start, which
+// is the boundary checkpoint).  A state is [mean D*M row-major | covariance
+// upper triangle, row by row (tri_index) | pad] (the covariance is exactly
+// symmetric in every kernel family, so its upper triangle is the whole
+// state).  States are stored as a structure of arrays over groups of 32
+// chains: float f of state (chunk ci, slot j) of chain c is at
+//     ((((c / 32) * nb + ci) * slots + j - 1) * SF + f) * 32 + c % 32,
+// so float f of a group's 32 chains is one contiguous 128-byte line.
 constexpr int kReplaySpan = 4;
 
 // Position of covariance entry (i, j) in the row-by-row upper triangle.
@@ -55,29 +59,71 @@ __host__ __device__ constexpr int tri_index(int d, int i, int j) {
 }
 __host__ __device__ constexpr int tri_size(int d) { return d * (d + 1) / 2; }
 
-// Row `row` of a covariance (D floats) to / from the packed upper triangle.
-template <int D>
-__device__ __forceinline__ void store_row_packed(float *packed, int row, const float (&v)[D]) {
-#pragma unroll
-    for (int j = 0; j < D; ++j)
-        if (j >= row) packed[tri_index(D, row, j)] = v[j];
-}
-template <int D>
-__device__ __forceinline__ void load_row_packed(const float *packed, int row, float (&v)[D]) {
-#pragma unroll
-    for (int j = 0; j < D; ++j) v[j] = packed[tri_index(D, row, j)];
-}
 __host__ __device__ inline long replay_slots_per_chunk(long t, int chunks) {
     const long span = chunks < t ? chunks : t;
     const long nsub = (span + kReplaySpan - 1) / kReplaySpan;
     return nsub > 1 ? nsub - 1 : 0;
 }
-// Floats per saved state, padded to a 16-byte multiple so that every slot
-// starts 16-byte aligned (the lanes move it with 128-bit accesses).
+// Floats per state, a multiple of 4.
 __host__ __device__ constexpr int replay_state_floats(int d, int m) { return (d * m + tri_size(d) + 3) / 4 * 4; }
-__host__ __device__ inline float *replay_slot(const float *rs, long chain, long nb, long slots, long ci,
-                                              long j, int d, int m) {
-    return const_cast<float *>(rs) + ((chain * nb + ci) * slots + (j - 1)) * static_cast<long>(replay_state_floats(d, m));
+__host__ __device__ inline long replay_groups(long n) { return (n + 31) / 32; }
+// Index of float 0 of chain `chain`'s state (ci, j >= 1); float f is at +32 f.
+__host__ __device__ inline long replay_state_base(long chain, long nb, long slots, long ci, long j, int sf) {
+    return ((((chain >> 5) * nb + ci) * slots + (j - 1)) * sf) * 32 + (chain & 31);
+}
+// Floats of the state part of the buffer.
+__host__ __device__ inline long replay_state_part(long n, long t, int chunks, int d, int m) {
+    const long nb = (t + chunks - 1) / chunks;
+    return replay_groups(n) * 32 * nb * replay_slots_per_chunk(t, chunks) * replay_state_floats(d, m);
+}
+
+// A lane's mean columns / a covariance row to or from a state (base from
+// replay_state_base).
+template <int D, int M, int CPL>
+__device__ __forceinline__ void rs_put_mean_cols(float *rs, long base, int col0, const float (&Mc)[CPL][D]) {
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int l = 0; l < CPL; ++l) rs[base + static_cast<long>(i * M + col0 + l) * 32] = Mc[l][i];
+}
+template <int D, int M, int CPL>
+__device__ __forceinline__ void rs_get_mean_cols(const float *rs, long base, int col0, float (&Mc)[CPL][D]) {
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int l = 0; l < CPL; ++l) Mc[l][i] = rs[base + static_cast<long>(i * M + col0 + l) * 32];
+}
+template <int D, int M>
+__device__ __forceinline__ void rs_put_row(float *rs, long base, int row, const float (&v)[D]) {
+#pragma unroll
+    for (int j = 0; j < D; ++j)
+        if (j >= row) rs[base + static_cast<long>(D * M + tri_index(D, row, j)) * 32] = v[j];
+}
+template <int D, int M>
+__device__ __forceinline__ void rs_get_row(const float *rs, long base, int row, float (&v)[D]) {
+#pragma unroll
+    for (int j = 0; j < D; ++j) v[j] = rs[base + static_cast<long>(D * M + tri_index(D, row, j)) * 32];
+}
+
+// After the states, the replay buffer holds every token's gain and scalars
+// as the forward computed them: u [N][T][D], then beta [N][T], then s [N][T]
+// (each part starting 16-byte aligned).  A backward can replay the mean
+// from these without waiting for the covariance replay.
+__host__ __device__ inline long round4(long x) { return (x + 3) / 4 * 4; }
+struct Gains {
+    float *u, *beta, *s;
+};
+__host__ __device__ inline Gains replay_gains(const float *rs, long n, long t, int chunks, int d, int m) {
+    float *g = const_cast<float *>(rs) + replay_state_part(n, t, chunks, d, m);
+    Gains r;
+    r.u = g;
+    r.beta = g + round4(n * t * d);
+    r.s = r.beta + round4(n * t);
+    return r;
+}
+// Floats of the whole replay buffer.
+__host__ __device__ inline long replay_floats(long n, long t, int chunks, int d, int m) {
+    return replay_state_part(n, t, chunks, d, m) + round4(n * t * d) + 2 * round4(n * t);
 }
 
 // Error reporting (thread-local message behind bssm_last_error()).
@@ -134,7 +180,7 @@ int staged_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a
 // Thread-per-chain kernels (bssm_chain.cu): shapes with 16-byte rows and
 // T, chunk length multiples of kReplaySpan.  The backward needs the forward's
 // replay states whenever a chunk is longer than kReplaySpan tokens.
-template <typename TIn> bool chain_eligible(int d, long n, long t, int chunks);
+template <typename TIn> bool chain_eligible(int d, long n, long t, int chunks, bool forward);
 template <typename TIn> int chain_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st);
 template <typename TIn>
 int chain_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st);

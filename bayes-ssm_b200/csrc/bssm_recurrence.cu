@@ -238,9 +238,10 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
             store_vec<D>(bc + c * D * D + own * D, P);
             ++c;
         } else if (A.rs != nullptr && in_chunk % kReplaySpan == 0) {
-            float *slot = replay_slot(A.rs, chain, nb, rs_slots, c - 1, in_chunk / kReplaySpan, D, M);
-            store_mean_cols<D, M>(slot, col0, Mc);
-            store_row_packed<D>(slot + D * M, own, P);
+            const long base = replay_state_base(chain, nb, rs_slots, c - 1, in_chunk / kReplaySpan,
+                                                replay_state_floats(D, M));
+            rs_put_mean_cols<D, M, CPL>(A.rs, base, col0, Mc);
+            rs_put_row<D, M>(A.rs, base, own, P);
         }
         if (++in_chunk == L) in_chunk = 0;
         const long row = chain * T + ti;
@@ -249,6 +250,14 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
                                                  A.process, A.observation, nullptr, row + 1, col0);
         StepInfo<D, M> si;
         forward_step<D, M>(g, cur, Mc, P, A.floor, si);
+        if (A.rs != nullptr) {
+            const Gains gn = replay_gains(A.rs, A.n, T, L, D, M);
+            gn.u[row * D + own] = si.u_own;
+            if (own == 0) {
+                gn.beta[row] = si.beta;
+                gn.s[row] = si.s;
+            }
+        }
         float y[CPL];
         readout<D, M>(cur, Mc, y);
         store_vec<CPL>(A.out + row * M + col0, y);
@@ -442,9 +451,9 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
                 load_mean_cols<D, M>(bm + ci * D * M, col0, Mc);
                 load_vec<D>(bc + ci * D * D + own * D, P);
             } else if (A.rs != nullptr) {
-                const float *slot = replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j, D, M);
-                load_mean_cols<D, M>(slot, col0, Mc);
-                load_row_packed<D>(slot + D * M, own, P);
+                const long base = replay_state_base(chain, nb, nsub_max - 1, ci, j, replay_state_floats(D, M));
+                rs_get_mean_cols<D, M, CPL>(A.rs, base, col0, Mc);
+                rs_get_row<D, M>(A.rs, base, own, P);
             } else {
                 const float *slot = ws + static_cast<long>(j - 1) * SL::kChain + own * SL::kLane;
                 // written earlier by this kernel: coherent loads, not the read-only path
@@ -750,10 +759,7 @@ inline bool supported(int d, int m) { return m == 8 && (d == 1 || d == 2 || d ==
 
 inline size_t replay_bytes(int d, int m, long n, long t, int chunks) {
     if (n <= 0 || t <= 0 || chunks <= 0) return 0;
-    const long nb = (t + chunks - 1) / chunks;
-    return static_cast<size_t>(n) * static_cast<size_t>(nb) *
-           static_cast<size_t>(replay_slots_per_chunk(t, chunks)) *
-           static_cast<size_t>(replay_state_floats(d, m)) * sizeof(float);
+    return static_cast<size_t>(replay_floats(n, t, chunks, d, m)) * sizeof(float);
 }
 
 // Kernel families.  Three independently written implementations of the same
@@ -779,9 +785,9 @@ inline Family forced_family() {
 }
 
 template <typename TIn>
-Family pick_family(int d, long n, long t, int chunks, bool chain_ok) {
+Family pick_family(int d, long n, long t, int chunks, bool chain_ok, bool forward) {
     const Family f = forced_family();
-    chain_ok = chain_ok && chain_eligible<TIn>(d, n, t, chunks);
+    chain_ok = chain_ok && chain_eligible<TIn>(d, n, t, chunks, forward);
     if (f == kV1) return kV1;
     if (f == kChain && chain_ok) return kChain;
     if (f == kAuto && chain_ok && n >= kChainMinChains) return kChain;
@@ -794,7 +800,7 @@ thread_local int g_last_family = 0;
 
 template <typename TIn>
 int forward_dispatch(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
-    const Family f = pick_family<TIn>(d, a.n, a.t, a.chunks, true);
+    const Family f = pick_family<TIn>(d, a.n, a.t, a.chunks, true, true);
     g_last_family = f;
     if (f == kChain) return chain_forward<TIn>(d, fixed, a, st);
     if (f == kStaged) return staged_forward<TIn>(d, fixed, a, st);
@@ -810,7 +816,7 @@ int forward_dispatch(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
 template <typename TIn>
 int backward_dispatch(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
     const bool chain_ok = a.rs != nullptr || replay_slots_per_chunk(a.t, a.chunks) == 0;
-    const Family f = pick_family<TIn>(d, a.n, a.t, a.chunks, chain_ok);
+    const Family f = pick_family<TIn>(d, a.n, a.t, a.chunks, chain_ok, false);
     g_last_family = (f == kStaged && a.t == 0) ? kV1 : f;
     if (f == kChain) return chain_backward<TIn>(d, fixed, dyn, init, a, st);
     if (f == kStaged && a.t > 0) return staged_backward<TIn>(d, fixed, dyn, init, a, st);

@@ -502,17 +502,28 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
                 ++ckpt;
             } else if (A.rs != nullptr && (t - (ckpt - 1) * L) % kReplaySpan == 0) {
                 if (active) {
-                    float *slot = replay_slot(A.rs, chain, nb, rs_slots, ckpt - 1,
-                                              (t - (ckpt - 1) * L) / kReplaySpan, D, M);
-                    store_mean_cols_g<D, M, CPL>(slot, col0, Mc);
+                    const long base = replay_state_base(chain, nb, rs_slots, ckpt - 1,
+                                                        (t - (ckpt - 1) * L) / kReplaySpan,
+                                                        replay_state_floats(D, M));
+                    rs_put_mean_cols<D, M, CPL>(A.rs, base, col0, Mc);
 #pragma unroll
-                    for (int r = 0; r < RPL; ++r) store_row_packed<D>(slot + D * M, row0 + r, P[r]);
+                    for (int r = 0; r < RPL; ++r) rs_put_row<D, M>(A.rs, base, row0 + r, P[r]);
                 }
             }
             TokPlain<D, M, LPC> tk;
             read_tok_plain<D, M, LPC, FIXED, TIn>(stage, c, tau, sub, tk);
             float u[D], u_own[RPL], e[CPL], beta, s;
             forward_step_plain<D, M, LPC>(g, tk, A.floor, Mc, P, u, u_own, e, beta, s);
+            if (active && A.rs != nullptr) {
+                const Gains gn = replay_gains(A.rs, A.n, T, L, D, M);
+                const long grow = chain * T + t;
+#pragma unroll
+                for (int r = 0; r < RPL; ++r) gn.u[grow * D + row0 + r] = u_own[r];
+                if (sub == 0) {
+                    gn.beta[grow] = beta;
+                    gn.s[grow] = s;
+                }
+            }
             float qv[D];
             lds_vec<D>(reinterpret_cast<const TIn *>(stage + G::oQ + c * G::csK + tau * G::rbK), qv);
             float y[CPL];
@@ -736,13 +747,17 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 #pragma unroll
                 for (int r = 0; r < RPL; ++r) ldg_row<D, LPC>(bc + ci * D * D + (row0 + r) * D, sub, P[r]);
             } else if (have_rs) {
-                const float *slot = replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j, D, M);
-                ldg_mean_cols<D, M, LPC>(slot, col0, sub, Mc);
+                const long base = replay_state_base(chain, nb, nsub_max - 1, ci, j, replay_state_floats(D, M));
+#pragma unroll
+                for (int x = 0; x < D; ++x)
+#pragma unroll
+                    for (int l = 0; l < CPL; ++l)
+                        Mc[l][x] = A.rs[base + static_cast<long>(lane_row<D, LPC>(x, sub) * M + col0 + l) * 32];
 #pragma unroll
                 for (int r = 0; r < RPL; ++r)
 #pragma unroll
                     for (int x = 0; x < D; ++x)
-                        P[r][x] = slot[D * M + tri_index(D, row0 + r, lane_row<D, LPC>(x, sub))];
+                        P[r][x] = A.rs[base + static_cast<long>(D * M + tri_index(D, row0 + r, lane_row<D, LPC>(x, sub))) * 32];
             } else {
                 // written by this kernel in phase A: coherent loads
                 float flat[G::kWsLane];
@@ -756,24 +771,14 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
 #pragma unroll
                     for (int jj = 0; jj < D; ++jj) P[r][jj] = flat[G::hMB + r * D + jj];
             }
-            // the state of the next sub-chunk to be processed: start its fetch now
+            // the boundary checkpoint the next sub-chunk starts from: start its fetch now
             if (active && have_rs) {
-                if (j > 1) {
-                    prefetch_state_l2<LPC>(replay_slot(A.rs, chain, nb, nsub_max - 1, ci, j - 1, D, M),
-                                           replay_state_floats(D, M), sub);
-                } else if (j == 1) {
+                if (j == 1) {
                     prefetch_state_l2<LPC>(bm + ci * D * M, D * M, sub);
                     prefetch_state_l2<LPC>(bc + ci * D * D, D * D, sub);
-                } else if (ci > 0) {
-                    const int len_prev = L;  // chunks before the last are full
-                    const int nsub_prev = (len_prev + kS - 1) / kS;
-                    if (nsub_prev > 1) {
-                        prefetch_state_l2<LPC>(replay_slot(A.rs, chain, nb, nsub_max - 1, ci - 1, nsub_prev - 1, D, M),
-                                               replay_state_floats(D, M), sub);
-                    } else {
-                        prefetch_state_l2<LPC>(bm + (ci - 1) * D * M, D * M, sub);
-                        prefetch_state_l2<LPC>(bc + (ci - 1) * D * D, D * D, sub);
-                    }
+                } else if (j == 0 && ci > 0 && (L + kS - 1) / kS <= 1) {
+                    prefetch_state_l2<LPC>(bm + (ci - 1) * D * M, D * M, sub);
+                    prefetch_state_l2<LPC>(bc + (ci - 1) * D * D, D * D, sub);
                 }
             }
             // replay into history

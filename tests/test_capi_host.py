@@ -72,18 +72,32 @@ def test_null_pointers_rejected_without_gpu(lib):
     assert rc == 1
 
 
+def _gains_floats(n, t, d):
+    """Per-token gains after the states: u [N,T,D], beta [N,T], s [N,T], each
+    part padded to 4 floats."""
+    r4 = lambda x: (x + 3) // 4 * 4
+    return r4(n * t * d) + 2 * r4(n * t)
+
+
+def _group_chains(n):
+    """States are stored per group of 32 chains (structure of arrays)."""
+    return (n + 31) // 32 * 32
+
+
 def test_replay_states_size_formula(lib):
-    # chunks <= 4: nothing between boundary checkpoints to save
-    assert lib.bssm_replay_states_bytes(8, 8, 100, 512, 4) == 0
+    # chunks <= 4: no state between boundary checkpoints, only the gains
+    assert lib.bssm_replay_states_bytes(8, 8, 100, 512, 4) == _gains_floats(100, 512, 8) * 4
     # D8M8, chunk 64: 15 states per chunk, 8 chunks; 64 mean + 36 packed
     # covariance floats each
-    assert lib.bssm_replay_states_bytes(8, 8, 10, 512, 64) == 10 * 8 * 15 * (64 + 36) * 4
+    assert lib.bssm_replay_states_bytes(8, 8, 64, 512, 64) == (64 * 8 * 15 * (64 + 36) + _gains_floats(64, 512, 8)) * 4
+    # a partial group of chains is padded to 32
+    assert lib.bssm_replay_states_bytes(8, 8, 10, 512, 64) == (32 * 8 * 15 * 100 + _gains_floats(10, 512, 8)) * 4
     # D4M8: 32 + 10 floats, padded to 44
-    assert lib.bssm_replay_states_bytes(4, 8, 2, 64, 64) == 2 * 1 * 15 * 44 * 4
+    assert lib.bssm_replay_states_bytes(4, 8, 2, 64, 64) == (_group_chains(2) * 1 * 15 * 44 + _gains_floats(2, 64, 4)) * 4
     # partial last chunk: slots are sized by the full chunk length; D2: 16 + 3 -> 20
-    assert lib.bssm_replay_states_bytes(2, 8, 3, 70, 32) == 3 * 3 * 7 * 20 * 4
-    # D1: 8 + 1 floats per state, padded to 12 so every slot is 16-byte aligned
-    assert lib.bssm_replay_states_bytes(1, 8, 5, 64, 64) == 5 * 1 * 15 * 12 * 4
+    assert lib.bssm_replay_states_bytes(2, 8, 3, 70, 32) == (_group_chains(3) * 3 * 7 * 20 + _gains_floats(3, 70, 2)) * 4
+    # D1: 8 + 1 floats per state, padded to 12
+    assert lib.bssm_replay_states_bytes(1, 8, 5, 64, 64) == (_group_chains(5) * 1 * 15 * 12 + _gains_floats(5, 64, 1)) * 4
 
 
 def test_workspace_size_formula(lib):
