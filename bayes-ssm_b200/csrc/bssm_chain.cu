@@ -48,6 +48,8 @@ namespace chain {
 constexpr int kS = kReplaySpan;  // tokens per tile = replay sub-chunk
 constexpr int kWarps = 4;        // one warp per TMEM lane quarter
 constexpr int kThreads = 32 * kWarps;
+constexpr int kSplitWarps = 8;  // two warps per chain group
+constexpr int kSplitThreads = 32 * kSplitWarps;
 constexpr int kSmemMax = 227 * 1024;
 
 constexpr int al128(int x) { return (x + 127) / 128 * 128; }
@@ -81,6 +83,9 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 __device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, int bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
@@ -510,6 +515,266 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
         store_cov_full<D>(bc + nb * D * D, P);
         store_mean<D, M>(A.mean_final + chain * D * M, Mm);
         store_cov_full<D>(A.cov_final + chain * D * D, P);
+    }
+    if (lane == 0) bulk_wait_all();
+}
+
+// ===========================================================================
+// Forward with two warps per chain group (D = M = 8)
+//
+// Group g's covariance warp (warp g) runs the covariance recursion -- P, u,
+// s, beta -- and writes the gains of each tile into a double-buffered
+// shared-memory block; the mean warp (warp g + 4) reads them there and runs
+// the mean recursion and the readout, one tile behind.  Both warps store
+// their half of each replay state directly (structure-of-arrays rows), the
+// covariance warp stores the gains (TMA), the mean warp the readout (TMA,
+// staged in the tile's own decay slots once they are dead).
+// ===========================================================================
+template <int D, int M, bool FIXED, typename TIn>
+struct FSplitGeo {
+    using Tl = Tile<D, M, FIXED, false, TIn>;
+    static constexpr bool kInPlaceY = !FIXED && D == M;  // readout rows fit the decay slots
+    static constexpr int gU = 0, gB = kS * 32 * D * 4, gS = gB + 32 * kS * 4;
+    static constexpr int kGB = gS + 32 * kS * 4;           // one gains block
+    static constexpr int kYB = kInPlaceY ? 0 : kS * 32 * M * 4;
+    static constexpr int kPerStage = 4 * Tl::kBytes;
+    static constexpr int kBars = 2 * 4 + 4;                // full[4] empty[4] gfull[2] gfree[2]
+    static constexpr int kFixed = 4 * (2 * kGB + kYB) + 4 * kBars * 8 + 256;
+    static constexpr int kFit = (kSmemMax - kFixed) / kPerStage;
+    static constexpr int kStages = kFit < 4 ? kFit : 4;
+    static constexpr bool kFits = kStages >= 3;
+    static constexpr int oT = 0;                                      // [stage][group][tile]
+    static constexpr int oG = kStages * kPerStage;                    // [group][2][kGB]
+    static constexpr int oY = oG + 4 * 2 * kGB;                       // [group][kYB]
+    static constexpr int oBar = al128(oY + 4 * kYB);                  // [group][kBars]
+    static constexpr int kSmem = oBar + 4 * kBars * 8 + 128;
+};
+
+template <int D, int M, bool FIXED, typename TIn>
+__global__ void __launch_bounds__(kSplitThreads, 1)
+    forward_split(const FwdArgs<TIn> A, const __grid_constant__ FwdMaps mp) {
+    using G = FSplitGeo<D, M, FIXED, TIn>;
+    using Tl = typename G::Tl;
+    constexpr int NS = G::kStages, TRI = tri_size(D), SF = replay_state_floats(D, M);
+    extern __shared__ __align__(128) char smem_raw[];
+    char *const smem = smem_base(smem_raw);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int grp = warp & 3;
+    const bool cov_warp = warp < 4;
+    const int chain0 = static_cast<int>(blockIdx.x) * 128 + grp * 32;
+    const long chain = chain0 + lane;
+    const bool active = chain < A.n;
+    const long T = A.t;
+    const int L = A.chunks;
+    const long nb = (T + L - 1) / L;
+    const long rs_slots = replay_slots_per_chunk(T, L);
+    char *const tiles = smem + G::oT + grp * Tl::kBytes;  // + stage * G::kPerStage
+    char *const gbuf = smem + G::oG + grp * 2 * G::kGB;   // + b * G::kGB
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + grp * G::kBars;
+    uint64_t *const full = bars, *const empty = bars + 4, *const gfull = bars + 8, *const gfree = bars + 10;
+    float *const bm = A.bmean + chain * (nb + 1) * D * M;
+    float *const bc = A.bcov + chain * (nb + 1) * D * D;
+    const bool gains_out = A.rs != nullptr;
+
+    if (cov_warp && lane == 0) {
+        for (int x = 0; x < 4; ++x) {
+            mbar_init(full + x, 1);
+            mbar_init(empty + x, 2);
+        }
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(gfull + x, 32);
+            mbar_init(gfree + x, 32);
+        }
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    FwdItems cons;
+    cons.init(T, L);
+    if (cov_warp) {
+        // ------------------------------------------------------------------
+        // covariance warp; its lane 0 also issues the tiles
+        // ------------------------------------------------------------------
+        float P[TRI];
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+#pragma unroll
+            for (int j = i; j < D; ++j) P[tri_index(D, i, j)] = (i == j) ? 1.f : 0.f;
+        if (active && A.cov0 != nullptr) {
+            const float *c0 = A.cov0 + chain * D * D;
+#pragma unroll
+            for (int i = 0; i < D; ++i)
+#pragma unroll
+                for (int j = i; j < D; ++j) P[tri_index(D, i, j)] = 0.5f * (c0[i * D + j] + c0[j * D + i]);
+        }
+        // tiles run NS - 2 ahead: the stage a new tile goes to held the tile
+        // two before the current one, which the mean warp released
+        FwdItems prod = cons;
+        if (lane == 0) {
+            for (int s = 0; s < NS - 2 && !prod.done; ++s) {
+                issue_tile<D, M, FIXED, false, TIn>(tiles + s * G::kPerStage, mp, chain0, static_cast<int>(prod.t0()),
+                                                    false, full + s, 0);
+                prod.advance();
+            }
+        } else {
+            for (int s = 0; s < NS - 2 && !prod.done; ++s) prod.advance();
+        }
+        long q = 0;
+        while (!cons.done) {
+            if (!prod.done) {
+                const long nq = q + NS - 2;
+                if (lane == 0) {
+                    if (nq >= NS) mbar_wait(empty + nq % NS, static_cast<uint32_t>(((nq - NS) / NS) & 1));
+                    issue_tile<D, M, FIXED, false, TIn>(tiles + (nq % NS) * G::kPerStage, mp, chain0,
+                                                        static_cast<int>(prod.t0()), false, full + nq % NS, 0);
+                }
+                prod.advance();
+            }
+            mbar_wait(full + q % NS, static_cast<uint32_t>((q / NS) & 1));
+            const TileRead<D, M, FIXED, false, TIn> rd{tiles + (q % NS) * G::kPerStage, lane};
+            const long ci = cons.ci;
+            const int t0 = static_cast<int>(cons.t0());
+            if (active) {
+                if (cons.j == 0) {
+                    store_cov_full<D>(bc + ci * D * D, P);
+                } else if (A.rs != nullptr) {
+                    const long base = replay_state_base(chain, nb, rs_slots, ci, cons.j, SF);
+#pragma unroll
+                    for (int t = 0; t < TRI; ++t) A.rs[base + static_cast<long>(D * M + t) * 32] = P[t];
+                }
+            }
+            // gains block q & 1: free once the mean warp read tile q-2's gains
+            // and this warp's store of them read its source
+            const int b = static_cast<int>(q & 1);
+            char *const gb = gbuf + b * G::kGB;
+            if (q >= 2) mbar_wait(gfree + b, static_cast<uint32_t>(((q - 2) >> 1) & 1));
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+            float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = b4;
+            rd.noise(p4, r4);
+#pragma unroll 1
+            for (int tau = 0; tau < kS; ++tau) {
+                float k[D], a[D], u[D], beta, s;
+                rd.keys(tau, k);
+                rd.decay(tau, a);
+                cov_step<D>(P, k, a, sel4v(p4, tau), sel4v(r4, tau), A.floor, u, beta, s);
+                sts_vec<D>(reinterpret_cast<float *>(gb + G::gU) + (tau * 32 + lane) * D, u);
+                b4.x = tau == 0 ? beta : b4.x;
+                b4.y = tau == 1 ? beta : b4.y;
+                b4.z = tau == 2 ? beta : b4.z;
+                b4.w = tau == 3 ? beta : b4.w;
+                s4.x = tau == 0 ? s : s4.x;
+                s4.y = tau == 1 ? s : s4.y;
+                s4.z = tau == 2 ? s : s4.z;
+                s4.w = tau == 3 ? s : s4.w;
+            }
+            reinterpret_cast<float4 *>(gb + G::gB)[lane] = b4;
+            reinterpret_cast<float4 *>(gb + G::gS)[lane] = s4;
+            fence_proxy_async();
+            mbar_arrive(gfull + b);
+            __syncwarp();
+            if (lane == 0) {
+                if (gains_out && chain0 < A.n) {
+                    tma_store_3d(&mp.gu, 0, chain0, t0, gb + G::gU);
+                    tma_store_2d(&mp.gb, t0, chain0, gb + G::gB);
+                    tma_store_2d(&mp.gs, t0, chain0, gb + G::gS);
+                }
+                bulk_commit();
+                mbar_arrive(empty + q % NS);  // this warp is done with the tile
+            }
+            cons.advance();
+            ++q;
+        }
+        if (active) {
+            store_cov_full<D>(bc + nb * D * D, P);
+            store_cov_full<D>(A.cov_final + chain * D * D, P);
+        }
+    } else {
+        // ------------------------------------------------------------------
+        // mean warp
+        // ------------------------------------------------------------------
+        float Mm[D][M];
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+#pragma unroll
+            for (int c = 0; c < M; ++c) Mm[i][c] = 0.f;
+        if (active && A.mean0 != nullptr) {
+#pragma unroll
+            for (int i = 0; i < D; ++i) load_vec<M>(A.mean0 + chain * D * M + i * M, Mm[i]);
+        }
+        char *const ysep = smem + G::oY + grp * G::kYB;
+        long q = 0;
+        while (!cons.done) {
+            if constexpr (G::kInPlaceY) {
+                // the previous tile's readout store has read its decay slots:
+                // release that stage before waiting for this tile
+                if (lane == 0 && q >= 1) {
+                    bulk_wait_read<0>();
+                    mbar_arrive(empty + (q - 1) % NS);
+                }
+            }
+            mbar_wait(full + q % NS, static_cast<uint32_t>((q / NS) & 1));
+            const int b = static_cast<int>(q & 1);
+            mbar_wait(gfull + b, static_cast<uint32_t>((q >> 1) & 1));
+            char *const tile = tiles + (q % NS) * G::kPerStage;
+            const TileRead<D, M, FIXED, false, TIn> rd{tile, lane};
+            const char *const gb = gbuf + b * G::kGB;
+            const long ci = cons.ci;
+            const int t0 = static_cast<int>(cons.t0());
+            if (active) {
+                if (cons.j == 0) {
+                    store_mean<D, M>(bm + ci * D * M, Mm);
+                } else if (A.rs != nullptr) {
+                    const long base = replay_state_base(chain, nb, rs_slots, ci, cons.j, SF);
+#pragma unroll
+                    for (int i = 0; i < D; ++i)
+#pragma unroll
+                        for (int c = 0; c < M; ++c) A.rs[base + static_cast<long>(i * M + c) * 32] = Mm[i][c];
+                }
+            }
+            float *yb;
+            if constexpr (G::kInPlaceY) {
+                yb = reinterpret_cast<float *>(tile + Tl::oA);  // decay rows die token by token
+            } else {
+                yb = reinterpret_cast<float *>(ysep);
+                if (lane == 0) bulk_wait_read<0>();  // the previous readout store
+                __syncwarp();
+            }
+            const float4 b4 = reinterpret_cast<const float4 *>(gb + G::gB)[lane];
+#pragma unroll 1
+            for (int tau = 0; tau < kS; ++tau) {
+                float k[D], a[D], v[M], qv[D], u[D], e[M];
+                rd.keys(tau, k);
+                rd.decay(tau, a);
+                rd.values(tau, v);
+                lds_vec<D>(reinterpret_cast<const float *>(gb + G::gU) + (tau * 32 + lane) * D, u);
+                mean_step<D, M>(Mm, k, a, v, u, sel4v(b4, tau), e);
+                rd.queries(tau, qv);
+                float y[M];
+#pragma unroll
+                for (int c = 0; c < M; ++c) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int i = 0; i < D; ++i) acc = fmaf(Mm[i][c], qv[i], acc);
+                    y[c] = acc;
+                }
+                sts_vec<M>(yb + (tau * 32 + lane) * M, y);
+            }
+            mbar_arrive(gfree + b);  // done with this gains block
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                if (chain0 < A.n) tma_store_3d(&mp.y, 0, chain0, t0, yb);
+                bulk_commit();
+                if constexpr (!G::kInPlaceY) mbar_arrive(empty + q % NS);
+            }
+            cons.advance();
+            ++q;
+        }
+        if (active) {
+            store_mean<D, M>(bm + nb * D * M, Mm);
+            store_mean<D, M>(A.mean_final + chain * D * M, Mm);
+        }
     }
     if (lane == 0) bulk_wait_all();
 }
@@ -1099,8 +1364,6 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
 // those inputs are dead (gk in keys, gv in queries, gq in values, ga in
 // decay, gp in process, gr in observation) and leave by TMA stores.
 // ===========================================================================
-constexpr int kSplitWarps = 8;
-constexpr int kSplitThreads = 32 * kSplitWarps;
 constexpr int kXSlots = 3;
 
 // TMEM columns of one lane in the two-warp backward.
@@ -1160,10 +1423,6 @@ struct SplitGeo {
     static constexpr int kSmem = oSlot + 16 + 128;
     static constexpr bool kFits = kSmem <= kSmemMax;
 };
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 // The covariance update of one token from its saved gain: P' = A P A + p I
 // - beta u u^T (the arithmetic of cov_step).
@@ -1793,6 +2052,33 @@ inline bool split_allowed() {
     return e == nullptr || std::strcmp(e, "chain1") != 0;
 }
 
+template <int D, int M, bool FIXED, typename TIn>
+int launch_fwd_split(const FwdArgs<TIn> &a, cudaStream_t st) {
+    using G = FSplitGeo<D, M, FIXED, TIn>;
+    auto k = forward_split<D, M, FIXED, TIn>;
+    static bool attr = [&] {
+        return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem) == cudaSuccess;
+    }();
+    if (!attr) return fail(BSSM_ERR_CUDA, "forward_split: shared-memory attribute refused");
+    if (a.out == nullptr) return fail(BSSM_ERR_INVALID, "forward_split: null output");
+    FwdMaps mp;
+    std::memset(&mp, 0, sizeof(mp));
+    bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
+              map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.y, a.out, M, a.n, a.t);
+    if (!FIXED)
+        ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
+             map_rows(&mp.r, a.observation, a.t, a.n, kS);
+    if (a.rs != nullptr) {
+        const Gains gn = replay_gains(a.rs, a.n, a.t, a.chunks, D, M);
+        ok = ok && map_tok(&mp.gu, static_cast<const float *>(gn.u), D, a.n, a.t) &&
+             map_rows(&mp.gb, gn.beta, a.t, a.n, kS) && map_rows(&mp.gs, gn.s, a.t, a.n, kS);
+    }
+    if (!ok) return fail(BSSM_ERR_CUDA, "forward_split: tensor-map encoding failed");
+    const long grid = (a.n + 127) / 128;
+    k<<<static_cast<unsigned>(grid), kSplitThreads, G::kSmem, st>>>(a, mp);
+    return check_launch("forward_split");
+}
+
 template <int D, typename TIn>
 constexpr bool fwd_fits() {
     if constexpr ((D * static_cast<int>(sizeof(TIn))) % 16 != 0) {
@@ -1807,6 +2093,12 @@ int fwd_d(int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
     if constexpr (!fwd_fits<D, TIn>()) {
         return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain forward: shape does not fit");
     } else {
+        if constexpr (D == 8) {
+            if constexpr (FSplitGeo<D, 8, false, TIn>::kFits && FSplitGeo<D, 8, true, TIn>::kFits) {
+                if (split_allowed())
+                    return fixed ? launch_fwd_split<D, 8, true, TIn>(a, st) : launch_fwd_split<D, 8, false, TIn>(a, st);
+            }
+        }
         return fixed ? launch_fwd<D, 8, true, TIn>(a, st) : launch_fwd<D, 8, false, TIn>(a, st);
     }
 }

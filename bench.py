@@ -54,11 +54,14 @@ BWD_FLOPS = (FWD_FLOPS - 2 * D * M) + (18 * D * D + 22 * D * M + 10 * D + M)
 # FP32 non-tensor peak: no measured figure exists on this pool, so the nominal
 # 148 SMs x 128 FP32 lanes x 2 flop x 1965 MHz is used and labelled as such.
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
-# DRAM traffic per backward launch (dram__bytes_read.sum + dram__bytes_write.sum)
-# from one ncu capture of the half-size case (8,192 chains, one full wave at
-# the same per-SM occupancy), scaled by chains to the 16,384-chain launch: every
-# chain moves the same bytes.  See profiles/backward_staged_d8m8_bf16.md.
-NCU_BWD_TRAFFIC_BYTES = 2 * (1043.770e6 + 348.490e6)
+# DRAM traffic of one backward launch (dram__bytes_read.sum +
+# dram__bytes_write.sum) from an ncu capture of this exact workload (16,384
+# chains, one launch).  See profiles/backward_split_d8m8_bf16.md.
+NCU_BWD_TRAFFIC_BYTES = 2.2057e9 + 0.7196e9
+# Canonical algorithmic figures per chain-step, FP32 at the reference ABI
+# (fwd + bwd): bytes 4 (9D + 5M + 6), flops 26D^2 + 34DM + 30D + 3M + 2.
+STEP_BYTES_F32 = 4 * (9 * D + 5 * M + 6)
+STEP_FLOPS = 26 * D * D + 34 * D * M + 30 * D + 3 * M + 2
 
 
 def _peaks():
@@ -70,9 +73,13 @@ def _peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons while the timed loop runs."""
+    """Samples nvidia-smi clocks and throttle reasons from before the warm-up
+    to after the timed loop; summary() keeps the samples stamped inside the
+    timed region (mark_start / mark_end), or, when that region is shorter than
+    the sampling interval, the nearest sample on each side of it (and says so).
+    """
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -80,17 +87,28 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.file = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
+            deadline = time.time() + 5.0  # wait for the first sample
+            while time.time() < deadline and os.path.getsize(self.file.name) == 0:
+                time.sleep(0.02)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+        time.sleep(0.12)  # let the sample after the region land
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -101,31 +119,41 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        if self.file is None:
+        from datetime import datetime
+
+        if self.file is None or self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()
         rows = []
         for line in Path(self.file.name).read_text().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
-                                 hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append(dict(t=ts, sm=float(parts[2]), smax=float(parts[3]), power=float(parts[4]),
+                                 hw=parts[6], hwt=parts[7], swt=parts[8], pcap=parts[9]))
             except ValueError:
                 continue
         os.unlink(self.file.name)
-        if not rows:
+        window = "timed region"
+        sel = [r for r in rows if self.t0 is not None and self.t0 <= r["t"] <= self.t1]
+        if not sel and rows and self.t0 is not None:
+            before = [r for r in rows if r["t"] < self.t0]
+            after = [r for r in rows if r["t"] > self.t1]
+            sel = ([before[-1]] if before else []) + ([after[0]] if after else [])
+            window = "nearest samples (timed region shorter than the 50 ms sampling interval)"
+        if not sel:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         reasons = []
         for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
                           ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
-            if any(r[key].lower() == "active" for r in rows):
+            if any(r[key].lower() == "active" for r in sel):
                 reasons.append(name)
-        return {"sm_mhz": statistics.median(r["sm"] for r in rows),
-                "sm_max_mhz": max(r["smax"] for r in rows),
-                "power_w_max": max(r["power"] for r in rows),
-                "samples": len(rows), "reasons": reasons}
+        return {"sm_mhz": statistics.median(r["sm"] for r in sel),
+                "sm_max_mhz": max(r["smax"] for r in sel),
+                "power_w_max": max(r["power"] for r in sel),
+                "samples": len(sel), "window": window, "reasons": reasons}
 
 
 def make_inputs(n: int, seed: int, device):
@@ -221,14 +249,14 @@ def workload_config(n_gpus: int, chains: int = N_CHAINS) -> dict:
             "chains_per_gpu": chains, "global_batch": chains // H * n_gpus, "seq_len": T,
             "io_dtype": "bf16 k/q/v, fp32 decay/noise/state",
             "gradients": "k, v, q, decay, process, observation (readout-only loss)",
-            "l2": "inputs larger than L2 (~0.74 GB read per step)",
+            "l2": "inputs and replay buffer larger than L2 (~5 GB moved per step)",
             "parallelism": f"dp{n_gpus} (chains sharded, no data-path collective)"}
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
@@ -291,16 +319,17 @@ def main() -> None:
                                gq, gd, gp, gr, None, None, None, 0, n, T, CHUNK, FLOOR, sp,
                                replay_states=rs)
 
-    for _ in range(args.warmup):
-        fwd()
-        bwd()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        for _ in range(args.warmup):
+            fwd()
+            bwd()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clocks.mark_start()
         start.record(stream)
         for i in range(args.steps):
             ev[i][0].record(stream)
@@ -310,6 +339,7 @@ def main() -> None:
             ev[i][2].record(stream)
         stop.record(stream)
         torch.cuda.synchronize()
+        clocks.mark_end()
     if world > 1:
         dist.barrier()
     total_ms = start.elapsed_time(stop)
@@ -337,8 +367,10 @@ def main() -> None:
         fwd_gbs = chain_steps * FWD_BYTES / (fwd_ms / 1e3) / 1e9
         fwd_tflops = chain_steps * FWD_FLOPS / (fwd_ms / 1e3) / 1e12
         traffic = NCU_BWD_TRAFFIC_BYTES if n == N_CHAINS else None
+        step_tflops = chain_steps * STEP_FLOPS / (step_ms / 1e3) / 1e12
+        step_gbs = chain_steps * (FWD_BYTES + BWD_BYTES) / (step_ms / 1e3) / 1e9
         roofline = {
-            "kernel": "backward_staged<8,8,4,0,1,0,bf16> (dominant: replay backward)",
+            "kernel": "backward_split<8,8,1,0,bf16> (dominant: two-warp replay backward)",
             "bound": "hbm", "achieved": round(bwd_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(bwd_gbs / hbm_peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
             "traffic": traffic,
@@ -350,6 +382,12 @@ def main() -> None:
                                "TFLOP/s": round(fwd_tflops, 2)},
             "backward_kernel": {"ms": round(bwd_ms, 4), "GB/s": round(bwd_gbs, 1),
                                 "TFLOP/s": round(bwd_tflops, 2)},
+            # the whole step (forward + backward) against both bounds; FP32 binds
+            "step": {"TFLOP/s": round(step_tflops, 2),
+                     "fp32_frac": round(step_tflops / FP32_NOMINAL_TFLOPS, 4),
+                     "GB/s": round(step_gbs, 1), "hbm_frac": round(step_gbs / hbm_peak, 4),
+                     "flops_per_chain_step": STEP_FLOPS,
+                     "bytes_per_chain_step_bf16_io": FWD_BYTES + BWD_BYTES},
         }
         cpu = None
         if world == 1 and not args.no_cpu:

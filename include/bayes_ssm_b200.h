@@ -61,10 +61,12 @@ int bssm_version(void);
  * backward replays from.  fixed != 0 ignores decay/process/observation (may
  * be NULL) and uses A = 0.97 I, Q = 0.1 I, R = 1.  mean0 == NULL means zeros,
  * cov0 == NULL means identity.  The covariance enters as (cov0 + cov0^T)/2.
- * replay_states (optional, may be NULL): when given, the forward also saves
- * the state at every 4-token boundary inside each chunk
- * (bssm_replay_states_bytes(...) bytes); a backward given the same buffer
- * skips recomputing them.
+ * replay_states (optional, may be NULL): the replay buffer,
+ * bssm_replay_states_bytes(...) bytes.  When given, the forward also saves
+ * the state at every 4-token boundary inside each chunk and every token's
+ * gain u, 1/s and s; a backward given the same buffer replays from them
+ * instead of recomputing the chunk (and its thread-per-chain form replays
+ * the mean from the saved gains).  The layout is internal to the library.
  * Replaces forward_chunked / forward_chunked_fixed,
  * bayes_ssm/persistent_bayes_chunked_d8.cu:530-548.
  */
