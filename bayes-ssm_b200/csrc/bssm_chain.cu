@@ -150,10 +150,10 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // (kS tokens, 32 chains); the replay-state map (float, chain) with a box of
 // (one state, 32 chains).
 struct FwdMaps {
-    CUtensorMap k, q, v, a, p, r, y, rs, gu, gb, gs;
+    CUtensorMap k, q, v, a, p, r, y, gu, gb;  // gu, gb: gains and signed gain scales
 };
 struct BwdMaps {
-    CUtensorMap k, q, v, a, p, r, gy, rs, gk, gv, gq, ga, gp, gr, gu, gb, gs;
+    CUtensorMap k, q, v, a, p, r, gy, rs, gk, gv, gq, ga, gp, gr, gu, gb;
 };
 
 // Shared-memory geometry of one warp's tile (one stage), box layouts.
@@ -334,8 +334,8 @@ struct FwdGeo {
     static constexpr int SF = replay_state_floats(D, M);
     // a warp's outputs of one tile, box layouts: readout [tau][chain][M],
     // gains [tau][chain][D], beta and s [chain][tau]
-    static constexpr int yY = 0, yU = kS * 32 * M * 4, yB = yU + kS * 32 * D * 4, yS = yB + 32 * kS * 4;
-    static constexpr int kYB = yS + 32 * kS * 4;
+    static constexpr int yY = 0, yU = kS * 32 * M * 4, yB = yU + kS * 32 * D * 4;
+    static constexpr int kYB = yB + 32 * kS * 4;
     static constexpr int kPerStage = kWarps * Tl::kBytes;
     static constexpr int kFixed = kWarps * kYB + 128 + kWarps * 4 * 8;
     static constexpr int kFit = (kSmemMax - kFixed) / kPerStage;
@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
         }
         float *const yb = reinterpret_cast<float *>(ob + G::yY);
         const bool gains = A.rs != nullptr;
-        float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = b4;
+        float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f);
         rd.noise(p4, r4);
         auto step = [&](int tau) {
             float k[D], a[D], v[M], qv[D];
@@ -478,22 +478,16 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
             sts_vec<M>(yb + (tau * 32 + lane) * M, y);
             if (gains) {
                 sts_vec<D>(reinterpret_cast<float *>(ob + G::yU) + (tau * 32 + lane) * D, u);
-                b4.x = tau == 0 ? beta : b4.x;
-                b4.y = tau == 1 ? beta : b4.y;
-                b4.z = tau == 2 ? beta : b4.z;
-                b4.w = tau == 3 ? beta : b4.w;
-                s4.x = tau == 0 ? s : s4.x;
-                s4.y = tau == 1 ? s : s4.y;
-                s4.z = tau == 2 ? s : s4.z;
-                s4.w = tau == 3 ? s : s4.w;
+                const float bt = signed_gain_scale(beta, s, A.floor);
+                b4.x = tau == 0 ? bt : b4.x;
+                b4.y = tau == 1 ? bt : b4.y;
+                b4.z = tau == 2 ? bt : b4.z;
+                b4.w = tau == 3 ? bt : b4.w;
             }
         };
 #pragma unroll 1
         for (int tau = 0; tau < kS; ++tau) step(tau);
-        if (gains) {
-            reinterpret_cast<float4 *>(ob + G::yB)[lane] = b4;
-            reinterpret_cast<float4 *>(ob + G::yS)[lane] = s4;
-        }
+        if (gains) reinterpret_cast<float4 *>(ob + G::yB)[lane] = b4;
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
@@ -502,7 +496,6 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
                 if (gains) {
                     tma_store_3d(&mp.gu, 0, chain0, t0, ob + G::yU);
                     tma_store_2d(&mp.gb, t0, chain0, ob + G::yB);
-                    tma_store_2d(&mp.gs, t0, chain0, ob + G::yS);
                 }
             }
             bulk_commit();
@@ -534,8 +527,8 @@ template <int D, int M, bool FIXED, typename TIn>
 struct FSplitGeo {
     using Tl = Tile<D, M, FIXED, false, TIn>;
     static constexpr bool kInPlaceY = !FIXED && D == M;  // readout rows fit the decay slots
-    static constexpr int gU = 0, gB = kS * 32 * D * 4, gS = gB + 32 * kS * 4;
-    static constexpr int kGB = gS + 32 * kS * 4;           // one gains block
+    static constexpr int gU = 0, gB = kS * 32 * D * 4;
+    static constexpr int kGB = gB + 32 * kS * 4;           // one gains block: u, signed scale
     static constexpr int kYB = kInPlaceY ? 0 : kS * 32 * M * 4;
     static constexpr int kPerStage = 4 * Tl::kBytes;
     static constexpr int kBars = 2 * 4 + 4;                // full[4] empty[4] gfull[2] gfree[2]
@@ -650,7 +643,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             if (q >= 2) mbar_wait(gfree + b, static_cast<uint32_t>(((q - 2) >> 1) & 1));
             if (lane == 0) bulk_wait_read<1>();
             __syncwarp();
-            float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = b4;
+            float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f);
             rd.noise(p4, r4);
 #pragma unroll 1
             for (int tau = 0; tau < kS; ++tau) {
@@ -659,17 +652,13 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.decay(tau, a);
                 cov_step<D>(P, k, a, sel4v(p4, tau), sel4v(r4, tau), A.floor, u, beta, s);
                 sts_vec<D>(reinterpret_cast<float *>(gb + G::gU) + (tau * 32 + lane) * D, u);
-                b4.x = tau == 0 ? beta : b4.x;
-                b4.y = tau == 1 ? beta : b4.y;
-                b4.z = tau == 2 ? beta : b4.z;
-                b4.w = tau == 3 ? beta : b4.w;
-                s4.x = tau == 0 ? s : s4.x;
-                s4.y = tau == 1 ? s : s4.y;
-                s4.z = tau == 2 ? s : s4.z;
-                s4.w = tau == 3 ? s : s4.w;
+                const float bt = signed_gain_scale(beta, s, A.floor);
+                b4.x = tau == 0 ? bt : b4.x;
+                b4.y = tau == 1 ? bt : b4.y;
+                b4.z = tau == 2 ? bt : b4.z;
+                b4.w = tau == 3 ? bt : b4.w;
             }
             reinterpret_cast<float4 *>(gb + G::gB)[lane] = b4;
-            reinterpret_cast<float4 *>(gb + G::gS)[lane] = s4;
             fence_proxy_async();
             mbar_arrive(gfull + b);
             __syncwarp();
@@ -677,7 +666,6 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 if (gains_out && chain0 < A.n) {
                     tma_store_3d(&mp.gu, 0, chain0, t0, gb + G::gU);
                     tma_store_2d(&mp.gb, t0, chain0, gb + G::gB);
-                    tma_store_2d(&mp.gs, t0, chain0, gb + G::gS);
                 }
                 bulk_commit();
                 mbar_arrive(empty + q % NS);  // this warp is done with the tile
@@ -748,7 +736,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.decay(tau, a);
                 rd.values(tau, v);
                 lds_vec<D>(reinterpret_cast<const float *>(gb + G::gU) + (tau * 32 + lane) * D, u);
-                mean_step<D, M>(Mm, k, a, v, u, sel4v(b4, tau), e);
+                mean_step<D, M>(Mm, k, a, v, u, fabsf(sel4v(b4, tau)), e);
                 rd.queries(tau, qv);
                 float y[M];
 #pragma unroll
@@ -1408,11 +1396,11 @@ struct SplitGeo {
     using Tl = Tile<D, M, false, true, TIn>;
     static_assert(D == M, "in-place gradient staging needs D == M");
     static constexpr int SF = replay_state_floats(D, M);
-    // per group and stage: the token tile, then the gains [tau][chain][D],
-    // beta and s [chain][tau]
-    static constexpr int oU = Tl::kBytes, oB = oU + kS * 32 * D * 4, oS = oB + 32 * kS * 4;
-    static constexpr int kTileBytes = al128(oS + 32 * kS * 4);
-    static constexpr int kTx = Tl::kTx + kS * 32 * D * 4 + 2 * 32 * kS * 4;  // without gy, without state
+    // per group and stage: the token tile, then the gains [tau][chain][D]
+    // and the signed gain scales [chain][tau]
+    static constexpr int oU = Tl::kBytes, oB = oU + kS * 32 * D * 4;
+    static constexpr int kTileBytes = al128(oB + 32 * kS * 4);
+    static constexpr int kTx = Tl::kTx + kS * 32 * D * 4 + 32 * kS * 4;  // without gy, without state
     static constexpr int kSB = 32 * SF * 4;  // a group's start states [chain][SF]
     static constexpr int kPerStage = 4 * kTileBytes;
     static constexpr int oT = 0;                        // [stage][group][tile]
@@ -1510,7 +1498,6 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         if (has_gy) tma_load_3d(t + Tl::oG, &mp.gy, 0, chain0, t0, full + stage);
         tma_load_3d(t + G::oU, &mp.gu, 0, chain0, t0, full + stage);
         tma_load_2d(t + G::oB, &mp.gb, t0, chain0, full + stage);
-        tma_load_2d(t + G::oS, &mp.gs, t0, chain0, full + stage);
         if (saved) tma_load_2d(sbox, &mp.rs, 0, state_row(chain0, nb, rs_slots, it.ci, it.j, SF), full + stage);
     };
     auto issue_checkpoint_part = [&](const BwdItems &it) {
@@ -1568,7 +1555,6 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             float4 p4, r4;
             rd.noise(p4, r4);
             const float4 b4 = reinterpret_cast<const float4 *>(tile + G::oB)[lane];
-            const float4 s4 = reinterpret_cast<const float4 *>(tile + G::oS)[lane];
             float P[TRI];
 #pragma unroll
             for (int t = 0; t < TRI; ++t) P[t] = state[(D * M + t) * 32];
@@ -1593,7 +1579,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.decay(tau, a);
                 gains(tile, tau, u);
                 put<TL, kSPp, TRI>(tb, tau, P);
-                cov_update<D>(P, a, sel4v(p4, tau), u, sel4v(b4, tau));
+                cov_update<D>(P, a, sel4v(p4, tau), u, fabsf(sel4v(b4, tau)));
             }
             tmem::wait_st();
             // reverse: covariance adjoint
@@ -1611,7 +1597,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.keys(tau, k);
                 rd.decay(tau, a);
                 gains(tile, tau, u);
-                const float p = sel4v(p4, tau), beta = sel4v(b4, tau), s = sel4v(s4, tau);
+                const float p = sel4v(p4, tau), bt = sel4v(b4, tau), beta = fabsf(bt);
                 float gb = xv[3 * D];
                 float Ru[D], trR = 0.f;
 #pragma unroll
@@ -1623,7 +1609,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                     gb = fmaf(-u[i], acc, gb);
                     if constexpr (NEED_DYN) trR += Rp[tri_index(D, i, i)];
                 }
-                const float gs = (s >= floor_) ? -beta * beta * gb : 0.f;
+                const float gs = gain_scale_passes(bt) ? -beta * beta * gb : 0.f;
                 float gu[D], ag[D];
 #pragma unroll
                 for (int i = 0; i < D; ++i) {
@@ -1747,6 +1733,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.decay(tau, a);
                 rd.values(tau, v);
                 gains(tile, tau, u);
+                const float beta = fabsf(sel4v(b4, tau));
                 {
                     float flat[D * M];
 #pragma unroll
@@ -1755,7 +1742,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                         for (int c = 0; c < M; ++c) flat[i * M + c] = Mm[i][c];
                     put<TL, kSMp, D * M>(tb, tau, flat);
                 }
-                mean_step<D, M>(Mm, k, a, v, u, sel4v(b4, tau), e);
+                mean_step<D, M>(Mm, k, a, v, u, beta, e);
                 put<TL, kSE, M>(tb, tau, e);
                 float gq[D];
                 if (has_gy) {
@@ -1784,7 +1771,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.decay(tau, a);
                 gains(tile, tau, u);
                 get<TL, kSE, M>(tb, tau, e);
-                const float beta = sel4v(b4, tau);
+                const float beta = fabsf(sel4v(b4, tau));
                 if (has_gy) {
                     float qv[D], gy[M];
                     rd.queries(tau, qv);
@@ -1949,9 +1936,9 @@ int launch_fwd(const FwdArgs<TIn> &a, cudaStream_t st) {
         ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
              map_rows(&mp.r, a.observation, a.t, a.n, kS);
     if (a.rs != nullptr) {
-        const Gains gn = replay_gains(a.rs, a.n, a.t, a.chunks, D, M);
-        ok = ok && map_tok(&mp.gu, static_cast<const float *>(gn.u), D, a.n, a.t) &&
-             map_rows(&mp.gb, gn.beta, a.t, a.n, kS) && map_rows(&mp.gs, gn.s, a.t, a.n, kS);
+        ok = ok && map_tok(&mp.gu, static_cast<const float *>(replay_gains(a.rs, a.n, a.t, a.chunks, D, M)), D,
+                           a.n, a.t) &&
+             map_rows(&mp.gb, replay_gain_scales(a.rs, a.n, a.t, a.chunks, D, M), a.t, a.n, kS);
     }
     if (!ok) return fail(BSSM_ERR_CUDA, "forward_chain: tensor-map encoding failed");
     const long grid = (a.n + kThreads - 1) / kThreads;
@@ -2036,9 +2023,9 @@ int launch_split(const BwdArgs<TIn> &a, cudaStream_t st) {
     if (NEED_DYN)
         ok = ok && map_tok(&mp.ga, a.ga, D, a.n, a.t) && map_rows(&mp.gp, a.gp, a.t, a.n, kS) &&
              map_rows(&mp.gr, a.gr, a.t, a.n, kS);
-    const Gains gn = replay_gains(a.rs, a.n, a.t, a.chunks, D, M);
-    ok = ok && map_tok(&mp.gu, static_cast<const float *>(gn.u), D, a.n, a.t) &&
-         map_rows(&mp.gb, gn.beta, a.t, a.n, kS) && map_rows(&mp.gs, gn.s, a.t, a.n, kS);
+    ok = ok && map_tok(&mp.gu, static_cast<const float *>(replay_gains(a.rs, a.n, a.t, a.chunks, D, M)), D, a.n,
+                       a.t) &&
+         map_rows(&mp.gb, replay_gain_scales(a.rs, a.n, a.t, a.chunks, D, M), a.t, a.n, kS);
     if (!ok) return fail(BSSM_ERR_CUDA, "backward_split: tensor-map encoding failed");
     const long grid = (a.n + 127) / 128;
     k<<<static_cast<unsigned>(grid), kSplitThreads, smem, st>>>(a, mp);
@@ -2069,9 +2056,9 @@ int launch_fwd_split(const FwdArgs<TIn> &a, cudaStream_t st) {
         ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
              map_rows(&mp.r, a.observation, a.t, a.n, kS);
     if (a.rs != nullptr) {
-        const Gains gn = replay_gains(a.rs, a.n, a.t, a.chunks, D, M);
-        ok = ok && map_tok(&mp.gu, static_cast<const float *>(gn.u), D, a.n, a.t) &&
-             map_rows(&mp.gb, gn.beta, a.t, a.n, kS) && map_rows(&mp.gs, gn.s, a.t, a.n, kS);
+        ok = ok && map_tok(&mp.gu, static_cast<const float *>(replay_gains(a.rs, a.n, a.t, a.chunks, D, M)), D,
+                           a.n, a.t) &&
+             map_rows(&mp.gb, replay_gain_scales(a.rs, a.n, a.t, a.chunks, D, M), a.t, a.n, kS);
     }
     if (!ok) return fail(BSSM_ERR_CUDA, "forward_split: tensor-map encoding failed");
     const long grid = (a.n + 127) / 128;

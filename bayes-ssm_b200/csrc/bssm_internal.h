@@ -105,26 +105,28 @@ __device__ __forceinline__ void rs_get_row(const float *rs, long base, int row, 
     for (int j = 0; j < D; ++j) v[j] = rs[base + static_cast<long>(D * M + tri_index(D, row, j)) * 32];
 }
 
-// After the states, the replay buffer holds every token's gain and scalars
-// as the forward computed them: u [N][T][D], then beta [N][T], then s [N][T]
-// (each part starting 16-byte aligned).  A backward can replay the mean
-// from these without waiting for the covariance replay.
+// After the states, the replay buffer holds every token's gain u [N][T][D]
+// as the forward computed it, then its signed gain scale [N][T]: beta when
+// s >= floor (the clamp passes the gradient to s), -beta when not.  beta is
+// positive or NaN, so the sign carries the clamp mask and |.| the value; a
+// NaN s gives -NaN, masked as s >= floor would.  Each part starts 16-byte
+// aligned.  With them a backward replays the mean without waiting for the
+// covariance replay.
 __host__ __device__ inline long round4(long x) { return (x + 3) / 4 * 4; }
-struct Gains {
-    float *u, *beta, *s;
-};
-__host__ __device__ inline Gains replay_gains(const float *rs, long n, long t, int chunks, int d, int m) {
-    float *g = const_cast<float *>(rs) + replay_state_part(n, t, chunks, d, m);
-    Gains r;
-    r.u = g;
-    r.beta = g + round4(n * t * d);
-    r.s = r.beta + round4(n * t);
-    return r;
+__host__ __device__ inline float *replay_gains(const float *rs, long n, long t, int chunks, int d, int m) {
+    return const_cast<float *>(rs) + replay_state_part(n, t, chunks, d, m);
+}
+__host__ __device__ inline float *replay_gain_scales(const float *rs, long n, long t, int chunks, int d, int m) {
+    return replay_gains(rs, n, t, chunks, d, m) + round4(n * t * d);
 }
 // Floats of the whole replay buffer.
 __host__ __device__ inline long replay_floats(long n, long t, int chunks, int d, int m) {
-    return replay_state_part(n, t, chunks, d, m) + round4(n * t * d) + 2 * round4(n * t);
+    return replay_state_part(n, t, chunks, d, m) + round4(n * t * d) + round4(n * t);
 }
+__device__ __forceinline__ float signed_gain_scale(float beta, float s, float floor_) {
+    return s >= floor_ ? beta : -beta;
+}
+__device__ __forceinline__ bool gain_scale_passes(float bt) { return !signbit(bt); }
 
 // Error reporting (thread-local message behind bssm_last_error()).
 extern thread_local std::string g_last_error;

@@ -251,12 +251,8 @@ __global__ void __launch_bounds__(Launch<D>::kThreads)
         StepInfo<D, M> si;
         forward_step<D, M>(g, cur, Mc, P, A.floor, si);
         if (A.rs != nullptr) {
-            const Gains gn = replay_gains(A.rs, A.n, T, L, D, M);
-            gn.u[row * D + own] = si.u_own;
-            if (own == 0) {
-                gn.beta[row] = si.beta;
-                gn.s[row] = si.s;
-            }
+            replay_gains(A.rs, A.n, T, L, D, M)[row * D + own] = si.u_own;
+            if (own == 0) replay_gain_scales(A.rs, A.n, T, L, D, M)[row] = signed_gain_scale(si.beta, si.s, A.floor);
         }
         float y[CPL];
         readout<D, M>(cur, Mc, y);

@@ -515,14 +515,11 @@ __global__ void __launch_bounds__(32) forward_staged(const FwdArgs<TIn> A) {
             float u[D], u_own[RPL], e[CPL], beta, s;
             forward_step_plain<D, M, LPC>(g, tk, A.floor, Mc, P, u, u_own, e, beta, s);
             if (active && A.rs != nullptr) {
-                const Gains gn = replay_gains(A.rs, A.n, T, L, D, M);
-                const long grow = chain * T + t;
+                float *const gu = replay_gains(A.rs, A.n, T, L, D, M) + (chain * T + t) * D + row0;
 #pragma unroll
-                for (int r = 0; r < RPL; ++r) gn.u[grow * D + row0 + r] = u_own[r];
-                if (sub == 0) {
-                    gn.beta[grow] = beta;
-                    gn.s[grow] = s;
-                }
+                for (int r = 0; r < RPL; ++r) gu[r] = u_own[r];
+                if (sub == 0)
+                    replay_gain_scales(A.rs, A.n, T, L, D, M)[chain * T + t] = signed_gain_scale(beta, s, A.floor);
             }
             float qv[D];
             lds_vec<D>(reinterpret_cast<const TIn *>(stage + G::oQ + c * G::csK + tau * G::rbK), qv);

@@ -73,10 +73,10 @@ def test_null_pointers_rejected_without_gpu(lib):
 
 
 def _gains_floats(n, t, d):
-    """Per-token gains after the states: u [N,T,D], beta [N,T], s [N,T], each
-    part padded to 4 floats."""
+    """Per-token gains after the states: u [N,T,D], then the signed gain
+    scales [N,T], each part padded to 4 floats."""
     r4 = lambda x: (x + 3) // 4 * 4
-    return r4(n * t * d) + 2 * r4(n * t)
+    return r4(n * t * d) + r4(n * t)
 
 
 def _group_chains(n):

@@ -157,6 +157,33 @@ def test_replay_states_shared_across_families(fwd_family, bwd_family, monkeypatc
         assert_parity(got[key], ref[key], what=f"grad {key}")
 
 
+@pytest.mark.parametrize("fwd_family,bwd_family", [("chain", "chain"), ("staged", "chain"), ("v1", "chain"),
+                                                    ("chain", "staged"), ("chain1", "chain1")])
+def test_clamped_innovation_across_families(fwd_family, bwd_family, monkeypatch):
+    """Tokens whose innovation variance s = r + k.u falls below the floor: the
+    clamp must block the gradient to s.  The saved gain scale carries that
+    mask in its sign, so it must survive a forward of one family and a
+    backward of another."""
+    n, t = 40, 32
+    inp = make_inputs(n, t, 8, 8, seed=92, init="random", io_dtype=torch.bfloat16)
+    for tok in (0, 5, 13, 22, 31):
+        inp["k"][:, tok, :] = 0.0
+        inp["r"][:, tok] = 1e-9
+    monkeypatch.setenv("BSSM_KERNELS", fwd_family)
+    fwd = capi_forward(inp, chunks=16)
+    y, mt, pt = _oracle_fwd(inp)
+    assert_parity(fwd["y"], y, rel=1e-4, what="y")
+    monkeypatch.setenv("BSSM_KERNELS", bwd_family)
+    gy, gmt, gpt = _grads_out(n, t, 8, 8, 6)
+    got = capi_backward(inp, fwd, gy, gmt, gpt, chunks=16)
+    ref = _oracle_bwd(inp, gy, gmt, gpt)
+    for key in ("k", "v", "q"):
+        assert_parity(got[key], ref[key], rel=4e-3, what=f"grad {key}")
+    for key in ("a", "p", "r", "M0", "P0"):
+        assert_parity(got[key], ref[key], rel=1e-4, what=f"grad {key}")
+    assert torch.all(got["r"][:, (0, 5, 13, 22, 31)] == 0), "clamped tokens pass no gradient to r"
+
+
 @pytest.mark.parametrize("d", DIMS)
 def test_dynamic_unit_distribution(d):
     inp = make_inputs(19, 33, d, 8, seed=7 + d, dist="unit", init="random")
