@@ -55,9 +55,10 @@ BWD_FLOPS = (FWD_FLOPS - 2 * D * M) + (18 * D * D + 22 * D * M + 10 * D + M)
 # 148 SMs x 128 FP32 lanes x 2 flop x 1965 MHz is used and labelled as such.
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 # DRAM traffic of one backward launch (dram__bytes_read.sum +
-# dram__bytes_write.sum) from an ncu capture of this exact workload (16,384
-# chains, one launch).  See profiles/backward_split_d8m8_bf16.md.
-NCU_BWD_TRAFFIC_BYTES = 2.2057e9 + 0.7196e9
+# dram__bytes_write.sum) from an ncu capture of a quarter of this workload
+# (4,096 chains, one CTA per SM as in the full launch), scaled by 4: traffic
+# grows with the chains.  See profiles/backward_split_d8m8_bf16.md.
+NCU_BWD_TRAFFIC_BYTES = 4 * (540.64e6 + 162.54e6)
 # Canonical algorithmic figures per chain-step, FP32 at the reference ABI
 # (fwd + bwd): bytes 4 (9D + 5M + 6), flops 26D^2 + 34DM + 30D + 3M + 2.
 STEP_BYTES_F32 = 4 * (9 * D + 5 * M + 6)
