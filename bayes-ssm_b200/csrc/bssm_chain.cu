@@ -53,6 +53,7 @@ constexpr int kSplitThreads = 32 * kSplitWarps;
 constexpr int kSmemMax = 227 * 1024;
 
 constexpr int al128(int x) { return (x + 127) / 128 * 128; }
+constexpr int al1024(int x) { return (x + 1023) / 1024 * 1024; }
 
 // N consecutive floats from 16-byte aligned shared memory.
 template <int N>
@@ -110,25 +111,12 @@ __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // ---- TMA tensor copies (no multicast) ------------------------------------------
-__device__ __forceinline__ void tma_load_3d(void *sdst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];" ::"r"(smem_u32(sdst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-        : "memory");
-}
 __device__ __forceinline__ void tma_load_2d(void *sdst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
         "[%4];" ::"r"(smem_u32(sdst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
-}
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, int x, int y, int z, const void *ssrc) {
-    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y), "r"(z), "r"(smem_u32(ssrc))
-                 : "memory");
 }
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *ssrc) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
@@ -145,8 +133,8 @@ __device__ __forceinline__ void bulk_wait_read() {
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Tensor maps of one launch.  Token maps traverse (row, chain, token) with a
-// box of (row, 32 chains, kS tokens); noise maps (token, chain) with a box of
+// Tensor maps of one launch.  Token maps traverse (row x token, chain) with a
+// line box of (kS rows, 32 chains); noise maps (token, chain) with a box of
 // (kS tokens, 32 chains); the replay-state map (float, chain) with a box of
 // (one state, 32 chains).
 struct FwdMaps {
@@ -156,15 +144,72 @@ struct BwdMaps {
     CUtensorMap k, q, v, a, p, r, gy, rs, gk, gv, gq, ga, gp, gr, gu, gb;
 };
 
-// Shared-memory geometry of one warp's tile (one stage), box layouts.
+// ---- Line layout -------------------------------------------------------------
+// Token tensors [N, T, row] travel as line boxes: for each of 32 consecutive
+// chains, the kS rows of tokens [t0, t0 + kS) form one line of
+// L = kS * rowbytes bytes (64 or 128), contiguous in global memory, so TMA
+// moves one segment per chain.  TMA writes (and reads back) a box with the
+// swizzle of span L: the 16-byte chunk x of chain c's line sits at chunk
+// x ^ s(c), with s(c) = (c >> 1) & 3 for L = 64 and c & 7 for L = 128 (bits
+// [4, ..) of the offset in a 1024-byte aligned region XOR bits [7, ..)).  A
+// warp's 16-byte accesses to one row of its 32 chains then fall in distinct
+// banks within each quarter warp.
+template <int RB>
+__device__ __forceinline__ int line_off(int c, int tau, int h) {
+    static_assert(RB == 16 || RB == 32, "row bytes");
+    if constexpr (RB == 16) {
+        return c * 64 + ((tau ^ ((c >> 1) & 3)) << 4);
+    } else {
+        return c * 128 + (((2 * tau + h) ^ (c & 7)) << 4);
+    }
+}
+
+// One 16-byte chunk: 4 floats, or 8 floats rounded to BF16.
+__device__ __forceinline__ void sts_chunk(float *p, const float *x) {
+    *reinterpret_cast<float4 *>(p) = make_float4(x[0], x[1], x[2], x[3]);
+}
+__device__ __forceinline__ void sts_chunk(__nv_bfloat16 *p, const float *x) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Row tau (N elements of T) of chain c, from or to a line region.
+template <int N, typename T>
+__device__ __forceinline__ void line_load(const char *region, int c, int tau, float (&o)[N]) {
+    constexpr int RB = N * static_cast<int>(sizeof(T)), EC = 16 / static_cast<int>(sizeof(T));
+#pragma unroll
+    for (int h = 0; h < RB / 16; ++h) {
+        float x[EC];
+        lds_vec<EC>(reinterpret_cast<const T *>(region + line_off<RB>(c, tau, h)), x);
+#pragma unroll
+        for (int e = 0; e < EC; ++e) o[h * EC + e] = x[e];
+    }
+}
+template <int N, typename T>
+__device__ __forceinline__ void line_store(char *region, int c, int tau, const float (&v)[N]) {
+    constexpr int RB = N * static_cast<int>(sizeof(T)), EC = 16 / static_cast<int>(sizeof(T));
+#pragma unroll
+    for (int h = 0; h < RB / 16; ++h) sts_chunk(reinterpret_cast<T *>(region + line_off<RB>(c, tau, h)), v + h * EC);
+}
+
+// Shared-memory geometry of one warp's tile (one stage): line boxes of the
+// token tensors, [chain][tau] boxes of the noise.
 template <int D, int M, bool FIXED, bool BWD, typename TIn>
 struct Tile {
     static constexpr int rbK = D * static_cast<int>(sizeof(TIn)), rbV = M * static_cast<int>(sizeof(TIn));
     static constexpr int szK = kS * 32 * rbK, szV = kS * 32 * rbV, szA = FIXED ? 0 : kS * 32 * D * 4;
     static constexpr int szP = FIXED ? 0 : 32 * kS * 4, szG = BWD ? kS * 32 * M * 4 : 0;
-    static constexpr int oK = 0, oQ = al128(oK + szK), oV = al128(oQ + szK), oA = al128(oV + szV);
-    static constexpr int oP = al128(oA + szA), oR = al128(oP + szP), oG = al128(oR + szP);
-    static constexpr int kBytes = al128(oG + szG);
+    // line regions (whole KB each, so every one stays 1024-byte aligned),
+    // then the [chain][tau] noise rows
+    static constexpr int oK = 0, oQ = oK + szK, oV = oQ + szK, oA = oV + szV, oG = oA + szA;
+    static constexpr int oP = oG + szG, oR = oP + szP;
+    static constexpr int kBytes = al1024(oR + szP);
+    static_assert(szK % 1024 == 0 && szV % 1024 == 0 && szA % 1024 == 0 && szG % 1024 == 0, "line regions");
     static constexpr int kTx = 2 * szK + szV + szA + 2 * szP;  // bytes the token maps deliver, without gy
 };
 
@@ -175,16 +220,16 @@ __device__ __forceinline__ void issue_tile(char *tile, const Maps &mp, int chain
                                            uint64_t *bar, int extra_bytes) {
     using Tl = Tile<D, M, FIXED, BWD, TIn>;
     mbar_arrive_tx(bar, Tl::kTx + (with_gy ? Tl::szG : 0) + extra_bytes);
-    tma_load_3d(tile + Tl::oK, &mp.k, 0, chain0, t0, bar);
-    tma_load_3d(tile + Tl::oQ, &mp.q, 0, chain0, t0, bar);
-    tma_load_3d(tile + Tl::oV, &mp.v, 0, chain0, t0, bar);
+    tma_load_2d(tile + Tl::oK, &mp.k, t0 * D, chain0, bar);
+    tma_load_2d(tile + Tl::oQ, &mp.q, t0 * D, chain0, bar);
+    tma_load_2d(tile + Tl::oV, &mp.v, t0 * M, chain0, bar);
     if constexpr (!FIXED) {
-        tma_load_3d(tile + Tl::oA, &mp.a, 0, chain0, t0, bar);
+        tma_load_2d(tile + Tl::oA, &mp.a, t0 * D, chain0, bar);
         tma_load_2d(tile + Tl::oP, &mp.p, t0, chain0, bar);
         tma_load_2d(tile + Tl::oR, &mp.r, t0, chain0, bar);
     }
     if constexpr (BWD) {
-        if (with_gy) tma_load_3d(tile + Tl::oG, &mp.gy, 0, chain0, t0, bar);
+        if (with_gy) tma_load_2d(tile + Tl::oG, &mp.gy, t0 * M, chain0, bar);
     }
 }
 
@@ -195,20 +240,20 @@ struct TileRead {
     const char *t;
     int c;
     __device__ __forceinline__ void keys(int tau, float (&k)[D]) const {
-        lds_vec<D>(reinterpret_cast<const TIn *>(t + Tl::oK) + (tau * 32 + c) * D, k);
+        line_load<D, TIn>(t + Tl::oK, c, tau, k);
     }
     __device__ __forceinline__ void queries(int tau, float (&q)[D]) const {
-        lds_vec<D>(reinterpret_cast<const TIn *>(t + Tl::oQ) + (tau * 32 + c) * D, q);
+        line_load<D, TIn>(t + Tl::oQ, c, tau, q);
     }
     __device__ __forceinline__ void values(int tau, float (&v)[M]) const {
-        lds_vec<M>(reinterpret_cast<const TIn *>(t + Tl::oV) + (tau * 32 + c) * M, v);
+        line_load<M, TIn>(t + Tl::oV, c, tau, v);
     }
     __device__ __forceinline__ void decay(int tau, float (&a)[D]) const {
         if constexpr (FIXED) {
 #pragma unroll
             for (int j = 0; j < D; ++j) a[j] = kFixedDecay;
         } else {
-            lds_vec<D>(reinterpret_cast<const float *>(t + Tl::oA) + (tau * 32 + c) * D, a);
+            line_load<D, float>(t + Tl::oA, c, tau, a);
         }
     }
     __device__ __forceinline__ void noise(float4 &p4, float4 &r4) const {
@@ -221,7 +266,7 @@ struct TileRead {
         }
     }
     __device__ __forceinline__ void gy(int tau, float (&g)[M]) const {
-        lds_vec<M>(reinterpret_cast<const float *>(t + Tl::oG) + (tau * 32 + c) * M, g);
+        line_load<M, float>(t + Tl::oG, c, tau, g);
     }
 };
 
@@ -332,26 +377,26 @@ template <int D, int M, bool FIXED, typename TIn>
 struct FwdGeo {
     using Tl = Tile<D, M, FIXED, false, TIn>;
     static constexpr int SF = replay_state_floats(D, M);
-    // a warp's outputs of one tile, box layouts: readout [tau][chain][M],
-    // gains [tau][chain][D], beta and s [chain][tau]
+    // a warp's outputs of one tile: readout and gains as line boxes, the
+    // signed gain scales [chain][tau]
     static constexpr int yY = 0, yU = kS * 32 * M * 4, yB = yU + kS * 32 * D * 4;
-    static constexpr int kYB = yB + 32 * kS * 4;
+    static constexpr int kYB = al1024(yB + 32 * kS * 4);
     static constexpr int kPerStage = kWarps * Tl::kBytes;
-    static constexpr int kFixed = kWarps * kYB + 128 + kWarps * 4 * 8;
+    static constexpr int kFixed = kWarps * kYB + 1024 + kWarps * 4 * 8;
     static constexpr int kFit = (kSmemMax - kFixed) / kPerStage;
     static constexpr bool kFits = kFit >= 2;  // else the shape goes to another family
     static constexpr int kStages = kFit < 2 ? 2 : (kFit < 4 ? kFit : 4);
     static constexpr int oY = 0;                            // [warp][kYB]
-    static constexpr int oT = al128(oY + kWarps * kYB);     // [stage][warp][tile]
+    static constexpr int oT = oY + kWarps * kYB;            // [stage][warp][tile]
     static constexpr int oBar = oT + kStages * kPerStage;   // [warp][stage]
-    static constexpr int kSmem = oBar + kWarps * kStages * 8 + 128;  // + alignment slack
+    static constexpr int kSmem = oBar + kWarps * kStages * 8 + 1024;  // + alignment slack
     static_assert(!kFits || kSmem <= kSmemMax, "forward shared memory");
 };
 
-// 128-byte aligned start of dynamic shared memory.
+// 1024-byte aligned start of dynamic shared memory (swizzled line boxes).
 __device__ __forceinline__ char *smem_base(char *raw) {
     const uint32_t a = smem_u32(raw);
-    return raw + ((128 - (a & 127)) & 127);
+    return raw + ((1024 - (a & 1023)) & 1023);
 }
 
 // ===========================================================================
@@ -448,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
 #pragma unroll
             for (int t = 0; t < TRI; ++t) A.rs[base + static_cast<long>(D * M + t) * 32] = P[t];
         }
-        float *const yb = reinterpret_cast<float *>(ob + G::yY);
+        char *const yb = ob + G::yY;
         const bool gains = A.rs != nullptr;
         float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f);
         rd.noise(p4, r4);
@@ -475,9 +520,9 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
                 if (lane == 0) bulk_wait_read<0>();
                 __syncwarp();
             }
-            sts_vec<M>(yb + (tau * 32 + lane) * M, y);
+            line_store<M, float>(yb, lane, tau, y);
             if (gains) {
-                sts_vec<D>(reinterpret_cast<float *>(ob + G::yU) + (tau * 32 + lane) * D, u);
+                line_store<D, float>(ob + G::yU, lane, tau, u);
                 const float bt = signed_gain_scale(beta, s, A.floor);
                 b4.x = tau == 0 ? bt : b4.x;
                 b4.y = tau == 1 ? bt : b4.y;
@@ -492,9 +537,9 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
         __syncwarp();
         if (lane == 0) {
             if (chain0 < A.n) {
-                tma_store_3d(&mp.y, 0, chain0, t0, yb);
+                tma_store_2d(&mp.y, t0 * M, chain0, yb);
                 if (gains) {
-                    tma_store_3d(&mp.gu, 0, chain0, t0, ob + G::yU);
+                    tma_store_2d(&mp.gu, t0 * D, chain0, ob + G::yU);
                     tma_store_2d(&mp.gb, t0, chain0, ob + G::yB);
                 }
             }
@@ -528,11 +573,11 @@ struct FSplitGeo {
     using Tl = Tile<D, M, FIXED, false, TIn>;
     static constexpr bool kInPlaceY = !FIXED && D == M;  // readout rows fit the decay slots
     static constexpr int gU = 0, gB = kS * 32 * D * 4;
-    static constexpr int kGB = gB + 32 * kS * 4;           // one gains block: u, signed scale
+    static constexpr int kGB = al1024(gB + 32 * kS * 4);   // one gains block: u (line box), signed scale
     static constexpr int kYB = kInPlaceY ? 0 : kS * 32 * M * 4;
     static constexpr int kPerStage = 4 * Tl::kBytes;
     static constexpr int kBars = 2 * 4 + 4;                // full[4] empty[4] gfull[2] gfree[2]
-    static constexpr int kFixed = 4 * (2 * kGB + kYB) + 4 * kBars * 8 + 256;
+    static constexpr int kFixed = 4 * (2 * kGB + kYB) + 4 * kBars * 8 + 1024 + 128;
     static constexpr int kFit = (kSmemMax - kFixed) / kPerStage;
     static constexpr int kStages = kFit < 4 ? kFit : 4;
     static constexpr bool kFits = kStages >= 3;
@@ -540,7 +585,7 @@ struct FSplitGeo {
     static constexpr int oG = kStages * kPerStage;                    // [group][2][kGB]
     static constexpr int oY = oG + 4 * 2 * kGB;                       // [group][kYB]
     static constexpr int oBar = al128(oY + 4 * kYB);                  // [group][kBars]
-    static constexpr int kSmem = oBar + 4 * kBars * 8 + 128;
+    static constexpr int kSmem = oBar + 4 * kBars * 8 + 1024;  // + alignment slack
 };
 
 template <int D, int M, bool FIXED, typename TIn>
@@ -651,7 +696,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.keys(tau, k);
                 rd.decay(tau, a);
                 cov_step<D>(P, k, a, sel4v(p4, tau), sel4v(r4, tau), A.floor, u, beta, s);
-                sts_vec<D>(reinterpret_cast<float *>(gb + G::gU) + (tau * 32 + lane) * D, u);
+                line_store<D, float>(gb + G::gU, lane, tau, u);
                 const float bt = signed_gain_scale(beta, s, A.floor);
                 b4.x = tau == 0 ? bt : b4.x;
                 b4.y = tau == 1 ? bt : b4.y;
@@ -664,7 +709,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             __syncwarp();
             if (lane == 0) {
                 if (gains_out && chain0 < A.n) {
-                    tma_store_3d(&mp.gu, 0, chain0, t0, gb + G::gU);
+                    tma_store_2d(&mp.gu, t0 * D, chain0, gb + G::gU);
                     tma_store_2d(&mp.gb, t0, chain0, gb + G::gB);
                 }
                 bulk_commit();
@@ -720,11 +765,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                         for (int c = 0; c < M; ++c) A.rs[base + static_cast<long>(i * M + c) * 32] = Mm[i][c];
                 }
             }
-            float *yb;
+            char *yb;
             if constexpr (G::kInPlaceY) {
-                yb = reinterpret_cast<float *>(tile + Tl::oA);  // decay rows die token by token
+                yb = tile + Tl::oA;  // decay rows die token by token
             } else {
-                yb = reinterpret_cast<float *>(ysep);
+                yb = ysep;
                 if (lane == 0) bulk_wait_read<0>();  // the previous readout store
                 __syncwarp();
             }
@@ -735,7 +780,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.keys(tau, k);
                 rd.decay(tau, a);
                 rd.values(tau, v);
-                lds_vec<D>(reinterpret_cast<const float *>(gb + G::gU) + (tau * 32 + lane) * D, u);
+                line_load<D, float>(gb + G::gU, lane, tau, u);
                 mean_step<D, M>(Mm, k, a, v, u, fabsf(sel4v(b4, tau)), e);
                 rd.queries(tau, qv);
                 float y[M];
@@ -746,13 +791,13 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                     for (int i = 0; i < D; ++i) acc = fmaf(Mm[i][c], qv[i], acc);
                     y[c] = acc;
                 }
-                sts_vec<M>(yb + (tau * 32 + lane) * M, y);
+                line_store<M, float>(yb, lane, tau, y);
             }
             mbar_arrive(gfree + b);  // done with this gains block
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) {
-                if (chain0 < A.n) tma_store_3d(&mp.y, 0, chain0, t0, yb);
+                if (chain0 < A.n) tma_store_2d(&mp.y, t0 * M, chain0, yb);
                 bulk_commit();
                 if constexpr (!G::kInPlaceY) mbar_arrive(empty + q % NS);
             }
@@ -916,29 +961,29 @@ struct BwdGeo {
     using Tl = Tile<D, M, FIXED, true, TIn>;
     static constexpr int SF = replay_state_floats(D, M);
     static constexpr int kSB = 32 * SF * 4;  // a warp's start states, box layout [chain][SF]
-    // a warp's gradient rows of one sub-chunk, box layouts: keys, values,
-    // queries, decay [tau][chain][row]; process, observation [chain][tau]
+    // a warp's gradient rows of one sub-chunk: keys, values, queries, decay
+    // as line boxes (whole KB each); process, observation [chain][tau]
     static constexpr int rbK = Tl::rbK, rbV = Tl::rbV;
-    static constexpr int gK = 0, gV = al128(gK + kS * 32 * rbK), gQ = al128(gV + kS * 32 * rbV);
-    static constexpr int gA = al128(gQ + kS * 32 * rbK), gP = al128(gA + kS * 32 * D * 4);
-    static constexpr int gR = al128(gP + 32 * kS * 4), kOB = al128(gR + 32 * kS * 4);
+    static constexpr int gK = 0, gV = gK + kS * 32 * rbK, gQ = gV + kS * 32 * rbV;
+    static constexpr int gA = gQ + kS * 32 * rbK, gP = gA + kS * 32 * D * 4;
+    static constexpr int gR = gP + 32 * kS * 4, kOB = al1024(gR + 32 * kS * 4);
     static constexpr int kPerStage = kWarps * Tl::kBytes;
     static constexpr int oT = 0;                              // [stage][warp][tile]
     static constexpr int oS = oT + 2 * kPerStage;             // [warp][kSB]
-    static constexpr int oO = al128(oS + kWarps * kSB);       // [warp][kOB]
-    static constexpr bool kStageOut = oO + kWarps * kOB + kWarps * 2 * 8 + 16 + 128 <= kSmemMax;
+    static constexpr int oO = al1024(oS + kWarps * kSB);      // [warp][kOB]
+    static constexpr bool kStageOut = oO + kWarps * kOB + kWarps * 2 * 8 + 16 + 1024 <= kSmemMax;
     static constexpr int oBar = kStageOut ? oO + kWarps * kOB : oO;  // [warp][stage]
     static constexpr int oSlot = oBar + kWarps * 2 * 8;
-    static constexpr int kSmem = oSlot + 16 + 128;  // + alignment slack
+    static constexpr int kSmem = oSlot + 16 + 1024;  // + alignment slack
     static_assert(kSmem <= kSmemMax, "backward shared memory");
 };
 
-// One gradient row of token tau: into the staging box (written back at the
-// sub-chunk's end), or straight to global memory.
+// One gradient row of token tau: into the staging line box (written back at
+// the sub-chunk's end), or straight to global memory.
 template <bool STAGE, int N, typename T>
-__device__ __forceinline__ void put_row(T *stage_row, T *gdst, const float (&v)[N], bool active) {
+__device__ __forceinline__ void put_row(char *region, int c, int tau, T *gdst, const float (&v)[N], bool active) {
     if constexpr (STAGE) {
-        store_vec<N>(stage_row, v);
+        line_store<N, T>(region, c, tau, v);
     } else if (active) {
         store_vec<N>(gdst, v);
     }
@@ -1127,8 +1172,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
 #pragma unroll
                     for (int i = 0; i < D; ++i) gq[i] = 0.f;
                 }
-                put_row<G::kStageOut, D>(reinterpret_cast<TIn *>(out + G::gQ) + (tau * 32 + lane) * D,
-                                         A.gq + (row0 + tau) * D, gq, active);
+                put_row<G::kStageOut, D>(out + G::gQ, lane, tau, A.gq + (row0 + tau) * D, gq, active);
             };
 #pragma unroll 1
             for (int tau = 0; tau < kS; ++tau) mstep(tau);
@@ -1252,10 +1296,8 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
                     }
                     Rp[t] = (a[i] * a[j]) * S;
                 }
-            put_row<G::kStageOut, D>(reinterpret_cast<TIn *>(out + G::gK) + (tau * 32 + lane) * D, A.gk + row * D, gk,
-                                     active);
-            put_row<G::kStageOut, M>(reinterpret_cast<TIn *>(out + G::gV) + (tau * 32 + lane) * M, A.gv + row * M, ge,
-                                     active);
+            put_row<G::kStageOut, D>(out + G::gK, lane, tau, A.gk + row * D, gk, active);
+            put_row<G::kStageOut, M>(out + G::gV, lane, tau, A.gv + row * M, ge, active);
             if constexpr (NEED_DYN) {
                 float ga[D], gpv, grv;
                 if constexpr (FIXED) {
@@ -1273,8 +1315,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
                     gpv = trR + gpk;
                     grv = gs;
                 }
-                put_row<G::kStageOut, D>(reinterpret_cast<float *>(out + G::gA) + (tau * 32 + lane) * D,
-                                         A.ga + row * D, ga, active);
+                put_row<G::kStageOut, D>(out + G::gA, lane, tau, A.ga + row * D, ga, active);
                 if constexpr (G::kStageOut) {
                     gp4.x = tau == 0 ? gpv : gp4.x;
                     gp4.y = tau == 1 ? gpv : gp4.y;
@@ -1300,11 +1341,11 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
             fence_proxy_async();
             __syncwarp();
             if (lane == 0 && chain0 < A.n) {
-                tma_store_3d(&mp.gk, 0, chain0, t0, out + G::gK);
-                tma_store_3d(&mp.gv, 0, chain0, t0, out + G::gV);
-                tma_store_3d(&mp.gq, 0, chain0, t0, out + G::gQ);
+                tma_store_2d(&mp.gk, t0 * D, chain0, out + G::gK);
+                tma_store_2d(&mp.gv, t0 * M, chain0, out + G::gV);
+                tma_store_2d(&mp.gq, t0 * D, chain0, out + G::gQ);
                 if constexpr (NEED_DYN) {
-                    tma_store_3d(&mp.ga, 0, chain0, t0, out + G::gA);
+                    tma_store_2d(&mp.ga, t0 * D, chain0, out + G::gA);
                     tma_store_2d(&mp.gp, t0, chain0, out + G::gP);
                     tma_store_2d(&mp.gr, t0, chain0, out + G::gR);
                 }
@@ -1396,10 +1437,10 @@ struct SplitGeo {
     using Tl = Tile<D, M, false, true, TIn>;
     static_assert(D == M, "in-place gradient staging needs D == M");
     static constexpr int SF = replay_state_floats(D, M);
-    // per group and stage: the token tile, then the gains [tau][chain][D]
-    // and the signed gain scales [chain][tau]
+    // per group and stage: the token tile, then the gains (line box) and the
+    // signed gain scales [chain][tau]
     static constexpr int oU = Tl::kBytes, oB = oU + kS * 32 * D * 4;
-    static constexpr int kTileBytes = al128(oB + 32 * kS * 4);
+    static constexpr int kTileBytes = al1024(oB + 32 * kS * 4);
     static constexpr int kTx = Tl::kTx + kS * 32 * D * 4 + 32 * kS * 4;  // without gy, without state
     static constexpr int kSB = 32 * SF * 4;  // a group's start states [chain][SF]
     static constexpr int kPerStage = 4 * kTileBytes;
@@ -1408,7 +1449,7 @@ struct SplitGeo {
     static constexpr int oBar = al128(oSt + 4 * kSB);   // [group][kBars]
     static constexpr int kBars = 5 + 2 * kXSlots;      // full[2] empty[2] sfree xfull[3] xempty[3]
     static constexpr int oSlot = oBar + 4 * kBars * 8;
-    static constexpr int kSmem = oSlot + 16 + 128;
+    static constexpr int kSmem = oSlot + 16 + 1024;  // + alignment slack
     static constexpr bool kFits = kSmem <= kSmemMax;
 };
 
@@ -1489,14 +1530,14 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         char *const t = tiles + stage * G::kPerStage;
         const int t0 = static_cast<int>(it.t0());
         mbar_arrive_tx(full + stage, G::kTx + (has_gy ? Tl::szG : 0) + (saved ? G::kSB : 0));
-        tma_load_3d(t + Tl::oK, &mp.k, 0, chain0, t0, full + stage);
-        tma_load_3d(t + Tl::oQ, &mp.q, 0, chain0, t0, full + stage);
-        tma_load_3d(t + Tl::oV, &mp.v, 0, chain0, t0, full + stage);
-        tma_load_3d(t + Tl::oA, &mp.a, 0, chain0, t0, full + stage);
+        tma_load_2d(t + Tl::oK, &mp.k, t0 * D, chain0, full + stage);
+        tma_load_2d(t + Tl::oQ, &mp.q, t0 * D, chain0, full + stage);
+        tma_load_2d(t + Tl::oV, &mp.v, t0 * M, chain0, full + stage);
+        tma_load_2d(t + Tl::oA, &mp.a, t0 * D, chain0, full + stage);
         tma_load_2d(t + Tl::oP, &mp.p, t0, chain0, full + stage);
         tma_load_2d(t + Tl::oR, &mp.r, t0, chain0, full + stage);
-        if (has_gy) tma_load_3d(t + Tl::oG, &mp.gy, 0, chain0, t0, full + stage);
-        tma_load_3d(t + G::oU, &mp.gu, 0, chain0, t0, full + stage);
+        if (has_gy) tma_load_2d(t + Tl::oG, &mp.gy, t0 * M, chain0, full + stage);
+        tma_load_2d(t + G::oU, &mp.gu, t0 * D, chain0, full + stage);
         tma_load_2d(t + G::oB, &mp.gb, t0, chain0, full + stage);
         if (saved) tma_load_2d(sbox, &mp.rs, 0, state_row(chain0, nb, rs_slots, it.ci, it.j, SF), full + stage);
     };
@@ -1517,7 +1558,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     };
     // token tau's gain and scalars from the tile
     auto gains = [&](const char *t, int tau, float (&u)[D]) {
-        lds_vec<D>(reinterpret_cast<const float *>(t + G::oU) + (tau * 32 + lane) * D, u);
+        line_load<D, float>(t + G::oU, lane, tau, u);
     };
 
     BwdItems cur, nxt;
@@ -1645,7 +1686,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                         Rp[t] = (a[i] * a[j]) * S;
                     }
                 // keys and decay of this token are dead: their slots take gk, ga
-                store_vec<D>(reinterpret_cast<TIn *>(tile + Tl::oK) + (tau * 32 + lane) * D, gk);
+                line_store<D, TIn>(tile + Tl::oK, lane, tau, gk);
                 if constexpr (NEED_DYN) {
                     float ga[D], gpk = 0.f;
 #pragma unroll
@@ -1653,7 +1694,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                         ga[i] = fmaf(2.f, gaP[i], xv[2 * D + i]);
                         gpk = fmaf(gu[i], k[i], gpk);
                     }
-                    store_vec<D>(reinterpret_cast<float *>(tile + Tl::oA) + (tau * 32 + lane) * D, ga);
+                    line_store<D, float>(tile + Tl::oA, lane, tau, ga);
                     const float gpv = trR + gpk;
                     gp4.x = tau == 0 ? gpv : gp4.x;
                     gp4.y = tau == 1 ? gpv : gp4.y;
@@ -1673,9 +1714,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             __syncwarp();
             if (lane == 0) {
                 if (chain0 < A.n) {
-                    tma_store_3d(&mp.gk, 0, chain0, t0, tile + Tl::oK);
+                    tma_store_2d(&mp.gk, t0 * D, chain0, tile + Tl::oK);
                     if constexpr (NEED_DYN) {
-                        tma_store_3d(&mp.ga, 0, chain0, t0, tile + Tl::oA);
+                        tma_store_2d(&mp.ga, t0 * D, chain0, tile + Tl::oA);
                         tma_store_2d(&mp.gp, t0, chain0, tile + Tl::oP);
                         tma_store_2d(&mp.gr, t0, chain0, tile + Tl::oR);
                     }
@@ -1759,7 +1800,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 #pragma unroll
                     for (int i = 0; i < D; ++i) gq[i] = 0.f;
                 }
-                store_vec<D>(reinterpret_cast<TIn *>(tile + Tl::oV) + (tau * 32 + lane) * D, gq);
+                line_store<D, TIn>(tile + Tl::oV, lane, tau, gq);
             }
             tmem::wait_st();
             // reverse: mean adjoint; the covariance warp's inputs go through
@@ -1824,7 +1865,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 }
                 xv[3 * D] = gb;
                 // the token's query slot is dead: it takes gv
-                store_vec<M>(reinterpret_cast<TIn *>(tile + Tl::oQ) + (tau * 32 + lane) * M, ge);
+                line_store<M, TIn>(tile + Tl::oQ, lane, tau, ge);
                 const int xs = static_cast<int>(ntok % kXSlots);
                 if (ntok >= kXSlots) {
                     mbar_wait(xempty + xs, static_cast<uint32_t>(((ntok - kXSlots) / kXSlots) & 1));
@@ -1839,8 +1880,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             __syncwarp();
             if (lane == 0) {
                 if (chain0 < A.n) {
-                    tma_store_3d(&mp.gq, 0, chain0, t0, tile + Tl::oV);
-                    tma_store_3d(&mp.gv, 0, chain0, t0, tile + Tl::oQ);
+                    tma_store_2d(&mp.gq, t0 * D, chain0, tile + Tl::oV);
+                    tma_store_2d(&mp.gv, t0 * M, chain0, tile + Tl::oQ);
                 }
                 bulk_commit();
                 bulk_wait_read<0>();
@@ -1883,18 +1924,21 @@ constexpr CUtensorMapDataType dtype_of() {
     return sizeof(T) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
 }
 
-// Token-major map of a [N, T, rowelems] tensor: dims (row, chain, token),
-// box (row, 32 chains, kS tokens).
+// Line map of a [N, T, rowelems] tensor: dims (row x token, chain), box
+// (kS rows, 32 chains), swizzled with the line's span.
 template <typename T>
 bool map_tok(CUtensorMap *m, const T *base, int rowelems, long n, long t) {
     if (base == nullptr) return true;
     const cuuint64_t es = sizeof(T);
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(rowelems), static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(t)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(t) * rowelems * es, rowelems * es};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(rowelems), 32, kS};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    return encode_fn()(m, dtype_of<T>(), 3, const_cast<T *>(base), dims, strides, box, estr,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+    const long span = static_cast<long>(kS) * rowelems * static_cast<long>(es);
+    if (span != 64 && span != 128) return false;
+    const CUtensorMapSwizzle sw = span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rowelems) * t, static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(t) * rowelems * es};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(rowelems * kS), 32};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode_fn()(m, dtype_of<T>(), 2, const_cast<T *>(base), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 // Map of a [n, w] float tensor: dims (column, row), box (bw columns, bh rows).
