@@ -292,12 +292,15 @@ __device__ __forceinline__ void cov_step(float (&P)[tri_size(D)], const float (&
 #pragma unroll
     for (int j = 0; j < D; ++j) s = fmaf(k[j], u[j], s);
     beta = 1.0f / (s < floor_ ? floor_ : s);  // clamp_min: NaN stays NaN
+    float nbu[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) nbu[i] = -beta * u[i];
 #pragma unroll
     for (int i = 0; i < D; ++i)
 #pragma unroll
         for (int j = i; j < D; ++j) {
             const int t = tri_index(D, i, j);
-            const float upd = fmaf(-beta, u[i] * u[j], (a[i] * a[j]) * P[t]);
+            const float upd = fmaf(nbu[i], u[j], (a[i] * a[j]) * P[t]);
             P[t] = (i == j) ? upd + p : upd;
         }
 }
@@ -1279,16 +1282,19 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
                 gk[i] = fmaf(-a[i], pk[i], fmaf(gs, u[i], gk3));
             }
             float gaP[D];
+            float hg[D];  // gu / 2
 #pragma unroll
-            for (int i = 0; i < D; ++i) gaP[i] = 0.f;
+            for (int i = 0; i < D; ++i) {
+                gaP[i] = 0.f;
+                hg[i] = 0.5f * gu[i];
+            }
 #pragma unroll
             for (int i = 0; i < D; ++i)
 #pragma unroll
                 for (int j = i; j < D; ++j) {
                     const int t = tri_index(D, i, j);
-                    // S = R + sym(gu k^T): rounded products and sum, never contracted
-                    const float x = __fadd_rn(__fmul_rn(gu[i], k[j]), __fmul_rn(gu[j], k[i]));
-                    const float S = fmaf(0.5f, x, Rp[t]);
+                    // S = R + sym(gu k^T), upper triangle
+                    const float S = i == j ? fmaf(gu[i], k[i], Rp[t]) : fmaf(hg[i], k[j], fmaf(hg[j], k[i], Rp[t]));
                     if constexpr (NEED_DYN) {
                         const float w = S * Pp[t];
                         gaP[i] = fmaf(w, a[j], gaP[i]);
@@ -1458,12 +1464,15 @@ struct SplitGeo {
 template <int D>
 __device__ __forceinline__ void cov_update(float (&P)[tri_size(D)], const float (&a)[D], float p,
                                            const float (&u)[D], float beta) {
+    float nbu[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) nbu[i] = -beta * u[i];
 #pragma unroll
     for (int i = 0; i < D; ++i)
 #pragma unroll
         for (int j = i; j < D; ++j) {
             const int t = tri_index(D, i, j);
-            const float upd = fmaf(-beta, u[i] * u[j], (a[i] * a[j]) * P[t]);
+            const float upd = fmaf(nbu[i], u[j], (a[i] * a[j]) * P[t]);
             P[t] = (i == j) ? upd + p : upd;
         }
 }
@@ -1669,15 +1678,20 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                     gk[i] = fmaf(-a[i], xv[D + i], fmaf(gs, u[i], gk3));
                 }
                 float gaP[D];
+                float hg[D];  // gu / 2
 #pragma unroll
-                for (int i = 0; i < D; ++i) gaP[i] = 0.f;
+                for (int i = 0; i < D; ++i) {
+                    gaP[i] = 0.f;
+                    hg[i] = 0.5f * gu[i];
+                }
 #pragma unroll
                 for (int i = 0; i < D; ++i)
 #pragma unroll
                     for (int j = i; j < D; ++j) {
                         const int t = tri_index(D, i, j);
-                        const float x = __fadd_rn(__fmul_rn(gu[i], k[j]), __fmul_rn(gu[j], k[i]));
-                        const float S = fmaf(0.5f, x, Rp[t]);
+                        // S = R + sym(gu k^T), upper triangle
+                        const float S =
+                            i == j ? fmaf(gu[i], k[i], Rp[t]) : fmaf(hg[i], k[j], fmaf(hg[j], k[i], Rp[t]));
                         if constexpr (NEED_DYN) {
                             const float w = S * Pp[t];
                             gaP[i] = fmaf(w, a[j], gaP[i]);
