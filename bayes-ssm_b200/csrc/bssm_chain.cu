@@ -197,6 +197,51 @@ __device__ __forceinline__ void line_store(char *region, int c, int tau, const f
     for (int h = 0; h < RB / 16; ++h) sts_chunk(reinterpret_cast<T *>(region + line_off<RB>(c, tau, h)), v + h * EC);
 }
 
+// A lane's replay state as float quads: quad x at +128 x floats, both in the
+// global state part (from replay_state_base) and in a group's state box
+// [SF / 4][32 chains][4] (from box + 4 lane).
+template <int D, int M>
+struct StateQuads {
+    static constexpr int SF = replay_state_floats(D, M), DM = D * M, TRI = tri_size(D);
+    static_assert(DM % 4 == 0, "mean in whole quads");
+    __device__ __forceinline__ static void put_mean(float *dst, const float (&Mm)[D][M]) {
+#pragma unroll
+        for (int f = 0; f < DM; f += 4)
+            *reinterpret_cast<float4 *>(dst + f * 32) =
+                make_float4(Mm[f / M][f % M], Mm[(f + 1) / M][(f + 1) % M], Mm[(f + 2) / M][(f + 2) % M],
+                            Mm[(f + 3) / M][(f + 3) % M]);
+    }
+    __device__ __forceinline__ static void put_cov(float *dst, const float (&P)[TRI]) {
+#pragma unroll
+        for (int f = 0; f < SF - DM; f += 4) {
+            float x[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) x[e] = f + e < TRI ? P[f + e] : 0.f;
+            *reinterpret_cast<float4 *>(dst + (DM + f) * 32) = make_float4(x[0], x[1], x[2], x[3]);
+        }
+    }
+    __device__ __forceinline__ static void get_mean(const float *src, float (&Mm)[D][M]) {
+#pragma unroll
+        for (int f = 0; f < DM; f += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(src + f * 32);
+            Mm[f / M][f % M] = v.x;
+            Mm[(f + 1) / M][(f + 1) % M] = v.y;
+            Mm[(f + 2) / M][(f + 2) % M] = v.z;
+            Mm[(f + 3) / M][(f + 3) % M] = v.w;
+        }
+    }
+    __device__ __forceinline__ static void get_cov(const float *src, float (&P)[TRI]) {
+#pragma unroll
+        for (int f = 0; f < SF - DM; f += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(src + (DM + f) * 32);
+            const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (f + e < TRI) P[f + e] = x[e];
+        }
+    }
+};
+
 // Shared-memory geometry of one warp's tile (one stage): line boxes of the
 // token tensors, [chain][tau] boxes of the noise.
 template <int D, int M, bool FIXED, bool BWD, typename TIn>
@@ -486,15 +531,11 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
             }
         }
         if (cons.j != 0 && A.rs != nullptr && active) {
-            // the state, float by float: each store of the warp is one
-            // contiguous line of the structure-of-arrays layout
-            const long base = replay_state_base(chain, nb, rs_slots, ci, cons.j, SF);
-#pragma unroll
-            for (int i = 0; i < D; ++i)
-#pragma unroll
-                for (int c = 0; c < M; ++c) A.rs[base + static_cast<long>(i * M + c) * 32] = Mm[i][c];
-#pragma unroll
-            for (int t = 0; t < TRI; ++t) A.rs[base + static_cast<long>(D * M + t) * 32] = P[t];
+            // the state, quad by quad: each store of the warp is one
+            // contiguous 512-byte line of the state part
+            float *const dst = A.rs + replay_state_base(chain, nb, rs_slots, ci, cons.j, SF);
+            StateQuads<D, M>::put_mean(dst, Mm);
+            StateQuads<D, M>::put_cov(dst, P);
         }
         char *const yb = ob + G::yY;
         const bool gains = A.rs != nullptr;
@@ -679,9 +720,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 if (cons.j == 0) {
                     store_cov_full<D>(bc + ci * D * D, P);
                 } else if (A.rs != nullptr) {
-                    const long base = replay_state_base(chain, nb, rs_slots, ci, cons.j, SF);
-#pragma unroll
-                    for (int t = 0; t < TRI; ++t) A.rs[base + static_cast<long>(D * M + t) * 32] = P[t];
+                    StateQuads<D, M>::put_cov(A.rs + replay_state_base(chain, nb, rs_slots, ci, cons.j, SF), P);
                 }
             }
             // gains block q & 1: free once the mean warp read tile q-2's gains
@@ -761,11 +800,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 if (cons.j == 0) {
                     store_mean<D, M>(bm + ci * D * M, Mm);
                 } else if (A.rs != nullptr) {
-                    const long base = replay_state_base(chain, nb, rs_slots, ci, cons.j, SF);
-#pragma unroll
-                    for (int i = 0; i < D; ++i)
-#pragma unroll
-                        for (int c = 0; c < M; ++c) A.rs[base + static_cast<long>(i * M + c) * 32] = Mm[i][c];
+                    StateQuads<D, M>::put_mean(A.rs + replay_state_base(chain, nb, rs_slots, ci, cons.j, SF), Mm);
                 }
             }
             char *yb;
@@ -963,7 +998,7 @@ template <int D, int M, bool FIXED, typename TIn>
 struct BwdGeo {
     using Tl = Tile<D, M, FIXED, true, TIn>;
     static constexpr int SF = replay_state_floats(D, M);
-    static constexpr int kSB = 32 * SF * 4;  // a warp's start states, box layout [chain][SF]
+    static constexpr int kSB = 32 * SF * 4;  // a warp's start states, box layout [SF / 4][chain][4]
     // a warp's gradient rows of one sub-chunk: keys, values, queries, decay
     // as line boxes (whole KB each); process, observation [chain][tau]
     static constexpr int rbK = Tl::rbK, rbV = Tl::rbV;
@@ -994,21 +1029,23 @@ __device__ __forceinline__ void put_row(char *region, int c, int tau, T *gdst, c
 
 // Copy a sub-chunk's start state from a boundary checkpoint (full
 // covariance, by its upper triangle) into this thread's state row.
-// (The state box is [float][32 chains]: this thread's float f at sdst + 128 f.)
+// (The state box is [SF / 4][32 chains][4]: this thread's float f at
+// sdst + 4 rs_at(0, f).)
 template <int D, int M>
 __device__ __forceinline__ void issue_checkpoint(uint32_t sdst, const float *ck_mean, const float *ck_cov) {
 #pragma unroll
-    for (int x = 0; x < D * M; ++x) cp_async<4>(sdst + 128 * x, ck_mean + x);
+    for (int x = 0; x < D * M; ++x) cp_async<4>(sdst + 4 * rs_at(0, x), ck_mean + x);
 #pragma unroll
     for (int i = 0; i < D; ++i)
 #pragma unroll
-        for (int j = i; j < D; ++j) cp_async<4>(sdst + 128 * (D * M + tri_index(D, i, j)), ck_cov + i * D + j);
+        for (int j = i; j < D; ++j)
+            cp_async<4>(sdst + 4 * rs_at(0, D * M + tri_index(D, i, j)), ck_cov + i * D + j);
 }
 
-// First row of a group's state (ci, j) in the [rows][32 chains] view of the
-// structure-of-arrays state part.
+// First row of a group's state (ci, j) in the [rows][32 chains x 4] view of
+// the quad-interleaved state part.
 __device__ __forceinline__ int state_row(int chain0, long nb, long slots, long ci, long j, int sf) {
-    return static_cast<int>((((static_cast<long>(chain0) >> 5) * nb + ci) * slots + (j - 1)) * sf);
+    return static_cast<int>((((static_cast<long>(chain0) >> 5) * nb + ci) * slots + (j - 1)) * (sf / 4));
 }
 
 template <int D, int M, bool FIXED, bool NEED_DYN, bool NEED_INIT, typename TIn>
@@ -1031,14 +1068,14 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
     const bool has_gy = A.gy != nullptr;
     char *const tiles = smem + G::oT + warp * Tl::kBytes;  // + stage * G::kPerStage
     float *const sbox = reinterpret_cast<float *>(smem + G::oS + warp * G::kSB);  // [SF][32 chains]
-    float *const state = sbox + lane;                                             // float f at [32 f]
+    float *const state = sbox + 4 * lane;                                         // quads at +128 x
     char *const out = smem + G::oO + warp * G::kOB;
     uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + warp * 2;
     uint32_t *const slot = reinterpret_cast<uint32_t *>(smem + G::oSlot);
     const float *const bm = A.bmean + chain * (nb + 1) * D * M;
     const float *const bc = A.bcov + chain * (nb + 1) * D * D;
 
-    for (int x = 0; x < SF; ++x) state[x * 32] = 0.f;  // idle lanes replay finite zeros
+    for (int x = 0; x < SF; ++x) state[rs_at(0, x)] = 0.f;  // idle lanes replay finite zeros
     if (lane == 0) {
         mbar_init(bars, 1);
         mbar_init(bars + 1, 1);
@@ -1110,8 +1147,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
         // ---- covariance pass: pre-step covariance, gain, beta and s per token
         {
             float P[TRI];
-#pragma unroll
-            for (int t = 0; t < TRI; ++t) P[t] = state[(D * M + t) * 32];
+            StateQuads<D, M>::get_cov(state, P);
             auto cstep = [&](int tau) {
                 float k[D], a[D], u[D], bs[2];
                 rd.keys(tau, k);
@@ -1128,10 +1164,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
         // ---- mean pass: pre-step mean and innovation per token; gq = M' gy
         {
             float Mm[D][M];
-#pragma unroll
-            for (int i = 0; i < D; ++i)
-#pragma unroll
-                for (int c = 0; c < M; ++c) Mm[i][c] = state[(i * M + c) * 32];
+            StateQuads<D, M>::get_mean(state, Mm);
             // every lane has read its start state and is done with the other
             // stage: fetch the next sub-chunk while this one is processed
             __syncwarp();
@@ -1448,7 +1481,7 @@ struct SplitGeo {
     static constexpr int oU = Tl::kBytes, oB = oU + kS * 32 * D * 4;
     static constexpr int kTileBytes = al1024(oB + 32 * kS * 4);
     static constexpr int kTx = Tl::kTx + kS * 32 * D * 4 + 32 * kS * 4;  // without gy, without state
-    static constexpr int kSB = 32 * SF * 4;  // a group's start states [chain][SF]
+    static constexpr int kSB = 32 * SF * 4;  // a group's start states [SF / 4][chain][4]
     static constexpr int kPerStage = 4 * kTileBytes;
     static constexpr int oT = 0;                        // [stage][group][tile]
     static constexpr int oSt = oT + 2 * kPerStage;      // [group][kSB]
@@ -1500,7 +1533,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     const bool has_gy = A.gy != nullptr;
     char *const tiles = smem + G::oT + grp * G::kTileBytes;  // + stage * G::kPerStage
     float *const sbox = reinterpret_cast<float *>(smem + G::oSt + grp * G::kSB);  // [SF][32 chains]
-    float *const state = sbox + lane;                                              // float f at [32 f]
+    float *const state = sbox + 4 * lane;                                          // quads at +128 x
     uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + G::oBar) + grp * G::kBars;
     uint64_t *const full = bars, *const empty = bars + 2, *const sfree = bars + 4;
     uint64_t *const xfull = bars + 5, *const xempty = bars + 5 + kXSlots;
@@ -1509,7 +1542,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     const float *const bc = A.bcov + chain * (nb + 1) * D * D;
 
     if (cov_warp) {
-        for (int x = 0; x < SF; ++x) state[x * 32] = 0.f;  // idle lanes replay finite zeros
+        for (int x = 0; x < SF; ++x) state[rs_at(0, x)] = 0.f;  // idle lanes replay finite zeros
         if (lane == 0) {
             mbar_init(full, 1);
             mbar_init(full + 1, 1);
@@ -1552,17 +1585,17 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     };
     auto issue_checkpoint_part = [&](const BwdItems &it) {
         if (it.j > 0 || !active) return;
-        const uint32_t s = smem_u32(state);  // float f at s + 128 f
+        const uint32_t s = smem_u32(state);  // float f at s + 4 rs_at(0, f)
         if (cov_warp) {
             const float *ck = bc + it.ci * D * D;
 #pragma unroll
             for (int i = 0; i < D; ++i)
 #pragma unroll
-                for (int j = i; j < D; ++j) cp_async<4>(s + 128 * (D * M + tri_index(D, i, j)), ck + i * D + j);
+                for (int j = i; j < D; ++j) cp_async<4>(s + 4 * rs_at(0, D * M + tri_index(D, i, j)), ck + i * D + j);
         } else {
             const float *ck = bm + it.ci * D * M;
 #pragma unroll
-            for (int x = 0; x < D * M; ++x) cp_async<4>(s + 128 * x, ck + x);
+            for (int x = 0; x < D * M; ++x) cp_async<4>(s + 4 * rs_at(0, x), ck + x);
         }
     };
     // token tau's gain and scalars from the tile
@@ -1606,8 +1639,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             rd.noise(p4, r4);
             const float4 b4 = reinterpret_cast<const float4 *>(tile + G::oB)[lane];
             float P[TRI];
-#pragma unroll
-            for (int t = 0; t < TRI; ++t) P[t] = state[(D * M + t) * 32];
+            StateQuads<D, M>::get_cov(state, P);
             __syncwarp();
             if (lane == 0) mbar_arrive(sfree);
             if (!nxt.done) issue_checkpoint_part(nxt);  // this warp's part of the row is read
@@ -1768,10 +1800,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             const int t0 = static_cast<int>(cur.t0());
             const float4 b4 = reinterpret_cast<const float4 *>(tile + G::oB)[lane];
             float Mm[D][M];
-#pragma unroll
-            for (int i = 0; i < D; ++i)
-#pragma unroll
-                for (int c = 0; c < M; ++c) Mm[i][c] = state[(i * M + c) * 32];
+            StateQuads<D, M>::get_mean(state, Mm);
             __syncwarp();
             if (lane == 0) mbar_arrive(sfree);
             if (!nxt.done) {
@@ -2032,13 +2061,13 @@ int launch_bwd(const BwdArgs<TIn> &a, cudaStream_t st) {
     BwdMaps mp;
     std::memset(&mp, 0, sizeof(mp));
     const long nb = (a.t + a.chunks - 1) / a.chunks;
-    const long W = replay_state_part(a.n, a.t, a.chunks, D, M) / 32;  // rows of 32 chains
+    const long W = replay_state_part(a.n, a.t, a.chunks, D, M) / 128;  // rows of 32 chains x 4
     bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
               map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.gy, a.gy, M, a.n, a.t);
     if (!FIXED)
         ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
              map_rows(&mp.r, a.observation, a.t, a.n, kS);
-    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, 32, W, 32, replay_state_floats(D, M));
+    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, 128, W, 128, replay_state_floats(D, M) / 4);
     if (G::kStageOut) {
         ok = ok && map_tok(&mp.gk, a.gk, D, a.n, a.t) && map_tok(&mp.gv, a.gv, M, a.n, a.t) &&
              map_tok(&mp.gq, a.gq, D, a.n, a.t);
@@ -2071,13 +2100,13 @@ int launch_split(const BwdArgs<TIn> &a, cudaStream_t st) {
     BwdMaps mp;
     std::memset(&mp, 0, sizeof(mp));
     const long nb = (a.t + a.chunks - 1) / a.chunks;
-    const long W = replay_state_part(a.n, a.t, a.chunks, D, M) / 32;  // rows of 32 chains
+    const long W = replay_state_part(a.n, a.t, a.chunks, D, M) / 128;  // rows of 32 chains x 4
     bool ok = map_tok(&mp.k, a.keys, D, a.n, a.t) && map_tok(&mp.q, a.queries, D, a.n, a.t) &&
               map_tok(&mp.v, a.values, M, a.n, a.t) && map_tok(&mp.gy, a.gy, M, a.n, a.t) &&
               map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
               map_rows(&mp.r, a.observation, a.t, a.n, kS) && map_tok(&mp.gk, a.gk, D, a.n, a.t) &&
               map_tok(&mp.gv, a.gv, M, a.n, a.t) && map_tok(&mp.gq, a.gq, D, a.n, a.t);
-    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, 32, W, 32, replay_state_floats(D, M));
+    if (a.rs != nullptr && W > 0) ok = ok && map_rows(&mp.rs, a.rs, 128, W, 128, replay_state_floats(D, M) / 4);
     if (NEED_DYN)
         ok = ok && map_tok(&mp.ga, a.ga, D, a.n, a.t) && map_rows(&mp.gp, a.gp, a.t, a.n, kS) &&
              map_rows(&mp.gr, a.gr, a.t, a.n, kS);

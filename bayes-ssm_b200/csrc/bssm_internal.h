@@ -47,10 +47,11 @@ struct BwdArgs {
 // is the boundary checkpoint).  A state is [mean D*M row-major | covariance
 // upper triangle, row by row (tri_index) | pad] (the covariance is exactly
 // symmetric in every kernel family, so its upper triangle is the whole
-// state).  States are stored as a structure of arrays over groups of 32
-// chains: float f of state (chunk ci, slot j) of chain c is at
-//     ((((c / 32) * nb + ci) * slots + j - 1) * SF + f) * 32 + c % 32,
-// so float f of a group's 32 chains is one contiguous 128-byte line.
+// state).  States are stored as a structure of arrays of float quads over
+// groups of 32 chains: float f of state (chunk ci, slot j) of chain c is at
+//     (((((c / 32) * nb + ci) * slots + j - 1) * SF / 4 + f / 4) * 32 + c % 32) * 4 + f % 4,
+// so quad f / 4 of a group's 32 chains is one contiguous 512-byte line: a
+// warp moves it with one 16-byte access per lane.
 constexpr int kReplaySpan = 4;
 
 // Position of covariance entry (i, j) in the row-by-row upper triangle.
@@ -67,10 +68,12 @@ __host__ __device__ inline long replay_slots_per_chunk(long t, int chunks) {
 // Floats per state, a multiple of 4.
 __host__ __device__ constexpr int replay_state_floats(int d, int m) { return (d * m + tri_size(d) + 3) / 4 * 4; }
 __host__ __device__ inline long replay_groups(long n) { return (n + 31) / 32; }
-// Index of float 0 of chain `chain`'s state (ci, j >= 1); float f is at +32 f.
+// Index of float 0 of chain `chain`'s state (ci, j >= 1); float f is at
+// rs_at(base, f).
 __host__ __device__ inline long replay_state_base(long chain, long nb, long slots, long ci, long j, int sf) {
-    return ((((chain >> 5) * nb + ci) * slots + (j - 1)) * sf) * 32 + (chain & 31);
+    return (((((chain >> 5) * nb + ci) * slots + (j - 1)) * (sf / 4)) * 32 + (chain & 31)) * 4;
 }
+__host__ __device__ constexpr long rs_at(long base, int f) { return base + (f >> 2) * 128 + (f & 3); }
 // Floats of the state part of the buffer.
 __host__ __device__ inline long replay_state_part(long n, long t, int chunks, int d, int m) {
     const long nb = (t + chunks - 1) / chunks;
@@ -84,25 +87,25 @@ __device__ __forceinline__ void rs_put_mean_cols(float *rs, long base, int col0,
 #pragma unroll
     for (int i = 0; i < D; ++i)
 #pragma unroll
-        for (int l = 0; l < CPL; ++l) rs[base + static_cast<long>(i * M + col0 + l) * 32] = Mc[l][i];
+        for (int l = 0; l < CPL; ++l) rs[rs_at(base, i * M + col0 + l)] = Mc[l][i];
 }
 template <int D, int M, int CPL>
 __device__ __forceinline__ void rs_get_mean_cols(const float *rs, long base, int col0, float (&Mc)[CPL][D]) {
 #pragma unroll
     for (int i = 0; i < D; ++i)
 #pragma unroll
-        for (int l = 0; l < CPL; ++l) Mc[l][i] = rs[base + static_cast<long>(i * M + col0 + l) * 32];
+        for (int l = 0; l < CPL; ++l) Mc[l][i] = rs[rs_at(base, i * M + col0 + l)];
 }
 template <int D, int M>
 __device__ __forceinline__ void rs_put_row(float *rs, long base, int row, const float (&v)[D]) {
 #pragma unroll
     for (int j = 0; j < D; ++j)
-        if (j >= row) rs[base + static_cast<long>(D * M + tri_index(D, row, j)) * 32] = v[j];
+        if (j >= row) rs[rs_at(base, D * M + tri_index(D, row, j))] = v[j];
 }
 template <int D, int M>
 __device__ __forceinline__ void rs_get_row(const float *rs, long base, int row, float (&v)[D]) {
 #pragma unroll
-    for (int j = 0; j < D; ++j) v[j] = rs[base + static_cast<long>(D * M + tri_index(D, row, j)) * 32];
+    for (int j = 0; j < D; ++j) v[j] = rs[rs_at(base, D * M + tri_index(D, row, j))];
 }
 
 // After the states, the replay buffer holds every token's gain u [N][T][D]

@@ -749,12 +749,12 @@ __global__ void __launch_bounds__(32) backward_staged(const BwdArgs<TIn> A) {
                 for (int x = 0; x < D; ++x)
 #pragma unroll
                     for (int l = 0; l < CPL; ++l)
-                        Mc[l][x] = A.rs[base + static_cast<long>(lane_row<D, LPC>(x, sub) * M + col0 + l) * 32];
+                        Mc[l][x] = A.rs[rs_at(base, lane_row<D, LPC>(x, sub) * M + col0 + l)];
 #pragma unroll
                 for (int r = 0; r < RPL; ++r)
 #pragma unroll
                     for (int x = 0; x < D; ++x)
-                        P[r][x] = A.rs[base + static_cast<long>(D * M + tri_index(D, row0 + r, lane_row<D, LPC>(x, sub))) * 32];
+                        P[r][x] = A.rs[rs_at(base, D * M + tri_index(D, row0 + r, lane_row<D, LPC>(x, sub)))];
             } else {
                 // written by this kernel in phase A: coherent loads
                 float flat[G::kWsLane];
