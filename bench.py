@@ -58,7 +58,7 @@ FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 # dram__bytes_write.sum) from an ncu capture of a quarter of this workload
 # (4,096 chains, one CTA per SM as in the full launch), scaled by 4: traffic
 # grows with the chains.  See profiles/backward_split_d8m8_bf16.md.
-NCU_BWD_TRAFFIC_BYTES = 4 * (540.64e6 + 162.54e6)
+NCU_BWD_TRAFFIC_BYTES = 4 * (540.62e6 + 164.73e6)
 # Canonical algorithmic figures per chain-step, FP32 at the reference ABI
 # (fwd + bwd): bytes 4 (9D + 5M + 6), flops 26D^2 + 34DM + 30D + 3M + 2.
 STEP_BYTES_F32 = 4 * (9 * D + 5 * M + 6)
