@@ -110,7 +110,7 @@ __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity) {
     atomicAdd(&g_wait_timeouts, 1u);
 }
 
-// ---- TMA tensor copies (no multicast) ------------------------------------------
+// ---- TMA tensor copies (this CTA's shared memory only) ----------------------
 __device__ __forceinline__ void tma_load_2d(void *sdst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
