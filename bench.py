@@ -182,6 +182,9 @@ def run_reference(args, rank: int) -> None:
     import numpy as np
     from oracle import oracle
 
+    # torchrun sets OMP_NUM_THREADS=1 per worker; this arm uses every host
+    # thread it may run on (set before the oracle library starts OpenMP)
+    oracle.set_threads(len(os.sched_getaffinity(0)))
     line = cpu_baseline_measure(steps=args.steps, warmup=args.warmup)
     value = line["value"]
     print(json.dumps({
