@@ -17,6 +17,8 @@ LIB_PATH = Path(os.environ.get("BAYES_SSM_B200_LIB", PKG_ROOT / "lib" / "libbaye
 BSSM_OK = 0
 BSSM_F32 = 0
 BSSM_BF16 = 1
+BSSM_F16 = 2
+CHECK_NONFINITE, CHECK_NOT_POSITIVE, CHECK_NEGATIVE = 1, 2, 4
 SUPPORTED = ((1, 8), (2, 8), (4, 8), (8, 8))
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -44,6 +46,7 @@ _SIGNATURES = {
     "bssm_assoc_scan_ex": ([_i, _i] + [_vp] * 10 + [_l, _l, _d, _vp], _i),
     "bssm_backward_noalloc_max_scratch_bytes": ([], _sz),
     "bssm_backward_chunked_noalloc": ([_i, _i, _i, _i, _i, _i] + [_vp] * 21 + [_l, _l, _i, _d, _vp], _i),
+    "bssm_check_values": ([_vp, _l, _i, _vp, _vp], _i),
     "bssm_debug_wait_timeouts": ([], ctypes.c_uint),
     "bssm_debug_last_family": ([], _i),
 }
@@ -141,6 +144,22 @@ def backward_chunked_noalloc(key_dim, value_dim, io_dtype, fixed, need_dynamics,
         ptr(bmean), ptr(bcov), ptr(gy), ptr(gmf), ptr(gcf), ptr(gk), ptr(gv), ptr(gq), ptr(gd),
         ptr(gp), ptr(gr), ptr(gm0), ptr(gc0), n, t, chunks, float(floor), stream)
     check(rc, "bssm_backward_chunked_noalloc")
+
+
+def check_values(tensors) -> list[int]:
+    """Flags (CHECK_*) of each contiguous CUDA tensor in ``tensors`` (float32,
+    bfloat16 or float16), from one pass per tensor on the current stream and
+    one read-back for all of them."""
+    import torch
+    codes = {torch.float32: BSSM_F32, torch.bfloat16: BSSM_BF16, torch.float16: BSSM_F16}
+    lib = load()
+    dev = tensors[0].device
+    flags = torch.zeros(len(tensors), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for i, x in enumerate(tensors):
+        check(lib.bssm_check_values(ptr(x), x.numel(), codes[x.dtype], flags.data_ptr() + 4 * i, stream),
+              "check_values")
+    return [int(f) for f in flags.tolist()]
 
 
 def wait_timeouts() -> int:

@@ -88,14 +88,62 @@ def _skip_host_checks(x: Tensor) -> bool:
     return torch.compiler.is_compiling() or _is_cuda_graph_capturing(x)
 
 
+_DEVICE_CHECK_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+
+
+def _device_flags(tensors) -> Optional[list]:
+    """Check flags of CUDA tensors from the library's one-pass check kernel
+    (one read-back for all of them), or None where the torch checks apply
+    (CPU or non-contiguous tensors, other dtypes, no library)."""
+    if not all(x.is_cuda and x.dtype in _DEVICE_CHECK_DTYPES and x.is_contiguous() for x in tensors):
+        return None
+    from . import _capi
+    try:
+        _capi.load()
+    except _capi.ExtensionUnavailable:
+        return None
+    return _capi.check_values([x.detach() for x in tensors])
+
+
+def _check_finite_many(pairs) -> None:
+    """_check_finite on each (tensor, name) in order: the first failure raises."""
+    pairs = [(x, name) for x, name in pairs if not _skip_host_checks(x)]
+    flags = _device_flags([x for x, _ in pairs]) if pairs else None
+    if flags is None:
+        for x, name in pairs:
+            _check_finite(x, name)
+        return
+    from ._capi import CHECK_NONFINITE
+    for (x, name), f in zip(pairs, flags):
+        if f & CHECK_NONFINITE:
+            raise ValueError(f"{name} must contain only finite values")
+
+
 def _check_finite(x: Tensor, name: str) -> None:
     if _skip_host_checks(x):
+        return
+    flags = _device_flags([x])
+    if flags is not None:
+        from ._capi import CHECK_NONFINITE
+        if flags[0] & CHECK_NONFINITE:
+            raise ValueError(f"{name} must contain only finite values")
         return
     if x.numel() and not bool(torch.isfinite(x).all()):
         raise ValueError(f"{name} must contain only finite values")
 
 
 def _validate_variance(x: Tensor, name: str, *, strictly_positive: bool) -> None:
+    if not _skip_host_checks(x):
+        flags = _device_flags([x])
+        if flags is not None:  # the same checks in the same order, one pass
+            from ._capi import CHECK_NEGATIVE, CHECK_NONFINITE, CHECK_NOT_POSITIVE
+            if flags[0] & CHECK_NONFINITE:
+                raise ValueError(f"{name} must contain only finite values")
+            if strictly_positive and flags[0] & CHECK_NOT_POSITIVE:
+                raise ValueError(f"{name} must be strictly positive")
+            if not strictly_positive and flags[0] & CHECK_NEGATIVE:
+                raise ValueError(f"{name} must be nonnegative")
+            return
     _check_finite(x, name)
     if _skip_host_checks(x) or x.numel() == 0:
         return
@@ -243,12 +291,15 @@ def bayesian_layer(
     # every other path sees the promoted FP32 tensors.
     all_bf16 = keys.dtype == values.dtype == queries.dtype == torch.bfloat16
     raw_keys, raw_values, raw_queries = keys, values, queries
-    keys = keys.to(dtype)
-    values = values.to(dtype)
-    queries = queries.to(dtype)
-    _check_finite(keys, "keys")
-    _check_finite(values, "values")
-    _check_finite(queries, "queries")
+    # FP32 / BF16 / FP16 projections are checked as they are and widened only
+    # where a path needs FP32 (widening keeps every value and its finiteness);
+    # other low-precision dtypes are promoted first, as the reference does
+    # (bayesian_layer.py:823-830).
+    if not all(x.dtype in _DEVICE_CHECK_DTYPES for x in (keys, values, queries)):
+        keys = keys.to(dtype)
+        values = values.to(dtype)
+        queries = queries.to(dtype)
+    _check_finite_many(((keys, "keys"), (values, "values"), (queries, "queries")))
     if (rotation_radii is None) != (rotation_angles is None):
         raise ValueError("rotation_radii and rotation_angles must be supplied together")
     if transitions is not None and transition_diagonals is not None:
@@ -425,8 +476,9 @@ def bayesian_layer(
             transitions = eye.expand(*batch_shape, t, d, d)
         if process_covariances is None:
             process_covariances = process_variances[..., None, None] * eye
-    return _dense_recurrence(keys, values, queries, transitions, process_covariances,
-                             observation_variances, mean, covariance, float(denominator_floor))
+    return _dense_recurrence(keys.to(dtype), values.to(dtype), queries.to(dtype), transitions,
+                             process_covariances, observation_variances, mean, covariance,
+                             float(denominator_floor))
 
 
 class BayesianLayer(nn.Module):

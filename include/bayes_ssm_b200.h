@@ -45,6 +45,7 @@ extern "C" {
 
 #define BSSM_F32 0
 #define BSSM_BF16 1
+#define BSSM_F16 2 /* bssm_check_values only */
 
 /* Message for the last failing call on this thread ("" after success). */
 const char *bssm_last_error(void);
@@ -260,6 +261,21 @@ int bssm_backward_chunked_noalloc(int key_dim, int value_dim, int io_dtype, int 
                                   float *grad_mean0, float *grad_cov0,
                                   long n, long t, int chunks, double denominator_floor,
                                   void *stream);
+
+/*
+ * Input checks of bayesian_layer in one pass (replaces the torch.isfinite(x)
+ * .all() and x.min() validation of bayes_ssm/bayesian_layer.py:105-128).
+ *
+ * Reads n elements of x (BSSM_F32, BSSM_BF16 or BSSM_F16) once on `stream`
+ * and ORs into the device word *flags: BSSM_CHECK_NONFINITE if any element
+ * is NaN or infinite, BSSM_CHECK_NOT_POSITIVE if any is <= 0,
+ * BSSM_CHECK_NEGATIVE if any is < 0.  The caller zeroes *flags first and
+ * reads it back (after the stream has run) to raise its own errors.
+ */
+#define BSSM_CHECK_NONFINITE 1u
+#define BSSM_CHECK_NOT_POSITIVE 2u
+#define BSSM_CHECK_NEGATIVE 4u
+int bssm_check_values(const void *x, long n, int dtype, unsigned *flags, void *stream);
 
 /*
  * Diagnostics (no counterpart in the reference).

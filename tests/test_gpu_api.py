@@ -171,3 +171,64 @@ def test_assoc_scan_rejects_small_variance_on_gpu():
     with pytest.raises(ValueError, match="denominator_floor"):
         bayes_ssm.associative_static_bayesian_cuda(k, torch.randn(2, 8, 3, device="cuda"), k,
                                                    observation_variances=r)
+
+
+@pytest.mark.parametrize("dtype", (torch.float32, torch.bfloat16, torch.float16))
+def test_check_values_flags_match_torch(dtype):
+    """The one-pass input check (C ABI) agrees with torch's isfinite / sign
+    tests, on aligned and unaligned views and ragged lengths."""
+    from bayes_ssm import _capi
+    base = (torch.rand(1003, device="cuda") + 0.5).to(dtype)
+
+    def want(x):
+        xf = x.float()
+        return ((_capi.CHECK_NONFINITE if bool((~torch.isfinite(xf)).any()) else 0)
+                | (_capi.CHECK_NOT_POSITIVE if bool((xf <= 0).any()) else 0)
+                | (_capi.CHECK_NEGATIVE if bool((xf < 0).any()) else 0))
+
+    for pos, val in ((None, None), (3, float("nan")), (1002, float("inf")), (500, 0.0), (7, -1.0),
+                     (64, float("-inf")), (0, -0.0)):
+        x = base.clone()
+        if pos is not None:
+            x[pos] = val
+        views = (x, x[1:], x[:997], x[5:13], x[:0])
+        got = _capi.check_values(list(views))
+        assert got == [want(v) for v in views], (pos, val, got)
+
+
+@pytest.mark.parametrize("dtype", (torch.float32, torch.bfloat16, torch.float16))
+def test_api_validation_errors_on_gpu(dtype):
+    """CUDA inputs raise the reference's validation errors, first failing
+    check first (keys before values, finiteness before sign)."""
+    import bayes_ssm
+    inp = make_inputs(4, 12, 4, 8, seed=9)
+    base = {k: (None if v is None else v.cuda()) for k, v in inp.items()}
+    for key in ("k", "v", "q"):
+        base[key] = base[key].to(dtype)
+
+    def call(**over):
+        x = {**base, **over}
+        return bayes_ssm.bayesian_layer(x["k"], x["v"], x["q"], transition_diagonals=x["a"],
+                                        process_variances=x["p"], observation_variances=x["r"],
+                                        chunk_length=4, optimized=True)
+
+    def poked(name, value, idx=(1, 2)):
+        t = base[name].clone()
+        t[idx] = value
+        return t
+
+    call()
+    with pytest.raises(ValueError, match="^keys must contain only finite values$"):
+        call(k=poked("k", float("nan")), v=poked("v", float("inf")))
+    with pytest.raises(ValueError, match="^values must contain only finite values$"):
+        call(v=poked("v", float("inf")))
+    with pytest.raises(ValueError, match="^queries must contain only finite values$"):
+        call(q=poked("q", float("-inf")))
+    with pytest.raises(ValueError, match="^transition_diagonals must contain only finite values$"):
+        call(a=poked("a", float("nan")))
+    with pytest.raises(ValueError, match="^process_variances must be nonnegative$"):
+        call(p=poked("p", -1e-3))
+    with pytest.raises(ValueError, match="^process_variances must contain only finite values$"):
+        call(p=poked("p", float("nan")))
+    with pytest.raises(ValueError, match="^observation_variances must be strictly positive$"):
+        call(r=poked("r", 0.0))
