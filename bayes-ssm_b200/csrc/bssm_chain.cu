@@ -147,20 +147,24 @@ struct BwdMaps {
 // ---- Line layout -------------------------------------------------------------
 // Token tensors [N, T, row] travel as line boxes: for each of 32 consecutive
 // chains, the kS rows of tokens [t0, t0 + kS) form one line of
-// L = kS * rowbytes bytes (64 or 128), contiguous in global memory, so TMA
-// moves one segment per chain.  TMA writes (and reads back) a box with the
-// swizzle of span L: the 16-byte chunk x of chain c's line sits at chunk
-// x ^ s(c), with s(c) = (c >> 1) & 3 for L = 64 and c & 7 for L = 128 (bits
-// [4, ..) of the offset in a 1024-byte aligned region XOR bits [7, ..)).  A
-// warp's 16-byte accesses to one row of its 32 chains then fall in distinct
-// banks within each quarter warp.
-template <int RB>
-__device__ __forceinline__ int line_off(int c, int tau, int h) {
-    static_assert(RB == 16 || RB == 32, "row bytes");
-    if constexpr (RB == 16) {
-        return c * 64 + ((tau ^ ((c >> 1) & 3)) << 4);
+// L = kS * rowbytes bytes (16, 32, 64 or 128), contiguous in global memory,
+// so TMA moves one segment per chain.  TMA writes (and reads back) a box with
+// the swizzle of span L: the 16-byte chunk x of chain c's line sits at chunk
+// x ^ s(c), with s(c) = (c >> 2) & 1, (c >> 1) & 3 and c & 7 for L = 32, 64
+// and 128 (bits [4, ..) of the offset in a 1024-byte aligned region XOR bits
+// [7, ..)); 16-byte lines are not swizzled.  A warp's 16-byte accesses to one
+// chunk of its 32 chains then fall in distinct banks within each quarter warp.
+template <int L>
+__device__ __forceinline__ int line_chunk(int c, int x) {
+    static_assert(L == 16 || L == 32 || L == 64 || L == 128, "line span");
+    if constexpr (L == 16) {
+        return c * 16;
+    } else if constexpr (L == 32) {
+        return c * 32 + ((x ^ ((c >> 2) & 1)) << 4);
+    } else if constexpr (L == 64) {
+        return c * 64 + ((x ^ ((c >> 1) & 3)) << 4);
     } else {
-        return c * 128 + (((2 * tau + h) ^ (c & 7)) << 4);
+        return c * 128 + ((x ^ (c & 7)) << 4);
     }
 }
 
@@ -177,24 +181,68 @@ __device__ __forceinline__ void sts_chunk(__nv_bfloat16 *p, const float *x) {
     }
     *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
 }
+__device__ __forceinline__ uint32_t word_of(const uint4 &w, int i) {
+    return i == 0 ? w.x : i == 1 ? w.y : i == 2 ? w.z : w.w;
+}
 
-// Row tau (N elements of T) of chain c, from or to a line region.
+// Row tau (N elements of T) of chain c, from or to a line region.  Rows of
+// 16 bytes or more are whole chunks; shorter rows (4 or 8 bytes) are words of
+// one chunk.
 template <int N, typename T>
 __device__ __forceinline__ void line_load(const char *region, int c, int tau, float (&o)[N]) {
-    constexpr int RB = N * static_cast<int>(sizeof(T)), EC = 16 / static_cast<int>(sizeof(T));
+    constexpr int RB = N * static_cast<int>(sizeof(T)), L = kS * RB, EC = 16 / static_cast<int>(sizeof(T));
+    static_assert(RB % 4 == 0, "rows of whole words");
+    if constexpr (RB >= 16) {
 #pragma unroll
-    for (int h = 0; h < RB / 16; ++h) {
-        float x[EC];
-        lds_vec<EC>(reinterpret_cast<const T *>(region + line_off<RB>(c, tau, h)), x);
+        for (int h = 0; h < RB / 16; ++h) {
+            float x[EC];
+            lds_vec<EC>(reinterpret_cast<const T *>(region + line_chunk<L>(c, tau * (RB / 16) + h)), x);
 #pragma unroll
-        for (int e = 0; e < EC; ++e) o[h * EC + e] = x[e];
+            for (int e = 0; e < EC; ++e) o[h * EC + e] = x[e];
+        }
+    } else {
+        const int byte = tau * RB;
+        const uint4 w = *reinterpret_cast<const uint4 *>(region + line_chunk<L>(c, byte >> 4));
+        const int w0 = (byte & 15) >> 2;
+#pragma unroll
+        for (int i = 0; i < RB / 4; ++i) {
+            const uint32_t x = word_of(w, w0 + i);
+            if constexpr (sizeof(T) == 4) {
+                o[i] = __uint_as_float(x);
+            } else {
+                o[2 * i] = bf16_lo(x);
+                o[2 * i + 1] = bf16_hi(x);
+            }
+        }
     }
 }
 template <int N, typename T>
 __device__ __forceinline__ void line_store(char *region, int c, int tau, const float (&v)[N]) {
-    constexpr int RB = N * static_cast<int>(sizeof(T)), EC = 16 / static_cast<int>(sizeof(T));
+    constexpr int RB = N * static_cast<int>(sizeof(T)), L = kS * RB, EC = 16 / static_cast<int>(sizeof(T));
+    static_assert(RB % 4 == 0, "rows of whole words");
+    if constexpr (RB >= 16) {
 #pragma unroll
-    for (int h = 0; h < RB / 16; ++h) sts_chunk(reinterpret_cast<T *>(region + line_off<RB>(c, tau, h)), v + h * EC);
+        for (int h = 0; h < RB / 16; ++h)
+            sts_chunk(reinterpret_cast<T *>(region + line_chunk<L>(c, tau * (RB / 16) + h)), v + h * EC);
+    } else {
+        uint32_t x[RB / 4];
+#pragma unroll
+        for (int i = 0; i < RB / 4; ++i) {
+            if constexpr (sizeof(T) == 4) {
+                x[i] = __float_as_uint(v[i]);
+            } else {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                x[i] = *reinterpret_cast<const uint32_t *>(&h);
+            }
+        }
+        const int byte = tau * RB;
+        char *const dst = region + line_chunk<L>(c, byte >> 4) + (byte & 15);
+        if constexpr (RB == 4) {
+            *reinterpret_cast<uint32_t *>(dst) = x[0];
+        } else {
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(x[0], x[1]);
+        }
+    }
 }
 
 // A lane's replay state as float quads: quad x at +128 x floats, both in the
@@ -249,12 +297,11 @@ struct Tile {
     static constexpr int rbK = D * static_cast<int>(sizeof(TIn)), rbV = M * static_cast<int>(sizeof(TIn));
     static constexpr int szK = kS * 32 * rbK, szV = kS * 32 * rbV, szA = FIXED ? 0 : kS * 32 * D * 4;
     static constexpr int szP = FIXED ? 0 : 32 * kS * 4, szG = BWD ? kS * 32 * M * 4 : 0;
-    // line regions (whole KB each, so every one stays 1024-byte aligned),
-    // then the [chain][tau] noise rows
-    static constexpr int oK = 0, oQ = oK + szK, oV = oQ + szK, oA = oV + szV, oG = oA + szA;
-    static constexpr int oP = oG + szG, oR = oP + szP;
+    // line regions, each 1024-byte aligned for the swizzle, then the
+    // [chain][tau] noise rows
+    static constexpr int oK = 0, oQ = al1024(oK + szK), oV = al1024(oQ + szK), oA = al1024(oV + szV);
+    static constexpr int oG = al1024(oA + szA), oP = al1024(oG + szG), oR = oP + szP;
     static constexpr int kBytes = al1024(oR + szP);
-    static_assert(szK % 1024 == 0 && szV % 1024 == 0 && szA % 1024 == 0 && szG % 1024 == 0, "line regions");
     static constexpr int kTx = 2 * szK + szV + szA + 2 * szP;  // bytes the token maps deliver, without gy
 };
 
@@ -336,7 +383,10 @@ __device__ __forceinline__ void cov_step(float (&P)[tri_size(D)], const float (&
     s = r;
 #pragma unroll
     for (int j = 0; j < D; ++j) s = fmaf(k[j], u[j], s);
-    beta = 1.0f / (s < floor_ ? floor_ : s);  // clamp_min: NaN stays NaN
+    // clamp_min (NaN stays NaN), then the fast reciprocal: 2 ulp, well inside
+    // the FP32 parity bar, and it shortens the covariance warp's serial
+    // chain; the saved gain scale carries this same value to the backward
+    beta = __fdividef(1.0f, s < floor_ ? floor_ : s);
     float nbu[D];
 #pragma unroll
     for (int i = 0; i < D; ++i) nbu[i] = -beta * u[i];
@@ -427,7 +477,7 @@ struct FwdGeo {
     static constexpr int SF = replay_state_floats(D, M);
     // a warp's outputs of one tile: readout and gains as line boxes, the
     // signed gain scales [chain][tau]
-    static constexpr int yY = 0, yU = kS * 32 * M * 4, yB = yU + kS * 32 * D * 4;
+    static constexpr int yY = 0, yU = al1024(kS * 32 * M * 4), yB = yU + kS * 32 * D * 4;
     static constexpr int kYB = al1024(yB + 32 * kS * 4);
     static constexpr int kPerStage = kWarps * Tl::kBytes;
     static constexpr int kFixed = kWarps * kYB + 1024 + kWarps * 4 * 8;
@@ -1002,8 +1052,8 @@ struct BwdGeo {
     // a warp's gradient rows of one sub-chunk: keys, values, queries, decay
     // as line boxes (whole KB each); process, observation [chain][tau]
     static constexpr int rbK = Tl::rbK, rbV = Tl::rbV;
-    static constexpr int gK = 0, gV = gK + kS * 32 * rbK, gQ = gV + kS * 32 * rbV;
-    static constexpr int gA = gQ + kS * 32 * rbK, gP = gA + kS * 32 * D * 4;
+    static constexpr int gK = 0, gV = al1024(gK + kS * 32 * rbK), gQ = al1024(gV + kS * 32 * rbV);
+    static constexpr int gA = al1024(gQ + kS * 32 * rbK), gP = al1024(gA + kS * 32 * D * 4);
     static constexpr int gR = gP + 32 * kS * 4, kOB = al1024(gR + 32 * kS * 4);
     static constexpr int kPerStage = kWarps * Tl::kBytes;
     static constexpr int oT = 0;                              // [stage][warp][tile]
@@ -1974,8 +2024,11 @@ bool map_tok(CUtensorMap *m, const T *base, int rowelems, long n, long t) {
     if (base == nullptr) return true;
     const cuuint64_t es = sizeof(T);
     const long span = static_cast<long>(kS) * rowelems * static_cast<long>(es);
-    if (span != 64 && span != 128) return false;
-    const CUtensorMapSwizzle sw = span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    if (span != 16 && span != 32 && span != 64 && span != 128) return false;
+    const CUtensorMapSwizzle sw = span == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : span == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                  : span == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                               : CU_TENSOR_MAP_SWIZZLE_NONE;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rowelems) * t, static_cast<cuuint64_t>(n)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(t) * rowelems * es};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(rowelems * kS), 32};
@@ -1996,13 +2049,14 @@ inline bool map_rows(CUtensorMap *m, const float *base, long w, long n, int bw, 
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Shapes the TMA path serves: 16-byte rows everywhere, every tile start on a
-// 16-byte boundary of the noise rows, coordinates within int32.
+// Shapes the TMA path serves: rows of whole 4-byte words (lines of 16 bytes
+// or more), every tile start on a 16-byte boundary of the noise rows,
+// coordinates within int32.
 template <typename TIn>
 bool eligible(int d, int m, long n, long t, int chunks) {
     const int es = static_cast<int>(sizeof(TIn));
-    return (d == 4 || d == 8) && m == 8 && (d * es) % 16 == 0 && (m * es) % 16 == 0 && t > 0 && t % kS == 0 &&
-           chunks % kS == 0 && n < (1L << 30) && t < (1L << 30) && encode_fn() != nullptr;
+    return (d == 1 || d == 2 || d == 4 || d == 8) && m == 8 && (d * es) % 4 == 0 && (m * es) % 4 == 0 && t > 0 &&
+           t % kS == 0 && chunks % kS == 0 && n < (1L << 30) && t < (1L << 30) && encode_fn() != nullptr;
 }
 
 template <int D, int M, bool FIXED, typename TIn>
@@ -2155,7 +2209,7 @@ int launch_fwd_split(const FwdArgs<TIn> &a, cudaStream_t st) {
 
 template <int D, typename TIn>
 constexpr bool fwd_fits() {
-    if constexpr ((D * static_cast<int>(sizeof(TIn))) % 16 != 0) {
+    if constexpr ((D * static_cast<int>(sizeof(TIn))) % 4 != 0) {
         return false;
     } else {
         return FwdGeo<D, 8, false, TIn>::kFits && FwdGeo<D, 8, true, TIn>::kFits;
@@ -2197,8 +2251,8 @@ int bwd_f(bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
 
 template <int D, typename TIn>
 int bwd_d(int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
-    if constexpr ((D * static_cast<int>(sizeof(TIn))) % 16 != 0) {
-        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels need 16-byte key rows");
+    if constexpr ((D * static_cast<int>(sizeof(TIn))) % 4 != 0) {
+        return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels need key rows of whole words");
     } else {
         return fixed ? bwd_f<D, true, TIn>(dyn, init, a, st) : bwd_f<D, false, TIn>(dyn, init, a, st);
     }
@@ -2210,7 +2264,13 @@ template <typename TIn>
 bool chain_eligible(int d, long n, long t, int chunks, bool forward) {
     if (!chain::eligible<TIn>(d, 8, n, t, chunks)) return false;
     if (!forward) return true;
-    return d == 8 ? chain::fwd_fits<8, TIn>() : chain::fwd_fits<4, TIn>();
+    switch (d) {
+        case 1: return chain::fwd_fits<1, TIn>();
+        case 2: return chain::fwd_fits<2, TIn>();
+        case 4: return chain::fwd_fits<4, TIn>();
+        case 8: return chain::fwd_fits<8, TIn>();
+    }
+    return false;
 }
 
 template <typename TIn>
@@ -2219,6 +2279,8 @@ int chain_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
     if (!chain_eligible<TIn>(d, a.n, a.t, a.chunks, true))
         return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain kernels: shape not supported");
     switch (d) {
+        case 1: return chain::fwd_d<1, TIn>(fixed, a, st);
+        case 2: return chain::fwd_d<2, TIn>(fixed, a, st);
         case 4: return chain::fwd_d<4, TIn>(fixed, a, st);
         case 8: return chain::fwd_d<8, TIn>(fixed, a, st);
     }
@@ -2233,6 +2295,8 @@ int chain_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a,
     if (a.rs == nullptr && replay_slots_per_chunk(a.t, a.chunks) > 0)
         return fail(BSSM_ERR_UNSUPPORTED, "thread-per-chain backward needs the forward's replay states");
     switch (d) {
+        case 1: return chain::bwd_d<1, TIn>(fixed, dyn, init, a, st);
+        case 2: return chain::bwd_d<2, TIn>(fixed, dyn, init, a, st);
         case 4: return chain::bwd_d<4, TIn>(fixed, dyn, init, a, st);
         case 8: return chain::bwd_d<8, TIn>(fixed, dyn, init, a, st);
     }

@@ -115,11 +115,13 @@ def test_replay_states_match_recomputed_states():
         assert_parity(a[key], b[key].cpu().numpy(), rel=1e-6, cos=0.999999, what=f"grad {key}")
 
 
-@pytest.mark.parametrize("d,io", [(8, "bf16"), (8, "f32"), (4, "f32")])
+@pytest.mark.parametrize("d,io", [(8, "bf16"), (8, "f32"), (4, "f32"), (4, "bf16"), (2, "bf16"), (2, "f32"),
+                                  (1, "f32")])
 @pytest.mark.parametrize("chunks", [4, 16, 48])
 def test_tma_eligible_shapes(d, io, chunks, family):
     """Shapes the thread-per-chain family serves (T and chunk multiples of 4,
-    16-byte rows): a partial warp, several warps, full and ragged chunks."""
+    rows of whole 4-byte words, so lines of 16 to 128 bytes): a partial warp,
+    several warps, full and ragged chunks."""
     from bayes_ssm import _capi
     dt = torch.bfloat16 if io == "bf16" else torch.float32
     inp = make_inputs(70, 48, d, 8, seed=100 + d + chunks, init="random", io_dtype=dt)
