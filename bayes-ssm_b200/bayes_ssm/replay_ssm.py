@@ -93,8 +93,17 @@ class ReplaySSM(nn.Module):
 
 
 def _scan_inputs(keys, values, queries, observation_variances, initial_mean, initial_covariance,
-                 denominator_floor):
-    """Validation and promotion shared by the PyTorch and CUDA scans."""
+                 denominator_floor, *, kernel_checks: bool = False):
+    """Validation and promotion shared by the PyTorch and CUDA scans
+    (reference ``replay_ssm.py:183-242``).
+
+    With ``kernel_checks`` (the CUDA scan) the defaults are not built — the
+    identity covariance and zero mean are valid by construction and are
+    returned as ``None`` — and float32 observation variances are left to the
+    kernel, which flags a non-finite value or one below the floor while it
+    stages each token (the same comparison in the same dtype; the caller
+    raises the same ``ValueError`` after the launch).
+    """
     if keys.ndim < 2 or values.ndim < 2 or queries.ndim < 2:
         raise ValueError("keys, values and queries must have time and feature dimensions")
     if not all(value.is_floating_point() for value in (keys, values, queries)):
@@ -116,25 +125,27 @@ def _scan_inputs(keys, values, queries, observation_variances, initial_mean, ini
     batch = keys.shape[:-2]
     device = keys.device
     if initial_covariance is None:
-        covariance0 = torch.eye(d, device=device, dtype=dtype).expand(*batch, d, d)
+        covariance0 = None if kernel_checks else torch.eye(d, device=device, dtype=dtype).expand(*batch, d, d)
     else:
         covariance0 = initial_covariance.to(device=device, dtype=dtype)
-    if covariance0.shape[-2:] != (d, d):
-        raise ValueError("initial_covariance must end in [key_dim, key_dim]")
-    if not _broadcastable(covariance0.shape[:-2], batch):
-        raise ValueError("initial_covariance batch dimensions are not broadcastable to keys")
-    covariance0 = covariance0.expand(*batch, d, d)
-    _validate_covariance(covariance0, "initial_covariance", d)
+    if covariance0 is not None:
+        if covariance0.shape[-2:] != (d, d):
+            raise ValueError("initial_covariance must end in [key_dim, key_dim]")
+        if not _broadcastable(covariance0.shape[:-2], batch):
+            raise ValueError("initial_covariance batch dimensions are not broadcastable to keys")
+        covariance0 = covariance0.expand(*batch, d, d)
+        _validate_covariance(covariance0, "initial_covariance", d)
     if initial_mean is None:
-        mean0 = torch.zeros(*batch, d, m, device=device, dtype=dtype)
+        mean0 = None if kernel_checks else torch.zeros(*batch, d, m, device=device, dtype=dtype)
     else:
         mean0 = initial_mean.to(device=device, dtype=dtype)
-    if mean0.shape[-2:] != (d, m):
-        raise ValueError("initial_mean must end in [key_dim, value_dim]")
-    if not _broadcastable(mean0.shape[:-2], batch):
-        raise ValueError("initial_mean batch dimensions are not broadcastable to keys")
-    mean0 = mean0.expand(*batch, d, m)
-    _check_finite(mean0, "initial_mean")
+    if mean0 is not None:
+        if mean0.shape[-2:] != (d, m):
+            raise ValueError("initial_mean must end in [key_dim, value_dim]")
+        if not _broadcastable(mean0.shape[:-2], batch):
+            raise ValueError("initial_mean batch dimensions are not broadcastable to keys")
+        mean0 = mean0.expand(*batch, d, m)
+        _check_finite(mean0, "initial_mean")
     if not isinstance(denominator_floor, Real) or not torch.isfinite(
         torch.tensor(float(denominator_floor))
     ) or denominator_floor <= 0:
@@ -143,7 +154,9 @@ def _scan_inputs(keys, values, queries, observation_variances, initial_mean, ini
     r2 = torch.broadcast_to(r2, (*batch, t))
     # The information form divides by r itself; a variance below the floor
     # would make it disagree with the floored dense recurrence, so reject it.
-    if r2.numel() and (not bool(torch.isfinite(r2).all()) or bool((r2 < float(denominator_floor)).any())):
+    on_kernel = kernel_checks and dtype == torch.float32
+    if r2.numel() and not on_kernel and (not bool(torch.isfinite(r2).all())
+                                         or bool((r2 < float(denominator_floor)).any())):
         raise ValueError(
             "associative_static_bayesian requires finite observation_variances "
             "greater than or equal to denominator_floor"
@@ -196,11 +209,14 @@ def associative_static_bayesian_cuda(keys: Tensor, values: Tensor, queries: Tens
 
     (keys, values, queries, r2, mean0, covariance0, batch, t, d, m, dtype,
      device) = _scan_inputs(keys, values, queries, observation_variances, initial_mean,
-                            initial_covariance, denominator_floor)
+                            initial_covariance, denominator_floor, kernel_checks=True)
     if t == 0:
+        if mean0 is None:
+            mean0 = torch.zeros(*batch, d, m, device=device, dtype=dtype)
+        if covariance0 is None:
+            covariance0 = torch.eye(d, device=device, dtype=dtype).expand(*batch, d, d)
         return torch.empty(*batch, 0, m, device=device, dtype=dtype), mean0, covariance0
-    return assoc_scan_cuda(keys, values, queries, r2, mean0 if initial_mean is not None else None,
-                           covariance0 if initial_covariance is not None else None, batch=batch,
+    return assoc_scan_cuda(keys, values, queries, r2, mean0, covariance0, batch=batch,
                            denominator_floor=float(denominator_floor))
 
 

@@ -29,6 +29,7 @@ constexpr int kScanWarps = 8;
 constexpr int kScanThreads = kScanWarps * 32;
 constexpr int kScanMaxD = 32;
 constexpr int kScanMaxM = 256;
+constexpr int kScanChunk = 32;  // prefix tokens staged per round
 
 // status bits written by the kernel
 constexpr int kScanNotPD = 1;       // a Cholesky pivot was <= 0 or not finite
@@ -43,25 +44,27 @@ struct ScanArgs {
     float floor;
 };
 
-// Left-looking Cholesky of the D x D row-major matrix in A (lower triangle
-// receives L).  Lane i owns row i.  Returns false (in every lane) when a pivot
-// is not positive.
-__device__ bool warp_cholesky(float *A, int D, int lane) {
+// Left-looking Cholesky of the D x D matrix in A, rows `ld` floats apart (ld
+// = D + 1 keeps a warp's row-per-lane accesses on distinct banks); the lower
+// triangle receives L.  Lane i owns row i.  Returns false (in every lane)
+// when a pivot is not positive.
+__device__ bool warp_cholesky(float *A, int D, int ld, int lane) {
     bool ok = true;
     for (int j = 0; j < D; ++j) {
         if (lane == j) {
-            float s = A[j * D + j];
-            for (int k = 0; k < j; ++k) s = fmaf(-A[j * D + k], A[j * D + k], s);
+            float s = A[j * ld + j];
+            for (int k = 0; k < j; ++k) s = fmaf(-A[j * ld + k], A[j * ld + k], s);
             const bool good = s > 0.f && s < 3.0e38f;
-            A[j * D + j] = good ? sqrtf(s) : -1.f;  // -1 marks a failed pivot
+            A[j * ld + j] = good ? sqrtf(s) : -1.f;  // -1 marks a failed pivot
         }
         __syncwarp();
-        const float piv = A[j * D + j];
+        const float piv = A[j * ld + j];
         ok = ok && (piv > 0.f);
+        const float rpiv = 1.0f / piv;  // one division per column
         if (lane > j && lane < D) {
-            float z = A[lane * D + j];
-            for (int k = 0; k < j; ++k) z = fmaf(-A[lane * D + k], A[j * D + k], z);
-            A[lane * D + j] = z / piv;
+            float z = A[lane * ld + j];
+            for (int k = 0; k < j; ++k) z = fmaf(-A[lane * ld + k], A[j * ld + k], z);
+            A[lane * ld + j] = z * rpiv;
         }
         __syncwarp();
     }
@@ -69,45 +72,54 @@ __device__ bool warp_cholesky(float *A, int D, int lane) {
 }
 
 // Solve (L L^T) x = b for one right-hand side; lane i holds b_i / x_i.
-__device__ float warp_chol_solve(const float *L, int D, int lane, float b) {
+// Each lane takes the reciprocal of its own pivot once, so the serial
+// substitution steps multiply instead of divide.
+__device__ float warp_chol_solve(const float *L, int D, int ld, int lane, float b) {
+    const float rdi = lane < D ? 1.0f / L[lane * ld + lane] : 0.f;
     float z = 0.f;
     for (int k = 0; k < D; ++k) {  // forward: L z = b
-        const float zk = __shfl_sync(0xffffffffu, b, k) / L[k * D + k];
+        const float zk = __shfl_sync(0xffffffffu, b * rdi, k);
         if (lane == k) z = zk;
-        if (lane > k && lane < D) b = fmaf(-L[lane * D + k], zk, b);
+        if (lane > k && lane < D) b = fmaf(-L[lane * ld + k], zk, b);
     }
     float x = 0.f;
     for (int k = D - 1; k >= 0; --k) {  // backward: L^T x = z
-        const float xk = __shfl_sync(0xffffffffu, z, k) / L[k * D + k];
+        const float xk = __shfl_sync(0xffffffffu, z * rdi, k);
         if (lane == k) x = xk;
-        if (lane < k) z = fmaf(-L[k * D + lane], xk, z);
+        if (lane < k) z = fmaf(-L[k * ld + lane], xk, z);
     }
     return x;
 }
 
-// Column `col` of (L L^T)^{-1}: per-thread substitution, rows in registers.
-__device__ void chol_inverse_column(const float *L, int D, int col, float (&x)[kScanMaxD]) {
-    float z[kScanMaxD];
-#pragma unroll
-    for (int i = 0; i < kScanMaxD; ++i) {
-        if (i < D) {
-            float s = (i == col) ? 1.f : 0.f;
-#pragma unroll
-            for (int k = 0; k < kScanMaxD; ++k)
-                if (k < i) s = fmaf(-L[i * D + k], z[k], s);
-            z[i] = s / L[i * D + i];
+// (L L^T)^{-1} from the Cholesky factor L (rows `ld` apart), by the whole
+// CTA, in rolled loops (this runs once per CTA, so straight-line code would
+// cost more in instruction fetch than it saves).  Thread c < D forms column c
+// of L^{-1} by forward substitution into `linv`; then each entry
+// out_ij = sum_{k >= max(i,j)} Linv_ki Linv_kj, which is exactly symmetric
+// because the products commute.  `rd` receives 1 / L_ii.  Contains
+// __syncthreads: every thread of the CTA calls it.
+__device__ void block_chol_inverse(const float *L, int D, int ld, float *linv, float *rd, float *out,
+                                   int ldo, int tid) {
+    if (tid < D) rd[tid] = 1.0f / L[tid * ld + tid];
+    __syncthreads();
+    if (tid < D) {
+        const int c = tid;
+        for (int i = 0; i < c; ++i) linv[i * ld + c] = 0.f;
+        linv[c * ld + c] = rd[c];
+        for (int i = c + 1; i < D; ++i) {
+            float s = 0.f;
+            for (int k = c; k < i; ++k) s = fmaf(-L[i * ld + k], linv[k * ld + c], s);
+            linv[i * ld + c] = s * rd[i];
         }
     }
-#pragma unroll
-    for (int ii = kScanMaxD - 1; ii >= 0; --ii) {
-        if (ii < D) {
-            float s = z[ii];
-#pragma unroll
-            for (int k = 0; k < kScanMaxD; ++k)
-                if (k > ii && k < D) s = fmaf(-L[k * D + ii], x[k], s);
-            x[ii] = s / L[ii * D + ii];
-        }
+    __syncthreads();
+    for (int e = tid; e < D * D; e += kScanThreads) {
+        const int i = e / D, j = e % D;
+        float acc = 0.f;
+        for (int k = i > j ? i : j; k < D; ++k) acc = fmaf(linv[k * ld + i], linv[k * ld + j], acc);
+        out[i * ldo + j] = acc;
     }
+    __syncthreads();
 }
 
 __global__ void __launch_bounds__(kScanThreads) assoc_scan_kernel(const ScanArgs A) {
@@ -119,79 +131,81 @@ __global__ void __launch_bounds__(kScanThreads) assoc_scan_kernel(const ScanArgs
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nblock = static_cast<int>((T - t0) < kScanWarps ? (T - t0) : kScanWarps);
 
-    float *lam = sm;                 // D*D   prefix precision before t0
-    float *nat = lam + D * D;        // D*M   prefix natural parameter before t0
+    const int LD = D + 1;            // row stride of the D x D matrices
+    float *lam = sm;                 // D*LD  prefix precision before t0
+    float *nat = lam + D * LD;       // D*M   prefix natural parameter before t0
     float *bk = nat + D * M;         // 8*D   block keys
     float *bw = bk + kScanWarps * D; // 8*D   block keys / r
     float *bv = bw + kScanWarps * D; // 8*M   block values
-    float *ptm = bv + kScanWarps * M;                 // D*D  P_T (last block only)
-    float *wsc = ptm + D * D;                         // per warp: D*D + 2*D + 8
-    float *mine = wsc + warp * (D * D + 2 * D + kScanWarps);
-    float *xv = mine + D * D;        // D   solution x
+    float *ptm = bv + kScanWarps * M;                 // D*LD  P_T (last block only)
+    float *wsc = ptm + D * LD;                        // per warp: D*LD + 2*D + 8
+    float *mine = wsc + warp * (D * LD + 2 * D + kScanWarps);
+    float *xv = mine + D * LD;       // D   solution x
     float *dots = xv + D;            // 8   w_s . x
+    float *stg = wsc + kScanWarps * (D * LD + 2 * D + kScanWarps);  // prefix chunk: keys, keys / r, values
+    float *sk = stg, *sw = sk + kScanChunk * D, *sv = sw + kScanChunk * D;
     const float *kc = A.keys + chain * T * D;
     const float *vc = A.values + chain * T * M;
     const float *rc = A.obs + chain * T;
 
     // ---- 1. Lambda_0 = inv(sym(P0)), N_0 = Lambda_0 M0 (identity / zero defaults)
     if (A.cov0 == nullptr) {
-        for (int e = tid; e < D * D; e += kScanThreads) lam[e] = (e / D == e % D) ? 1.f : 0.f;
+        for (int e = tid; e < D * D; e += kScanThreads) lam[(e / D) * LD + e % D] = (e / D == e % D) ? 1.f : 0.f;
         for (int e = tid; e < D * M; e += kScanThreads)
             nat[e] = A.mean0 ? A.mean0[chain * D * M + e] : 0.f;
         __syncthreads();
     } else {
         const float *c0 = A.cov0 + chain * D * D;
         if (warp == 0) {
-            for (int e = lane; e < D * D; e += 32) mine[e] = 0.5f * (c0[e] + c0[(e % D) * D + e / D]);
+            for (int e = lane; e < D * D; e += 32) mine[(e / D) * LD + e % D] = 0.5f * (c0[e] + c0[(e % D) * D + e / D]);
             __syncwarp();
-            if (!warp_cholesky(mine, D, lane)) {
+            if (!warp_cholesky(mine, D, LD, lane)) {
                 if (lane == 0) atomicOr(A.status, kScanNotPD);
             }
-            __syncwarp();
-            if (lane < D) {
-                float x[kScanMaxD];
-                chol_inverse_column(mine, D, lane, x);
-                for (int i = 0; i < D; ++i) lam[i * D + lane] = x[i];
-            }
         }
         __syncthreads();
-        for (int e = tid; e < D * D; e += kScanThreads) {  // symmetrise Lambda_0
-            const int i = e / D, j = e % D;
-            if (i < j) {
-                const float s = 0.5f * (lam[i * D + j] + lam[j * D + i]);
-                lam[i * D + j] = s;
-                lam[j * D + i] = s;
-            }
-        }
-        __syncthreads();
+        // Lambda_0 (exactly symmetric); L^{-1} and 1/L_ii in the prefix staging area
+        block_chol_inverse(wsc, D, LD, stg, stg + D * LD, lam, LD, tid);  // wsc: warp 0's factor
         for (int e = tid; e < D * M; e += kScanThreads) {
             const int i = e / M, c = e % M;
             float acc = 0.f;
             if (A.mean0)
-                for (int j = 0; j < D; ++j) acc = fmaf(lam[i * D + j], A.mean0[chain * D * M + j * M + c], acc);
+                for (int j = 0; j < D; ++j) acc = fmaf(lam[i * LD + j], A.mean0[chain * D * M + j * M + c], acc);
             nat[e] = acc;
         }
         __syncthreads();
     }
 
-    // ---- 2. add every token before t0 (entry-parallel)
-    for (int e = tid; e < D * D + D * M; e += kScanThreads) {
-        float acc = 0.f;
-        if (e < D * D) {
-            const int i = e / D, j = e % D;
-            for (long s = 0; s < t0; ++s) acc = fmaf(kc[s * D + i], kc[s * D + j] / rc[s], acc);
-            lam[e] += acc;
-        } else {
-            const int i = (e - D * D) / M, c = (e - D * D) % M;
-            for (long s = 0; s < t0; ++s) acc = fmaf(kc[s * D + i] / rc[s], vc[s * M + c], acc);
-            nat[e - D * D] += acc;
+    // ---- 2. add every token before t0: chunks of kScanChunk tokens staged in
+    // shared memory (one division per key element), then entry-parallel sums
+    for (long s0 = 0; s0 < t0; s0 += kScanChunk) {
+        const int ns = static_cast<int>((t0 - s0) < kScanChunk ? (t0 - s0) : kScanChunk);
+        __syncthreads();  // the previous chunk is consumed
+        for (int e = tid; e < ns * D; e += kScanThreads) {
+            const float kv = kc[s0 * D + e];
+            sk[e] = kv;
+            sw[e] = kv / rc[s0 + e / D];
+        }
+        for (int e = tid; e < ns * M; e += kScanThreads) sv[e] = vc[s0 * M + e];
+        __syncthreads();
+        for (int e = tid; e < D * D + D * M; e += kScanThreads) {
+            float acc = 0.f;
+            if (e < D * D) {
+                const int i = e / D, j = e % D;
+                for (int s = 0; s < ns; ++s) acc = fmaf(sk[s * D + i], sw[s * D + j], acc);
+                lam[i * LD + j] += acc;
+            } else {
+                const int i = (e - D * D) / M, c = (e - D * D) % M;
+                for (int s = 0; s < ns; ++s) acc = fmaf(sw[s * D + i], sv[s * M + c], acc);
+                nat[e - D * D] += acc;
+            }
         }
     }
     // ---- 3. stage this block's tokens
     for (int e = tid; e < nblock * D; e += kScanThreads) {
         const int s = e / D, i = e % D;
         const float r = rc[t0 + s];
-        if (!(r >= A.floor) || !(r < 3.0e38f)) atomicOr(A.status, kScanBadVariance);
+        if (!(r >= A.floor) || !isfinite(r)) atomicOr(A.status, kScanBadVariance);
         bk[e] = kc[(t0 + s) * D + i];
         bw[e] = kc[(t0 + s) * D + i] / r;
     }
@@ -203,19 +217,19 @@ __global__ void __launch_bounds__(kScanThreads) assoc_scan_kernel(const ScanArgs
         const long t = t0 + warp;
         for (int e = lane; e < D * D; e += 32) {
             const int i = e / D, j = e % D;
-            float lij = lam[i * D + j], lji = lam[j * D + i];
+            float lij = lam[i * LD + j], lji = lam[j * LD + i];
             for (int s = 0; s <= warp; ++s) {
                 lij = fmaf(bk[s * D + i], bw[s * D + j], lij);
                 lji = fmaf(bk[s * D + j], bw[s * D + i], lji);
             }
-            mine[e] = 0.5f * (lij + lji);
+            mine[i * LD + j] = 0.5f * (lij + lji);
         }
         __syncwarp();
-        if (!warp_cholesky(mine, D, lane)) {
+        if (!warp_cholesky(mine, D, LD, lane)) {
             if (lane == 0) atomicOr(A.status, kScanNotPD);
         }
         const float qi = lane < D ? A.queries[(chain * T + t) * D + lane] : 0.f;
-        const float x = warp_chol_solve(mine, D, lane, qi);
+        const float x = warp_chol_solve(mine, D, LD, lane, qi);
         if (lane < D) xv[lane] = x;
         __syncwarp();
         if (lane <= warp) {
@@ -230,29 +244,28 @@ __global__ void __launch_bounds__(kScanThreads) assoc_scan_kernel(const ScanArgs
             for (int s = 0; s <= warp; ++s) y = fmaf(dots[s], bv[s * M + c], y);
             A.out[(chain * T + t) * M + c] = y;
         }
-        // ---- 5. final state at T-1: P_T = Lambda^{-1}, M_T = P_T N_T
-        if (t == T - 1) {
-            if (lane < D) {
-                float xcol[kScanMaxD];
-                chol_inverse_column(mine, D, lane, xcol);
-                for (int i = 0; i < D; ++i) ptm[i * D + lane] = xcol[i];
-            }
-            __syncwarp();
-            for (int e = lane; e < D * D; e += 32) {
-                const int i = e / D, j = e % D;
-                A.cov_final[chain * D * D + e] = 0.5f * (ptm[i * D + j] + ptm[j * D + i]);
-            }
-            __syncwarp();
-            for (int e = lane; e < D * M; e += 32) {
-                const int i = e / M, c = e % M;
-                float acc = 0.f;
-                for (int j = 0; j < D; ++j) {
-                    float ntj = nat[j * M + c];
-                    for (int s = 0; s <= warp; ++s) ntj = fmaf(bw[s * D + j], bv[s * M + c], ntj);
-                    acc = fmaf(0.5f * (ptm[i * D + j] + ptm[j * D + i]), ntj, acc);
-                }
-                A.mean_final[chain * D * M + e] = acc;
-            }
+    }
+    // ---- 5. final state, by the CTA that holds T-1: P_T = Lambda_T^{-1}
+    // from the last warp's factor, N_T = N_{t0} + this block's tokens,
+    // M_T = P_T N_T
+    if (t0 + nblock == T) {
+        __syncthreads();
+        const float *lf = wsc + (nblock - 1) * (D * LD + 2 * D + kScanWarps);
+        float *ntm = stg, *linv = ntm + D * M, *rd = linv + D * LD;
+        for (int e = tid; e < D * M; e += kScanThreads) {
+            const int i = e / M, c = e % M;
+            float acc = nat[e];
+            for (int s = 0; s < nblock; ++s) acc = fmaf(bw[s * D + i], bv[s * M + c], acc);
+            ntm[e] = acc;
+        }
+        block_chol_inverse(lf, D, LD, linv, rd, ptm, LD, tid);
+        for (int e = tid; e < D * D; e += kScanThreads)
+            A.cov_final[chain * D * D + e] = ptm[(e / D) * LD + e % D];
+        for (int e = tid; e < D * M; e += kScanThreads) {
+            const int i = e / M, c = e % M;
+            float acc = 0.f;
+            for (int j = 0; j < D; ++j) acc = fmaf(ptm[i * LD + j], ntm[j * M + c], acc);
+            A.mean_final[chain * D * M + e] = acc;
         }
     }
 }
@@ -283,8 +296,10 @@ int bssm_assoc_scan_ex(int key_dim, int value_dim, const float *keys, const floa
     const long blocks_t = (t + kScanWarps - 1) / kScanWarps;
     if (blocks_t > 0x7fffffffL) return fail(BSSM_ERR_INVALID, "assoc scan: sequence too long");
     const int D = key_dim, M = value_dim;
+    const int LD = D + 1;
     const size_t smem = sizeof(float) * static_cast<size_t>(
-        D * D + D * M + kScanWarps * (2 * D + M) + D * D + kScanWarps * (D * D + 2 * D + kScanWarps));
+        D * LD + D * M + kScanWarps * (2 * D + M) + D * LD + kScanWarps * (D * LD + 2 * D + kScanWarps) +
+        kScanChunk * (2 * D + M));
     if (smem > 48 * 1024) {
         cudaError_t err = cudaFuncSetAttribute(assoc_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(smem));

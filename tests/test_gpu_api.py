@@ -173,6 +173,55 @@ def test_assoc_scan_rejects_small_variance_on_gpu():
                                                    observation_variances=r)
 
 
+@pytest.mark.parametrize("bad", [float("nan"), float("inf"), float("-inf"), 0.0, -1.0, 9.9e-7, "scalar"])
+def test_assoc_scan_variance_errors_match_eager(bad):
+    """The kernel flags the observation variances the eager scan rejects
+    (non-finite, or below the floor; any chain, any token, scalar broadcast)
+    and accepts the floor itself and the largest finite float."""
+    import bayes_ssm
+    g = torch.Generator().manual_seed(5)
+    k = (torch.randn(3, 21, 4, generator=g) / 2).cuda()
+    v = torch.randn(3, 21, 5, generator=g).cuda()
+    if bad == "scalar":
+        r = 5e-7
+    else:
+        r = torch.full((3, 21), 0.5, device="cuda")
+        r[2, 20] = bad
+    for fn in (bayes_ssm.associative_static_bayesian, bayes_ssm.associative_static_bayesian_cuda):
+        with torch.no_grad(), pytest.raises(ValueError, match="denominator_floor"):
+            fn(k, v, k, observation_variances=r)
+    # accepted boundary values (a variance at the floor makes the precision
+    # ~1e5 and both FP32 scans ill-conditioned: acceptance only, no parity)
+    ok = torch.full((3, 21), 0.5, device="cuda")
+    ok[0, 0], ok[1, 7] = 1e-6, torch.finfo(torch.float32).max
+    with torch.no_grad():
+        y, _, _ = bayes_ssm.associative_static_bayesian_cuda(k, v, k, observation_variances=ok)
+    assert torch.isfinite(y).all()
+
+
+def test_assoc_scan_default_state_equals_explicit():
+    """Omitting the initial state (identity covariance, zero mean; not built
+    on the CUDA path) gives the same result as passing it explicitly, and
+    T = 0 returns the defaults."""
+    import bayes_ssm
+    g = torch.Generator().manual_seed(6)
+    k = (torch.randn(2, 3, 17, 8, generator=g) / 3).cuda()
+    v = torch.randn(2, 3, 17, 6, generator=g).cuda()
+    r = (torch.rand(2, 3, 17, generator=g) + 0.1).cuda()
+    with torch.no_grad():
+        a = bayes_ssm.associative_static_bayesian_cuda(k, v, k, observation_variances=r)
+        b = bayes_ssm.associative_static_bayesian_cuda(
+            k, v, k, observation_variances=r, initial_mean=torch.zeros(2, 3, 8, 6, device="cuda"),
+            initial_covariance=torch.eye(8, device="cuda"))
+        for x, y in zip(a, b):
+            assert x.shape == y.shape
+            assert float((x - y).norm()) <= 1e-5 * float(y.norm())
+        y0, m0, p0 = bayes_ssm.associative_static_bayesian_cuda(k[..., :0, :], v[..., :0, :], k[..., :0, :])
+    assert y0.shape == (2, 3, 0, 6)
+    assert torch.equal(m0, torch.zeros(2, 3, 8, 6, device="cuda"))
+    assert torch.equal(p0, torch.eye(8, device="cuda").expand(2, 3, 8, 8))
+
+
 @pytest.mark.parametrize("dtype", (torch.float32, torch.bfloat16, torch.float16))
 def test_check_values_flags_match_torch(dtype):
     """The one-pass input check (C ABI) agrees with torch's isfinite / sign
