@@ -79,6 +79,80 @@ __device__ __forceinline__ float sel4v(const float4 &x, int i) {
     return i == 0 ? x.x : i == 1 ? x.y : i == 2 ? x.z : x.w;
 }
 
+// ---- packed FP32 pairs (sm_100 f32x2 arithmetic) -----------------------------
+// Row-major D x M means pair up along the value dimension: pr(x, c) is
+// (x[c], x[c+1]).  One f32x2 instruction does the two lanes' IEEE operations,
+// so a loop over value pairs computes exactly what the scalar loop over
+// values would, in half the instructions.
+__device__ __forceinline__ float2 bc2(float s) { return make_float2(s, s); }
+__device__ __forceinline__ float2 pr(const float *x, int c) { return make_float2(x[c], x[c + 1]); }
+__device__ __forceinline__ void spr(float *x, int c, float2 v) {
+    x[c] = v.x;
+    x[c + 1] = v.y;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+// sum_c x[c] y[c] over M (even) values: pairwise partial sums, then one add
+template <int M>
+__device__ __forceinline__ float dot2(const float *x, const float *y) {
+    static_assert(M % 2 == 0, "value pairs");
+    float2 acc = mul2(pr(x, 0), pr(y, 0));
+#pragma unroll
+    for (int c = 2; c < M; c += 2) acc = fma2(pr(x, c), pr(y, c), acc);
+    return acc.x + acc.y;
+}
+// y[c] = sum_i X[i][c] w[i] for every value c (value pairs, i in order)
+template <int D, int M>
+__device__ __forceinline__ void colsum2(const float (&X)[D][M], const float (&w)[D], float (&y)[M]) {
+    static_assert(M % 2 == 0, "value pairs");
+#pragma unroll
+    for (int c = 0; c < M; c += 2) {
+        float2 acc = mul2(pr(X[0], c), bc2(w[0]));
+#pragma unroll
+        for (int i = 1; i < D; ++i) acc = fma2(pr(X[i], c), bc2(w[i]), acc);
+        spr(y, c, acc);
+    }
+}
+// dL/dM' += q gy^T
+template <int D, int M>
+__device__ __forceinline__ void add_outer2(float (&gM)[D][M], const float (&qv)[D], const float (&gy)[M]) {
+#pragma unroll
+    for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int c = 0; c < M; c += 2) spr(gM[i], c, fma2(bc2(qv[i]), pr(gy, c), pr(gM[i], c)));
+}
+// acc = gM^T u; ge = beta acc (the value gradient); returns e . acc (= u^T gM e)
+template <int D, int M>
+__device__ __forceinline__ float gain_adjoint2(const float (&gM)[D][M], const float (&u)[D], const float (&e)[M],
+                                               float beta, float (&ge)[M]) {
+    float acc[M];
+    colsum2<D, M>(gM, u, acc);
+#pragma unroll
+    for (int c = 0; c < M; c += 2) spr(ge, c, mul2(bc2(beta), pr(acc, c)));
+    return dot2<M>(e, acc);
+}
+// One row i of the mean adjoint through the update, given the pre-step mean
+// row mp: pk = mp . ge; g = gM_i - k_i ge; ga = g . mp (with DYN); gM_i = a_i g.
+template <int M, bool DYN>
+__device__ __forceinline__ void mean_row_adjoint2(float (&gmi)[M], const float (&mp)[M], const float (&ge)[M],
+                                                  float k, float a, float &pk, float &ga) {
+    static_assert(M % 2 == 0, "value pairs");
+    const float2 nk = bc2(-k), a2 = bc2(a);
+    float2 g = fma2(nk, pr(ge, 0), pr(gmi, 0));
+    float2 pacc = mul2(pr(mp, 0), pr(ge, 0)), gacc = mul2(g, pr(mp, 0));
+    spr(gmi, 0, mul2(a2, g));
+#pragma unroll
+    for (int c = 2; c < M; c += 2) {
+        pacc = fma2(pr(mp, c), pr(ge, c), pacc);
+        g = fma2(nk, pr(ge, c), pr(gmi, c));
+        if constexpr (DYN) gacc = fma2(g, pr(mp, c), gacc);
+        spr(gmi, c, mul2(a2, g));
+    }
+    pk = pacc.x + pacc.y;
+    ga = DYN ? gacc.x + gacc.y : 0.f;
+}
+
 // ---- mbarriers ---------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -400,24 +474,26 @@ __device__ __forceinline__ void cov_step(float (&P)[tri_size(D)], const float (&
         }
 }
 
+// e = v - (A M)^T k and M' = A M + beta u e^T, in value pairs.
 template <int D, int M>
 __device__ __forceinline__ void mean_step(float (&Mm)[D][M], const float (&k)[D], const float (&a)[D],
                                           const float (&v)[M], const float (&u)[D], float beta, float (&e)[M]) {
-    float wk[D];
+    static_assert(M % 2 == 0, "value pairs");
+    float nwk[D];
 #pragma unroll
-    for (int i = 0; i < D; ++i) wk[i] = a[i] * k[i];
+    for (int i = 0; i < D; ++i) nwk[i] = -(a[i] * k[i]);
 #pragma unroll
-    for (int c = 0; c < M; ++c) {
-        float acc = 0.f;
+    for (int c = 0; c < M; c += 2) {
+        float2 acc = mul2(pr(Mm[0], c), bc2(nwk[0]));
 #pragma unroll
-        for (int i = 0; i < D; ++i) acc = fmaf(Mm[i][c], wk[i], acc);
-        e[c] = v[c] - acc;
+        for (int i = 1; i < D; ++i) acc = fma2(pr(Mm[i], c), bc2(nwk[i]), acc);
+        spr(e, c, add2(pr(v, c), acc));
     }
 #pragma unroll
-    for (int c = 0; c < M; ++c) {
-        const float be = beta * e[c];
+    for (int c = 0; c < M; c += 2) {
+        const float2 be = mul2(bc2(beta), pr(e, c));
 #pragma unroll
-        for (int i = 0; i < D; ++i) Mm[i][c] = fmaf(a[i], Mm[i][c], be * u[i]);
+        for (int i = 0; i < D; ++i) spr(Mm[i], c, fma2(bc2(a[i]), pr(Mm[i], c), mul2(be, bc2(u[i]))));
     }
 }
 
@@ -602,13 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
             mean_step<D, M>(Mm, k, a, v, u, beta, e);
             rd.queries(tau, qv);
             float y[M];
-#pragma unroll
-            for (int c = 0; c < M; ++c) {
-                float acc = 0.f;
-#pragma unroll
-                for (int i = 0; i < D; ++i) acc = fmaf(Mm[i][c], qv[i], acc);
-                y[c] = acc;
-            }
+            colsum2<D, M>(Mm, qv, y);
             if (tau == 0) {
                 // the output staging was last read by tile q-1's output stores
                 if (lane == 0) bulk_wait_read<0>();
@@ -872,13 +942,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 mean_step<D, M>(Mm, k, a, v, u, fabsf(sel4v(b4, tau)), e);
                 rd.queries(tau, qv);
                 float y[M];
-#pragma unroll
-                for (int c = 0; c < M; ++c) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int i = 0; i < D; ++i) acc = fmaf(Mm[i][c], qv[i], acc);
-                    y[c] = acc;
-                }
+                colsum2<D, M>(Mm, qv, y);
                 line_store<M, float>(yb, lane, tau, y);
             }
             mbar_arrive(gfree + b);  // done with this gains block
@@ -1248,12 +1312,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
                     float gy[M];
                     rd.gy(tau, gy);
 #pragma unroll
-                    for (int i = 0; i < D; ++i) {
-                        float acc = 0.f;
-#pragma unroll
-                        for (int c = 0; c < M; ++c) acc = fmaf(Mm[i][c], gy[c], acc);
-                        gq[i] = acc;
-                    }
+                    for (int i = 0; i < D; ++i) gq[i] = dot2<M>(Mm[i], gy);
                 } else {
 #pragma unroll
                     for (int i = 0; i < D; ++i) gq[i] = 0.f;
@@ -1284,27 +1343,12 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
                 float qv[D], gy[M];
                 rd.queries(tau, qv);
                 rd.gy(tau, gy);
-#pragma unroll
-                for (int i = 0; i < D; ++i)
-#pragma unroll
-                    for (int c = 0; c < M; ++c) gM[i][c] = fmaf(qv[i], gy[c], gM[i][c]);
+                add_outer2<D, M>(gM, qv, gy);
             }
-            float ge[M], h[D], gb = 0.f;
+            float ge[M], h[D];
+            float gb = gain_adjoint2<D, M>(gM, u, e, beta, ge);  // u^T gM' e
 #pragma unroll
-            for (int c = 0; c < M; ++c) {
-                float acc = 0.f;
-#pragma unroll
-                for (int i = 0; i < D; ++i) acc = fmaf(gM[i][c], u[i], acc);
-                ge[c] = beta * acc;
-                gb = fmaf(e[c], acc, gb);  // u^T gM' e
-            }
-#pragma unroll
-            for (int i = 0; i < D; ++i) {
-                float acc = 0.f;
-#pragma unroll
-                for (int c = 0; c < M; ++c) acc = fmaf(gM[i][c], e[c], acc);
-                h[i] = acc;
-            }
+            for (int i = 0; i < D; ++i) h[i] = dot2<M>(gM[i], e);
             // pre-step mean: -A M ge (keys), decay gradient, dL/d(pre-step mean)
             float pk[D], gam[D];
             constexpr int RB = (D * M >= 32) ? 32 / M : D;  // rows per TMEM load
@@ -1323,16 +1367,7 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
 #pragma unroll
                 for (int ii = 0; ii < RB; ++ii) {
                     const int i = r0 + ii;
-                    float pki = 0.f, gai = 0.f;
-#pragma unroll
-                    for (int c = 0; c < M; ++c) {
-                        pki = fmaf(Mp[ii][c], ge[c], pki);
-                        const float gmb = fmaf(-k[i], ge[c], gM[i][c]);
-                        if constexpr (NEED_DYN) gai = fmaf(gmb, Mp[ii][c], gai);
-                        gM[i][c] = a[i] * gmb;
-                    }
-                    pk[i] = pki;
-                    gam[i] = gai;
+                    mean_row_adjoint2<M, NEED_DYN>(gM[i], Mp[ii], ge, k[i], a[i], pk[i], gam[i]);
                 }
             }
             // covariance adjoint
@@ -1883,12 +1918,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                     float gy[M];
                     rd.gy(tau, gy);
 #pragma unroll
-                    for (int i = 0; i < D; ++i) {
-                        float acc = 0.f;
-#pragma unroll
-                        for (int c = 0; c < M; ++c) acc = fmaf(Mm[i][c], gy[c], acc);
-                        gq[i] = acc;
-                    }
+                    for (int i = 0; i < D; ++i) gq[i] = dot2<M>(Mm[i], gy);
                 } else {
 #pragma unroll
                     for (int i = 0; i < D; ++i) gq[i] = 0.f;
@@ -1910,28 +1940,13 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                     float qv[D], gy[M];
                     rd.queries(tau, qv);
                     rd.gy(tau, gy);
-#pragma unroll
-                    for (int i = 0; i < D; ++i)
-#pragma unroll
-                        for (int c = 0; c < M; ++c) gM[i][c] = fmaf(qv[i], gy[c], gM[i][c]);
+                    add_outer2<D, M>(gM, qv, gy);
                 }
                 float xv[XF];  // h, pk, gam, u.gM'.e
-                float ge[M], gb = 0.f;
+                float ge[M];
+                const float gb = gain_adjoint2<D, M>(gM, u, e, beta, ge);
 #pragma unroll
-                for (int c = 0; c < M; ++c) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int i = 0; i < D; ++i) acc = fmaf(gM[i][c], u[i], acc);
-                    ge[c] = beta * acc;
-                    gb = fmaf(e[c], acc, gb);
-                }
-#pragma unroll
-                for (int i = 0; i < D; ++i) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int c = 0; c < M; ++c) acc = fmaf(gM[i][c], e[c], acc);
-                    xv[i] = acc;
-                }
+                for (int i = 0; i < D; ++i) xv[i] = dot2<M>(gM[i], e);
                 constexpr int RB = 32 / M;  // rows per TMEM load
 #pragma unroll
                 for (int r0 = 0; r0 < D; r0 += RB) {
@@ -1944,16 +1959,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 #pragma unroll
                     for (int ii = 0; ii < RB; ++ii) {
                         const int i = r0 + ii;
-                        float pki = 0.f, gai = 0.f;
-#pragma unroll
-                        for (int c = 0; c < M; ++c) {
-                            pki = fmaf(Mp[ii][c], ge[c], pki);
-                            const float gmb = fmaf(-k[i], ge[c], gM[i][c]);
-                            if constexpr (NEED_DYN) gai = fmaf(gmb, Mp[ii][c], gai);
-                            gM[i][c] = a[i] * gmb;
-                        }
-                        xv[D + i] = pki;
-                        xv[2 * D + i] = gai;
+                        mean_row_adjoint2<M, NEED_DYN>(gM[i], Mp[ii], ge, k[i], a[i], xv[D + i], xv[2 * D + i]);
                     }
                 }
                 xv[3 * D] = gb;
