@@ -47,6 +47,10 @@ _SIGNATURES = {
     "bssm_backward_noalloc_max_scratch_bytes": ([], _sz),
     "bssm_backward_chunked_noalloc": ([_i, _i, _i, _i, _i, _i] + [_vp] * 21 + [_l, _l, _i, _d, _vp], _i),
     "bssm_check_values": ([_vp, _l, _i, _vp, _vp], _i),
+    "bssm_envelope_partial_floats": ([_l, _l, _i, _i, _i], _l),
+    "bssm_envelope_prologue": ([_vp, _i, _l, _l, _i, _i, _i, _l] + [_vp] * 5 + [_i] + [_vp] * 4, _i),
+    "bssm_envelope_prologue_backward": ([_vp, _i, _l, _l, _i, _i, _i, _l] + [_vp] * 5 + [_i] + [_vp] * 4
+                                        + [_l, _vp, _vp, _vp, _l, _vp], _i),
     "bssm_debug_wait_timeouts": ([], ctypes.c_uint),
     "bssm_debug_last_family": ([], _i),
 }
@@ -173,3 +177,26 @@ FAMILIES = {0: None, 1: "chain", 2: "staged", 3: "v1"}
 def last_family() -> str | None:
     """Kernel family of this thread's last forward/backward call."""
     return FAMILIES[int(load().bssm_debug_last_family())]
+
+
+def envelope_partial_floats(batch, tokens, heads, key_dim, head_dim) -> int:
+    return int(load().bssm_envelope_partial_floats(batch, tokens, heads, key_dim, head_dim))
+
+
+def envelope_prologue(projected, in_dtype, batch, tokens, heads, key_dim, head_dim, row_stride, conv_weight,
+                      aux_bias, keys, queries, values, out_dtype, decay, process, observation, stream) -> None:
+    rc = load().bssm_envelope_prologue(ptr(projected), in_dtype, batch, tokens, heads, key_dim, head_dim,
+                                       row_stride, ptr(conv_weight), ptr(aux_bias), ptr(keys), ptr(queries),
+                                       ptr(values), out_dtype, ptr(decay), ptr(process), ptr(observation), stream)
+    check(rc, "bssm_envelope_prologue")
+
+
+def envelope_prologue_backward(projected, in_dtype, batch, tokens, heads, key_dim, head_dim, row_stride,
+                               conv_weight, aux_bias, gk, gq, gv, out_dtype, gdecay, gprocess, gobservation,
+                               gprojected, grad_row_stride, gconv_weight, gaux_bias, workspace, stream) -> None:
+    rc = load().bssm_envelope_prologue_backward(
+        ptr(projected), in_dtype, batch, tokens, heads, key_dim, head_dim, row_stride, ptr(conv_weight),
+        ptr(aux_bias), ptr(gk), ptr(gq), ptr(gv), out_dtype, ptr(gdecay), ptr(gprocess), ptr(gobservation),
+        ptr(gprojected), grad_row_stride, ptr(gconv_weight), ptr(gaux_bias), ptr(workspace),
+        0 if workspace is None else workspace.numel(), stream)
+    check(rc, "bssm_envelope_prologue_backward")

@@ -1,0 +1,168 @@
+"""BayesianMixer paper-feature prologue: projection rows -> recurrence inputs.
+
+catid/bayes-ssm ``example/train_6layer.py`` builds the recurrence's inputs
+from one fused projection per token (``BayesianMixer.forward``, :579-700, with
+``fuse_paper_qkv`` / ``fuse_paper_projection`` and learned dynamics):
+
+* a causal depthwise length-4 convolution over the Q/K/V channels
+  (``CausalDepthwise4``, :160-191; ``nn.Conv1d`` with left padding 3 is the
+  same map);
+* SiLU on each stream, then per-head ``F.normalize`` of q and k (:629-639);
+* process / observation variance ``softplus(noise + bias) + 1e-4`` (:665-666)
+  and decay ``exp(-softplus(logit + bias))`` (:698);
+* every stream permuted to chain-major ``[B*H, T, .]`` (:647-650, :699-701).
+
+:func:`paper_prologue` does all of it in one sm_100a kernel on CUDA tensors
+(``csrc/bssm_envelope.cu``), with a one-kernel backward that also sums the
+convolution-weight and auxiliary-bias gradients deterministically.  On CPU
+tensors it runs :func:`paper_prologue_torch`, the same op chain in PyTorch.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor
+
+from . import _capi
+
+_DTYPES = {torch.float32: _capi.BSSM_F32, torch.bfloat16: _capi.BSSM_BF16}
+
+
+def _widths(heads: int, key_dim: int, head_dim: int) -> tuple[int, int, int, int]:
+    sw, w = heads * key_dim, heads * head_dim
+    return sw, w, 2 * sw + w, sw + 2 * heads  # state width, width, conv channels, aux channels
+
+
+def paper_prologue_torch(projected: Tensor, conv_weight: Tensor, aux_bias: Optional[Tensor], *, heads: int,
+                         key_dim: int, head_dim: int):
+    """The reference's op chain in PyTorch, computed in float32.
+
+    Returns ``(keys, queries, values, decay, process, observation)`` shaped
+    ``[B*H, T, D]``, ``[B*H, T, D]``, ``[B*H, T, head_dim]``, ``[B*H, T, D]``,
+    ``[B*H, T]``, ``[B*H, T]``.
+    """
+    b, t, _ = projected.shape
+    sw, w, c, aux_w = _widths(heads, key_dim, head_dim)
+    x = projected.float()
+    qkv = x[..., :c]
+    aux = x[..., c:c + aux_w]
+    if aux_bias is not None:
+        aux = aux + aux_bias.float()
+    taps = conv_weight.float().reshape(c, 4)
+    padded = F.pad(qkv.transpose(1, 2), (3, 0))
+    y = padded[..., :t] * taps[:, 0].view(1, -1, 1)
+    y = y + padded[..., 1:t + 1] * taps[:, 1].view(1, -1, 1)
+    y = y + padded[..., 2:t + 2] * taps[:, 2].view(1, -1, 1)
+    y = y + padded[..., 3:t + 3] * taps[:, 3].view(1, -1, 1)
+    q_in, k_in, v_in = y.transpose(1, 2).split((sw, sw, w), dim=-1)
+
+    def heads_first(z, dim):
+        return z.reshape(b, t, heads, dim).permute(0, 2, 1, 3).reshape(b * heads, t, dim)
+
+    q = heads_first(F.normalize(F.silu(q_in).view(b, t, heads, key_dim), dim=-1), key_dim)
+    k = heads_first(F.normalize(F.silu(k_in).view(b, t, heads, key_dim), dim=-1), key_dim)
+    v = heads_first(F.silu(v_in), head_dim)
+    noise = aux[..., sw:].view(b, t, heads, 2)
+    process = (F.softplus(noise[..., 0]) + 1e-4).permute(0, 2, 1).reshape(b * heads, t)
+    observation = (F.softplus(noise[..., 1]) + 1e-4).permute(0, 2, 1).reshape(b * heads, t)
+    decay = heads_first(torch.exp(-F.softplus(aux[..., :sw])), key_dim)
+    return k, q, v, decay, process, observation
+
+
+def _rows(x: Tensor) -> int:
+    """Row stride (elements) of a [B, T, P] tensor whose rows are evenly spaced."""
+    if x.stride(-1) != 1 or (x.shape[0] > 1 and x.stride(0) != x.shape[1] * x.stride(1)):
+        raise ValueError("projected must have unit channel stride and evenly spaced token rows")
+    return x.stride(1)
+
+
+class _PaperPrologue(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, projected, conv_weight, aux_bias, heads, key_dim, head_dim, out_dtype):
+        b, t, _ = projected.shape
+        sw, w, c, aux_w = _widths(heads, key_dim, head_dim)
+        dev = projected.device
+        wt = conv_weight.detach().float().reshape(c, 4).contiguous()
+        bias = None if aux_bias is None else aux_bias.detach().float().contiguous()
+        n = b * heads
+        keys = torch.empty(n, t, key_dim, device=dev, dtype=out_dtype)
+        queries = torch.empty_like(keys)
+        values = torch.empty(n, t, head_dim, device=dev, dtype=out_dtype)
+        decay = torch.empty(n, t, key_dim, device=dev, dtype=torch.float32)
+        process = torch.empty(n, t, device=dev, dtype=torch.float32)
+        observation = torch.empty_like(process)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        with torch.cuda.device(dev):
+            _capi.envelope_prologue(projected, _DTYPES[projected.dtype], b, t, heads, key_dim, head_dim,
+                                    _rows(projected), wt, bias, keys, queries, values, _DTYPES[out_dtype], decay,
+                                    process, observation, stream)
+        ctx.save_for_backward(projected, wt, bias)
+        ctx.dims = (heads, key_dim, head_dim, out_dtype, conv_weight.dtype,
+                    None if aux_bias is None else aux_bias.dtype, tuple(conv_weight.shape))
+        ctx.set_materialize_grads(False)
+        return keys, queries, values, decay, process, observation
+
+    @staticmethod
+    def backward(ctx, gk, gq, gv, gd, gp, go):
+        projected, wt, bias = ctx.saved_tensors
+        heads, key_dim, head_dim, out_dtype, w_dtype, b_dtype, w_shape = ctx.dims
+        b, t, p = projected.shape
+        dev = projected.device
+
+        def prep(g, dtype):
+            return None if g is None else g.to(dtype).contiguous()
+
+        gk, gq, gv = prep(gk, out_dtype), prep(gq, out_dtype), prep(gv, out_dtype)
+        gd, gp, go = prep(gd, torch.float32), prep(gp, torch.float32), prep(go, torch.float32)
+        gx = torch.empty(b, t, p, device=dev, dtype=projected.dtype)
+        gw = torch.empty(wt.shape, device=dev, dtype=torch.float32)
+        gb = None if bias is None else torch.empty_like(bias)
+        ws = torch.empty(_capi.envelope_partial_floats(b, t, heads, key_dim, head_dim), device=dev,
+                         dtype=torch.float32)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        with torch.cuda.device(dev):
+            _capi.envelope_prologue_backward(projected, _DTYPES[projected.dtype], b, t, heads, key_dim, head_dim,
+                                             _rows(projected), wt, bias, gk, gq, gv, _DTYPES[out_dtype], gd, gp, go,
+                                             gx, p, gw, gb, ws, stream)
+        gw = gw.reshape(w_shape).to(w_dtype)
+        if gb is not None:
+            gb = gb.to(b_dtype)
+        return gx, gw, gb, None, None, None, None
+
+
+def paper_prologue(projected: Tensor, conv_weight: Tensor, aux_bias: Optional[Tensor] = None, *, heads: int,
+                   key_dim: int, head_dim: int, out_dtype: torch.dtype = torch.float32):
+    """Recurrence inputs from the fused projection (see the module docstring).
+
+    ``projected`` is ``[B, T, 2*H*D + H*head_dim + H*D + 2*H]``: the q, k and v
+    streams, the decay logits and the per-head (process, observation) noise
+    pairs.  ``conv_weight`` is the depthwise Conv1d weight ``[C, 1, 4]`` over
+    the q/k/v channels; ``aux_bias`` is added to the auxiliary channels.
+    ``out_dtype`` (float32 or bfloat16) is the dtype of keys, queries and
+    values; decay and the variances are float32.  Gradients flow to
+    ``projected``, ``conv_weight`` and ``aux_bias``.
+    """
+    if projected.ndim != 3:
+        raise ValueError("projected must be [batch, tokens, channels]")
+    sw, w, c, aux_w = _widths(heads, key_dim, head_dim)
+    if projected.shape[-1] != c + aux_w:
+        raise ValueError(f"projected must have {c + aux_w} channels (q, k, v, decay logits, noise), "
+                         f"got {projected.shape[-1]}")
+    if conv_weight.numel() != 4 * c:
+        raise ValueError(f"conv_weight must be [{c}, 1, 4]")
+    if aux_bias is not None and aux_bias.numel() != aux_w:
+        raise ValueError(f"aux_bias must have {aux_w} entries")
+    if not projected.is_cuda:
+        return paper_prologue_torch(projected, conv_weight, aux_bias, heads=heads, key_dim=key_dim,
+                                    head_dim=head_dim)
+    if projected.dtype not in _DTYPES or out_dtype not in _DTYPES:
+        raise TypeError("paper_prologue on CUDA takes float32 or bfloat16 projections and outputs")
+    if key_dim < 2 or key_dim > 64 or key_dim & (key_dim - 1) or head_dim % 2:
+        raise NotImplementedError("paper_prologue on CUDA needs key_dim a power of two in [2, 64] and an even "
+                                  f"head_dim (got {key_dim}, {head_dim}); use paper_prologue_torch")
+    return _PaperPrologue.apply(projected, conv_weight, aux_bias, heads, key_dim, head_dim, out_dtype)
+
+
+__all__ = ["paper_prologue", "paper_prologue_torch"]

@@ -278,6 +278,48 @@ int bssm_backward_chunked_noalloc(int key_dim, int value_dim, int io_dtype, int 
 int bssm_check_values(const void *x, long n, int dtype, unsigned *flags, void *stream);
 
 /*
+ * BayesianMixer paper-feature prologue (replaces the op chain of
+ * example/train_6layer.py:579-700 for the fused Q/K/V + auxiliary projection
+ * with learned diagonal dynamics: CausalDepthwise4 :160-191 over the Q/K/V
+ * channels, F.silu :629-637, F.normalize of q and k :638-639, softplus noise
+ * :665-666, exp(-softplus) decay :698, and the permutes to [B*H, T, .]
+ * :647-650,699-701).
+ *
+ * `projected` is [batch, tokens, row_stride] (BSSM_F32 or BSSM_BF16), whose
+ * first 2 SW + W + SW + 2H channels are, in order, the q (SW = heads *
+ * key_dim), k (SW) and v (W = heads * head_dim) streams, the decay logits (SW)
+ * and the per-head (process, observation) noise pairs (2H).  conv_weight is
+ * the Conv1d weight [2 SW + W, 1, 4] as float32; aux_bias [SW + 2H] float32 is
+ * added to the auxiliary channels (may be null).  Outputs: keys and queries
+ * [batch*heads, tokens, key_dim] and values [batch*heads, tokens, head_dim]
+ * in out_dtype; decay [batch*heads, tokens, key_dim], process and observation
+ * [batch*heads, tokens] in float32.  key_dim must be a power of two in
+ * [2, 64] and head_dim even; row_stride even; tensors 8-byte aligned.
+ */
+int bssm_envelope_prologue(const void *projected, int in_dtype, long batch, long tokens, int heads, int key_dim,
+                           int head_dim, long row_stride, const float *conv_weight, const float *aux_bias,
+                           void *keys, void *queries, void *values, int out_dtype, float *decay, float *process,
+                           float *observation, void *stream);
+
+/*
+ * Backward of bssm_envelope_prologue.  Gradients of the six outputs (any may
+ * be null = zero; keys/queries/values gradients in out_dtype) give
+ * grad_projected (the prologue's channels of [batch, tokens,
+ * grad_row_stride] in in_dtype; other channels are not written),
+ * grad_conv_weight [2 SW + W, 4] and grad_aux_bias [SW + 2H] (null to skip),
+ * both float32 and summed deterministically.  `workspace` (32-byte aligned)
+ * holds bssm_envelope_partial_floats() floats of per-span partial sums.
+ */
+long bssm_envelope_partial_floats(long batch, long tokens, int heads, int key_dim, int head_dim);
+int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long batch, long tokens, int heads,
+                                    int key_dim, int head_dim, long row_stride, const float *conv_weight,
+                                    const float *aux_bias, const void *grad_keys, const void *grad_queries,
+                                    const void *grad_values, int out_dtype, const float *grad_decay,
+                                    const float *grad_process, const float *grad_observation, void *grad_projected,
+                                    long grad_row_stride, float *grad_conv_weight, float *grad_aux_bias,
+                                    float *workspace, long workspace_floats, void *stream);
+
+/*
  * Diagnostics (no counterpart in the reference).
  *
  * The thread-per-chain kernels wait on shared-memory barriers for their own
