@@ -27,6 +27,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "bayes_ssm_b200.h"
 #include "bssm_internal.h"
@@ -35,6 +36,25 @@ namespace bssm {
 namespace env {
 
 constexpr int kThreads = 256;
+// Tokens per span (one thread walks one span) and the widest channel group,
+// per direction, as measured at the config-3 mixer shape (B256 T512 H64 D8):
+// forward 4 channels over 64 tokens (0.72 ms; 2 over 128: 0.87 ms; 8 over
+// 32: 1.27 ms), backward 2 over 128 (2.0 ms; 4 over 64 and 32 no faster).
+// Both kernels are bound by instruction issue and load latency, not DRAM.
+#ifndef BSSM_ENV_FWD_SPAN
+#define BSSM_ENV_FWD_SPAN 64
+#endif
+#ifndef BSSM_ENV_BWD_SPAN
+#define BSSM_ENV_BWD_SPAN 128
+#endif
+#ifndef BSSM_ENV_FWD_CW
+#define BSSM_ENV_FWD_CW 4
+#endif
+#ifndef BSSM_ENV_BWD_CW
+#define BSSM_ENV_BWD_CW 2
+#endif
+constexpr int kFwdSpan = BSSM_ENV_FWD_SPAN, kBwdSpan = BSSM_ENV_BWD_SPAN;
+constexpr int kFwdCW = BSSM_ENV_FWD_CW, kBwdCW = BSSM_ENV_BWD_CW;
 constexpr float kNormEps = 1e-12f;  // F.normalize's default
 constexpr float kNoiseFloor = 1e-4f;
 
@@ -71,33 +91,124 @@ __host__ __device__ __forceinline__ Chan classify(const Shape &s, int pair) {
     return {kIdle, 0, 0};
 }
 
-template <bool BF>
-__device__ __forceinline__ float2 ld2(const void *base, long idx) {
+// N consecutive elements (N = 2, 4 or 8) as floats; idx is a multiple of N
+// and the base is aligned for the N-element vector.  Inputs are read-only for
+// the whole launch, so they load through the non-coherent path: that also
+// lets the compiler issue a later token's loads ahead of this token's stores,
+// which it could not otherwise prove independent.
+template <bool BF, int N>
+__device__ __forceinline__ void ldn(const void *base, long idx, float *v) {
     if constexpr (BF) {
-        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162 *>(static_cast<const __nv_bfloat16 *>(base) + idx);
-        return __bfloat1622float2(v);
+        const __nv_bfloat16 *p = static_cast<const __nv_bfloat16 *>(base) + idx;
+        if constexpr (N == 2) {
+            const unsigned raw = __ldg(reinterpret_cast<const unsigned *>(p));
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&raw));
+            v[0] = f.x, v[1] = f.y;
+        } else {
+            using V = typename std::conditional<N == 4, uint2, uint4>::type;
+            const V raw = __ldg(reinterpret_cast<const V *>(p));
+            const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) {
+                const float2 f = __bfloat1622float2(h[i]);
+                v[2 * i] = f.x, v[2 * i + 1] = f.y;
+            }
+        }
     } else {
-        return *reinterpret_cast<const float2 *>(static_cast<const float *>(base) + idx);
+        const float *p = static_cast<const float *>(base) + idx;
+        if constexpr (N == 2) {
+            const float2 f = __ldg(reinterpret_cast<const float2 *>(p));
+            v[0] = f.x, v[1] = f.y;
+        } else {
+#pragma unroll
+            for (int i = 0; i < N; i += 4) {
+                const float4 f = __ldg(reinterpret_cast<const float4 *>(p + i));
+                v[i] = f.x, v[i + 1] = f.y, v[i + 2] = f.z, v[i + 3] = f.w;
+            }
+        }
     }
 }
-template <bool BF>
-__device__ __forceinline__ void st2(void *base, long idx, float2 v) {
+template <bool BF, int N>
+__device__ __forceinline__ void stn(void *base, long idx, const float *v) {
     if constexpr (BF) {
-        *reinterpret_cast<__nv_bfloat162 *>(static_cast<__nv_bfloat16 *>(base) + idx) = __float22bfloat162_rn(v);
+        __nv_bfloat16 *p = static_cast<__nv_bfloat16 *>(base) + idx;
+        if constexpr (N == 2) {
+            *reinterpret_cast<__nv_bfloat162 *>(p) = __float22bfloat162_rn(make_float2(v[0], v[1]));
+        } else {
+            using V = typename std::conditional<N == 4, uint2, uint4>::type;
+            V raw;
+            __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&raw);
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) h[i] = __float22bfloat162_rn(make_float2(v[2 * i], v[2 * i + 1]));
+            *reinterpret_cast<V *>(p) = raw;
+        }
     } else {
-        *reinterpret_cast<float2 *>(static_cast<float *>(base) + idx) = v;
+        float *p = static_cast<float *>(base) + idx;
+        if constexpr (N == 2) {
+            *reinterpret_cast<float2 *>(p) = make_float2(v[0], v[1]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < N; i += 4) *reinterpret_cast<float4 *>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
+    }
+}
+// CW / d whole heads of d channels (d = 2 or 4, d < CW) at consecutive
+// chains: head gi of the thread is row ((chain + gi) * T + t) of width d.
+// Every array offset is a compile-time constant, so v stays in registers.
+template <bool BF, int CW>
+__device__ __forceinline__ void st_heads(void *base, long chain, long t, long T, int d, const float *v) {
+    if (d == 2) {
+#pragma unroll
+        for (int gi = 0; gi < CW / 2; ++gi) stn<BF, 2>(base, ((chain + gi) * T + t) * 2, v + 2 * gi);
+    } else {
+        if constexpr (CW >= 8) {
+#pragma unroll
+            for (int gi = 0; gi < CW / 4; ++gi) stn<BF, 4>(base, ((chain + gi) * T + t) * 4, v + 4 * gi);
+        }
+    }
+}
+template <bool BF, int CW>
+__device__ __forceinline__ void ld_heads(const void *base, long chain, long t, long T, int d, float *v) {
+    if (d == 2) {
+#pragma unroll
+        for (int gi = 0; gi < CW / 2; ++gi) ldn<BF, 2>(base, ((chain + gi) * T + t) * 2, v + 2 * gi);
+    } else {
+        if constexpr (CW >= 8) {
+#pragma unroll
+            for (int gi = 0; gi < CW / 4; ++gi) ldn<BF, 4>(base, ((chain + gi) * T + t) * 4, v + 4 * gi);
+        }
     }
 }
 
-__device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+// The SiLU, normalisation and decay use the fast exponential and division
+// intrinsics (a few ulp; the parity tests bound the result); the variances
+// keep softplus exact, since a small variance is read relative to 1e-4.
+__device__ __forceinline__ float sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 // torch.nn.functional.softplus with beta 1, threshold 20
 __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
-__device__ __forceinline__ float softplus_grad(float x) { return x > 20.f ? 1.f : sigmoid(x); }
+__device__ __forceinline__ float softplus_grad(float x) { return x > 20.f ? 1.f : 1.0f / (1.0f + expf(-x)); }
+// exp(-softplus(z)) = 1 / (1 + e^z)
+__device__ __forceinline__ float decay_of(float z) { return __fdividef(1.0f, 1.0f + __expf(z)); }
+// 1 / max(sqrt(ss), eps) for F.normalize
+__device__ __forceinline__ float inv_norm(float ss) { return rsqrtf(fmaxf(ss, kNormEps * kNormEps)); }
 
-// Sum over the D/2 lanes of this lane's head group (all lanes call it).
-__device__ __forceinline__ float head_sum(float v, int group) {
-    for (int off = 1; off < group; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+// Sum over `lanes` consecutive lanes (a power of two; all lanes call it).
+__device__ __forceinline__ float lane_sum(float v, int lanes) {
+    for (int off = 1; off < lanes; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
     return v;
+}
+
+// How a thread's CW channels map onto heads of D (q, k, decay): one head
+// spread over D / CW lanes (D >= CW), or CW / D whole heads (D < CW).
+struct HeadMap {
+    int dg;     // channels per head group inside the thread
+    int ng;     // head groups inside the thread
+    int lanes;  // lanes per head
+    int shift;  // log2(dg): channel j of the thread is in head group j >> shift
+};
+template <int CW>
+__device__ __forceinline__ HeadMap head_map(int d) {
+    return d >= CW ? HeadMap{CW, 1, d / CW, 31 - __clz(CW)} : HeadMap{d, CW / d, 1, 31 - __clz(d)};
 }
 
 struct ProArgs {
@@ -109,66 +220,105 @@ struct ProArgs {
     float *process, *observation;  // [B*H, T]
 };
 
-template <bool IN_BF, bool OUT_BF>
+// Thread = CW adjacent channels of one stream (every stream and head row
+// boundary falls on a multiple of CW), walking one token span.
+template <bool IN_BF, bool OUT_BF, int CW>
 __global__ void __launch_bounds__(kThreads) prologue_kernel(const Shape s, const ProArgs a) {
-    const int pair = static_cast<int>(blockIdx.x) * kThreads + threadIdx.x;
+    const int grp = static_cast<int>(blockIdx.x) * kThreads + threadIdx.x;
     const long bb = blockIdx.z;
     const long span = (s.t + s.tsplit - 1) / s.tsplit;
     const long t0 = static_cast<long>(blockIdx.y) * span;
     const long t1 = t0 + span < s.t ? t0 + span : s.t;
-    const Chan ch = pair < s.pairs() ? classify(s, pair) : Chan{kIdle, 0, 0};
-    const int group = s.d / 2;
-    const int c0 = 2 * pair;
-    const void *xrow = a.x;
+    const int c0 = CW * grp;
+    const Chan ch = c0 < s.conv_channels() + s.aux_channels() ? classify(s, c0 / 2) : Chan{kIdle, 0, 0};
+    const HeadMap hm = head_map<CW>(s.d);
     const long row0 = bb * s.t;
     const long chain = bb * s.heads + ch.head;
     const bool conv = ch.kind <= kV;
-    float2 w0{0.f, 0.f}, w1 = w0, w2 = w0, w3 = w0, bias = w0;
-    if (conv) {
-        w0 = make_float2(a.w[c0 * 4 + 0], a.w[c0 * 4 + 4]);
-        w1 = make_float2(a.w[c0 * 4 + 1], a.w[c0 * 4 + 5]);
-        w2 = make_float2(a.w[c0 * 4 + 2], a.w[c0 * 4 + 6]);
-        w3 = make_float2(a.w[c0 * 4 + 3], a.w[c0 * 4 + 7]);
-    } else if ((ch.kind == kDecay || ch.kind == kNoise) && a.bias != nullptr) {
-        const int ac = c0 - s.conv_channels();
-        bias = make_float2(a.bias[ac], a.bias[ac + 1]);
+    float w[4][CW], bias[CW];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+        bias[j] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w[k][j] = 0.f;
     }
-    // the window x[t-3], x[t-2], x[t-1]
-    float2 xm3{0.f, 0.f}, xm2 = xm3, xm1 = xm3;
     if (conv) {
-        if (t0 - 3 >= 0) xm3 = ld2<IN_BF>(xrow, (row0 + t0 - 3) * s.in_stride + c0);
-        if (t0 - 2 >= 0) xm2 = ld2<IN_BF>(xrow, (row0 + t0 - 2) * s.in_stride + c0);
-        if (t0 - 1 >= 0) xm1 = ld2<IN_BF>(xrow, (row0 + t0 - 1) * s.in_stride + c0);
+#pragma unroll
+        for (int j = 0; j < CW; ++j) {
+            const float4 wj = *reinterpret_cast<const float4 *>(a.w + (c0 + j) * 4);
+            w[0][j] = wj.x, w[1][j] = wj.y, w[2][j] = wj.z, w[3][j] = wj.w;
+        }
+    } else if (ch.kind != kIdle && a.bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < CW; ++j) bias[j] = a.bias[c0 - s.conv_channels() + j];
+    }
+    float xm3[CW], xm2[CW], xm1[CW], x[CW], o[CW];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) xm3[j] = xm2[j] = xm1[j] = 0.f;
+    if (conv) {
+        if (t0 - 3 >= 0) ldn<IN_BF, CW>(a.x, (row0 + t0 - 3) * s.in_stride + c0, xm3);
+        if (t0 - 2 >= 0) ldn<IN_BF, CW>(a.x, (row0 + t0 - 2) * s.in_stride + c0, xm2);
+        if (t0 - 1 >= 0) ldn<IN_BF, CW>(a.x, (row0 + t0 - 1) * s.in_stride + c0, xm1);
     }
 #pragma unroll 4
     for (long t = t0; t < t1; ++t) {
-        float2 x{0.f, 0.f};
-        if (ch.kind != kIdle) x = ld2<IN_BF>(xrow, (row0 + t) * s.in_stride + c0);
-        float2 o{0.f, 0.f};
-        float ss = 0.f;
-        if (conv) {
-            const float cx = fmaf(w3.x, x.x, fmaf(w2.x, xm1.x, fmaf(w1.x, xm2.x, w0.x * xm3.x)));
-            const float cy = fmaf(w3.y, x.y, fmaf(w2.y, xm1.y, fmaf(w1.y, xm2.y, w0.y * xm3.y)));
-            o = make_float2(cx * sigmoid(cx), cy * sigmoid(cy));
-            ss = ch.kind == kV ? 0.f : o.x * o.x + o.y * o.y;
-            xm3 = xm2;
-            xm2 = xm1;
-            xm1 = x;
+#pragma unroll
+        for (int j = 0; j < CW; ++j) x[j] = 0.f;
+        if (ch.kind != kIdle) ldn<IN_BF, CW>(a.x, (row0 + t) * s.in_stride + c0, x);
+        float ss[CW];
+#pragma unroll
+        for (int j = 0; j < CW; ++j) {
+            const float c = fmaf(w[3][j], x[j], fmaf(w[2][j], xm1[j], fmaf(w[1][j], xm2[j], w[0][j] * xm3[j])));
+            o[j] = c * sigmoid(c);
+            ss[j] = o[j] * o[j];
+            xm3[j] = xm2[j];
+            xm2[j] = xm1[j];
+            xm1[j] = x[j];
         }
-        ss = head_sum(ss, group);  // q and k heads only; other groups sum zeros
-        if (ch.kind == kQ || ch.kind == kK) {
-            const float r = 1.0f / fmaxf(sqrtf(ss), kNormEps);
-            o.x *= r;
-            o.y *= r;
-            st2<OUT_BF>(ch.kind == kQ ? a.q : a.k, (chain * s.t + t) * s.d + ch.within, o);
-        } else if (ch.kind == kV) {
-            st2<OUT_BF>(a.v, (chain * s.t + t) * s.hd + ch.within, o);
+        const bool qk = ch.kind == kQ || ch.kind == kK;
+        if (hm.ng == 1) {  // one head (part) per thread: reduce across its lanes
+            float tot = 0.f;
+#pragma unroll
+            for (int j = 0; j < CW; ++j) tot += ss[j];
+            tot = lane_sum(qk ? tot : 0.f, hm.lanes);
+            if (qk) {
+                const float r = inv_norm(tot);
+#pragma unroll
+                for (int j = 0; j < CW; ++j) o[j] *= r;
+                stn<OUT_BF, CW>(ch.kind == kQ ? a.q : a.k, (chain * s.t + t) * s.d + ch.within, o);
+            }
+        } else if (qk) {  // CW / D whole heads
+#pragma unroll
+            for (int gi = 0; gi < CW / 2; ++gi) {
+                if (gi >= hm.ng) break;
+                float tot = 0.f;
+#pragma unroll
+                for (int j = 0; j < CW; ++j)
+                    if ((j >> hm.shift) == gi) tot += ss[j];
+                const float r = inv_norm(tot);
+#pragma unroll
+                for (int j = 0; j < CW; ++j)
+                    if ((j >> hm.shift) == gi) o[j] *= r;
+            }
+            st_heads<OUT_BF, CW>(ch.kind == kQ ? a.q : a.k, chain, t, s.t, s.d, o);
+        }
+        if (ch.kind == kV) {
+            stn<OUT_BF, CW>(a.v, (chain * s.t + t) * s.hd + ch.within, o);
         } else if (ch.kind == kDecay) {
-            const float2 dcy = make_float2(expf(-softplus(x.x + bias.x)), expf(-softplus(x.y + bias.y)));
-            *reinterpret_cast<float2 *>(a.decay + (chain * s.t + t) * s.d + ch.within) = dcy;
+            float dcy[CW];
+#pragma unroll
+            for (int j = 0; j < CW; ++j) dcy[j] = decay_of(x[j] + bias[j]);
+            if (hm.ng == 1) {
+                stn<false, CW>(a.decay, (chain * s.t + t) * s.d + ch.within, dcy);
+            } else {
+                st_heads<false, CW>(a.decay, chain, t, s.t, s.d, dcy);
+            }
         } else if (ch.kind == kNoise) {
-            a.process[chain * s.t + t] = softplus(x.x + bias.x) + kNoiseFloor;
-            a.observation[chain * s.t + t] = softplus(x.y + bias.y) + kNoiseFloor;
+#pragma unroll
+            for (int i = 0; i < CW / 2; ++i) {
+                a.process[(chain + i) * s.t + t] = softplus(x[2 * i] + bias[2 * i]) + kNoiseFloor;
+                a.observation[(chain + i) * s.t + t] = softplus(x[2 * i + 1] + bias[2 * i + 1]) + kNoiseFloor;
+            }
         }
     }
 }
@@ -180,7 +330,7 @@ struct EnvBwdArgs {
     const float *gdecay, *gprocess, *gobservation;
     void *gx;        // [B, T, gx_stride] (the prologue's channels only)
     long gx_stride;
-    float *partial;  // [B * tsplit][4 C + SW + 2H]
+    float *partial;  // [B * tsplit][partial_cols]
 };
 
 // Backward of one token span: walk the tokens downwards, recompute the
@@ -188,122 +338,179 @@ struct EnvBwdArgs {
 // gx[t] = sum_j w_j gc[t + 3 - j].  The span also recomputes the 3 tokens
 // after it (their gc feeds its last gx) without counting them in the weight
 // gradient, which their own span does.
-template <bool IN_BF, bool OUT_BF>
+template <bool IN_BF, bool OUT_BF, int CW>
 __global__ void __launch_bounds__(kThreads) prologue_backward_kernel(const Shape s, const EnvBwdArgs a) {
-    const int pair = static_cast<int>(blockIdx.x) * kThreads + threadIdx.x;
+    const int grp = static_cast<int>(blockIdx.x) * kThreads + threadIdx.x;
     const long bb = blockIdx.z;
     const long span = (s.t + s.tsplit - 1) / s.tsplit;
     const long t0 = static_cast<long>(blockIdx.y) * span;
     const long t1 = t0 + span < s.t ? t0 + span : s.t;
     const long hi = t1 + 3 < s.t ? t1 + 3 : s.t;
-    const Chan ch = pair < s.pairs() ? classify(s, pair) : Chan{kIdle, 0, 0};
-    const int group = s.d / 2;
-    const int c0 = 2 * pair;
+    const int c0 = CW * grp;
+    const int C = s.conv_channels();
+    const Chan ch = c0 < C + s.aux_channels() ? classify(s, c0 / 2) : Chan{kIdle, 0, 0};
+    const HeadMap hm = head_map<CW>(s.d);
     const long row0 = bb * s.t;
     const long chain = bb * s.heads + ch.head;
     const bool conv = ch.kind <= kV;
-    const int C = s.conv_channels();
+    const bool qk = ch.kind == kQ || ch.kind == kK;
     float *const part = a.partial + (bb * s.tsplit + blockIdx.y) * static_cast<long>(s.partial_cols());
-    float2 w0{0.f, 0.f}, w1 = w0, w2 = w0, w3 = w0, bias = w0;
+    float w[4][CW], bias[CW], gw[4][CW], gb[CW];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+        bias[j] = gb[j] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w[k][j] = gw[k][j] = 0.f;
+    }
     if (conv) {
-        w0 = make_float2(a.w[c0 * 4 + 0], a.w[c0 * 4 + 4]);
-        w1 = make_float2(a.w[c0 * 4 + 1], a.w[c0 * 4 + 5]);
-        w2 = make_float2(a.w[c0 * 4 + 2], a.w[c0 * 4 + 6]);
-        w3 = make_float2(a.w[c0 * 4 + 3], a.w[c0 * 4 + 7]);
-    } else if ((ch.kind == kDecay || ch.kind == kNoise) && a.bias != nullptr) {
-        const int ac = c0 - C;
-        bias = make_float2(a.bias[ac], a.bias[ac + 1]);
+#pragma unroll
+        for (int j = 0; j < CW; ++j) {
+            const float4 wj = *reinterpret_cast<const float4 *>(a.w + (c0 + j) * 4);
+            w[0][j] = wj.x, w[1][j] = wj.y, w[2][j] = wj.z, w[3][j] = wj.w;
+        }
+    } else if (ch.kind != kIdle && a.bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < CW; ++j) bias[j] = a.bias[c0 - C + j];
     }
-    auto ldx = [&](long t) -> float2 {
-        return (t >= 0 && ch.kind != kIdle) ? ld2<IN_BF>(a.x, (row0 + t) * s.in_stride + c0) : make_float2(0.f, 0.f);
+    auto ldx = [&](long t, float *v) {
+#pragma unroll
+        for (int j = 0; j < CW; ++j) v[j] = 0.f;
+        if (t >= 0 && ch.kind != kIdle) ldn<IN_BF, CW>(a.x, (row0 + t) * s.in_stride + c0, v);
     };
-    // x[t-3 .. t] for t = hi - 1 (conv channels only)
-    float2 x3{0.f, 0.f}, x2 = x3, x1 = x3, x0 = x3;  // x0 = x[t], x1 = x[t-1], ...
+    const void *gsrc = ch.kind == kQ ? a.gq : ch.kind == kK ? a.gk : a.gv;
+    const int grow = ch.kind == kV ? s.hd : s.d;
+    // x0 = x[t], x1 = x[t-1], x2 = x[t-2], x3 = x[t-3] (conv channels)
+    float x0[CW], x1[CW], x2[CW], x3[CW];
+    float gp1[CW], gp2[CW], gp3[CW];  // gc[t+1], gc[t+2], gc[t+3]
+#pragma unroll
+    for (int j = 0; j < CW; ++j) x0[j] = x1[j] = x2[j] = x3[j] = gp1[j] = gp2[j] = gp3[j] = 0.f;
     if (conv && hi > t0) {
-        x0 = ldx(hi - 1);
-        x1 = ldx(hi - 2);
-        x2 = ldx(hi - 3);
+        ldx(hi - 1, x0);
+        ldx(hi - 2, x1);
+        ldx(hi - 3, x2);
     }
-    float2 gp1{0.f, 0.f}, gp2 = gp1, gp3 = gp1;  // gc[t+1], gc[t+2], gc[t+3]
-    float2 gw0{0.f, 0.f}, gw1 = gw0, gw2 = gw0, gw3 = gw0, gb = gw0;
-#pragma unroll 2
+#pragma unroll 1
     for (long t = hi - 1; t >= t0; --t) {
-        float2 gc{0.f, 0.f};
-        float ss = 0.f, dot = 0.f;
-        float2 o{0.f, 0.f}, g{0.f, 0.f}, ds{0.f, 0.f};
+        float gc[CW], g[CW], o[CW], ds[CW];
+#pragma unroll
+        for (int j = 0; j < CW; ++j) gc[j] = g[j] = o[j] = ds[j] = 0.f;
         if (conv) {
-            x3 = ldx(t - 3);
-            const float cx = fmaf(w3.x, x0.x, fmaf(w2.x, x1.x, fmaf(w1.x, x2.x, w0.x * x3.x)));
-            const float cy = fmaf(w3.y, x0.y, fmaf(w2.y, x1.y, fmaf(w1.y, x2.y, w0.y * x3.y)));
-            const float sx = sigmoid(cx), sy = sigmoid(cy);
-            o = make_float2(cx * sx, cy * sy);
-            ds = make_float2(sx * fmaf(cx, 1.f - sx, 1.f), sy * fmaf(cy, 1.f - sy, 1.f));  // silu'
-            const void *gsrc = ch.kind == kQ ? a.gq : ch.kind == kK ? a.gk : a.gv;
-            if (gsrc != nullptr)
-                g = ld2<OUT_BF>(gsrc, (chain * s.t + t) * (ch.kind == kV ? s.hd : s.d) + ch.within);
-            if (ch.kind != kV) ss = o.x * o.x + o.y * o.y;
+            ldx(t - 3, x3);
+#pragma unroll
+            for (int j = 0; j < CW; ++j) {
+                const float c = fmaf(w[3][j], x0[j], fmaf(w[2][j], x1[j], fmaf(w[1][j], x2[j], w[0][j] * x3[j])));
+                const float sg = sigmoid(c);
+                o[j] = c * sg;
+                ds[j] = sg * fmaf(c, 1.f - sg, 1.f);  // silu'
+            }
+            if (gsrc != nullptr) {
+                if (hm.ng == 1 || ch.kind == kV) {
+                    ldn<OUT_BF, CW>(gsrc, (chain * s.t + t) * grow + ch.within, g);
+                } else {
+                    ld_heads<OUT_BF, CW>(gsrc, chain, t, s.t, s.d, g);
+                }
+            }
         }
-        ss = head_sum(ss, group);
-        if (ch.kind == kQ || ch.kind == kK) {
-            const float n = sqrtf(ss);
-            const float r = 1.0f / fmaxf(n, kNormEps);
-            o.x *= r;  // the normalised output y
-            o.y *= r;
-            dot = o.x * g.x + o.y * g.y;
+        // q, k: y = s / max(|s|, eps); dy/ds = (I - y y^T) / |s| above eps, I / eps below
+        if (hm.ng == 1) {
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < CW; ++j) ss += o[j] * o[j];
+            ss = lane_sum(qk ? ss : 0.f, hm.lanes);
+            const float r = inv_norm(ss);
+            const bool above = ss > kNormEps * kNormEps;
+            float dot = 0.f;
+#pragma unroll
+            for (int j = 0; j < CW; ++j) dot += o[j] * r * g[j];
+            dot = lane_sum(qk ? dot : 0.f, hm.lanes);
+            if (qk) {
+                const float dd = above ? dot : 0.f;
+#pragma unroll
+                for (int j = 0; j < CW; ++j) gc[j] = (g[j] - o[j] * r * dd) * r * ds[j];
+            }
+        } else if (qk) {
+            for (int gi = 0; gi < hm.ng; ++gi) {
+                float ss = 0.f, dot = 0.f;
+#pragma unroll
+                for (int j = 0; j < CW; ++j)
+                    if ((j >> hm.shift) == gi) ss += o[j] * o[j];
+                const float r = inv_norm(ss);
+#pragma unroll
+                for (int j = 0; j < CW; ++j)
+                    if ((j >> hm.shift) == gi) dot += o[j] * r * g[j];
+                const float dd = ss > kNormEps * kNormEps ? dot : 0.f;
+#pragma unroll
+                for (int j = 0; j < CW; ++j)
+                    if ((j >> hm.shift) == gi) gc[j] = (g[j] - o[j] * r * dd) * r * ds[j];
+            }
         }
-        dot = head_sum(dot, group);
-        if (ch.kind == kQ || ch.kind == kK) {
-            // y = s / max(|s|, eps): dy/ds = (I - y y^T) / |s| above eps, I / eps below
-            const float n = sqrtf(ss), r = 1.0f / fmaxf(n, kNormEps);
-            const float dd = n > kNormEps ? dot : 0.f;
-            gc = make_float2((g.x - o.x * dd) * r * ds.x, (g.y - o.y * dd) * r * ds.y);
-        } else if (ch.kind == kV) {
-            gc = make_float2(g.x * ds.x, g.y * ds.y);
+        if (ch.kind == kV) {
+#pragma unroll
+            for (int j = 0; j < CW; ++j) gc[j] = g[j] * ds[j];
         }
         if (t < t1) {
             if (conv) {
-                const float2 gx = make_float2(fmaf(w0.x, gp3.x, fmaf(w1.x, gp2.x, fmaf(w2.x, gp1.x, w3.x * gc.x))),
-                                              fmaf(w0.y, gp3.y, fmaf(w1.y, gp2.y, fmaf(w2.y, gp1.y, w3.y * gc.y))));
-                st2<IN_BF>(a.gx, (row0 + t) * a.gx_stride + c0, gx);
-                gw0 = make_float2(fmaf(gc.x, x3.x, gw0.x), fmaf(gc.y, x3.y, gw0.y));
-                gw1 = make_float2(fmaf(gc.x, x2.x, gw1.x), fmaf(gc.y, x2.y, gw1.y));
-                gw2 = make_float2(fmaf(gc.x, x1.x, gw2.x), fmaf(gc.y, x1.y, gw2.y));
-                gw3 = make_float2(fmaf(gc.x, x0.x, gw3.x), fmaf(gc.y, x0.y, gw3.y));
-            } else if (ch.kind == kDecay) {
-                const float2 xv = ldx(t);
-                const float2 gd = a.gdecay != nullptr
-                                      ? *reinterpret_cast<const float2 *>(a.gdecay + (chain * s.t + t) * s.d + ch.within)
-                                      : make_float2(0.f, 0.f);
-                const float zx = xv.x + bias.x, zy = xv.y + bias.y;
-                // d/dz exp(-softplus(z)) = -exp(-softplus(z)) softplus'(z)
-                const float2 gz = make_float2(-gd.x * expf(-softplus(zx)) * softplus_grad(zx),
-                                              -gd.y * expf(-softplus(zy)) * softplus_grad(zy));
-                st2<IN_BF>(a.gx, (row0 + t) * a.gx_stride + c0, gz);
-                gb = make_float2(gb.x + gz.x, gb.y + gz.y);
-            } else if (ch.kind == kNoise) {
-                const float2 xv = ldx(t);
-                const float gpv = a.gprocess != nullptr ? a.gprocess[chain * s.t + t] : 0.f;
-                const float gov = a.gobservation != nullptr ? a.gobservation[chain * s.t + t] : 0.f;
-                const float2 gz = make_float2(gpv * softplus_grad(xv.x + bias.x), gov * softplus_grad(xv.y + bias.y));
-                st2<IN_BF>(a.gx, (row0 + t) * a.gx_stride + c0, gz);
-                gb = make_float2(gb.x + gz.x, gb.y + gz.y);
+                float gx[CW];
+#pragma unroll
+                for (int j = 0; j < CW; ++j) {
+                    gx[j] = fmaf(w[0][j], gp3[j], fmaf(w[1][j], gp2[j], fmaf(w[2][j], gp1[j], w[3][j] * gc[j])));
+                    gw[0][j] = fmaf(gc[j], x3[j], gw[0][j]);
+                    gw[1][j] = fmaf(gc[j], x2[j], gw[1][j]);
+                    gw[2][j] = fmaf(gc[j], x1[j], gw[2][j]);
+                    gw[3][j] = fmaf(gc[j], x0[j], gw[3][j]);
+                }
+                stn<IN_BF, CW>(a.gx, (row0 + t) * a.gx_stride + c0, gx);
+            } else if (ch.kind == kDecay || ch.kind == kNoise) {
+                float xv[CW], gz[CW];
+                ldx(t, xv);
+                if (ch.kind == kDecay) {
+                    float gd[CW];
+#pragma unroll
+                    for (int j = 0; j < CW; ++j) gd[j] = 0.f;
+                    if (a.gdecay != nullptr) {
+                        if (hm.ng == 1) {
+                            ldn<false, CW>(a.gdecay, (chain * s.t + t) * s.d + ch.within, gd);
+                        } else {
+                            ld_heads<false, CW>(a.gdecay, chain, t, s.t, s.d, gd);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < CW; ++j) {
+                        // d/dz 1 / (1 + e^z) = -decay (1 - decay)
+                        const float dcy = decay_of(xv[j] + bias[j]);
+                        gz[j] = -gd[j] * dcy * (1.f - dcy);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < CW / 2; ++i) {
+                        const float gpv = a.gprocess != nullptr ? __ldg(a.gprocess + (chain + i) * s.t + t) : 0.f;
+                        const float gov = a.gobservation != nullptr ? __ldg(a.gobservation + (chain + i) * s.t + t) : 0.f;
+                        gz[2 * i] = gpv * softplus_grad(xv[2 * i] + bias[2 * i]);
+                        gz[2 * i + 1] = gov * softplus_grad(xv[2 * i + 1] + bias[2 * i + 1]);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < CW; ++j) gb[j] += gz[j];
+                stn<IN_BF, CW>(a.gx, (row0 + t) * a.gx_stride + c0, gz);
             }
         }
-        gp3 = gp2;
-        gp2 = gp1;
-        gp1 = gc;
-        x0 = x1;
-        x1 = x2;
-        x2 = x3;
+#pragma unroll
+        for (int j = 0; j < CW; ++j) {
+            gp3[j] = gp2[j];
+            gp2[j] = gp1[j];
+            gp1[j] = gc[j];
+            x0[j] = x1[j];
+            x1[j] = x2[j];
+            x2[j] = x3[j];
+        }
     }
     if (conv) {
-        float4 *pw = reinterpret_cast<float4 *>(part + c0 * 4);  // [c][4], c0 even: 32-byte aligned
-        pw[0] = make_float4(gw0.x, gw1.x, gw2.x, gw3.x);
-        pw[1] = make_float4(gw0.y, gw1.y, gw2.y, gw3.y);
+#pragma unroll
+        for (int j = 0; j < CW; ++j)  // [c][4]: 16-byte aligned (rows are multiples of 8 floats)
+            *reinterpret_cast<float4 *>(part + (c0 + j) * 4) = make_float4(gw[0][j], gw[1][j], gw[2][j], gw[3][j]);
     } else if (ch.kind == kDecay || ch.kind == kNoise) {
-        const int ac = c0 - C;
-        part[4 * C + ac] = gb.x;
-        part[4 * C + ac + 1] = gb.y;
+#pragma unroll
+        for (int j = 0; j < CW; ++j) part[4 * C + (c0 - C) + j] = gb[j];
     }
 }
 
@@ -336,12 +543,49 @@ int check_shape(const Shape &s, int in_dtype, int out_dtype) {
     return BSSM_OK;
 }
 
-int pick_tsplit(long b, long t) {
-    // enough CTAs for every SM several times over, spans of at least 32 tokens
-    int ts = 1;
-    while (b * ts < 4 * 148 && t / (2 * ts) >= 32) ts *= 2;
-    return ts;
+// Channel-group width CW: every stream and head row boundary must fall on a
+// multiple of CW, and the vector accesses of CW >= 4 need 16-byte aligned
+// tensors.
+template <int CW>
+bool cw_fits(const Shape &s, long other_stride, const void *const *ptrs, int nptr) {
+    if (s.sw() % CW || s.hd % CW || (2 * s.heads) % CW || s.in_stride % CW || other_stride % CW) return false;
+    if (CW >= 4)
+        for (int i = 0; i < nptr; ++i)
+            if (reinterpret_cast<uintptr_t>(ptrs[i]) & 15) return false;
+    return true;
 }
+
+template <int CW>
+dim3 grid_of(const Shape &s) {
+    const int groups = (s.conv_channels() + s.aux_channels()) / CW;
+    return dim3((groups + kThreads - 1) / kThreads, s.tsplit, static_cast<unsigned>(s.b));
+}
+
+template <int CW>
+void launch_fwd(const Shape &s, const ProArgs &a, int in_dtype, int out_dtype, cudaStream_t st) {
+    const dim3 g = grid_of<CW>(s);
+    if (in_dtype == BSSM_BF16) {
+        if (out_dtype == BSSM_BF16) prologue_kernel<true, true, CW><<<g, kThreads, 0, st>>>(s, a);
+        else prologue_kernel<true, false, CW><<<g, kThreads, 0, st>>>(s, a);
+    } else {
+        if (out_dtype == BSSM_BF16) prologue_kernel<false, true, CW><<<g, kThreads, 0, st>>>(s, a);
+        else prologue_kernel<false, false, CW><<<g, kThreads, 0, st>>>(s, a);
+    }
+}
+
+template <int CW>
+void launch_bwd(const Shape &s, const EnvBwdArgs &a, int in_dtype, int out_dtype, cudaStream_t st) {
+    const dim3 g = grid_of<CW>(s);
+    if (in_dtype == BSSM_BF16) {
+        if (out_dtype == BSSM_BF16) prologue_backward_kernel<true, true, CW><<<g, kThreads, 0, st>>>(s, a);
+        else prologue_backward_kernel<true, false, CW><<<g, kThreads, 0, st>>>(s, a);
+    } else {
+        if (out_dtype == BSSM_BF16) prologue_backward_kernel<false, true, CW><<<g, kThreads, 0, st>>>(s, a);
+        else prologue_backward_kernel<false, false, CW><<<g, kThreads, 0, st>>>(s, a);
+    }
+}
+
+int pick_tsplit(long t, int span) { return static_cast<int>((t + span - 1) / span); }
 
 }  // namespace env
 }  // namespace bssm
@@ -353,7 +597,7 @@ extern "C" {
 
 long bssm_envelope_partial_floats(long batch, long tokens, int heads, int key_dim, int head_dim) {
     Shape s{batch, tokens, heads, key_dim, head_dim, 0, 1};
-    return batch * pick_tsplit(batch, tokens) * static_cast<long>(s.partial_cols());
+    return batch * pick_tsplit(tokens, kBwdSpan) * static_cast<long>(s.partial_cols());
 }
 
 int bssm_envelope_prologue(const void *projected, int in_dtype, long batch, long tokens, int heads, int key_dim,
@@ -372,17 +616,15 @@ int bssm_envelope_prologue(const void *projected, int in_dtype, long batch, long
     for (const void *p : aligned8)
         if (reinterpret_cast<uintptr_t>(p) & 7)
             return fail(BSSM_ERR_ALIGNMENT, "envelope prologue: tensors must be 8-byte aligned");
-    s.tsplit = pick_tsplit(batch, tokens);
+    if (reinterpret_cast<uintptr_t>(conv_weight) & 15)
+        return fail(BSSM_ERR_ALIGNMENT, "envelope prologue: conv_weight must be 16-byte aligned");
+    s.tsplit = pick_tsplit(tokens, kFwdSpan);
+    if (s.tsplit > 65535) return fail(BSSM_ERR_INVALID, "envelope: sequence too long (%ld tokens)", tokens);
     const ProArgs a{projected, conv_weight, aux_bias, keys, queries, values, decay, process, observation};
-    const dim3 grid((s.pairs() + kThreads - 1) / kThreads, s.tsplit, static_cast<unsigned>(batch));
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (in_dtype == BSSM_BF16) {
-        if (out_dtype == BSSM_BF16) prologue_kernel<true, true><<<grid, kThreads, 0, st>>>(s, a);
-        else prologue_kernel<true, false><<<grid, kThreads, 0, st>>>(s, a);
-    } else {
-        if (out_dtype == BSSM_BF16) prologue_kernel<false, true><<<grid, kThreads, 0, st>>>(s, a);
-        else prologue_kernel<false, false><<<grid, kThreads, 0, st>>>(s, a);
-    }
+    if (kFwdCW >= 8 && cw_fits<8>(s, 0, aligned8, 5)) launch_fwd<8>(s, a, in_dtype, out_dtype, st);
+    else if (kFwdCW >= 4 && cw_fits<4>(s, 0, aligned8, 5)) launch_fwd<4>(s, a, in_dtype, out_dtype, st);
+    else launch_fwd<2>(s, a, in_dtype, out_dtype, st);
     return check_launch("envelope prologue");
 }
 
@@ -410,7 +652,8 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
     }
     if (!projected || !conv_weight || !grad_projected || !workspace)
         return fail(BSSM_ERR_INVALID, "envelope backward: null pointer");
-    s.tsplit = pick_tsplit(batch, tokens);
+    s.tsplit = pick_tsplit(tokens, kBwdSpan);
+    if (s.tsplit > 65535) return fail(BSSM_ERR_INVALID, "envelope: sequence too long (%ld tokens)", tokens);
     const long need = batch * s.tsplit * static_cast<long>(pcols);
     if (workspace_floats < need)
         return fail(BSSM_ERR_WORKSPACE, "envelope backward: workspace of %ld floats, need %ld", workspace_floats, need);
@@ -420,17 +663,13 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
     for (const void *p : aligned8)
         if (reinterpret_cast<uintptr_t>(p) & 7)
             return fail(BSSM_ERR_ALIGNMENT, "envelope backward: tensors must be 8-byte aligned");
+    if (reinterpret_cast<uintptr_t>(conv_weight) & 15)
+        return fail(BSSM_ERR_ALIGNMENT, "envelope backward: conv_weight must be 16-byte aligned");
     const EnvBwdArgs a{projected, conv_weight, aux_bias, grad_keys, grad_queries, grad_values, grad_decay, grad_process,
                     grad_observation, grad_projected, grad_row_stride, workspace};
-    const dim3 grid((s.pairs() + kThreads - 1) / kThreads, s.tsplit, static_cast<unsigned>(batch));
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (in_dtype == BSSM_BF16) {
-        if (out_dtype == BSSM_BF16) prologue_backward_kernel<true, true><<<grid, kThreads, 0, st>>>(s, a);
-        else prologue_backward_kernel<true, false><<<grid, kThreads, 0, st>>>(s, a);
-    } else {
-        if (out_dtype == BSSM_BF16) prologue_backward_kernel<false, true><<<grid, kThreads, 0, st>>>(s, a);
-        else prologue_backward_kernel<false, false><<<grid, kThreads, 0, st>>>(s, a);
-    }
+    if (kBwdCW >= 4 && cw_fits<4>(s, grad_row_stride, aligned8, 6)) launch_bwd<4>(s, a, in_dtype, out_dtype, st);
+    else launch_bwd<2>(s, a, in_dtype, out_dtype, st);
     if (int rc = check_launch("envelope prologue backward")) return rc;
     reduce_rows_kernel<<<(cols + kThreads - 1) / kThreads, kThreads, 0, st>>>(workspace, batch * s.tsplit, cols, pcols,
                                                                                grad_conv_weight, 4 * C, grad_aux_bias);

@@ -12,6 +12,14 @@ measurement plan (the headline, config 3, is ``bench.py``).
   BF16 k/q/v: forward + backward (all dynamics gradients, readout loss)
   through the C ABI, as ``bench.py`` does for config 3, in tok/s.
 
+* ``--config envelope``: the BayesianMixer prologue at config 3's mixer
+  shape (B256 T512, 64 heads, key_dim 8, head_dim 8: a BF16 projection of
+  2,176 channels per token) -> the recurrence's inputs, forward + backward,
+  through the C ABI with FP32 outputs (the reference's state boundary) and
+  with BF16 k/q/v (the headline recurrence's input dtype), beside the eager
+  PyTorch op chain of the reference; bytes-roofline fractions against the
+  measured HBM copy bandwidth.
+
 Each run prints one JSON line.  Inputs are seeded synthetic tensors with
 the survey's distributions; timing is CUDA events after warm-up.
 """
@@ -136,13 +144,87 @@ def config4(steps: int, warmup: int) -> dict:
             "io_dtype": "bf16 k/q/v, fp32 decay/noise/state", "data": "synthetic"}
 
 
+def envelope(steps: int, warmup: int) -> dict:
+    import torch
+    from bayes_ssm import _capi
+    from bayes_ssm.envelope import paper_prologue_torch
+    b, t, h, d, hd = 256, 512, 64, 8, 8
+    sw, w = h * d, h * hd
+    c, aux = 2 * sw + w, sw + 2 * h
+    pch = c + aux
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(b, t, pch, generator=g, device=dev).to(torch.bfloat16)
+    wt = torch.randn(c, 4, generator=g, device=dev) * 0.5
+    bias = torch.randn(aux, generator=g, device=dev) * 0.1
+    n = b * h
+    f32 = dict(device=dev, dtype=torch.float32)
+    sp = torch.cuda.current_stream().cuda_stream
+    ws = torch.empty(_capi.envelope_partial_floats(b, t, h, d, hd), **f32)
+    gx = torch.empty_like(x)
+    gw, gb = torch.empty(c, 4, **f32), torch.empty(aux, **f32)
+    gd, gp, go = (torch.randn(n, t, d, generator=g, device=dev), torch.randn(n, t, generator=g, device=dev),
+                  torch.randn(n, t, generator=g, device=dev))
+    dec, proc, obs = torch.empty(n, t, d, **f32), torch.empty(n, t, **f32), torch.empty(n, t, **f32)
+    hbm = _peak_hbm()
+    res = {}
+    for name, odt in (("f32_out", torch.float32), ("bf16_out", torch.bfloat16)):
+        code = _capi.BSSM_F32 if odt == torch.float32 else _capi.BSSM_BF16
+        k, q = torch.empty(n, t, d, device=dev, dtype=odt), torch.empty(n, t, d, device=dev, dtype=odt)
+        v = torch.empty(n, t, hd, device=dev, dtype=odt)
+        gk, gq, gv = torch.randn_like(k), torch.randn_like(q), torch.randn_like(v)
+
+        def fwd():
+            _capi.envelope_prologue(x, _capi.BSSM_BF16, b, t, h, d, hd, pch, wt, bias, k, q, v, code, dec, proc,
+                                    obs, sp)
+
+        def bwd():
+            _capi.envelope_prologue_backward(x, _capi.BSSM_BF16, b, t, h, d, hd, pch, wt, bias, gk, gq, gv, code,
+                                             gd, gp, go, gx, pch, gw, gb, ws, sp)
+
+        es = k.element_size()
+        tok = b * t
+        fwd_bytes = tok * (pch * 2 + (2 * sw + w) * es + sw * 4 + 2 * h * 4)
+        bwd_bytes = tok * (pch * 2 + (2 * sw + w) * es + sw * 4 + 2 * h * 4 + pch * 2)
+        ms_f, ms_b = _time(fwd, steps, warmup), _time(bwd, steps, warmup)
+        res[name] = {"forward_ms": round(ms_f, 4), "backward_ms": round(ms_b, 4),
+                     "forward_GBps": round(fwd_bytes / ms_f / 1e6, 1), "backward_GBps": round(bwd_bytes / ms_b / 1e6, 1),
+                     "forward_frac": round(fwd_bytes / ms_f / 1e6 / hbm, 3),
+                     "backward_frac": round(bwd_bytes / ms_b / 1e6 / hbm, 3),
+                     "algorithmic_bytes": {"forward": fwd_bytes, "backward": bwd_bytes}}
+    xe = x.detach().clone().requires_grad_()
+    we = wt.reshape(c, 1, 4).detach().clone().requires_grad_()
+    be = bias.detach().clone().requires_grad_()
+
+    def eager():
+        outs = paper_prologue_torch(xe, we, be, heads=h, key_dim=d, head_dim=hd)
+        ups = [torch.ones_like(o) for o in outs]
+        torch.autograd.grad(outs, (xe, we, be), ups)
+
+    ms_e = _time(eager, max(3, steps // 4), warmup)
+    return {"config": "envelope", "workload": "BayesianMixer prologue, B256 T512 H64 D8 head_dim 8 "
+            "(BF16 projection, 2,176 channels), fwd + bwd", "metric": "ms per fwd+bwd", "unit": "ms",
+            "kernel": res, "eager_torch_fwd_bwd_ms": round(ms_e, 4),
+            "speedup_f32_out": round(ms_e / (res["f32_out"]["forward_ms"] + res["f32_out"]["backward_ms"]), 2),
+            "hbm_peak_GBps": hbm, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)",
+            "steps": steps, "warmup": warmup, "data": "synthetic"}
+
+
+def _peak_hbm() -> float:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"])
+    except (OSError, ValueError, KeyError):
+        return 6650.0
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", choices=("2", "4"), required=True)
+    ap.add_argument("--config", choices=("2", "4", "envelope"), required=True)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()
-    fn = config2 if args.config == "2" else config4
+    fn = {"2": config2, "4": config4, "envelope": envelope}[args.config]
     print(json.dumps(fn(args.steps, max(3, args.warmup))), flush=True)
 
 

@@ -34,8 +34,11 @@ def _inputs(b, t, h, d, hd, seed, dtype=torch.float32):
     return x.to(dtype).cuda(), wt.cuda(), bias.cuda()
 
 
+# (B, T, H, D, head_dim): channel-group widths 8/4/2 are picked by divisibility,
+# so these cover one head over several lanes (D >= width), several whole heads
+# per thread (D = 2, 4 below the width), and the 2-channel form
 CASES = [(2, 37, 4, 8, 8), (1, 300, 2, 8, 8), (3, 2, 3, 4, 6), (2, 65, 5, 2, 8), (1, 9, 2, 16, 4),
-         (4, 128, 8, 8, 8)]
+         (4, 128, 8, 8, 8), (2, 50, 4, 2, 8), (2, 50, 4, 4, 8), (1, 64, 8, 2, 8), (1, 33, 4, 32, 8)]
 
 
 @pytest.mark.parametrize("shape", CASES)
