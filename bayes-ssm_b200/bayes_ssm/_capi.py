@@ -51,6 +51,10 @@ _SIGNATURES = {
     "bssm_envelope_prologue": ([_vp, _i, _l, _l, _i, _i, _i, _l] + [_vp] * 5 + [_i] + [_vp] * 4, _i),
     "bssm_envelope_prologue_backward": ([_vp, _i, _l, _l, _i, _i, _i, _l] + [_vp] * 5 + [_i] + [_vp] * 4
                                         + [_l, _vp, _vp, _vp, _l, _vp], _i),
+    "bssm_envelope_epilogue_partial_floats": ([_l, _l, _i, _i], _l),
+    "bssm_envelope_epilogue": ([_vp, _i, _vp, _i, _l, _vp, ctypes.c_float, _l, _l, _i, _i, _vp, _vp], _i),
+    "bssm_envelope_epilogue_backward": ([_vp, _i, _vp, _i, _l, _vp, ctypes.c_float, _l, _l, _i, _i, _vp, _vp, _vp,
+                                         _l, _vp, _vp, _l, _vp], _i),
     "bssm_debug_wait_timeouts": ([], ctypes.c_uint),
     "bssm_debug_last_family": ([], _i),
 }
@@ -200,3 +204,24 @@ def envelope_prologue_backward(projected, in_dtype, batch, tokens, heads, key_di
         ptr(gprojected), grad_row_stride, ptr(gconv_weight), ptr(gaux_bias), ptr(workspace),
         0 if workspace is None else workspace.numel(), stream)
     check(rc, "bssm_envelope_prologue_backward")
+
+
+def envelope_epilogue_partial_floats(batch, tokens, heads, head_dim) -> int:
+    return int(load().bssm_envelope_epilogue_partial_floats(batch, tokens, heads, head_dim))
+
+
+def envelope_epilogue(read, read_dtype, gate, gate_dtype, gate_row_stride, norm_weight, eps, batch, tokens, heads,
+                      head_dim, out, stream) -> None:
+    rc = load().bssm_envelope_epilogue(ptr(read), read_dtype, ptr(gate), gate_dtype, gate_row_stride,
+                                       ptr(norm_weight), float(eps), batch, tokens, heads, head_dim, ptr(out), stream)
+    check(rc, "bssm_envelope_epilogue")
+
+
+def envelope_epilogue_backward(read, read_dtype, gate, gate_dtype, gate_row_stride, norm_weight, eps, batch, tokens,
+                               heads, head_dim, grad_out, grad_read, grad_gate, grad_gate_row_stride,
+                               grad_norm_weight, workspace, stream) -> None:
+    rc = load().bssm_envelope_epilogue_backward(
+        ptr(read), read_dtype, ptr(gate), gate_dtype, gate_row_stride, ptr(norm_weight), float(eps), batch, tokens,
+        heads, head_dim, ptr(grad_out), ptr(grad_read), ptr(grad_gate), grad_gate_row_stride, ptr(grad_norm_weight),
+        ptr(workspace), 0 if workspace is None else workspace.numel(), stream)
+    check(rc, "bssm_envelope_epilogue_backward")

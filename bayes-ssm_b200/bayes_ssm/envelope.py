@@ -165,4 +165,87 @@ def paper_prologue(projected: Tensor, conv_weight: Tensor, aux_bias: Optional[Te
     return _PaperPrologue.apply(projected, conv_weight, aux_bias, heads, key_dim, head_dim, out_dtype)
 
 
-__all__ = ["paper_prologue", "paper_prologue_torch"]
+def read_epilogue_torch(read: Tensor, gate: Tensor, norm_weight: Tensor, *, heads: int,
+                        eps: Optional[float] = None) -> Tensor:
+    """The reference's readout in PyTorch (``train_6layer.py:719-729``): the
+    reads permuted to ``[B, T, H, hd]`` and cast to the gate's dtype, then
+    ``nn.RMSNorm(hd)`` (weight ``norm_weight``; ``eps=None`` is the dtype's
+    machine epsilon, as ``nn.RMSNorm`` uses) times ``SiLU(gate)``, reshaped to
+    ``[B, T, W]``."""
+    bh, t, hd = read.shape
+    b = bh // heads
+    r = read.view(b, heads, t, hd).permute(0, 2, 1, 3).to(gate.dtype)
+    normed = F.rms_norm(r, (hd,), norm_weight.to(gate.dtype), eps)
+    return (normed * F.silu(gate.reshape(b, t, heads, hd))).reshape(b, t, heads * hd)
+
+
+def _gate_rows(gate: Tensor) -> int:
+    if gate.stride(-1) != 1 or (gate.shape[0] > 1 and gate.stride(0) != gate.shape[1] * gate.stride(1)):
+        raise ValueError("gate must have unit channel stride and evenly spaced token rows")
+    return gate.stride(1)
+
+
+class _ReadEpilogue(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, read, gate, norm_weight, heads, eps):
+        bh, t, hd = read.shape
+        b = bh // heads
+        dev = read.device
+        w = norm_weight.detach().float().contiguous()
+        out = torch.empty(b, t, heads * hd, device=dev, dtype=gate.dtype)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        with torch.cuda.device(dev):
+            _capi.envelope_epilogue(read, _DTYPES[read.dtype], gate, _DTYPES[gate.dtype], _gate_rows(gate), w, eps, b,
+                                    t, heads, hd, out, stream)
+        ctx.save_for_backward(read, gate, w)
+        ctx.dims = (heads, eps, norm_weight.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        read, gate, w = ctx.saved_tensors
+        heads, eps, w_dtype = ctx.dims
+        bh, t, hd = read.shape
+        b = bh // heads
+        dev = read.device
+        go = grad_out.to(gate.dtype).contiguous()
+        g_read = torch.empty_like(read)
+        g_gate = torch.empty(b, t, heads * hd, device=dev, dtype=gate.dtype)
+        g_w = torch.empty(hd, device=dev, dtype=torch.float32)
+        ws = torch.empty(_capi.envelope_epilogue_partial_floats(b, t, heads, hd), device=dev, dtype=torch.float32)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        with torch.cuda.device(dev):
+            _capi.envelope_epilogue_backward(read, _DTYPES[read.dtype], gate, _DTYPES[gate.dtype], _gate_rows(gate), w,
+                                             eps, b, t, heads, hd, go, g_read, g_gate, heads * hd, g_w, ws, stream)
+        return g_read, g_gate.view(gate.shape), g_w.to(w_dtype), None, None
+
+
+def read_epilogue(read: Tensor, gate: Tensor, norm_weight: Tensor, *, heads: int,
+                  eps: Optional[float] = None) -> Tensor:
+    """The mixer's readout: ``read_norm(read) * SiLU(gate)`` as ``[B, T, W]``.
+
+    ``read`` is the recurrence's ``[B*H, T, hd]`` output, ``gate`` the gate
+    projection ``[B, T, W]`` (its rows may be a channel slice of a wider GEMM
+    output), ``norm_weight`` the ``nn.RMSNorm(hd)`` weight.  The result has the
+    gate's dtype, the dtype the reference casts the reads to.  On CUDA one
+    sm_100a kernel does it (and one its backward); on CPU this runs
+    :func:`read_epilogue_torch`.
+    """
+    if read.ndim != 3 or gate.ndim != 3:
+        raise ValueError("read must be [B*H, T, hd] and gate [B, T, W]")
+    bh, t, hd = read.shape
+    if bh % heads or gate.shape != (bh // heads, t, heads * hd) or norm_weight.numel() != hd:
+        raise ValueError("read, gate and norm_weight shapes do not agree")
+    if eps is None:
+        eps = torch.finfo(gate.dtype).eps
+    if not read.is_cuda:
+        return read_epilogue_torch(read, gate, norm_weight, heads=heads, eps=eps)
+    if read.dtype not in _DTYPES or gate.dtype not in _DTYPES:
+        raise TypeError("read_epilogue on CUDA takes float32 or bfloat16 tensors")
+    if hd not in (8, 16, 32, 64):
+        raise NotImplementedError(f"read_epilogue on CUDA needs head_dim 8, 16, 32 or 64 (got {hd}); "
+                                  "use read_epilogue_torch")
+    return _ReadEpilogue.apply(read.contiguous(), gate, norm_weight, heads, float(eps))
+
+
+__all__ = ["paper_prologue", "paper_prologue_torch", "read_epilogue", "read_epilogue_torch"]

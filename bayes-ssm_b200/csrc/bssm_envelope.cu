@@ -17,7 +17,11 @@
 // convolution weight and auxiliary bias (reduced by a second, deterministic
 // kernel).
 //
-// Work split: a thread owns two adjacent channels of one batch row and walks
+// The readout epilogue (train_6layer.py:719-729) is the second kernel pair
+// here: read [B*H, T, hd] -> read_norm (nn.RMSNorm over hd, after the
+// reference's cast to the residual dtype) * SiLU(gate) -> [B, T, W].
+//
+// Work split: a thread owns adjacent channels of one batch row and walks
 // a span of tokens, keeping the convolution window in registers, so every
 // input element is read once (plus a 3-token halo per span).  The channels of
 // one head sit in D/2 consecutive lanes, which reduce the head's squared norm
@@ -514,6 +518,123 @@ __global__ void __launch_bounds__(kThreads) prologue_backward_kernel(const Shape
     }
 }
 
+// ---- readout epilogue -----------------------------------------------------
+template <bool BF, int N>
+__device__ __forceinline__ void ldv(const void *base, long idx, float *v) {
+    static_assert(N % 8 == 0, "rows of 8k");
+#pragma unroll
+    for (int i = 0; i < N; i += 8) ldn<BF, 8>(base, idx + i, v + i);
+}
+template <bool BF, int N>
+__device__ __forceinline__ void stv(void *base, long idx, const float *v) {
+#pragma unroll
+    for (int i = 0; i < N; i += 8) stn<BF, 8>(base, idx + i, v + i);
+}
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+struct EpiArgs {
+    const void *read;  // [B*H, T, HD]
+    const void *gate;  // rows of [B, T, >= W], gate_stride apart
+    long gate_stride;
+    const float *w;    // [HD]
+    float eps;
+    long b, t;
+    int heads;
+    void *out;         // [B, T, W] (forward) / grad_out (backward)
+    void *gread, *ggate;
+    long ggate_stride;
+    float *partial;    // [CTAs][HD]
+};
+
+// Thread = one (token, head) row; consecutive threads are consecutive heads
+// of a token, so gate and output rows are contiguous across a warp and each
+// read row is one 32-byte-aligned segment.
+template <bool RBF, bool GBF, int HD>
+__global__ void __launch_bounds__(kThreads) epilogue_kernel(const EpiArgs a) {
+    const long row = static_cast<long>(blockIdx.x) * kThreads + threadIdx.x;
+    const long rows = a.b * a.t * a.heads;
+    if (row >= rows) return;
+    const long tok = row / a.heads;  // b * T + t
+    const int h = static_cast<int>(row - tok * a.heads);
+    const long bb = tok / a.t, t = tok - bb * a.t;
+    float r[HD], g[HD];
+    ldv<RBF, HD>(a.read, ((bb * a.heads + h) * a.t + t) * HD, r);
+    ldv<GBF, HD>(a.gate, tok * a.gate_stride + static_cast<long>(h) * HD, g);
+    float ms = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD; ++i) {
+        if constexpr (GBF) r[i] = round_bf16(r[i]);  // read.to(x.dtype)
+        ms = fmaf(r[i], r[i], ms);
+    }
+    const float inv = rsqrtf(ms * (1.0f / HD) + a.eps);
+    float o[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) o[i] = r[i] * inv * __ldg(a.w + i) * (g[i] * sigmoid(g[i]));
+    stv<GBF, HD>(a.out, tok * static_cast<long>(a.heads) * HD + static_cast<long>(h) * HD, o);
+}
+
+template <bool RBF, bool GBF, int HD>
+__global__ void __launch_bounds__(kThreads) epilogue_backward_kernel(const EpiArgs a) {
+    __shared__ float red[kThreads / 32][HD];
+    const long row = static_cast<long>(blockIdx.x) * kThreads + threadIdx.x;
+    const long rows = a.b * a.t * a.heads;
+    float gw[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) gw[i] = 0.f;
+    if (row < rows) {
+        const long tok = row / a.heads;
+        const int h = static_cast<int>(row - tok * a.heads);
+        const long bb = tok / a.t, t = tok - bb * a.t;
+        const long rix = ((bb * a.heads + h) * a.t + t) * HD;
+        float r[HD], g[HD], go[HD], w[HD];
+        ldv<RBF, HD>(a.read, rix, r);
+        ldv<GBF, HD>(a.gate, tok * a.gate_stride + static_cast<long>(h) * HD, g);
+        ldv<GBF, HD>(a.out, tok * static_cast<long>(a.heads) * HD + static_cast<long>(h) * HD, go);
+        float ms = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD; ++i) {
+            if constexpr (GBF) r[i] = round_bf16(r[i]);
+            w[i] = __ldg(a.w + i);
+            ms = fmaf(r[i], r[i], ms);
+        }
+        const float inv = rsqrtf(ms * (1.0f / HD) + a.eps);
+        float ggt[HD], gr[HD], dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD; ++i) {
+            const float sg = sigmoid(g[i]);
+            const float silu = g[i] * sg, dsilu = sg * fmaf(g[i], 1.f - sg, 1.f);
+            const float n = r[i] * inv;            // normalised, before the weight
+            ggt[i] = go[i] * n * w[i] * dsilu;     // d/dgate
+            const float gy = go[i] * silu;         // d/d(normalised * weight)
+            gw[i] = gy * n;
+            gr[i] = w[i] * gy;                     // z = w * gy
+            dot = fmaf(r[i], gr[i], dot);
+        }
+        // d/dr of r * inv: inv * z - r * inv^3 * (r . z) / HD
+        const float c3 = inv * inv * inv * dot * (1.0f / HD);
+#pragma unroll
+        for (int i = 0; i < HD; ++i) gr[i] = inv * gr[i] - r[i] * c3;
+        stv<RBF, HD>(a.gread, rix, gr);
+        stv<GBF, HD>(a.ggate, tok * a.ggate_stride + static_cast<long>(h) * HD, ggt);
+    }
+    // weight gradient: warp sums, then the CTA's warps in order
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < HD; ++i) {
+        float v = gw[i];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) red[warp][i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < HD) {
+        float acc = 0.f;
+#pragma unroll
+        for (int wv = 0; wv < kThreads / 32; ++wv) acc += red[wv][threadIdx.x];
+        a.partial[static_cast<long>(blockIdx.x) * HD + threadIdx.x] = acc;
+    }
+}
+
 // out[e] = sum over r of partial[r][e], rows in order (deterministic).
 __global__ void __launch_bounds__(kThreads) reduce_rows_kernel(const float *partial, long rows, int cols, int stride,
                                                                float *gw, int nw, float *gbias) {
@@ -526,6 +647,23 @@ __global__ void __launch_bounds__(kThreads) reduce_rows_kernel(const float *part
     } else if (gbias != nullptr) {
         gbias[e - nw] = acc;
     }
+}
+
+// The same for few columns and many rows: CTA e sums column e, thread i
+// taking rows i, i + 256, ... in order, then a fixed-shape tree over threads.
+__global__ void __launch_bounds__(kThreads) reduce_cols_kernel(const float *partial, long rows, int stride,
+                                                               float *out) {
+    __shared__ float red[kThreads];
+    const int e = blockIdx.x;
+    float acc = 0.f;
+    for (long r = threadIdx.x; r < rows; r += kThreads) acc += partial[r * stride + e];
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int half = kThreads / 2; half > 0; half >>= 1) {
+        if (threadIdx.x < half) red[threadIdx.x] += red[threadIdx.x + half];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[e] = red[0];
 }
 
 int check_shape(const Shape &s, int in_dtype, int out_dtype) {
@@ -586,6 +724,46 @@ void launch_bwd(const Shape &s, const EnvBwdArgs &a, int in_dtype, int out_dtype
 }
 
 int pick_tsplit(long t, int span) { return static_cast<int>((t + span - 1) / span); }
+
+int epi_check(long batch, long tokens, int heads, int head_dim, int read_dtype, int gate_dtype, long gate_stride) {
+    if (batch < 0 || tokens < 0 || heads <= 0) return fail(BSSM_ERR_INVALID, "envelope epilogue: bad sizes");
+    if (head_dim != 8 && head_dim != 16 && head_dim != 32 && head_dim != 64)
+        return fail(BSSM_ERR_UNSUPPORTED, "envelope epilogue: head_dim must be 8, 16, 32 or 64 (got %d)", head_dim);
+    if ((read_dtype != BSSM_F32 && read_dtype != BSSM_BF16) || (gate_dtype != BSSM_F32 && gate_dtype != BSSM_BF16))
+        return fail(BSSM_ERR_UNSUPPORTED, "envelope epilogue: dtypes must be float32 or bfloat16");
+    if (gate_stride < static_cast<long>(heads) * head_dim || gate_stride % 8)
+        return fail(BSSM_ERR_INVALID, "envelope epilogue: gate row stride %ld is short or not a multiple of 8",
+                    gate_stride);
+    return BSSM_OK;
+}
+
+template <int HD>
+void launch_epi(const EpiArgs &a, int rd, int gd, bool backward, cudaStream_t st) {
+    const long rows = a.b * a.t * a.heads;
+    const unsigned grid = static_cast<unsigned>((rows + kThreads - 1) / kThreads);
+#define BSSM_EPI(R, G)                                                                       \
+    do {                                                                                     \
+        if (backward) epilogue_backward_kernel<R, G, HD><<<grid, kThreads, 0, st>>>(a);     \
+        else epilogue_kernel<R, G, HD><<<grid, kThreads, 0, st>>>(a);                       \
+    } while (0)
+    if (rd == BSSM_BF16) {
+        if (gd == BSSM_BF16) BSSM_EPI(true, true);
+        else BSSM_EPI(true, false);
+    } else {
+        if (gd == BSSM_BF16) BSSM_EPI(false, true);
+        else BSSM_EPI(false, false);
+    }
+#undef BSSM_EPI
+}
+
+void launch_epi_hd(const EpiArgs &a, int hd, int rd, int gd, bool backward, cudaStream_t st) {
+    switch (hd) {
+        case 8: launch_epi<8>(a, rd, gd, backward, st); break;
+        case 16: launch_epi<16>(a, rd, gd, backward, st); break;
+        case 32: launch_epi<32>(a, rd, gd, backward, st); break;
+        default: launch_epi<64>(a, rd, gd, backward, st); break;
+    }
+}
 
 }  // namespace env
 }  // namespace bssm
@@ -674,6 +852,65 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
     reduce_rows_kernel<<<(cols + kThreads - 1) / kThreads, kThreads, 0, st>>>(workspace, batch * s.tsplit, cols, pcols,
                                                                                grad_conv_weight, 4 * C, grad_aux_bias);
     return check_launch("envelope reduction");
+}
+
+long bssm_envelope_epilogue_partial_floats(long batch, long tokens, int heads, int head_dim) {
+    const long rows = batch * tokens * heads;
+    return (rows + kThreads - 1) / kThreads * head_dim;
+}
+
+int bssm_envelope_epilogue(const void *read, int read_dtype, const void *gate, int gate_dtype, long gate_row_stride,
+                           const float *norm_weight, float eps, long batch, long tokens, int heads, int head_dim,
+                           void *out, void *stream) {
+    if (int rc = epi_check(batch, tokens, heads, head_dim, read_dtype, gate_dtype, gate_row_stride)) return rc;
+    if (batch == 0 || tokens == 0) {
+        g_last_error.clear();
+        return BSSM_OK;
+    }
+    if (!read || !gate || !norm_weight || !out) return fail(BSSM_ERR_INVALID, "envelope epilogue: null pointer");
+    const void *al[] = {read, gate, out};
+    for (const void *p : al)
+        if (reinterpret_cast<uintptr_t>(p) & 15)
+            return fail(BSSM_ERR_ALIGNMENT, "envelope epilogue: tensors must be 16-byte aligned");
+    EpiArgs a{read, gate, gate_row_stride, norm_weight, eps, batch, tokens, heads, out, nullptr, nullptr, 0, nullptr};
+    launch_epi_hd(a, head_dim, read_dtype, gate_dtype, false, static_cast<cudaStream_t>(stream));
+    return check_launch("envelope epilogue");
+}
+
+int bssm_envelope_epilogue_backward(const void *read, int read_dtype, const void *gate, int gate_dtype,
+                                    long gate_row_stride, const float *norm_weight, float eps, long batch, long tokens,
+                                    int heads, int head_dim, const void *grad_out, void *grad_read, void *grad_gate,
+                                    long grad_gate_row_stride, float *grad_norm_weight, float *workspace,
+                                    long workspace_floats, void *stream) {
+    if (int rc = epi_check(batch, tokens, heads, head_dim, read_dtype, gate_dtype, gate_row_stride)) return rc;
+    if (grad_gate_row_stride < static_cast<long>(heads) * head_dim || grad_gate_row_stride % 8)
+        return fail(BSSM_ERR_INVALID, "envelope epilogue backward: bad gate gradient row stride %ld",
+                    grad_gate_row_stride);
+    if (!grad_norm_weight) return fail(BSSM_ERR_INVALID, "envelope epilogue backward: null weight gradient");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (batch == 0 || tokens == 0) {
+        const cudaError_t err = cudaMemsetAsync(grad_norm_weight, 0, sizeof(float) * head_dim, st);
+        if (err != cudaSuccess) return fail(BSSM_ERR_CUDA, "envelope epilogue backward: %s", cudaGetErrorString(err));
+        g_last_error.clear();
+        return BSSM_OK;
+    }
+    if (!read || !gate || !norm_weight || !grad_out || !grad_read || !grad_gate || !workspace)
+        return fail(BSSM_ERR_INVALID, "envelope epilogue backward: null pointer");
+    const long need = bssm_envelope_epilogue_partial_floats(batch, tokens, heads, head_dim);
+    if (workspace_floats < need)
+        return fail(BSSM_ERR_WORKSPACE, "envelope epilogue backward: workspace of %ld floats, need %ld",
+                    workspace_floats, need);
+    const void *al[] = {read, gate, grad_out, grad_read, grad_gate};
+    for (const void *p : al)
+        if (reinterpret_cast<uintptr_t>(p) & 15)
+            return fail(BSSM_ERR_ALIGNMENT, "envelope epilogue backward: tensors must be 16-byte aligned");
+    EpiArgs a{read, gate, gate_row_stride, norm_weight, eps, batch, tokens, heads, const_cast<void *>(grad_out),
+              grad_read, grad_gate, grad_gate_row_stride, workspace};
+    launch_epi_hd(a, head_dim, read_dtype, gate_dtype, true, st);
+    if (int rc = check_launch("envelope epilogue backward")) return rc;
+    const long ctas = need / head_dim;
+    reduce_cols_kernel<<<head_dim, kThreads, 0, st>>>(workspace, ctas, head_dim, grad_norm_weight);
+    return check_launch("envelope epilogue reduction");
 }
 
 }  // extern "C"

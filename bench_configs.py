@@ -17,8 +17,9 @@ measurement plan (the headline, config 3, is ``bench.py``).
   2,176 channels per token) -> the recurrence's inputs, forward + backward,
   through the C ABI with FP32 outputs (the reference's state boundary) and
   with BF16 k/q/v (the headline recurrence's input dtype), beside the eager
-  PyTorch op chain of the reference; bytes-roofline fractions against the
-  measured HBM copy bandwidth.
+  PyTorch op chain of the reference; and the readout epilogue (FP32 reads,
+  BF16 gate and output) beside its PyTorch form; bytes-roofline fractions
+  against the measured HBM copy bandwidth.
 
 Each run prints one JSON line.  Inputs are seeded synthetic tensors with
 the survey's distributions; timing is CUDA events after warm-up.
@@ -202,9 +203,44 @@ def envelope(steps: int, warmup: int) -> dict:
         torch.autograd.grad(outs, (xe, we, be), ups)
 
     ms_e = _time(eager, max(3, steps // 4), warmup)
+    # readout epilogue: FP32 reads [B*H, T, hd], BF16 gate -> BF16 [B, T, W]
+    from bayes_ssm.envelope import read_epilogue_torch
+    read = torch.randn(n, t, hd, generator=g, device=dev)
+    gate = torch.randn(b, t, w, generator=g, device=dev).to(torch.bfloat16)
+    nw = torch.rand(hd, generator=g, device=dev) + 0.5
+    eps = float(torch.finfo(torch.bfloat16).eps)
+    out = torch.empty(b, t, w, device=dev, dtype=torch.bfloat16)
+    gout = torch.randn_like(out)
+    g_read, g_gate = torch.empty_like(read), torch.empty_like(gate)
+    g_nw = torch.empty(hd, **f32)
+    ews = torch.empty(_capi.envelope_epilogue_partial_floats(b, t, h, hd), **f32)
+
+    def efwd():
+        _capi.envelope_epilogue(read, _capi.BSSM_F32, gate, _capi.BSSM_BF16, w, nw, eps, b, t, h, hd, out, sp)
+
+    def ebwd():
+        _capi.envelope_epilogue_backward(read, _capi.BSSM_F32, gate, _capi.BSSM_BF16, w, nw, eps, b, t, h, hd, gout,
+                                         g_read, g_gate, w, g_nw, ews, sp)
+
+    tok = b * t
+    e_fwd_bytes = tok * w * (4 + 2 + 2)
+    e_bwd_bytes = tok * w * (4 + 2 + 2 + 4 + 2)
+    ms_ef, ms_eb = _time(efwd, steps, warmup), _time(ebwd, steps, warmup)
+    re_, ge_, we_ = (z.detach().clone().requires_grad_() for z in (read, gate, nw))
+
+    def eager_epi():
+        o = read_epilogue_torch(re_, ge_, we_, heads=h, eps=eps)
+        torch.autograd.grad(o, (re_, ge_, we_), gout)
+
+    ms_ee = _time(eager_epi, max(3, steps // 4), warmup)
+    epilogue = {"forward_ms": round(ms_ef, 4), "backward_ms": round(ms_eb, 4),
+                "forward_frac": round(e_fwd_bytes / ms_ef / 1e6 / hbm, 3),
+                "backward_frac": round(e_bwd_bytes / ms_eb / 1e6 / hbm, 3),
+                "algorithmic_bytes": {"forward": e_fwd_bytes, "backward": e_bwd_bytes},
+                "eager_torch_fwd_bwd_ms": round(ms_ee, 4)}
     return {"config": "envelope", "workload": "BayesianMixer prologue, B256 T512 H64 D8 head_dim 8 "
             "(BF16 projection, 2,176 channels), fwd + bwd", "metric": "ms per fwd+bwd", "unit": "ms",
-            "kernel": res, "eager_torch_fwd_bwd_ms": round(ms_e, 4),
+            "kernel": res, "eager_torch_fwd_bwd_ms": round(ms_e, 4), "readout_epilogue": epilogue,
             "speedup_f32_out": round(ms_e / (res["f32_out"]["forward_ms"] + res["f32_out"]["backward_ms"]), 2),
             "hbm_peak_GBps": hbm, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)",
             "steps": steps, "warmup": warmup, "data": "synthetic"}

@@ -320,6 +320,33 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
                                     float *workspace, long workspace_floats, void *stream);
 
 /*
+ * BayesianMixer readout epilogue (replaces example/train_6layer.py:719-729:
+ * the permute of the recurrence's reads to [B, T, H, hd], read.to(x.dtype),
+ * nn.RMSNorm(hd) with weight norm_weight and epsilon eps, times SiLU(gate),
+ * reshaped to [B, T, W]).  read is [batch*heads, tokens, head_dim]
+ * (read_dtype); gate holds rows of at least W = heads * head_dim channels,
+ * gate_row_stride elements apart (gate_dtype, which is also the output's
+ * dtype and the dtype the reads are rounded to before the norm).  out is
+ * [batch, tokens, W].  head_dim is 8, 16, 32 or 64; tensors 16-byte aligned.
+ */
+int bssm_envelope_epilogue(const void *read, int read_dtype, const void *gate, int gate_dtype, long gate_row_stride,
+                           const float *norm_weight, float eps, long batch, long tokens, int heads, int head_dim,
+                           void *out, void *stream);
+/*
+ * Backward of bssm_envelope_epilogue: grad_out [batch, tokens, W] (gate
+ * dtype) gives grad_read (read layout and dtype), grad_gate (rows
+ * grad_gate_row_stride apart, gate dtype) and grad_norm_weight [head_dim]
+ * (float32, summed in a fixed order).  workspace holds
+ * bssm_envelope_epilogue_partial_floats() floats.
+ */
+long bssm_envelope_epilogue_partial_floats(long batch, long tokens, int heads, int head_dim);
+int bssm_envelope_epilogue_backward(const void *read, int read_dtype, const void *gate, int gate_dtype,
+                                    long gate_row_stride, const float *norm_weight, float eps, long batch, long tokens,
+                                    int heads, int head_dim, const void *grad_out, void *grad_read, void *grad_gate,
+                                    long grad_gate_row_stride, float *grad_norm_weight, float *workspace,
+                                    long workspace_floats, void *stream);
+
+/*
  * Diagnostics (no counterpart in the reference).
  *
  * The thread-per-chain kernels wait on shared-memory barriers for their own

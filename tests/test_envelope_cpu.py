@@ -77,3 +77,22 @@ def test_argument_errors():
         paper_prologue(x, wt, bias[:-1], heads=2, key_dim=4, head_dim=4)
     with pytest.raises(ValueError, match="batch, tokens, channels"):
         paper_prologue(x[0], wt, bias, heads=2, key_dim=4, head_dim=4)
+
+
+def test_read_epilogue_torch_matches_module_chain():
+    """read_epilogue_torch is the reference's readout: nn.RMSNorm(hd) on the
+    permuted, dtype-cast reads times SiLU(gate)."""
+    from bayes_ssm.envelope import read_epilogue, read_epilogue_torch
+    g = torch.Generator().manual_seed(9)
+    b, t, h, hd = 2, 6, 3, 8
+    read = torch.randn(b * h, t, hd, generator=g)
+    gate = torch.randn(b, t, h * hd, generator=g)
+    norm = torch.nn.RMSNorm(hd)
+    with torch.no_grad():
+        norm.weight.copy_(torch.rand(hd, generator=g) + 0.5)
+    want = (norm(read.view(b, h, t, hd).permute(0, 2, 1, 3)) * F.silu(gate.view(b, t, h, hd))).reshape(b, t, h * hd)
+    got = read_epilogue_torch(read, gate, norm.weight, heads=h)
+    torch.testing.assert_close(got, want)
+    torch.testing.assert_close(read_epilogue(read, gate, norm.weight, heads=h), want)
+    with pytest.raises(ValueError, match="shapes"):
+        read_epilogue(read, gate[..., :-1], norm.weight, heads=h)

@@ -122,3 +122,38 @@ def test_prologue_feeds_the_recurrence():
     assert _rel(y1, y2) <= 1e-5
     assert _rel(gx1, gx2) <= 1e-4
     assert _rel(gw1, gw2) <= 1e-4
+
+
+@pytest.mark.parametrize("shape,read_dtype,gate_dtype", [
+    ((2, 37, 4, 8), torch.float32, torch.float32), ((3, 64, 64, 8), torch.float32, torch.bfloat16),
+    ((1, 19, 2, 16), torch.float32, torch.float32), ((2, 8, 3, 32), torch.bfloat16, torch.bfloat16),
+    ((1, 5, 2, 64), torch.float32, torch.float32)])
+def test_read_epilogue_forward_backward(shape, read_dtype, gate_dtype):
+    from bayes_ssm.envelope import read_epilogue, read_epilogue_torch
+    b, t, h, hd = shape
+    g = torch.Generator(device="cuda").manual_seed(b * t + hd)
+    read = torch.randn(b * h, t, hd, generator=g, device="cuda").to(read_dtype)
+    # the gate as a channel slice of a wider projection
+    wide = torch.randn(b, t, h * hd + 16, generator=g, device="cuda").to(gate_dtype)
+    gate = wide[..., 8:8 + h * hd]
+    w = torch.rand(hd, generator=g, device="cuda") + 0.5
+    ins_k = [x.detach().clone().requires_grad_() for x in (read, w)]
+    ins_r = [x.detach().clone().requires_grad_() for x in (read, w)]
+    gk_ = gate.detach().clone().requires_grad_()
+    gr_ = gate.detach().clone().requires_grad_()
+    out = read_epilogue(ins_k[0], gk_, ins_k[1], heads=h)
+    ref = read_epilogue_torch(ins_r[0].float(), gr_.float(), ins_r[1], heads=h,
+                              eps=torch.finfo(gate_dtype).eps)
+    tol_v = 1e-6 if gate_dtype == torch.float32 else 4e-3
+    if gate_dtype == torch.bfloat16:  # the reference rounds the reads to the gate dtype first
+        ref = read_epilogue_torch(ins_r[0].to(gate_dtype).float(), gr_.float(), ins_r[1], heads=h,
+                                  eps=torch.finfo(gate_dtype).eps)
+    assert out.dtype == gate_dtype and out.shape == (b, t, h * hd)
+    assert _rel(out.float(), ref) <= tol_v
+    up = torch.randn(out.shape, generator=g, device="cuda")
+    gk = torch.autograd.grad(out, (ins_k[0], gk_, ins_k[1]), up.to(gate_dtype))
+    gr = torch.autograd.grad(ref, (ins_r[0], gr_, ins_r[1]), up)
+    tol_g = 1e-5 if gate_dtype == torch.float32 and read_dtype == torch.float32 else 8e-3
+    for name, a_, b_ in zip(("read", "gate", "weight"), gk, gr):
+        assert a_.shape == b_.shape, name
+        assert _rel(a_.float(), b_.float()) <= tol_g, (name, _rel(a_.float(), b_.float()))
