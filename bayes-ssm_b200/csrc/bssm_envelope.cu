@@ -42,9 +42,10 @@ namespace env {
 constexpr int kThreads = 256;
 // Tokens per span (one thread walks one span) and the widest channel group,
 // per direction, as measured at the config-3 mixer shape (B256 T512 H64 D8):
-// forward 4 channels over 64 tokens (0.72 ms; 2 over 128: 0.87 ms; 8 over
-// 32: 1.27 ms), backward 2 over 128 (2.0 ms; 4 over 64 and 32 no faster).
-// Both kernels are bound by instruction issue and load latency, not DRAM.
+// forward 4 channels over 64 tokens (0.71 ms; 2 over 128: 0.87 ms; 8 over
+// 32: 1.27 ms), backward 2 over 128 without unrolling the walk (1.92 ms;
+// 4 over 64: 2.0-3.4 ms; unrolled by 2 or 4: 2.65 ms).  Both kernels are
+// bound by instruction issue and load latency, not DRAM.
 #ifndef BSSM_ENV_FWD_SPAN
 #define BSSM_ENV_FWD_SPAN 64
 #endif
@@ -57,8 +58,13 @@ constexpr int kThreads = 256;
 #ifndef BSSM_ENV_BWD_CW
 #define BSSM_ENV_BWD_CW 2
 #endif
+#ifndef BSSM_ENV_BWD_UNROLL
+#define BSSM_ENV_BWD_UNROLL 1
+#endif
 constexpr int kFwdSpan = BSSM_ENV_FWD_SPAN, kBwdSpan = BSSM_ENV_BWD_SPAN;
 constexpr int kFwdCW = BSSM_ENV_FWD_CW, kBwdCW = BSSM_ENV_BWD_CW;
+constexpr int kRowGroups = 64;  // first-pass row groups of the gradient sums
+constexpr int kBwdUnroll = BSSM_ENV_BWD_UNROLL;
 constexpr float kNormEps = 1e-12f;  // F.normalize's default
 constexpr float kNoiseFloor = 1e-4f;
 
@@ -393,7 +399,7 @@ __global__ void __launch_bounds__(kThreads) prologue_backward_kernel(const Shape
         ldx(hi - 2, x1);
         ldx(hi - 3, x2);
     }
-#pragma unroll 1
+#pragma unroll (kBwdUnroll)
     for (long t = hi - 1; t >= t0; --t) {
         float gc[CW], g[CW], o[CW], ds[CW];
 #pragma unroll
@@ -635,6 +641,20 @@ __global__ void __launch_bounds__(kThreads) epilogue_backward_kernel(const EpiAr
     }
 }
 
+// First pass of the many-column sum: CTA (x, y) sums rows [y * per, (y + 1) *
+// per) of its columns into row y of `out` (rows in order).
+__global__ void __launch_bounds__(kThreads) reduce_row_groups_kernel(const float *partial, long rows, int cols,
+                                                                     int stride, long per, float *out) {
+    const int e = static_cast<int>(blockIdx.x) * kThreads + threadIdx.x;
+    if (e >= cols) return;
+    const long r0 = static_cast<long>(blockIdx.y) * per;
+    const long r1 = r0 + per < rows ? r0 + per : rows;
+    float acc = 0.f;
+#pragma unroll 8
+    for (long r = r0; r < r1; ++r) acc += partial[r * stride + e];
+    out[static_cast<long>(blockIdx.y) * stride + e] = acc;
+}
+
 // out[e] = sum over r of partial[r][e], rows in order (deterministic).
 __global__ void __launch_bounds__(kThreads) reduce_rows_kernel(const float *partial, long rows, int cols, int stride,
                                                                float *gw, int nw, float *gbias) {
@@ -775,7 +795,8 @@ extern "C" {
 
 long bssm_envelope_partial_floats(long batch, long tokens, int heads, int key_dim, int head_dim) {
     Shape s{batch, tokens, heads, key_dim, head_dim, 0, 1};
-    return batch * pick_tsplit(tokens, kBwdSpan) * static_cast<long>(s.partial_cols());
+    // per-span partial rows, then the row-group sums of the first reduction pass
+    return (batch * pick_tsplit(tokens, kBwdSpan) + kRowGroups) * static_cast<long>(s.partial_cols());
 }
 
 int bssm_envelope_prologue(const void *projected, int in_dtype, long batch, long tokens, int heads, int key_dim,
@@ -832,7 +853,8 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
         return fail(BSSM_ERR_INVALID, "envelope backward: null pointer");
     s.tsplit = pick_tsplit(tokens, kBwdSpan);
     if (s.tsplit > 65535) return fail(BSSM_ERR_INVALID, "envelope: sequence too long (%ld tokens)", tokens);
-    const long need = batch * s.tsplit * static_cast<long>(pcols);
+    const long prow = batch * s.tsplit;
+    const long need = (prow + kRowGroups) * static_cast<long>(pcols);
     if (workspace_floats < need)
         return fail(BSSM_ERR_WORKSPACE, "envelope backward: workspace of %ld floats, need %ld", workspace_floats, need);
     if (reinterpret_cast<uintptr_t>(workspace) & 31)
@@ -849,7 +871,14 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
     if (kBwdCW >= 4 && cw_fits<4>(s, grad_row_stride, aligned8, 6)) launch_bwd<4>(s, a, in_dtype, out_dtype, st);
     else launch_bwd<2>(s, a, in_dtype, out_dtype, st);
     if (int rc = check_launch("envelope prologue backward")) return rc;
-    reduce_rows_kernel<<<(cols + kThreads - 1) / kThreads, kThreads, 0, st>>>(workspace, batch * s.tsplit, cols, pcols,
+    // two passes, each summing rows in order: row groups, then the groups
+    const long per = (prow + kRowGroups - 1) / kRowGroups;
+    const int groups = static_cast<int>((prow + per - 1) / per);
+    float *const sums = workspace + prow * pcols;
+    reduce_row_groups_kernel<<<dim3((cols + kThreads - 1) / kThreads, groups), kThreads, 0, st>>>(
+        workspace, prow, cols, pcols, per, sums);
+    if (int rc = check_launch("envelope reduction")) return rc;
+    reduce_rows_kernel<<<(cols + kThreads - 1) / kThreads, kThreads, 0, st>>>(sums, groups, cols, pcols,
                                                                                grad_conv_weight, 4 * C, grad_aux_bias);
     return check_launch("envelope reduction");
 }
