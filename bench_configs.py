@@ -21,6 +21,14 @@ measurement plan (the headline, config 3, is ``bench.py``).
   BF16 gate and output) beside its PyTorch form; bytes-roofline fractions
   against the measured HBM copy bandwidth.
 
+* ``--config mixer``: the whole BayesianMixer layer (``bayes_ssm.mixer``) at
+  config 3's shape (B256 T512, width 512, 64 heads, key_dim 8, BF16
+  parameters and activations): RMSNorm, projection GEMMs, the fused prologue,
+  the recurrence, the fused readout, the output GEMM; forward + backward of a
+  mean-square loss, with the FP32 state boundary (the reference's default) and
+  with BF16 k/q/v, beside the same layer with the PyTorch op chains for the
+  prologue and readout.
+
 Each run prints one JSON line.  Inputs are seeded synthetic tensors with
 the survey's distributions; timing is CUDA events after warm-up.
 """
@@ -246,6 +254,32 @@ def envelope(steps: int, warmup: int) -> dict:
             "steps": steps, "warmup": warmup, "data": "synthetic"}
 
 
+def mixer(steps: int, warmup: int) -> dict:
+    import torch
+    from bayes_ssm.mixer import BayesianMixer
+    b, t, width, heads, d = 256, 512, 512, 64, 8
+    torch.manual_seed(5)
+    x = torch.randn(b, t, width, device="cuda", dtype=torch.bfloat16)
+    res = {}
+    for name, bf16_io, fused in (("fused_fp32_state_io", False, True), ("fused_bf16_state_io", True, True),
+                                 ("torch_envelope_fp32_state_io", False, False)):
+        m = BayesianMixer(width, heads, key_dim=d, chunk_length=64, bf16_state_io=bf16_io, fused_envelope=fused,
+                          dtype=torch.bfloat16, device="cuda")
+
+        def step():
+            m.zero_grad(set_to_none=True)
+            y = m(x)
+            y.float().square().mean().backward()
+
+        ms = _time(step, max(3, steps // 2), warmup)
+        res[name] = {"ms_per_step": round(ms, 4), "tok_per_s": round(b * t / (ms / 1e3), 1)}
+        del m
+        torch.cuda.empty_cache()
+    return {"config": "mixer", "workload": "BayesianMixer layer fwd + bwd, B256 T512 width 512, 64 heads, key_dim 8, "
+            "BF16 (config 3's mixer; GEMMs and input RMSNorm by PyTorch)", "metric": "tok/s/GPU", "unit": "tok/s",
+            "results": res, "steps": max(3, steps // 2), "warmup": warmup, "data": "synthetic"}
+
+
 def _peak_hbm() -> float:
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -256,11 +290,11 @@ def _peak_hbm() -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", choices=("2", "4", "envelope"), required=True)
+    ap.add_argument("--config", choices=("2", "4", "envelope", "mixer"), required=True)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()
-    fn = {"2": config2, "4": config4, "envelope": envelope}[args.config]
+    fn = {"2": config2, "4": config4, "envelope": envelope, "mixer": mixer}[args.config]
     print(json.dumps(fn(args.steps, max(3, args.warmup))), flush=True)
 
 

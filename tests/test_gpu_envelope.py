@@ -157,3 +157,29 @@ def test_read_epilogue_forward_backward(shape, read_dtype, gate_dtype):
     for name, a_, b_ in zip(("read", "gate", "weight"), gk, gr):
         assert a_.shape == b_.shape, name
         assert _rel(a_.float(), b_.float()) <= tol_g, (name, _rel(a_.float(), b_.float()))
+
+
+@pytest.mark.parametrize("dtype,bf16_io", [(torch.float32, False), (torch.bfloat16, False), (torch.bfloat16, True)])
+def test_mixer_fused_envelope_matches_torch_envelope(dtype, bf16_io):
+    """The BayesianMixer layer with the fused prologue / readout kernels
+    against the same layer with the reference's PyTorch op chains."""
+    from bayes_ssm.mixer import BayesianMixer
+    torch.manual_seed(3)
+    m = BayesianMixer(128, 16, key_dim=8, chunk_length=64, bf16_state_io=bf16_io, dtype=dtype, device="cuda")
+    with torch.no_grad():
+        for p in m.parameters():
+            p.add_(0.05 * torch.randn_like(p))
+    x = torch.randn(2, 96, 128, device="cuda", dtype=dtype)
+    grads = []
+    outs = []
+    for fused in (True, False):
+        m.fused_envelope = fused
+        m.zero_grad()
+        y = m(x)
+        y.float().square().mean().backward()
+        outs.append(y.detach().float())
+        grads.append([p.grad.detach().float().clone() for p in m.parameters()])
+    tol = 1e-4 if dtype == torch.float32 else (2e-2 if bf16_io else 1e-2)
+    assert _rel(outs[0], outs[1]) <= tol
+    for (name, _), a_, b_ in zip(m.named_parameters(), grads[0], grads[1]):
+        assert _rel(a_, b_) <= 3 * tol, (name, _rel(a_, b_))
