@@ -52,6 +52,9 @@ _SIGNATURES = {
     "bssm_envelope_prologue_backward": ([_vp, _i, _l, _l, _i, _i, _i, _l] + [_vp] * 5 + [_i] + [_vp] * 4
                                         + [_l, _vp, _vp, _vp, _l, _vp], _i),
     "bssm_envelope_epilogue_partial_floats": ([_l, _l, _i, _i], _l),
+    "bssm_rms_norm": ([_vp, _i, _l, _i, _vp, ctypes.c_float, _vp, _vp], _i),
+    "bssm_rms_norm_partial_floats": ([_l, _i], _l),
+    "bssm_rms_norm_backward": ([_vp, _i, _l, _i, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _l, _vp], _i),
     "bssm_envelope_epilogue": ([_vp, _i, _vp, _i, _l, _vp, ctypes.c_float, _l, _l, _i, _i, _vp, _vp], _i),
     "bssm_envelope_epilogue_backward": ([_vp, _i, _vp, _i, _l, _vp, ctypes.c_float, _l, _l, _i, _i, _vp, _vp, _vp,
                                          _l, _vp, _vp, _l, _vp], _i),
@@ -225,3 +228,18 @@ def envelope_epilogue_backward(read, read_dtype, gate, gate_dtype, gate_row_stri
         heads, head_dim, ptr(grad_out), ptr(grad_read), ptr(grad_gate), grad_gate_row_stride, ptr(grad_norm_weight),
         ptr(workspace), 0 if workspace is None else workspace.numel(), stream)
     check(rc, "bssm_envelope_epilogue_backward")
+
+
+def rms_norm(x, dtype, rows, width, weight, eps, out, stream) -> None:
+    check(load().bssm_rms_norm(ptr(x), dtype, rows, width, ptr(weight), float(eps), ptr(out), stream), "bssm_rms_norm")
+
+
+def rms_norm_partial_floats(rows, width) -> int:
+    return int(load().bssm_rms_norm_partial_floats(rows, width))
+
+
+def rms_norm_backward(x, dtype, rows, width, weight, eps, grad_out, grad_x, grad_weight, workspace, stream) -> None:
+    rc = load().bssm_rms_norm_backward(ptr(x), dtype, rows, width, ptr(weight), float(eps), ptr(grad_out),
+                                       ptr(grad_x), ptr(grad_weight), ptr(workspace),
+                                       0 if workspace is None else workspace.numel(), stream)
+    check(rc, "bssm_rms_norm_backward")

@@ -248,4 +248,48 @@ def read_epilogue(read: Tensor, gate: Tensor, norm_weight: Tensor, *, heads: int
     return _ReadEpilogue.apply(read.contiguous(), gate, norm_weight, heads, float(eps))
 
 
-__all__ = ["paper_prologue", "paper_prologue_torch", "read_epilogue", "read_epilogue_torch"]
+class _RmsNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        width = x.shape[-1]
+        rows = x.numel() // width
+        w = weight.detach().float().contiguous()
+        out = torch.empty_like(x)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        with torch.cuda.device(x.device):
+            _capi.rms_norm(x, _DTYPES[x.dtype], rows, width, w, eps, out, stream)
+        ctx.save_for_backward(x, w)
+        ctx.dims = (eps, weight.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, w = ctx.saved_tensors
+        eps, w_dtype = ctx.dims
+        width = x.shape[-1]
+        rows = x.numel() // width
+        go = grad_out.to(x.dtype).contiguous()
+        gx = torch.empty_like(x)
+        gw = torch.empty(width, device=x.device, dtype=torch.float32)
+        ws = torch.empty(_capi.rms_norm_partial_floats(rows, width), device=x.device, dtype=torch.float32)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        with torch.cuda.device(x.device):
+            _capi.rms_norm_backward(x, _DTYPES[x.dtype], rows, width, w, eps, go, gx, gw, ws, stream)
+        return gx, gw.to(w_dtype), None
+
+
+def rms_norm(x: Tensor, weight: Tensor, eps: Optional[float] = None) -> Tensor:
+    """``nn.RMSNorm`` over the last dimension (the mixer's input norm): one
+    sm_100a kernel for the forward and one for the backward on CUDA
+    (float32 / bfloat16, width 256, 512, 768 or 1024); ``F.rms_norm``
+    otherwise.  ``eps=None`` is the dtype's machine epsilon, as in
+    ``nn.RMSNorm``."""
+    if eps is None:
+        eps = torch.finfo(x.dtype).eps
+    width = x.shape[-1]
+    if (not x.is_cuda or x.dtype not in _DTYPES or width % 256 or width > 1024 or weight.numel() != width):
+        return F.rms_norm(x, (width,), weight, eps)
+    return _RmsNorm.apply(x.contiguous(), weight, float(eps))
+
+
+__all__ = ["paper_prologue", "paper_prologue_torch", "read_epilogue", "read_epilogue_torch", "rms_norm"]

@@ -16,9 +16,10 @@ load either way:
 Forward (``:579-729``): RMSNorm -> projection GEMM -> the fused prologue
 (:func:`bayes_ssm.envelope.paper_prologue`) -> :func:`bayesian_layer` on the
 recurrence kernels -> the fused readout (:func:`bayes_ssm.envelope.read_epilogue`)
--> output GEMM.  The GEMMs and the input RMSNorm are PyTorch's (cuBLAS);
-``fused_envelope=False`` runs the prologue and readout as the reference's
-PyTorch op chains instead, for comparison.
+-> output GEMM.  The input RMSNorm is this package's kernel pair
+(:func:`bayes_ssm.envelope.rms_norm`); the GEMMs are PyTorch's (cuBLAS).
+``fused_envelope=False`` runs the norm, prologue and readout as the
+reference's PyTorch ops instead, for comparison.
 """
 from __future__ import annotations
 
@@ -29,7 +30,7 @@ import torch
 from torch import Tensor, nn
 
 from .bayesian_layer import bayesian_layer
-from .envelope import paper_prologue, paper_prologue_torch, read_epilogue, read_epilogue_torch
+from .envelope import paper_prologue, paper_prologue_torch, read_epilogue, read_epilogue_torch, rms_norm
 
 
 class BayesianMixer(nn.Module):
@@ -76,7 +77,7 @@ class BayesianMixer(nn.Module):
             self.aux_bias[self.state_width + 1::2].fill_(math.log(math.expm1(1.0)))
 
     def forward(self, x: Tensor) -> Tensor:
-        z = self.norm(x)
+        z = rms_norm(x, self.norm.weight, self.norm.eps) if self.fused_envelope else self.norm(x)
         projected = self.qkv_proj(z)
         kw = dict(heads=self.heads, key_dim=self.key_dim, head_dim=self.head_dim)
         if self.fused_envelope and projected.is_cuda:

@@ -655,6 +655,95 @@ __global__ void __launch_bounds__(kThreads) reduce_row_groups_kernel(const float
     out[static_cast<long>(blockIdx.y) * stride + e] = acc;
 }
 
+// ---- input RMSNorm (nn.RMSNorm over the width, the mixer's first op) -------
+// A warp owns a row; lane l holds chunks c * 32 + l of 8 elements (each chunk
+// index is one 16-byte vector), so every load and store is coalesced.
+constexpr int kNormRowsPerCta = kThreads / 32;
+
+template <bool BF, int CPL>
+__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const void *x, const float *w, void *out, long rows,
+                                                          float eps) {
+    constexpr int W = 256 * CPL;
+    const int lane = threadIdx.x & 31;
+    const long row = static_cast<long>(blockIdx.x) * kNormRowsPerCta + (threadIdx.x >> 5);
+    if (row >= rows) return;  // whole warps
+    float v[8 * CPL];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+        ldn<BF, 8>(x, row * W + (c * 32 + lane) * 8, v + 8 * c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(v[8 * c + i], v[8 * c + i], ss);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float inv = rsqrtf(ss * (1.0f / W) + eps);
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+        float wv[8];
+        ldn<false, 8>(w, (c * 32 + lane) * 8, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[8 * c + i] = v[8 * c + i] * inv * wv[i];
+        stn<BF, 8>(out, row * W + (c * 32 + lane) * 8, v + 8 * c);
+    }
+}
+
+// Backward: gx = inv (w gy) - x inv^3 (x . w gy) / W per row; the weight
+// gradient sum_rows gy x inv is kept per lane over the rows a warp visits
+// (grid-stride), then summed over the CTA's warps in order into one partial
+// row per CTA.
+template <bool BF, int CPL>
+__global__ void __launch_bounds__(kThreads) rmsnorm_backward_kernel(const void *x, const float *w, const void *gy,
+                                                                   void *gx, long rows, float eps, float *partial) {
+    constexpr int W = 256 * CPL;
+    __shared__ float red[kNormRowsPerCta][W];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float wv[8 * CPL], gw[8 * CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) ldn<false, 8>(w, (c * 32 + lane) * 8, wv + 8 * c);
+#pragma unroll
+    for (int i = 0; i < 8 * CPL; ++i) gw[i] = 0.f;
+    for (long row = static_cast<long>(blockIdx.x) * kNormRowsPerCta + warp; row < rows;
+         row += static_cast<long>(gridDim.x) * kNormRowsPerCta) {
+        float xv[8 * CPL], g[8 * CPL];
+        float ss = 0.f, dot = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            ldn<BF, 8>(x, row * W + (c * 32 + lane) * 8, xv + 8 * c);
+            ldn<BF, 8>(gy, row * W + (c * 32 + lane) * 8, g + 8 * c);
+        }
+#pragma unroll
+        for (int i = 0; i < 8 * CPL; ++i) ss = fmaf(xv[i], xv[i], ss);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float inv = rsqrtf(ss * (1.0f / W) + eps);
+#pragma unroll
+        for (int i = 0; i < 8 * CPL; ++i) {
+            gw[i] = fmaf(g[i] * xv[i], inv, gw[i]);  // gy x inv
+            g[i] *= wv[i];                           // z = w gy
+            dot = fmaf(xv[i], g[i], dot);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        const float c3 = inv * inv * inv * dot * (1.0f / W);
+#pragma unroll
+        for (int i = 0; i < 8 * CPL; ++i) g[i] = inv * g[i] - xv[i] * c3;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) stn<BF, 8>(gx, row * W + (c * 32 + lane) * 8, g + 8 * c);
+    }
+#pragma unroll
+    for (int c = 0; c < CPL; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) red[warp][(c * 32 + lane) * 8 + i] = gw[8 * c + i];
+    __syncthreads();
+    for (int e = threadIdx.x; e < W; e += kThreads) {
+        float acc = 0.f;
+#pragma unroll
+        for (int wp = 0; wp < kNormRowsPerCta; ++wp) acc += red[wp][e];
+        partial[static_cast<long>(blockIdx.x) * W + e] = acc;
+    }
+}
+
 // out[e] = sum over r of partial[r][e], rows in order (deterministic).
 __global__ void __launch_bounds__(kThreads) reduce_rows_kernel(const float *partial, long rows, int cols, int stride,
                                                                float *gw, int nw, float *gbias) {
@@ -785,6 +874,39 @@ void launch_epi_hd(const EpiArgs &a, int hd, int rd, int gd, bool backward, cuda
     }
 }
 
+template <int CPL>
+void launch_norm(const void *x, int dt, const float *w, const void *gy, void *out, long rows, float eps,
+                 float *partial, int ctas, cudaStream_t st) {
+    if (gy == nullptr) {
+        const unsigned grid = static_cast<unsigned>((rows + kNormRowsPerCta - 1) / kNormRowsPerCta);
+        if (dt == BSSM_BF16) rmsnorm_kernel<true, CPL><<<grid, kThreads, 0, st>>>(x, w, out, rows, eps);
+        else rmsnorm_kernel<false, CPL><<<grid, kThreads, 0, st>>>(x, w, out, rows, eps);
+    } else {
+        if (dt == BSSM_BF16) rmsnorm_backward_kernel<true, CPL><<<ctas, kThreads, 0, st>>>(x, w, gy, out, rows, eps, partial);
+        else rmsnorm_backward_kernel<false, CPL><<<ctas, kThreads, 0, st>>>(x, w, gy, out, rows, eps, partial);
+    }
+}
+
+void launch_norm_w(int width, const void *x, int dt, const float *w, const void *gy, void *out, long rows, float eps,
+                   float *partial, int ctas, cudaStream_t st) {
+    switch (width / 256) {
+        case 1: launch_norm<1>(x, dt, w, gy, out, rows, eps, partial, ctas, st); break;
+        case 2: launch_norm<2>(x, dt, w, gy, out, rows, eps, partial, ctas, st); break;
+        case 3: launch_norm<3>(x, dt, w, gy, out, rows, eps, partial, ctas, st); break;
+        default: launch_norm<4>(x, dt, w, gy, out, rows, eps, partial, ctas, st); break;
+    }
+}
+
+constexpr int kNormCtas = 4 * 148;  // backward grid: a few CTAs per SM, grid-stride over rows
+
+int norm_check(long rows, int width, int dtype) {
+    if (rows < 0) return fail(BSSM_ERR_INVALID, "rms_norm: negative rows");
+    if (width <= 0 || width % 256 || width > 1024)
+        return fail(BSSM_ERR_UNSUPPORTED, "rms_norm: width must be 256, 512, 768 or 1024 (got %d)", width);
+    if (dtype != BSSM_F32 && dtype != BSSM_BF16) return fail(BSSM_ERR_UNSUPPORTED, "rms_norm: float32 or bfloat16");
+    return BSSM_OK;
+}
+
 }  // namespace env
 }  // namespace bssm
 
@@ -881,6 +1003,58 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
     reduce_rows_kernel<<<(cols + kThreads - 1) / kThreads, kThreads, 0, st>>>(sums, groups, cols, pcols,
                                                                                grad_conv_weight, 4 * C, grad_aux_bias);
     return check_launch("envelope reduction");
+}
+
+long bssm_rms_norm_partial_floats(long rows, int width) {
+    (void)rows;
+    return static_cast<long>(kNormCtas + kRowGroups) * width;
+}
+
+int bssm_rms_norm(const void *x, int dtype, long rows, int width, const float *weight, float eps, void *out,
+                  void *stream) {
+    if (int rc = norm_check(rows, width, dtype)) return rc;
+    if (rows == 0) {
+        g_last_error.clear();
+        return BSSM_OK;
+    }
+    if (!x || !weight || !out) return fail(BSSM_ERR_INVALID, "rms_norm: null pointer");
+    const void *al[] = {x, weight, out};
+    for (const void *p : al)
+        if (reinterpret_cast<uintptr_t>(p) & 15) return fail(BSSM_ERR_ALIGNMENT, "rms_norm: tensors must be 16-byte aligned");
+    launch_norm_w(width, x, dtype, weight, nullptr, out, rows, eps, nullptr, 0, static_cast<cudaStream_t>(stream));
+    return check_launch("rms_norm");
+}
+
+int bssm_rms_norm_backward(const void *x, int dtype, long rows, int width, const float *weight, float eps,
+                           const void *grad_out, void *grad_x, float *grad_weight, float *workspace,
+                           long workspace_floats, void *stream) {
+    if (int rc = norm_check(rows, width, dtype)) return rc;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (!grad_weight) return fail(BSSM_ERR_INVALID, "rms_norm backward: null weight gradient");
+    if (rows == 0) {
+        const cudaError_t err = cudaMemsetAsync(grad_weight, 0, sizeof(float) * width, st);
+        if (err != cudaSuccess) return fail(BSSM_ERR_CUDA, "rms_norm backward: %s", cudaGetErrorString(err));
+        g_last_error.clear();
+        return BSSM_OK;
+    }
+    if (!x || !weight || !grad_out || !grad_x || !workspace) return fail(BSSM_ERR_INVALID, "rms_norm backward: null pointer");
+    if (workspace_floats < bssm_rms_norm_partial_floats(rows, width))
+        return fail(BSSM_ERR_WORKSPACE, "rms_norm backward: workspace too small");
+    const void *al[] = {x, weight, grad_out, grad_x, workspace};
+    for (const void *p : al)
+        if (reinterpret_cast<uintptr_t>(p) & 15)
+            return fail(BSSM_ERR_ALIGNMENT, "rms_norm backward: tensors must be 16-byte aligned");
+    launch_norm_w(width, x, dtype, weight, grad_out, grad_x, rows, eps, workspace, kNormCtas, st);
+    if (int rc = check_launch("rms_norm backward")) return rc;
+    const long per = (kNormCtas + kRowGroups - 1) / kRowGroups;
+    const int groups = static_cast<int>((kNormCtas + per - 1) / per);
+    float *const sums = workspace + static_cast<long>(kNormCtas) * width;
+    reduce_row_groups_kernel<<<dim3((width + kThreads - 1) / kThreads, groups), kThreads, 0, st>>>(
+        workspace, kNormCtas, width, width, per, sums);
+    if (int rc = check_launch("rms_norm reduction")) return rc;
+    reduce_rows_kernel<<<(width + kThreads - 1) / kThreads, kThreads, 0, st>>>(sums, groups, width, width, grad_weight,
+                                                                               width, nullptr);
+    return check_launch("rms_norm reduction");
 }
 
 long bssm_envelope_epilogue_partial_floats(long batch, long tokens, int heads, int head_dim) {

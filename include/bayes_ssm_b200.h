@@ -340,6 +340,21 @@ int bssm_envelope_epilogue(const void *read, int read_dtype, const void *gate, i
  * bssm_envelope_epilogue_partial_floats() floats.
  */
 long bssm_envelope_epilogue_partial_floats(long batch, long tokens, int heads, int head_dim);
+
+/*
+ * nn.RMSNorm over rows of `width` elements (the mixer's input norm,
+ * example/train_6layer.py:581): out = x * rsqrt(mean(x^2) + eps) * weight,
+ * computed in float32, stored in x's dtype (BSSM_F32 or BSSM_BF16).  width is
+ * 256, 512, 768 or 1024; x and out [rows, width] contiguous; weight float32.
+ * The backward writes grad_x (x's dtype) and grad_weight (float32, summed in
+ * a fixed order; workspace of bssm_rms_norm_partial_floats() floats).
+ */
+int bssm_rms_norm(const void *x, int dtype, long rows, int width, const float *weight, float eps, void *out,
+                  void *stream);
+long bssm_rms_norm_partial_floats(long rows, int width);
+int bssm_rms_norm_backward(const void *x, int dtype, long rows, int width, const float *weight, float eps,
+                           const void *grad_out, void *grad_x, float *grad_weight, float *workspace,
+                           long workspace_floats, void *stream);
 int bssm_envelope_epilogue_backward(const void *read, int read_dtype, const void *gate, int gate_dtype,
                                     long gate_row_stride, const float *norm_weight, float eps, long batch, long tokens,
                                     int heads, int head_dim, const void *grad_out, void *grad_read, void *grad_gate,

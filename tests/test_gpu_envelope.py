@@ -161,8 +161,13 @@ def test_read_epilogue_forward_backward(shape, read_dtype, gate_dtype):
 
 @pytest.mark.parametrize("dtype,bf16_io", [(torch.float32, False), (torch.bfloat16, False), (torch.bfloat16, True)])
 def test_mixer_fused_envelope_matches_torch_envelope(dtype, bf16_io):
-    """The BayesianMixer layer with the fused prologue / readout kernels
-    against the same layer with the reference's PyTorch op chains."""
+    """The BayesianMixer layer with the fused norm / prologue / readout kernels
+    against the same layer with the reference's PyTorch ops.  In float32 the
+    two agree closely; in bfloat16 each rounds at different points, so both
+    are measured against a float32 copy of the layer and the fused one must be
+    no less accurate than the PyTorch one (output and every parameter
+    gradient)."""
+    import copy
     from bayes_ssm.mixer import BayesianMixer
     torch.manual_seed(3)
     m = BayesianMixer(128, 16, key_dim=8, chunk_length=64, bf16_state_io=bf16_io, dtype=dtype, device="cuda")
@@ -170,16 +175,46 @@ def test_mixer_fused_envelope_matches_torch_envelope(dtype, bf16_io):
         for p in m.parameters():
             p.add_(0.05 * torch.randn_like(p))
     x = torch.randn(2, 96, 128, device="cuda", dtype=dtype)
-    grads = []
-    outs = []
-    for fused in (True, False):
-        m.fused_envelope = fused
-        m.zero_grad()
-        y = m(x)
+
+    def run(mod, fused, xin):
+        mod.fused_envelope = fused
+        mod.zero_grad()
+        y = mod(xin)
         y.float().square().mean().backward()
-        outs.append(y.detach().float())
-        grads.append([p.grad.detach().float().clone() for p in m.parameters()])
-    tol = 1e-4 if dtype == torch.float32 else (2e-2 if bf16_io else 1e-2)
-    assert _rel(outs[0], outs[1]) <= tol
-    for (name, _), a_, b_ in zip(m.named_parameters(), grads[0], grads[1]):
-        assert _rel(a_, b_) <= 3 * tol, (name, _rel(a_, b_))
+        return y.detach().float(), [p.grad.detach().float().clone() for p in mod.parameters()]
+
+    yf, gf = run(m, True, x)
+    yt, gt = run(m, False, x)
+    if dtype == torch.float32:
+        assert _rel(yf, yt) <= 1e-4
+        for (name, _), a_, b_ in zip(m.named_parameters(), gf, gt):
+            assert _rel(a_, b_) <= 3e-4, (name, _rel(a_, b_))
+        return
+    ref = copy.deepcopy(m).float()
+    ref.bf16_state_io = False
+    y32, g32 = run(ref, False, x.float())
+    assert _rel(yf, y32) <= max(1.5 * _rel(yt, y32), 2e-3), (_rel(yf, y32), _rel(yt, y32))
+    for (name, _), a_, b_, c_ in zip(m.named_parameters(), gf, gt, g32):
+        assert _rel(a_, c_) <= max(1.5 * _rel(b_, c_), 5e-3), (name, _rel(a_, c_), _rel(b_, c_))
+
+
+@pytest.mark.parametrize("width,dtype", [(512, torch.bfloat16), (512, torch.float32), (256, torch.float32),
+                                         (1024, torch.bfloat16), (768, torch.float32)])
+def test_rms_norm_matches_torch(width, dtype):
+    from bayes_ssm.envelope import rms_norm
+    g = torch.Generator(device="cuda").manual_seed(width)
+    x = (torch.randn(3, 77, width, generator=g, device="cuda") * 2).to(dtype)
+    w = (torch.rand(width, generator=g, device="cuda") + 0.5).to(dtype)
+    xk, wk = x.clone().requires_grad_(), w.clone().requires_grad_()
+    xr, wr = x.float().clone().requires_grad_(), w.float().clone().requires_grad_()
+    eps = torch.finfo(dtype).eps
+    y = rms_norm(xk, wk)
+    yr = torch.nn.functional.rms_norm(xr, (width,), wr, eps)
+    tol = 1e-6 if dtype == torch.float32 else 4e-3
+    assert y.dtype == dtype and _rel(y.float(), yr) <= tol
+    up = torch.randn(y.shape, generator=g, device="cuda")
+    gk = torch.autograd.grad(y, (xk, wk), up.to(dtype))
+    gr = torch.autograd.grad(yr, (xr, wr), up)
+    tol_g = 1e-5 if dtype == torch.float32 else 8e-3
+    for a_, b_ in zip(gk, gr):
+        assert _rel(a_.float(), b_.float()) <= tol_g
