@@ -1,6 +1,8 @@
 """Host side of the sm_100a static associative scan (``csrc/bssm_assoc_scan.cu``)."""
 from __future__ import annotations
 
+import contextlib
+
 import torch
 from torch import Tensor
 
@@ -10,6 +12,7 @@ from .bayesian_layer import _is_cuda_graph_capturing
 MAX_KEY_DIM = 32
 MAX_VALUE_DIM = 256
 MAX_CHAINS_PER_LAUNCH = 65535
+_NO_SWITCH = contextlib.nullcontext()  # the inputs' device is already current
 
 
 def assoc_scan_cuda(keys: Tensor, values: Tensor, queries: Tensor, r2: Tensor, mean0, cov0, *,
@@ -38,7 +41,11 @@ def assoc_scan_cuda(keys: Tensor, values: Tensor, queries: Tensor, r2: Tensor, m
     f32 = torch.float32
 
     def chains(x, tail):
-        return None if x is None else x.to(f32).expand(*batch, *tail).reshape(n, *tail).contiguous()
+        if x is None:
+            return None
+        if x.dtype == f32 and x.is_contiguous() and tuple(x.shape) == (*batch, *tail):
+            return x.view(n, *tail)  # already one row per chain: no expand / copy
+        return x.to(f32).expand(*batch, *tail).reshape(n, *tail).contiguous()
 
     k, v, q = chains(keys, (t, d)), chains(values, (t, m)), chains(queries, (t, d))
     r = chains(r2, (t,))
@@ -48,7 +55,7 @@ def assoc_scan_cuda(keys: Tensor, values: Tensor, queries: Tensor, r2: Tensor, m
     pt = torch.empty(n, d, d, device=dev, dtype=f32)
     status = torch.zeros(1, device=dev, dtype=torch.int32)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    with torch.cuda.device(dev):
+    with torch.cuda.device(dev) if dev.index != torch.cuda.current_device() else _NO_SWITCH:
         for lo in range(0, n, MAX_CHAINS_PER_LAUNCH):
             hi = min(n, lo + MAX_CHAINS_PER_LAUNCH)
             sl = slice(lo, hi)

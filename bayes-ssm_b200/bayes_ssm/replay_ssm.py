@@ -17,6 +17,7 @@ Same API as catid/bayes-ssm ``bayes_ssm/replay_ssm.py``: ``ReplaySSM`` (:34-145)
 """
 from __future__ import annotations
 
+import math
 from numbers import Real
 from typing import Optional
 
@@ -146,9 +147,8 @@ def _scan_inputs(keys, values, queries, observation_variances, initial_mean, ini
             raise ValueError("initial_mean batch dimensions are not broadcastable to keys")
         mean0 = mean0.expand(*batch, d, m)
         _check_finite(mean0, "initial_mean")
-    if not isinstance(denominator_floor, Real) or not torch.isfinite(
-        torch.tensor(float(denominator_floor))
-    ) or denominator_floor <= 0:
+    if not isinstance(denominator_floor, Real) or not math.isfinite(float(denominator_floor)) \
+            or denominator_floor <= 0:
         raise ValueError("denominator_floor must be finite and positive")
     r2 = torch.as_tensor(observation_variances, device=device, dtype=dtype)
     r2 = torch.broadcast_to(r2, (*batch, t))
