@@ -898,6 +898,30 @@ void launch_norm(const void *x, int dt, const float *w, const void *gy, void *ou
     }
 }
 
+// Backward grid: one full wave (resident CTAs per SM x SMs), at most `cap`.
+template <int CPL>
+int norm_wave(int dt, int cap) {
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return cap;
+    const cudaError_t err =
+        dt == BSSM_BF16
+            ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_backward_kernel<true, CPL>, kThreads, 0)
+            : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_backward_kernel<false, CPL>, kThreads, 0);
+    if (err != cudaSuccess || per_sm <= 0) return cap;
+    const long wave = static_cast<long>(per_sm) * sms;
+    return static_cast<int>(wave < cap ? wave : cap);
+}
+
+int norm_wave_w(int width, int dt, int cap) {
+    switch (width / 256) {
+        case 1: return norm_wave<1>(dt, cap);
+        case 2: return norm_wave<2>(dt, cap);
+        case 3: return norm_wave<3>(dt, cap);
+        default: return norm_wave<4>(dt, cap);
+    }
+}
+
 void launch_norm_w(int width, const void *x, int dt, const float *w, const void *gy, void *out, long rows, float eps,
                    float *partial, int ctas, cudaStream_t st) {
     switch (width / 256) {
@@ -908,7 +932,7 @@ void launch_norm_w(int width, const void *x, int dt, const float *w, const void 
     }
 }
 
-constexpr int kNormCtas = 4 * 148;  // backward grid: a few CTAs per SM, grid-stride over rows
+constexpr int kNormCtas = 4 * 148;  // most backward CTAs (grid-stride over rows); sizes the workspace
 
 int norm_check(long rows, int width, int dtype) {
     if (rows < 0) return fail(BSSM_ERR_INVALID, "rms_norm: negative rows");
@@ -1055,13 +1079,14 @@ int bssm_rms_norm_backward(const void *x, int dtype, long rows, int width, const
     for (const void *p : al)
         if (reinterpret_cast<uintptr_t>(p) & 15)
             return fail(BSSM_ERR_ALIGNMENT, "rms_norm backward: tensors must be 16-byte aligned");
-    launch_norm_w(width, x, dtype, weight, grad_out, grad_x, rows, eps, workspace, kNormCtas, st);
+    const int ctas = norm_wave_w(width, dtype, kNormCtas);
+    launch_norm_w(width, x, dtype, weight, grad_out, grad_x, rows, eps, workspace, ctas, st);
     if (int rc = check_launch("rms_norm backward")) return rc;
-    const long per = (kNormCtas + kRowGroups - 1) / kRowGroups;
-    const int groups = static_cast<int>((kNormCtas + per - 1) / per);
-    float *const sums = workspace + static_cast<long>(kNormCtas) * width;
+    const long per = (ctas + kRowGroups - 1) / kRowGroups;
+    const int groups = static_cast<int>((ctas + per - 1) / per);
+    float *const sums = workspace + static_cast<long>(ctas) * width;
     reduce_row_groups_kernel<<<dim3((width + kThreads - 1) / kThreads, groups), kThreads, 0, st>>>(
-        workspace, kNormCtas, width, width, per, sums);
+        workspace, ctas, width, width, per, sums);
     if (int rc = check_launch("rms_norm reduction")) return rc;
     reduce_rows_kernel<<<(width + kThreads - 1) / kThreads, kThreads, 0, st>>>(sums, groups, width, width, grad_weight,
                                                                                width, nullptr);

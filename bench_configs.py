@@ -241,6 +241,20 @@ def envelope(steps: int, warmup: int) -> dict:
         torch.autograd.grad(o, (re_, ge_, we_), gout)
 
     ms_ee = _time(eager_epi, max(3, steps // 4), warmup)
+    # input RMSNorm over the width: BF16 [B*T, W]
+    xr = torch.randn(b * t, w, generator=g, device=dev).to(torch.bfloat16)
+    nrm = torch.rand(w, generator=g, device=dev) + 0.5
+    xo, gxo = torch.empty_like(xr), torch.empty_like(xr)
+    gyn = torch.randn_like(xr)
+    gnw = torch.empty(w, **f32)
+    nws = torch.empty(_capi.rms_norm_partial_floats(b * t, w), **f32)
+    ms_nf = _time(lambda: _capi.rms_norm(xr, _capi.BSSM_BF16, b * t, w, nrm, eps, xo, sp), steps, warmup)
+    ms_nb = _time(lambda: _capi.rms_norm_backward(xr, _capi.BSSM_BF16, b * t, w, nrm, eps, gyn, gxo, gnw, nws, sp),
+                  steps, warmup)
+    n_bytes_f, n_bytes_b = b * t * w * 2 * 2, b * t * w * 2 * 3
+    norm = {"forward_ms": round(ms_nf, 4), "backward_ms": round(ms_nb, 4),
+            "forward_frac": round(n_bytes_f / ms_nf / 1e6 / hbm, 3),
+            "backward_frac": round(n_bytes_b / ms_nb / 1e6 / hbm, 3)}
     epilogue = {"forward_ms": round(ms_ef, 4), "backward_ms": round(ms_eb, 4),
                 "forward_frac": round(e_fwd_bytes / ms_ef / 1e6 / hbm, 3),
                 "backward_frac": round(e_bwd_bytes / ms_eb / 1e6 / hbm, 3),
@@ -248,7 +262,7 @@ def envelope(steps: int, warmup: int) -> dict:
                 "eager_torch_fwd_bwd_ms": round(ms_ee, 4)}
     return {"config": "envelope", "workload": "BayesianMixer prologue, B256 T512 H64 D8 head_dim 8 "
             "(BF16 projection, 2,176 channels), fwd + bwd", "metric": "ms per fwd+bwd", "unit": "ms",
-            "kernel": res, "eager_torch_fwd_bwd_ms": round(ms_e, 4), "readout_epilogue": epilogue,
+            "kernel": res, "eager_torch_fwd_bwd_ms": round(ms_e, 4), "readout_epilogue": epilogue, "input_rms_norm": norm,
             "speedup_f32_out": round(ms_e / (res["f32_out"]["forward_ms"] + res["f32_out"]["backward_ms"]), 2),
             "hbm_peak_GBps": hbm, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)",
             "steps": steps, "warmup": warmup, "data": "synthetic"}
