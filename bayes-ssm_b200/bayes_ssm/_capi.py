@@ -59,6 +59,10 @@ _SIGNATURES = {
     "bssm_envelope_epilogue_backward": ([_vp, _i, _vp, _i, _l, _vp, ctypes.c_float, _l, _l, _i, _i, _vp, _vp, _vp,
                                          _l, _vp, _vp, _l, _vp], _i),
     "bssm_debug_wait_timeouts": ([], ctypes.c_uint),
+    "bssm_stream_status": ([_vp], _i),
+    "bssm_debug_wait_probe": ([_i, _vp], _i),
+    "bssm_debug_fma_probe": ([_vp, _i, _i, _vp], _i),
+    "bssm_debug_fma_probe_flops": ([_i, _i], _l),
     "bssm_debug_last_family": ([], _i),
 }
 
@@ -176,6 +180,36 @@ def check_values(tensors) -> list[int]:
 def wait_timeouts() -> int:
     """Bounded in-kernel waits that gave up since load (0 in a healthy run)."""
     return int(load().bssm_debug_wait_timeouts())
+
+
+class WaitTimeout(KernelError):
+    """A bounded wait inside a recurrence kernel gave up: outputs are wrong."""
+
+
+BSSM_ERR_TIMEOUT = 6
+
+
+def stream_status(stream) -> None:
+    """Synchronise ``stream`` and raise :class:`WaitTimeout` if a bounded
+    in-kernel wait on this device gave up since the previous check (each
+    give-up is reported once), :class:`KernelError` on a CUDA error."""
+    lib = load()
+    rc = lib.bssm_stream_status(stream)
+    if rc == BSSM_ERR_TIMEOUT:
+        raise WaitTimeout(lib.bssm_last_error().decode(errors="replace"))
+    check(rc, "bssm_stream_status")
+
+
+def fma_probe(out, blocks, iters, stream) -> int:
+    """Enqueue the FP32 FMA throughput probe; returns its flop count."""
+    lib = load()
+    check(lib.bssm_debug_fma_probe(ptr(out), int(blocks), int(iters), stream), "bssm_debug_fma_probe")
+    return int(lib.bssm_debug_fma_probe_flops(int(blocks), int(iters)))
+
+
+def wait_probe(limit, stream) -> None:
+    """Diagnostic: make one bounded wait give up (see the C header)."""
+    check(load().bssm_debug_wait_probe(int(limit), stream), "bssm_debug_wait_probe")
 
 
 FAMILIES = {0: None, 1: "chain", 2: "staged", 3: "v1"}

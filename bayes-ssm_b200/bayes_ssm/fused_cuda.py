@@ -44,6 +44,21 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _status(device: torch.device) -> None:
+    """Raise if a bounded wait inside a kernel gave up (``_capi.WaitTimeout``).
+
+    The thread-per-chain kernels never hang on their own copies: a wait that
+    runs out is counted on the device and the kernel finishes with wrong
+    outputs.  This synchronises the stream and turns such a count into an
+    exception, so no call returns outputs or gradients after a give-up.  It is
+    skipped while a CUDA graph is being captured (no host synchronisation is
+    legal there); call ``_capi.stream_status`` after replaying a graph.
+    """
+    if torch.cuda.is_current_stream_capturing():
+        return
+    _capi.stream_status(_stream(device))
+
+
 class _ChunkedBayesianFunction(torch.autograd.Function):
     """Exact chunked recurrence: forward kernel + single-launch replay backward."""
 
@@ -78,6 +93,7 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
                                   initial_mean, initial_covariance, out, mean_final, cov_final,
                                   bmean, bcov, n, t, int(chunk_length), denominator_floor,
                                   _stream(dev), replay_states=rs)
+            _status(dev)
         ctx.save_for_backward(keys, values, queries, decay, process, observation, bmean, bcov, rs)
         ctx.chunk_length = int(chunk_length)
         ctx.denominator_floor = float(denominator_floor)
@@ -116,6 +132,7 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
                                    None, None, bmean, bcov, gy, gmf, gcf, gk, gv, gq, gd, gp, gr,
                                    gm0, gc0, ws, ws_bytes, n, t, ctx.chunk_length,
                                    ctx.denominator_floor, _stream(dev), replay_states=rs)
+            _status(dev)
         return (gk if needs[0] else None, gv if needs[1] else None, gq if needs[2] else None,
                 gd if needs[3] else None, gp if needs[4] else None, gr if needs[5] else None,
                 gm0 if needs[6] else None, gc0 if needs[7] else None, None, None, None)

@@ -166,22 +166,37 @@ __device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, int bytes) {
                  : "memory");
 }
 // Bounded wait for the phase of the given parity.  A wait that gives up is
-// counted (the results are then wrong, never a hang); the host reads the
-// count through bssm_debug_wait_timeouts().
+// counted in a device word (the kernel then runs on with wrong results
+// instead of hanging); bssm_stream_status() turns a new count into
+// BSSM_ERR_TIMEOUT, and the Python layer raises on it after every call.
 __device__ unsigned int g_wait_timeouts = 0;
 constexpr int kWaitLimit = 1 << 22;
-__device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_n(uint64_t *bar, uint32_t parity, int limit) {
     const uint32_t addr = smem_u32(bar);
-    for (int it = 0; it < kWaitLimit; ++it) {
+    for (int it = 0; it < limit; ++it) {
         uint32_t done;
         asm volatile(
             "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
             : "=r"(done)
             : "r"(addr), "r"(parity)
             : "memory");
-        if (done) return;
+        if (done) return true;
     }
     atomicAdd(&g_wait_timeouts, 1u);
+    return false;
+}
+__device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity) { mbar_wait_n(bar, parity, kWaitLimit); }
+
+// Diagnostic: one thread waits, with `limit` polls, on a barrier phase that
+// nothing completes, so the bounded wait gives up and is counted exactly as
+// a give-up inside a recurrence kernel would be.
+__global__ void wait_probe_kernel(int limit) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+        mbar_wait_n(&bar, 0, limit);
+    }
 }
 
 // ---- TMA tensor copies (this CTA's shared memory only) ----------------------
@@ -2315,6 +2330,46 @@ extern "C" unsigned int bssm_debug_wait_timeouts(void) {
     unsigned int v = 0;
     if (cudaMemcpyFromSymbol(&v, bssm::chain::g_wait_timeouts, sizeof(v)) != cudaSuccess) return ~0u;
     return v;
+}
+
+namespace {
+// Give-ups already reported by bssm_stream_status, per device.
+constexpr int kMaxDevices = 64;
+std::mutex g_status_mu;
+unsigned int g_status_seen[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int bssm_stream_status(void *stream) {
+    using bssm::fail;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return fail(BSSM_ERR_CUDA, "stream status: %s", cudaGetErrorString(err));
+    if (dev < 0 || dev >= kMaxDevices) return fail(BSSM_ERR_INVALID, "stream status: device %d out of range", dev);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned int count = 0;
+    // to pageable memory: returns once the stream's earlier work and the copy are done
+    err = cudaMemcpyFromSymbolAsync(&count, bssm::chain::g_wait_timeouts, sizeof(count), 0, cudaMemcpyDeviceToHost,
+                                    st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess) return fail(BSSM_ERR_CUDA, "stream status: %s", cudaGetErrorString(err));
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    if (count != g_status_seen[dev]) {
+        const unsigned int fresh = count - g_status_seen[dev];
+        g_status_seen[dev] = count;
+        return fail(BSSM_ERR_TIMEOUT,
+                    "%u bounded wait(s) in a recurrence kernel gave up on device %d: the outputs of the calls "
+                    "since the last status check are wrong",
+                    fresh, dev);
+    }
+    bssm::g_last_error.clear();
+    return BSSM_OK;
+}
+
+extern "C" int bssm_debug_wait_probe(int limit, void *stream) {
+    using bssm::fail;
+    if (limit < 1 || limit > (1 << 16)) return fail(BSSM_ERR_INVALID, "wait probe: limit %d not in [1, 65536]", limit);
+    bssm::chain::wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit);
+    return bssm::check_launch("wait probe");
 }
 
 namespace bssm {

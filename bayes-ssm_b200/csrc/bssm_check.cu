@@ -82,3 +82,42 @@ extern "C" int bssm_check_values(const void *x, long n, int dtype, unsigned *fla
     }
     return fail(BSSM_ERR_UNSUPPORTED, "check_values: dtype %d", dtype);
 }
+
+// ---------------------------------------------------------------------------
+// FP32 FMA throughput probe: the denominator of the recurrence kernels' FP32
+// roofline, measured on the GPU at hand rather than taken from a datasheet.
+// Every thread runs kChains independent FMA chains (enough instructions in
+// flight to hide the FMA latency on every sub-partition); the result is
+// stored only under a condition the values never meet, so no FMA is dead.
+namespace bssm {
+namespace {
+constexpr int kProbeChains = 8;
+__global__ void __launch_bounds__(256) fma_probe_kernel(float *out, int iters, float a, float b) {
+    float x[kProbeChains];
+#pragma unroll
+    for (int c = 0; c < kProbeChains; ++c) x[c] = static_cast<float>(threadIdx.x + c) * 1e-3f;
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int c = 0; c < kProbeChains; ++c) x[c] = fmaf(x[c], a, b);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < kProbeChains; ++c) s += x[c];
+    if (s == 1234.5678f) out[blockIdx.x * blockDim.x + threadIdx.x] = s;
+}
+}  // namespace
+}  // namespace bssm
+
+extern "C" long bssm_debug_fma_probe_flops(int blocks, int iters) {
+    return 2L * blocks * 256 * bssm::kProbeChains * 8 * iters;
+}
+
+extern "C" int bssm_debug_fma_probe(float *out, int blocks, int iters, void *stream) {
+    using namespace bssm;
+    if (blocks < 1 || iters < 1 || out == nullptr) return fail(BSSM_ERR_INVALID, "fma probe: bad arguments");
+    // a * x + b with |a| < 1 stays bounded: no overflow, no denormal slow path
+    fma_probe_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(out, iters, 0.999f, 1e-3f);
+    return check_launch("fma probe");
+}

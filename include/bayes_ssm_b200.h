@@ -42,6 +42,7 @@ extern "C" {
 #define BSSM_ERR_ALIGNMENT 3   /* a vector-loaded pointer is misaligned */
 #define BSSM_ERR_CUDA 4        /* CUDA launch or runtime error */
 #define BSSM_ERR_WORKSPACE 5   /* workspace missing or too small */
+#define BSSM_ERR_TIMEOUT 6     /* a bounded in-kernel wait gave up (bssm_stream_status) */
 
 #define BSSM_F32 0
 #define BSSM_BF16 1
@@ -362,16 +363,44 @@ int bssm_envelope_epilogue_backward(const void *read, int read_dtype, const void
                                     long workspace_floats, void *stream);
 
 /*
- * Diagnostics (no counterpart in the reference).
+ * Device status (no counterpart in the reference: its kernels have no waits).
  *
  * The thread-per-chain kernels wait on shared-memory barriers for their own
  * asynchronous copies.  Every such wait is bounded: one that gives up is
- * counted in a device word and the kernel runs on (its results are then
- * wrong) instead of hanging the GPU.  This returns that count on the current
- * device since the library was loaded -- 0 in a healthy process.  It
- * synchronises the device.
+ * counted in a device word and the kernel runs on (its outputs are then
+ * wrong) instead of hanging the GPU.  bssm_stream_status synchronises
+ * `stream` and returns BSSM_ERR_TIMEOUT, with a message, when the current
+ * device's count has grown since the previous bssm_stream_status call on
+ * that device (each give-up is reported once), BSSM_ERR_CUDA for a CUDA
+ * error, else BSSM_OK.  The word is device-wide: a give-up on another stream
+ * of the same device is reported too.  The Python layer calls this after
+ * every forward and backward launch (outside CUDA graph capture) and raises.
+ */
+int bssm_stream_status(void *stream);
+
+/*
+ * Diagnostics (no counterpart in the reference).
+ *
+ * bssm_debug_wait_timeouts: the give-up count on the current device since
+ * the library was loaded -- 0 in a healthy process.  It synchronises the
+ * device.
+ * bssm_debug_wait_probe: launches one thread that waits, polling `limit`
+ * times (1..65536), on a barrier phase nothing completes, so its bounded wait
+ * gives up and is counted like a give-up inside a recurrence kernel; it
+ * tests the reporting path without faulting or hanging anything.
  */
 unsigned int bssm_debug_wait_timeouts(void);
+int bssm_debug_wait_probe(int limit, void *stream);
+
+/*
+ * FP32 FMA throughput probe (measurement only): `blocks` CTAs of 256 threads,
+ * each running 8 independent FMA chains for 8 * iters steps, enqueued on
+ * `stream`; bssm_debug_fma_probe_flops gives its flop count (FMA = 2), so
+ * flops / CUDA-event time is the GPU's achievable FP32 (non-tensor) rate at
+ * its current clocks.  out holds blocks * 256 floats; it is not written.
+ */
+int bssm_debug_fma_probe(float *out, int blocks, int iters, void *stream);
+long bssm_debug_fma_probe_flops(int blocks, int iters);
 
 /*
  * Kernel family that served the calling thread's last forward or backward

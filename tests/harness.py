@@ -80,7 +80,8 @@ def capi_forward(inp, *, chunks, floor=1e-6, fixed=False, replay_states=True):
                           None if fixed else p, None if fixed else r, m0, p0, out, mt, pt, bm, bc,
                           n, t, chunks, floor, torch.cuda.current_stream().cuda_stream,
                           replay_states=rs)
-    torch.cuda.synchronize()
+    # synchronises; raises if a bounded in-kernel wait gave up
+    _capi.stream_status(torch.cuda.current_stream().cuda_stream)
     return dict(y=out, MT=mt, PT=pt, bm=bm, bc=bc, rs=rs)
 
 
@@ -105,7 +106,7 @@ def capi_backward(inp, fwd, gy, gmt, gpt, *, chunks, floor=1e-6, fixed=False, ne
                            None, fwd["bm"], fwd["bc"], cuda(gy), cuda(gmt), cuda(gpt), gk, gv, gq,
                            gd, gp, gr, gm0, gc0, ws, nbytes, n, t, chunks, floor,
                            torch.cuda.current_stream().cuda_stream, replay_states=rs)
-    torch.cuda.synchronize()
+    _capi.stream_status(torch.cuda.current_stream().cuda_stream)
     return dict(k=gk, v=gv, q=gq, a=gd, p=gp, r=gr, M0=gm0, P0=gc0)
 
 

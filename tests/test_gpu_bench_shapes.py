@@ -1,0 +1,160 @@
+"""GPU parity at the benchmarked shapes, vs the FP64 oracle on sampled chains.
+
+The timed workloads run the default dispatch at sizes the full oracle cannot
+check in seconds, so each case runs the whole launch on the GPU and checks a
+seeded sample of chains spread over the first, middle and last CTAs (and
+random ones) against the oracle:
+
+* config 3 (the headline): 16,384 chains x T=512, D8 M8, chunk 64, BF16
+  keys/values/queries, FP32 dynamics, full dynamics gradients of a
+  readout-only loss -- through the C ABI with the replay buffer, exactly as
+  ``bench.py`` times it, and through the public ``bayesian_layer`` API;
+* config 4: 65,536 chains x T=2048, D2 M8, chunk 64, BF16;
+* FP8 (e4m3) projection inputs through the public API.
+
+Tolerances are the north star's FP32 bar (relative L2 <= 1e-5, cosine >=
+0.99999); BF16 key/value/query gradients are rounded to BF16 by definition
+and use relative L2 <= 4e-3.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from harness import assert_parity, io_code
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+FLOOR = 1e-6
+
+
+def _inputs(n, t, d, m, seed, dtype=torch.bfloat16):
+    """The bench's distributions, generated on the GPU (seeded)."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    dev = "cuda"
+    k = F.normalize(torch.randn(n, t, d, generator=g, device=dev), dim=-1).to(dtype)
+    q = F.normalize(torch.randn(n, t, d, generator=g, device=dev), dim=-1).to(dtype)
+    v = (torch.randn(n, t, m, generator=g, device=dev) / math.sqrt(m)).to(dtype)
+    a = torch.sigmoid(2.0 + torch.randn(n, t, d, generator=g, device=dev))
+    p = F.softplus(-4.0 + torch.randn(n, t, generator=g, device=dev))
+    r = F.softplus(torch.randn(n, t, generator=g, device=dev)) + 1e-4
+    gy = torch.randn(n, t, m, generator=g, device=dev) / math.sqrt(m)
+    return dict(k=k, v=v, q=q, a=a, p=p, r=r, gy=gy)
+
+
+def _sample(n, seed=0, count=64):
+    """Chains of the first, middle and last 128-chain CTAs, plus random ones."""
+    rng = np.random.default_rng(seed)
+    fixed = [0, 1, 31, 32, 127, n // 2, n // 2 + 33, n - 128, n - 33, n - 1]
+    rest = rng.choice(n, size=count - len(fixed), replace=False)
+    return torch.tensor(sorted(set(fixed) | set(int(x) for x in rest)), dtype=torch.long)
+
+
+def _np(x, idx):
+    return x.index_select(0, idx.to(x.device)).double().cpu().numpy()
+
+
+def _check_sample(inp, idx, y, grads, *, what):
+    names = ("k", "v", "q", "a", "p", "r")
+    arrs = [_np(inp[x], idx) for x in names]
+    ry, _, _ = oracle.forward(*arrs, None, None, floor=FLOOR)
+    assert_parity(_np(y, idx), ry, what=f"{what}: y")
+    rg = oracle.backward(*arrs, None, None, _np(inp["gy"], idx), None, None, floor=FLOOR)
+    low = inp["k"].dtype != torch.float32
+    for x in names:
+        assert_parity(_np(grads[x], idx), rg[x], rel=4e-3 if (low and x in "kvq") else 1e-5,
+                      what=f"{what}: grad {x}")
+
+
+def _capi_step(inp, chunk):
+    """One bench step: forward with replay states, backward consuming them."""
+    from bayes_ssm import _capi
+    k = inp["k"]
+    n, t, d = k.shape
+    m = inp["v"].shape[-1]
+    nb = (t + chunk - 1) // chunk
+    f32 = dict(device="cuda", dtype=torch.float32)
+    out = torch.empty(n, t, m, **f32)
+    mt, pt = torch.empty(n, d, m, **f32), torch.empty(n, d, d, **f32)
+    bm, bc = torch.empty(n, nb + 1, d, m, **f32), torch.empty(n, nb + 1, d, d, **f32)
+    rs = torch.empty(max(_capi.replay_states_bytes(d, m, n, t, chunk) // 4, 1), **f32)
+    sp = torch.cuda.current_stream().cuda_stream
+    io = io_code(k.dtype)
+    _capi.forward_chunked(d, m, io, False, k, inp["v"], inp["q"], inp["a"], inp["p"], inp["r"], None, None,
+                          out, mt, pt, bm, bc, n, t, chunk, FLOOR, sp, replay_states=rs)
+    _capi.stream_status(sp)
+    assert _capi.last_family() == "chain"
+    g = dict(k=torch.empty_like(k), v=torch.empty_like(inp["v"]), q=torch.empty_like(inp["q"]),
+             a=torch.empty(n, t, d, **f32), p=torch.empty(n, t, **f32), r=torch.empty(n, t, **f32))
+    _capi.backward_chunked(d, m, io, False, True, False, k, inp["v"], inp["q"], inp["a"], inp["p"], inp["r"],
+                           None, None, bm, bc, inp["gy"], None, None, g["k"], g["v"], g["q"], g["a"], g["p"],
+                           g["r"], None, None, None, 0, n, t, chunk, FLOOR, sp, replay_states=rs)
+    _capi.stream_status(sp)
+    assert _capi.last_family() == "chain"
+    return out, g
+
+
+@pytest.fixture(autouse=True)
+def default_dispatch(monkeypatch):
+    monkeypatch.delenv("BSSM_KERNELS", raising=False)
+
+
+def test_config3_capi_sampled_chains():
+    """The exact launch bench.py times: 16,384 chains, T512, chunk 64, BF16."""
+    inp = _inputs(16384, 512, 8, 8, seed=3)
+    y, g = _capi_step(inp, 64)
+    _check_sample(inp, _sample(16384, seed=3), y, g, what="config 3 (C ABI)")
+
+
+def test_config3_api_sampled_chains():
+    """The same workload through bayesian_layer + autograd (B256 x H64)."""
+    import bayes_ssm
+    inp = _inputs(16384, 512, 8, 8, seed=4)
+    leaves = {x: inp[x].clone().requires_grad_() for x in ("k", "v", "q", "a", "p", "r")}
+    y, _, _ = bayes_ssm.bayesian_layer(leaves["k"], leaves["v"], leaves["q"], transition_diagonals=leaves["a"],
+                                       process_variances=leaves["p"], observation_variances=leaves["r"],
+                                       chunk_length=64, optimized=True)
+    y.backward(inp["gy"])
+    grads = {x: leaves[x].grad for x in leaves}
+    assert grads["k"].dtype == torch.bfloat16
+    _check_sample(inp, _sample(16384, seed=4), y.detach(), grads, what="config 3 (API)")
+
+
+def test_config4_capi_sampled_chains():
+    """Config 4: D2 M8, 65,536 chains x T2048, chunk 64, BF16."""
+    inp = _inputs(65536, 2048, 2, 8, seed=5)
+    y, g = _capi_step(inp, 64)
+    _check_sample(inp, _sample(65536, seed=5, count=32), y, g, what="config 4 (C ABI)")
+
+
+@pytest.mark.parametrize("fp8", ("float8_e4m3fn", "float8_e5m2"))
+def test_fp8_projection_inputs(fp8):
+    """FP8 keys/values/queries are promoted to FP32 (bayesian_layer.py:816-827):
+    outputs equal the FP32 path on the same values, and the FP8 leaves get the
+    FP32 gradients rounded to FP8; both match the oracle."""
+    import bayes_ssm
+    dt = getattr(torch, fp8)
+    inp = _inputs(4096, 128, 8, 8, seed=6, dtype=torch.float32)
+    for x in ("k", "v", "q"):
+        inp[x] = inp[x].to(dt)
+    lo = {x: inp[x].clone().requires_grad_() for x in ("k", "v", "q", "a", "p", "r")}
+    hi = {x: (inp[x].float() if x in "kvq" else inp[x]).clone().requires_grad_() for x in lo}
+    outs = []
+    for leaves in (lo, hi):
+        y, _, _ = bayes_ssm.bayesian_layer(leaves["k"], leaves["v"], leaves["q"], transition_diagonals=leaves["a"],
+                                           process_variances=leaves["p"], observation_variances=leaves["r"],
+                                           chunk_length=64, optimized=True)
+        y.backward(inp["gy"])
+        outs.append(y.detach())
+    assert torch.equal(outs[0], outs[1])
+    for x in lo:
+        want = hi[x].grad.to(dt) if x in "kvq" else hi[x].grad
+        assert lo[x].grad.dtype == want.dtype
+        assert torch.equal(lo[x].grad.float(), want.float()), x
+    ref = {**inp, **{x: inp[x].float() for x in "kvq"}}
+    _check_sample(ref, _sample(4096, seed=6), outs[1], {x: hi[x].grad for x in hi}, what=f"{fp8} (API)")

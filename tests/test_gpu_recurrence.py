@@ -289,6 +289,7 @@ def test_workspace_too_small_is_rejected():
 
 
 def test_zz_no_bounded_wait_gave_up():
-    """Every barrier wait inside the kernels of this module's runs completed."""
+    """Every barrier wait inside the kernels of this module's runs completed
+    (a give-up not yet reported by an earlier status check raises here)."""
     from bayes_ssm import _capi
-    assert _capi.wait_timeouts() == 0
+    _capi.stream_status(torch.cuda.current_stream().cuda_stream)
