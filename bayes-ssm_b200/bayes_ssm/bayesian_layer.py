@@ -105,18 +105,67 @@ def _device_flags(tensors) -> Optional[list]:
     return _capi.check_values([x.detach() for x in tensors])
 
 
-def _check_finite_many(pairs) -> None:
-    """_check_finite on each (tensor, name) in order: the first failure raises."""
-    pairs = [(x, name) for x, name in pairs if not _skip_host_checks(x)]
-    flags = _device_flags([x for x, _ in pairs]) if pairs else None
-    if flags is None:
-        for x, name in pairs:
+class _DeviceChecks:
+    """The value checks of one ``bayesian_layer`` call, raised in the
+    reference's order (bayesian_layer.py:798-985) but run together: checks of
+    contiguous CUDA tensors are queued and flushed as one pass per tensor with
+    a single read-back.  A flush happens before any check that must run on
+    the host and when an exception leaves the ``with`` block (so a queued
+    failure that precedes a host-side error is the one raised); otherwise the
+    caller flushes -- on the kernel path right after the forward kernel is
+    enqueued, so one read-back covers the checks and the kernel (whose outputs
+    are discarded if a check fails)."""
+
+    def __init__(self) -> None:
+        self.items = []
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, exc_type, exc, tb) -> bool:
+        if exc_type is not None:
+            self.flush()
+        return False
+
+    def finite(self, x: Tensor, name: str) -> None:
+        self._add(x, name, 0)
+
+    def variance(self, x: Tensor, name: str, *, strictly_positive: bool) -> None:
+        self._add(x, name, 2 if strictly_positive else 1)
+
+    def _add(self, x: Tensor, name: str, kind: int) -> None:
+        if _skip_host_checks(x):
+            return
+        if not (x.is_cuda and x.dtype in _DEVICE_CHECK_DTYPES and x.is_contiguous()):
+            self.flush()
+            self._run_now(x, name, kind)
+            return
+        self.items.append((x, name, kind))
+
+    @staticmethod
+    def _run_now(x: Tensor, name: str, kind: int) -> None:
+        if kind == 0:
             _check_finite(x, name)
-        return
-    from ._capi import CHECK_NONFINITE
-    for (x, name), f in zip(pairs, flags):
-        if f & CHECK_NONFINITE:
-            raise ValueError(f"{name} must contain only finite values")
+        else:
+            _validate_variance(x, name, strictly_positive=kind == 2)
+
+    def flush(self) -> None:
+        items, self.items = self.items, []
+        if not items:
+            return
+        flags = _device_flags([x for x, _, _ in items])
+        if flags is None:
+            for x, name, kind in items:
+                self._run_now(x, name, kind)
+            return
+        from ._capi import CHECK_NEGATIVE, CHECK_NONFINITE, CHECK_NOT_POSITIVE
+        for (x, name, kind), f in zip(items, flags):
+            if f & CHECK_NONFINITE:
+                raise ValueError(f"{name} must contain only finite values")
+            if kind == 2 and f & CHECK_NOT_POSITIVE:
+                raise ValueError(f"{name} must be strictly positive")
+            if kind == 1 and f & CHECK_NEGATIVE:
+                raise ValueError(f"{name} must be nonnegative")
 
 
 def _check_finite(x: Tensor, name: str) -> None:
@@ -197,9 +246,19 @@ def _dense_recurrence(keys: Tensor, values: Tensor, queries: Tensor, transitions
     return torch.stack(outputs, dim=-2), mean, covariance
 
 
+def _default_mean(mean, batch_shape, d, m, device, dtype):
+    return torch.zeros(*batch_shape, d, m, device=device, dtype=dtype) if mean is None else mean
+
+
+def _default_covariance(covariance, batch_shape, d, device, dtype):
+    if covariance is not None:
+        return covariance
+    return torch.eye(d, device=device, dtype=dtype).expand(*batch_shape, d, d).clone()
+
+
 def _fused_path(keys, values, queries, diagonal, process_variances, observation_variances,
                 mean, covariance, *, batch_shape, t, d, m, chunk_length, denominator_floor,
-                fixed_dynamics, kernel_dtype):
+                fixed_dynamics, kernel_dtype, pending_checks=None):
     """Flatten the batch to chains, run the CUDA kernels, restore the shape."""
     from .fused_cuda import fused_diagonal_bayesian
 
@@ -223,7 +282,7 @@ def _fused_path(keys, values, queries, diagonal, process_variances, observation_
         a = torch.ones((), device=dev, dtype=torch.float32).expand(n, t, d)
     y, mt, pt = fused_diagonal_bayesian(k, v, q, a, p, r, m0, c0, chunk_length=chunk_length,
                                         denominator_floor=denominator_floor,
-                                        fixed_dynamics=fixed_dynamics)
+                                        fixed_dynamics=fixed_dynamics, _pending_checks=pending_checks)
     return (y.reshape(*batch_shape, t, m), mt.reshape(*batch_shape, d, m),
             pt.reshape(*batch_shape, d, d))
 
@@ -299,147 +358,151 @@ def bayesian_layer(
         keys = keys.to(dtype)
         values = values.to(dtype)
         queries = queries.to(dtype)
-    _check_finite_many(((keys, "keys"), (values, "values"), (queries, "queries")))
-    if (rotation_radii is None) != (rotation_angles is None):
-        raise ValueError("rotation_radii and rotation_angles must be supplied together")
-    if transitions is not None and transition_diagonals is not None:
-        raise ValueError("pass transitions or transition_diagonals, not both")
-    if (rotation_radii is not None or rotation_angles is not None) and (
-        transitions is not None or transition_diagonals is not None
-    ):
-        raise ValueError("rotation dynamics are mutually exclusive with transitions and transition_diagonals")
-    if not isinstance(replay_ssm, bool):
-        raise TypeError("replay_ssm must be a bool")
-    if not isinstance(fixed_dynamics, bool):
-        raise TypeError("fixed_dynamics must be a bool")
+    with _DeviceChecks() as chk:
+        for x, name in ((keys, "keys"), (values, "values"), (queries, "queries")):
+            chk.finite(x, name)
+        if (rotation_radii is None) != (rotation_angles is None):
+            raise ValueError("rotation_radii and rotation_angles must be supplied together")
+        if transitions is not None and transition_diagonals is not None:
+            raise ValueError("pass transitions or transition_diagonals, not both")
+        if (rotation_radii is not None or rotation_angles is not None) and (
+            transitions is not None or transition_diagonals is not None
+        ):
+            raise ValueError("rotation dynamics are mutually exclusive with transitions and transition_diagonals")
+        if not isinstance(replay_ssm, bool):
+            raise TypeError("replay_ssm must be a bool")
+        if not isinstance(fixed_dynamics, bool):
+            raise TypeError("fixed_dynamics must be a bool")
 
-    diagonal = None
-    identity_dynamics = False
-    rotation = False
-    if rotation_radii is not None:
-        if d % 2:
-            raise ValueError("rotational dynamics require an even key dimension")
-        checked = []
-        for name, value in (("rotation_radii", rotation_radii), ("rotation_angles", rotation_angles)):
-            if not isinstance(value, Tensor) or value.ndim < 2:
-                raise ValueError(f"{name} must have shape [..., T={t}, D/2={d // 2}]")
-            if not value.is_floating_point():
-                raise TypeError(f"{name} must have a floating-point dtype")
-            if value.shape[-2:] != (t, d // 2):
-                raise ValueError(f"{name} must end in {(t, d // 2)}, got {tuple(value.shape)}")
-            if not _broadcastable(value.shape[:-2], batch_shape):
-                raise ValueError(f"{name} batch dimensions are not broadcastable to input batch")
-            value = value.to(device=device, dtype=dtype)
-            _check_finite(value, name)
-            checked.append(value)
-        rotation_radii, rotation_angles = checked
-        rotation = True
-    elif transition_diagonals is not None:
-        if not isinstance(transition_diagonals, Tensor) or transition_diagonals.ndim < 2:
-            raise ValueError(f"transition_diagonals must have shape [..., T={t}, D={d}]")
-        if not transition_diagonals.is_floating_point():
-            raise TypeError("transition_diagonals must have a floating-point dtype")
-        transition_diagonals = transition_diagonals.to(device=device, dtype=dtype)
-        if transition_diagonals.shape[-2:] != (t, d):
-            raise ValueError(f"transition_diagonals must end in {(t, d)}, got {tuple(transition_diagonals.shape)}")
-        if not _broadcastable(transition_diagonals.shape[:-2], batch_shape):
-            raise ValueError("transition_diagonals batch dimensions are not broadcastable to the input batch")
-        _check_finite(transition_diagonals, "transition_diagonals")
-        diagonal = transition_diagonals
-    elif transitions is None:
-        identity_dynamics = True
-    else:
-        if not isinstance(transitions, Tensor) or transitions.ndim < 3:
-            raise ValueError(f"transitions must have shape [..., T={t}, D={d}, D={d}]")
-        if not transitions.is_floating_point():
-            raise TypeError("transitions must have a floating-point dtype")
-        transitions = transitions.to(device=device, dtype=dtype)
-        if transitions.shape[-3:] != (t, d, d):
-            raise ValueError(f"transitions must end in {(t, d, d)}, got {tuple(transitions.shape)}")
-        if not _broadcastable(transitions.shape[:-3], batch_shape):
-            raise ValueError("transitions batch dimensions are not broadcastable to the input batch")
-        _check_finite(transitions, "transitions")
-
-    if rotation:
-        if process_covariances is not None:
-            raise ValueError("rotational dynamics require per-pair process_variances, not process_covariances")
-        if process_variances is None:
-            process_variances = torch.zeros(*batch_shape, t, d // 2, device=device, dtype=dtype)
+        diagonal = None
+        identity_dynamics = False
+        rotation = False
+        if rotation_radii is not None:
+            if d % 2:
+                raise ValueError("rotational dynamics require an even key dimension")
+            checked = []
+            for name, value in (("rotation_radii", rotation_radii), ("rotation_angles", rotation_angles)):
+                if not isinstance(value, Tensor) or value.ndim < 2:
+                    raise ValueError(f"{name} must have shape [..., T={t}, D/2={d // 2}]")
+                if not value.is_floating_point():
+                    raise TypeError(f"{name} must have a floating-point dtype")
+                if value.shape[-2:] != (t, d // 2):
+                    raise ValueError(f"{name} must end in {(t, d // 2)}, got {tuple(value.shape)}")
+                if not _broadcastable(value.shape[:-2], batch_shape):
+                    raise ValueError(f"{name} batch dimensions are not broadcastable to input batch")
+                value = value.to(device=device, dtype=dtype)
+                chk.finite(value, name)
+                checked.append(value)
+            rotation_radii, rotation_angles = checked
+            rotation = True
+        elif transition_diagonals is not None:
+            if not isinstance(transition_diagonals, Tensor) or transition_diagonals.ndim < 2:
+                raise ValueError(f"transition_diagonals must have shape [..., T={t}, D={d}]")
+            if not transition_diagonals.is_floating_point():
+                raise TypeError("transition_diagonals must have a floating-point dtype")
+            transition_diagonals = transition_diagonals.to(device=device, dtype=dtype)
+            if transition_diagonals.shape[-2:] != (t, d):
+                raise ValueError(f"transition_diagonals must end in {(t, d)}, got {tuple(transition_diagonals.shape)}")
+            if not _broadcastable(transition_diagonals.shape[:-2], batch_shape):
+                raise ValueError("transition_diagonals batch dimensions are not broadcastable to the input batch")
+            chk.finite(transition_diagonals, "transition_diagonals")
+            diagonal = transition_diagonals
+        elif transitions is None:
+            identity_dynamics = True
         else:
-            process_variances = _as_tensor(process_variances, device=device, dtype=dtype,
-                                           name="process_variances")
-            if process_variances.ndim == 0:
-                process_variances = process_variances.expand(*batch_shape, t, d // 2)
-            elif process_variances.shape[-2:] == (t, d // 2) and _broadcastable(
-                process_variances.shape[:-2], batch_shape
-            ):
-                process_variances = process_variances.expand(*batch_shape, t, d // 2)
+            if not isinstance(transitions, Tensor) or transitions.ndim < 3:
+                raise ValueError(f"transitions must have shape [..., T={t}, D={d}, D={d}]")
+            if not transitions.is_floating_point():
+                raise TypeError("transitions must have a floating-point dtype")
+            transitions = transitions.to(device=device, dtype=dtype)
+            if transitions.shape[-3:] != (t, d, d):
+                raise ValueError(f"transitions must end in {(t, d, d)}, got {tuple(transitions.shape)}")
+            if not _broadcastable(transitions.shape[:-3], batch_shape):
+                raise ValueError("transitions batch dimensions are not broadcastable to the input batch")
+            chk.finite(transitions, "transitions")
+
+        if rotation:
+            if process_covariances is not None:
+                raise ValueError("rotational dynamics require per-pair process_variances, not process_covariances")
+            if process_variances is None:
+                process_variances = torch.zeros(*batch_shape, t, d // 2, device=device, dtype=dtype)
             else:
-                raise ValueError(f"rotational process_variances must be scalar or end in {(t, d // 2)}")
-            _validate_variance(process_variances, "process_variances", strictly_positive=False)
-    elif process_covariances is not None and process_variances is not None:
-        raise ValueError("pass process_covariances or process_variances, not both")
-    elif process_covariances is not None:
-        if not isinstance(process_covariances, Tensor) or process_covariances.ndim < 3:
-            raise ValueError(f"process_covariances must have shape [..., T={t}, D={d}, D={d}]")
-        if not process_covariances.is_floating_point():
-            raise TypeError("process_covariances must have a floating-point dtype")
-        process_covariances = process_covariances.to(device=device, dtype=dtype)
-        if process_covariances.shape[-3:] != (t, d, d):
-            raise ValueError(f"process_covariances must end in {(t, d, d)}, got {tuple(process_covariances.shape)}")
-        if not _broadcastable(process_covariances.shape[:-3], batch_shape):
-            raise ValueError("process_covariances batch dimensions are not broadcastable to the input batch")
-        _validate_covariance(process_covariances, "process_covariances", d)
-    else:
-        if process_variances is None:
-            process_variances = 0.0
-        process_variances = _as_time_tensor(process_variances, t, batch_shape, "process_variances",
-                                            device=device, dtype=dtype)
-        _validate_variance(process_variances, "process_variances", strictly_positive=False)
-    if observation_variances is None:
-        observation_variances = 1.0
-    observation_variances = _as_time_tensor(observation_variances, t, batch_shape,
-                                            "observation_variances", device=device, dtype=dtype)
-    _validate_variance(observation_variances, "observation_variances", strictly_positive=True)
+                process_variances = _as_tensor(process_variances, device=device, dtype=dtype,
+                                               name="process_variances")
+                if process_variances.ndim == 0:
+                    process_variances = process_variances.expand(*batch_shape, t, d // 2)
+                elif process_variances.shape[-2:] == (t, d // 2) and _broadcastable(
+                    process_variances.shape[:-2], batch_shape
+                ):
+                    process_variances = process_variances.expand(*batch_shape, t, d // 2)
+                else:
+                    raise ValueError(f"rotational process_variances must be scalar or end in {(t, d // 2)}")
+                chk.variance(process_variances, "process_variances", strictly_positive=False)
+        elif process_covariances is not None and process_variances is not None:
+            raise ValueError("pass process_covariances or process_variances, not both")
+        elif process_covariances is not None:
+            if not isinstance(process_covariances, Tensor) or process_covariances.ndim < 3:
+                raise ValueError(f"process_covariances must have shape [..., T={t}, D={d}, D={d}]")
+            if not process_covariances.is_floating_point():
+                raise TypeError("process_covariances must have a floating-point dtype")
+            process_covariances = process_covariances.to(device=device, dtype=dtype)
+            if process_covariances.shape[-3:] != (t, d, d):
+                raise ValueError(f"process_covariances must end in {(t, d, d)}, got {tuple(process_covariances.shape)}")
+            if not _broadcastable(process_covariances.shape[:-3], batch_shape):
+                raise ValueError("process_covariances batch dimensions are not broadcastable to the input batch")
+            chk.flush()
+            _validate_covariance(process_covariances, "process_covariances", d)
+        else:
+            if process_variances is None:
+                process_variances = 0.0
+            process_variances = _as_time_tensor(process_variances, t, batch_shape, "process_variances",
+                                                device=device, dtype=dtype)
+            chk.variance(process_variances, "process_variances", strictly_positive=False)
+        if observation_variances is None:
+            observation_variances = 1.0
+        observation_variances = _as_time_tensor(observation_variances, t, batch_shape,
+                                                "observation_variances", device=device, dtype=dtype)
+        chk.variance(observation_variances, "observation_variances", strictly_positive=True)
 
-    user_mean = initial_mean is not None
-    user_cov = initial_covariance is not None
-    if initial_mean is None:
-        mean = torch.zeros(*batch_shape, d, m, device=device, dtype=dtype)
-    else:
-        if not isinstance(initial_mean, Tensor) or initial_mean.ndim < 2:
-            raise ValueError(f"initial_mean must have shape [..., D={d}, m={m}]")
-        if not initial_mean.is_floating_point():
-            raise TypeError("initial_mean must have a floating-point dtype")
-        mean = initial_mean.to(device=device, dtype=dtype)
-        if mean.shape[-2:] != (d, m) or not _broadcastable(mean.shape[:-2], batch_shape):
-            raise ValueError("initial_mean has incompatible dimensions or batch shape")
-        _check_finite(mean, "initial_mean")
-        mean = mean.expand(*batch_shape, d, m)
-    if initial_covariance is None:
-        covariance = torch.eye(d, device=device, dtype=dtype).expand(*batch_shape, d, d).clone()
-    else:
-        if not isinstance(initial_covariance, Tensor) or initial_covariance.ndim < 2:
-            raise ValueError(f"initial_covariance must have shape [..., D={d}, D={d}]")
-        if not initial_covariance.is_floating_point():
-            raise TypeError("initial_covariance must have a floating-point dtype")
-        covariance = initial_covariance.to(device=device, dtype=dtype)
-        if not _broadcastable(covariance.shape[:-2], batch_shape):
-            raise ValueError("initial_covariance batch dimensions are not broadcastable to the input batch")
-        _validate_covariance(covariance, "initial_covariance", d)
-        covariance = covariance.expand(*batch_shape, d, d)
+        user_mean = initial_mean is not None
+        user_cov = initial_covariance is not None
+        mean = covariance = None  # defaults (zeros, identity) are built only where used
+        if initial_mean is not None:
+            if not isinstance(initial_mean, Tensor) or initial_mean.ndim < 2:
+                raise ValueError(f"initial_mean must have shape [..., D={d}, m={m}]")
+            if not initial_mean.is_floating_point():
+                raise TypeError("initial_mean must have a floating-point dtype")
+            mean = initial_mean.to(device=device, dtype=dtype)
+            if mean.shape[-2:] != (d, m) or not _broadcastable(mean.shape[:-2], batch_shape):
+                raise ValueError("initial_mean has incompatible dimensions or batch shape")
+            chk.finite(mean, "initial_mean")
+            mean = mean.expand(*batch_shape, d, m)
+        if initial_covariance is not None:
+            if not isinstance(initial_covariance, Tensor) or initial_covariance.ndim < 2:
+                raise ValueError(f"initial_covariance must have shape [..., D={d}, D={d}]")
+            if not initial_covariance.is_floating_point():
+                raise TypeError("initial_covariance must have a floating-point dtype")
+            covariance = initial_covariance.to(device=device, dtype=dtype)
+            if not _broadcastable(covariance.shape[:-2], batch_shape):
+                raise ValueError("initial_covariance batch dimensions are not broadcastable to the input batch")
+            chk.flush()
+            _validate_covariance(covariance, "initial_covariance", d)
+            covariance = covariance.expand(*batch_shape, d, d)
 
-    if not isinstance(denominator_floor, Real) or not math.isfinite(float(denominator_floor)):
-        raise ValueError("denominator_floor must be finite")
-    if denominator_floor <= 0:
-        raise ValueError("denominator_floor must be positive")
-    if chunk_length is not None and (not isinstance(chunk_length, int) or isinstance(chunk_length, bool)
-                                     or chunk_length <= 0):
-        raise ValueError("chunk_length must be a positive integer or None")
-    if t == 0:
-        return torch.empty(*batch_shape, 0, m, device=device, dtype=dtype), mean, covariance
-    if chunk_length is None:
-        chunk_length = t
+        if not isinstance(denominator_floor, Real) or not math.isfinite(float(denominator_floor)):
+            raise ValueError("denominator_floor must be finite")
+        if denominator_floor <= 0:
+            raise ValueError("denominator_floor must be positive")
+        if chunk_length is not None and (not isinstance(chunk_length, int) or isinstance(chunk_length, bool)
+                                         or chunk_length <= 0):
+            raise ValueError("chunk_length must be a positive integer or None")
+        if t == 0:
+            chk.flush()
+            return (torch.empty(*batch_shape, 0, m, device=device, dtype=dtype),
+                    _default_mean(mean, batch_shape, d, m, device, dtype),
+                    _default_covariance(covariance, batch_shape, d, device, dtype))
+        if chunk_length is None:
+            chunk_length = t
 
     from .fused_cuda import kernel_supports
 
@@ -460,8 +523,11 @@ def bayesian_layer(
             mean if user_mean else None, covariance if user_cov else None,
             batch_shape=batch_shape, t=t, d=d, m=m, chunk_length=chunk_length,
             denominator_floor=float(denominator_floor), fixed_dynamics=fixed_dynamics,
-            kernel_dtype=kernel_dtype)
+            kernel_dtype=kernel_dtype, pending_checks=chk)
 
+    chk.flush()
+    mean = _default_mean(mean, batch_shape, d, m, device, dtype)
+    covariance = _default_covariance(covariance, batch_shape, d, device, dtype)
     # Dense PyTorch recurrence (reference semantics).
     if rotation:
         radius = rotation_radii.clamp_min(torch.finfo(dtype).tiny)

@@ -65,7 +65,7 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, keys, values, queries, decay, process, observation, initial_mean,
                 initial_covariance, chunk_length: int, denominator_floor: float,
-                fixed_dynamics: bool):
+                fixed_dynamics: bool, pending_checks=None):
         n, t, d = keys.shape
         m = values.shape[-1]
         dev = keys.device
@@ -93,6 +93,11 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
                                   initial_mean, initial_covariance, out, mean_final, cov_final,
                                   bmean, bcov, n, t, int(chunk_length), denominator_floor,
                                   _stream(dev), replay_states=rs)
+            if pending_checks is not None:
+                # the caller's input checks, read back after the kernel was
+                # enqueued: one synchronisation covers both; a failing check
+                # raises and the outputs are dropped
+                pending_checks.flush()
             _status(dev)
         ctx.save_for_backward(keys, values, queries, decay, process, observation, bmean, bcov, rs)
         ctx.chunk_length = int(chunk_length)
@@ -135,7 +140,7 @@ class _ChunkedBayesianFunction(torch.autograd.Function):
             _status(dev)
         return (gk if needs[0] else None, gv if needs[1] else None, gq if needs[2] else None,
                 gd if needs[3] else None, gp if needs[4] else None, gr if needs[5] else None,
-                gm0 if needs[6] else None, gc0 if needs[7] else None, None, None, None)
+                gm0 if needs[6] else None, gc0 if needs[7] else None, None, None, None, None)
 
 
 def _aligned(x: Tensor) -> Tensor:
@@ -160,6 +165,7 @@ def fused_diagonal_bayesian(
     chunk_length: int,
     denominator_floor: float,
     fixed_dynamics: bool = False,
+    _pending_checks=None,
 ) -> tuple[Tensor, Tensor, Tensor]:
     """Run the chunked CUDA recurrence on ``[N,T,*]`` inputs.
 
@@ -211,7 +217,7 @@ def fused_diagonal_bayesian(
     queries = _aligned(queries.contiguous())
     return _ChunkedBayesianFunction.apply(
         keys, values, queries, decay, process, observation, initial_mean, initial_covariance,
-        int(chunk_length), float(denominator_floor), bool(fixed_dynamics))
+        int(chunk_length), float(denominator_floor), bool(fixed_dynamics), _pending_checks)
 
 
 __all__ = ["fused_diagonal_bayesian", "kernel_supports", "SUPPORTED_DIMS"]

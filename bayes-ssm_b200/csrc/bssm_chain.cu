@@ -52,6 +52,29 @@ constexpr int kSplitWarps = 8;  // two warps per chain group
 constexpr int kSplitThreads = 32 * kSplitWarps;
 constexpr int kSmemMax = 227 * 1024;
 
+// Unroll factors of the per-token loops of the two-warp (split) kernels.
+// Measured at config 3 (16,384 chains, T 512, one B200): unrolling the
+// backward's two replay loops fully took it from 0.867 to 0.824 ms; fully
+// unrolled adjoint loops were slower (0.965 ms; 1.18 ms together with the
+// replays), 2-way neutral; the forward's loops were neutral at 2 and slower
+// at 4 (0.432 -> 0.472 ms).
+#ifndef BSSM_SPLIT_UNROLL_FWD
+#define BSSM_SPLIT_UNROLL_FWD 1
+#endif
+#ifndef BSSM_SPLIT_UNROLL_REPLAY
+#define BSSM_SPLIT_UNROLL_REPLAY 4
+#endif
+#ifndef BSSM_SPLIT_UNROLL_COV
+#define BSSM_SPLIT_UNROLL_COV 1
+#endif
+#ifndef BSSM_SPLIT_UNROLL_MEAN
+#define BSSM_SPLIT_UNROLL_MEAN 1
+#endif
+constexpr int kUnrollFwd = BSSM_SPLIT_UNROLL_FWD;        // forward_split, both warps
+constexpr int kUnrollReplay = BSSM_SPLIT_UNROLL_REPLAY;  // backward_split replays
+constexpr int kUnrollCov = BSSM_SPLIT_UNROLL_COV;        // backward_split covariance adjoint
+constexpr int kUnrollMean = BSSM_SPLIT_UNROLL_MEAN;      // backward_split mean adjoint
+
 constexpr int al128(int x) { return (x + 127) / 128 * 128; }
 constexpr int al1024(int x) { return (x + 1023) / 1024 * 1024; }
 
@@ -867,7 +890,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             __syncwarp();
             float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f);
             rd.noise(p4, r4);
-#pragma unroll 1
+#pragma unroll kUnrollFwd
             for (int tau = 0; tau < kS; ++tau) {
                 float k[D], a[D], u[D], beta, s;
                 rd.keys(tau, k);
@@ -947,7 +970,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 __syncwarp();
             }
             const float4 b4 = reinterpret_cast<const float4 *>(gb + G::gB)[lane];
-#pragma unroll 1
+#pragma unroll kUnrollFwd
             for (int tau = 0; tau < kS; ++tau) {
                 float k[D], a[D], v[M], qv[D], u[D], e[M];
                 rd.keys(tau, k);
@@ -1755,7 +1778,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 nxt.advance();
             }
             // replay: pre-step covariance per token, updated with the saved gains
-#pragma unroll 1
+#pragma unroll kUnrollReplay
             for (int tau = 0; tau < kS; ++tau) {
                 float a[D], u[D];
                 rd.decay(tau, a);
@@ -1766,7 +1789,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             tmem::wait_st();
             // reverse: covariance adjoint
             float4 gp4 = make_float4(0.f, 0.f, 0.f, 0.f), gr4 = gp4;
-#pragma unroll 1
+#pragma unroll kUnrollCov
             for (int tau = kS - 1; tau >= 0; --tau, ++ntok) {
                 const int xs = static_cast<int>(ntok % kXSlots);
                 mbar_wait(xfull + xs, static_cast<uint32_t>((ntok / kXSlots) & 1));
@@ -1910,7 +1933,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             cp_async_commit();
             // replay: pre-step mean and innovation; gq = M' gy into the
             // token's (dead) value slot
-#pragma unroll 1
+#pragma unroll kUnrollReplay
             for (int tau = 0; tau < kS; ++tau) {
                 float k[D], a[D], v[M], u[D], e[M];
                 rd.keys(tau, k);
@@ -1943,7 +1966,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             tmem::wait_st();
             // reverse: mean adjoint; the covariance warp's inputs go through
             // the exchange ring
-#pragma unroll 1
+#pragma unroll kUnrollMean
             for (int tau = kS - 1; tau >= 0; --tau, ++ntok) {
                 float k[D], a[D], u[D], e[M];
                 rd.keys(tau, k);

@@ -22,6 +22,8 @@
 // sub-chunk into shared-memory history and runs the reverse step over it
 // (phase B).  No per-token history ever reaches global memory and there is
 // no per-chunk launch.
+#include <cuda.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -861,13 +863,31 @@ namespace bssm {
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
-// Device address of g_noalloc_scratch for the current device.  The symbol's
+// Device address of g_noalloc_scratch in the current context.  The symbol's
 // name in host code is only a host-side stand-in, so the address is looked up
-// with cudaGetSymbolAddress once per device (with that device current) and
-// cached.  Returns nullptr after recording an error.
+// with cudaGetSymbolAddress (with the device current) once per CUDA context
+// and cached under that context: a context created after a device reset gets
+// its own lookup instead of a stale address.  Returns nullptr after recording
+// an error.
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
+static CUcontext current_context() {
+    static CtxGetCurrentFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<CtxGetCurrentFn>(nullptr);
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    CUcontext ctx = nullptr;
+    if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+    return ctx;
+}
+
 static void *noalloc_scratch_current_device() {
     static std::mutex mu;
-    static std::unordered_map<int, void *> cache;
+    static std::unordered_map<CUcontext, void *> cache;
     int dev = -1;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) {
@@ -875,16 +895,24 @@ static void *noalloc_scratch_current_device() {
         return nullptr;
     }
     std::lock_guard<std::mutex> lock(mu);
-    auto it = cache.find(dev);
-    if (it != cache.end()) return it->second;
+    CUcontext ctx = current_context();
+    if (ctx != nullptr) {
+        auto it = cache.find(ctx);
+        if (it != cache.end()) return it->second;
+    }
     void *ptr = nullptr;
-    err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);  // also makes the device's context current
     if (err != cudaSuccess || ptr == nullptr) {
         fail(BSSM_ERR_CUDA, "noalloc backward: cudaGetSymbolAddress on device %d: %s", dev,
              cudaGetErrorString(err));
         return nullptr;
     }
-    cache.emplace(dev, ptr);
+    ctx = current_context();
+    if (ctx == nullptr) {
+        fail(BSSM_ERR_CUDA, "noalloc backward: no current context on device %d", dev);
+        return nullptr;
+    }
+    cache[ctx] = ptr;
     return ptr;
 }
 

@@ -382,6 +382,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-api", action="store_true")
     ap.add_argument("--chains", type=int, default=None,
                     help="chains per GPU (default: the config's share of B*H; smaller for profiling)")
     args = ap.parse_args()
@@ -497,7 +498,7 @@ def main() -> None:
             dist.all_reduce(ok, op=dist.ReduceOp.MAX)
         parity["ok_all_ranks"] = bool(ok.item() == 0.0)
 
-    api = measure_api(args, wl, dev, world, bayes_ssm, inp, n)
+    api = None if args.no_api else measure_api(args, wl, dev, world, bayes_ssm, inp, n)
     e2e = None
     if not args.no_e2e:
         del rs, bm, bc

@@ -1,5 +1,5 @@
-"""Secondary measurements for the other configurations named in the survey's
-measurement plan (the headline, config 3, is ``bench.py``).
+"""Secondary measurements for the other benchmark configurations (the
+headline, config 3, is ``bench.py``).
 
 * ``--config 2``: the static associative scan (B4 T64 H8 -> 32 chains,
   D = M = 16), forward only.  It is latency-bound (2,048 chain-tokens), so
@@ -29,8 +29,24 @@ measurement plan (the headline, config 3, is ``bench.py``).
   with BF16 k/q/v, beside the same layer with the PyTorch op chains for the
   prologue and readout.
 
+* ``--config envelope-profile``: the prologue kernels alone at an eighth of
+  that shape (B32), untimed: the case the prologue's ncu captures run on.
+
+* ``--config refcuda``: the reference's own CUDA kernels on the same GPU --
+  catid/bayes-ssm installed unmodified into ``baseline/_ref`` (``pip install
+  --target``), its D8 extension JIT-built by its own loader
+  (``bayes_ssm/fused_cuda.py:23-55``, ``-O3``, here for sm_100 with
+  ``TORCH_CUDA_ARCH_LIST=10.0`` and ``TORCH_EXTENSIONS_DIR`` inside
+  ``baseline/_ref``) -- at config 3 (B256 T512 H64 D8 M8, chunk 64): the
+  public ``bayesian_layer(optimized=True)`` fwd+bwd (BF16 inputs promoted to
+  FP32, as the reference does) and its ``fused_diagonal_bayesian`` boundary
+  on FP32 inputs, with a sample of chains checked against the CPU oracle.
+  This process imports the reference's package in place of this one (both
+  are named ``bayes_ssm``).
+
 Each run prints one JSON line.  Inputs are seeded synthetic tensors with
-the survey's distributions; timing is CUDA events after warm-up.
+the distributions of the reference's mixer; timing is CUDA events after
+warm-up.
 """
 from __future__ import annotations
 
@@ -294,6 +310,139 @@ def mixer(steps: int, warmup: int) -> dict:
             "results": res, "steps": max(3, steps // 2), "warmup": warmup, "data": "synthetic"}
 
 
+def envelope_profile(steps: int, warmup: int) -> dict:
+    """The prologue kernels alone at an eighth of config 3's mixer shape
+    (B32 T512, 64 heads, key_dim 8, head_dim 8, BF16 projection, FP32
+    outputs): ``steps`` forward + backward pairs, untimed -- the small case an
+    ncu capture of ``prologue_kernel`` / ``prologue_backward_kernel`` runs on."""
+    import torch
+    from bayes_ssm import _capi
+    b, t, h, d, hd = 32, 512, 64, 8, 8
+    sw, w = h * d, h * hd
+    c, aux = 2 * sw + w, sw + 2 * h
+    pch = c + aux
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(b, t, pch, generator=g, device=dev).to(torch.bfloat16)
+    wt = torch.randn(c, 4, generator=g, device=dev) * 0.5
+    bias = torch.randn(aux, generator=g, device=dev) * 0.1
+    n = b * h
+    f32 = dict(device=dev, dtype=torch.float32)
+    k, q, v = torch.empty(n, t, d, **f32), torch.empty(n, t, d, **f32), torch.empty(n, t, hd, **f32)
+    dec, proc, obs = torch.empty(n, t, d, **f32), torch.empty(n, t, **f32), torch.empty(n, t, **f32)
+    gk, gq, gv = torch.randn_like(k), torch.randn_like(q), torch.randn_like(v)
+    gd, gp, go = torch.randn_like(dec), torch.randn_like(proc), torch.randn_like(obs)
+    gx = torch.empty_like(x)
+    gw, gb = torch.empty(c, 4, **f32), torch.empty(aux, **f32)
+    ws = torch.empty(_capi.envelope_partial_floats(b, t, h, d, hd), **f32)
+    sp = torch.cuda.current_stream().cuda_stream
+    for _ in range(steps):
+        _capi.envelope_prologue(x, _capi.BSSM_BF16, b, t, h, d, hd, pch, wt, bias, k, q, v, _capi.BSSM_F32, dec,
+                                proc, obs, sp)
+        _capi.envelope_prologue_backward(x, _capi.BSSM_BF16, b, t, h, d, hd, pch, wt, bias, gk, gq, gv,
+                                         _capi.BSSM_F32, gd, gp, go, gx, pch, gw, gb, ws, sp)
+    torch.cuda.synchronize()
+    return {"config": "envelope-profile", "workload": "prologue fwd + bwd, B32 T512 H64 D8 head_dim 8 (profiling "
+            "case)", "launches": 2 * steps, "timed": False}
+
+
+def refcuda(steps: int, warmup: int) -> dict:
+    """The reference's CUDA path at config 3 on this GPU (see the module doc)."""
+    import os
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "bayes_ssm" / "fused_cuda.py").exists():
+        return {"config": "refcuda", "unavailable": "baseline/_ref holds no reference install"}
+    os.environ.setdefault("TORCH_EXTENSIONS_DIR", str(ref / "_ext"))
+    os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    sys.path[:] = [p for p in sys.path if not p.endswith("bayes-ssm_b200")]
+    sys.path.insert(0, str(ref))
+    import time
+
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+
+    import bayes_ssm as ref_pkg
+    from bayes_ssm import fused_cuda as ref_fc
+    assert str(ref) in ref_pkg.__file__, ref_pkg.__file__
+    from oracle import oracle
+
+    b, t, h, d, m, chunk, floor = 256, 512, 64, 8, 8, 64, 1e-6
+    n = b * h
+    dev = torch.device("cuda")
+    t0 = time.perf_counter()
+    ext = ref_fc._load_extension(d)
+    build_s = time.perf_counter() - t0
+    if ext is None:
+        return {"config": "refcuda", "unavailable": f"reference extension did not load: {ref_fc._LOAD_ERRORS.get(d)}"}
+    g = torch.Generator(device=dev).manual_seed(3)
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=g, device=dev)
+
+    k = F.normalize(rn(n, t, d), dim=-1).to(torch.bfloat16)
+    q = F.normalize(rn(n, t, d), dim=-1).to(torch.bfloat16)
+    v = (rn(n, t, m) / math.sqrt(m)).to(torch.bfloat16)
+    a = torch.sigmoid(2.0 + rn(n, t, d))
+    p = F.softplus(-4.0 + rn(n, t))
+    r = F.softplus(rn(n, t)) + 1e-4
+    gy = rn(n, t, m) / math.sqrt(m)
+
+    def api_step():
+        leaves = [x.detach().requires_grad_() for x in (k, v, q, a, p, r)]
+        y, _, _ = ref_pkg.bayesian_layer(leaves[0], leaves[1], leaves[2], transition_diagonals=leaves[3],
+                                         process_variances=leaves[4], observation_variances=leaves[5],
+                                         chunk_length=chunk, optimized=True)
+        y.backward(gy)
+        return y, [x.grad for x in leaves]
+
+    kf, vf, qf = k.float(), v.float(), q.float()
+    m0 = torch.zeros(n, d, m, device=dev)
+    c0 = torch.eye(d, device=dev).expand(n, d, d).contiguous()
+
+    def boundary_step():
+        leaves = [x.detach().requires_grad_() for x in (kf, vf, qf, a, p, r)]
+        out = ref_fc.fused_diagonal_bayesian(*leaves, m0, c0, chunk_length=chunk, denominator_floor=floor)
+        out[0].backward(gy)
+        return out[0]
+
+    y, grads = api_step()
+    torch.cuda.synchronize()
+    if boundary_step() is None:
+        return {"config": "refcuda", "unavailable": "reference fused boundary declined the inputs"}
+    # the reference's own GPU outputs on a sample of chains vs the FP64 oracle
+    rng = np.random.default_rng(0)
+    idx = torch.tensor(sorted(set([0, n // 2, n - 1]) | set(int(i) for i in rng.choice(n, 13, replace=False))),
+                       device=dev)
+
+    def np64(x):
+        return x.index_select(0, idx).double().cpu().numpy()
+
+    arrs = [np64(x) for x in (k, v, q, a, p, r)]
+    ry, _, _ = oracle.forward(*arrs, None, None, floor=floor)
+    rg = oracle.backward(*arrs, None, None, np64(gy), None, None, floor=floor)
+
+    def rel(x, want):
+        return float(np.linalg.norm(np64(x) - want) / np.linalg.norm(want))
+
+    parity = {"y": rel(y.detach(), ry)}
+    for name, gr in zip("kvqapr", grads):
+        parity["grad_" + name] = rel(gr, rg[name])
+    ms_api = _time(api_step, steps, warmup)
+    ms_bnd = _time(boundary_step, steps, warmup)
+    tok = b * t
+    return {"config": "refcuda", "workload": "reference CUDA kernels (catid/bayes-ssm, unmodified, JIT-built for "
+            "sm_100) at config 3: B256 T512 H64 D8 M8, chunk 64, fwd + bwd, readout loss gradient",
+            "metric": "tok/s/GPU", "unit": "tok/s",
+            "api": {"ms_per_step": round(ms_api, 3), "tok_per_s": round(tok / (ms_api / 1e3), 1),
+                    "path": "reference bayesian_layer(optimized=True) + backward, BF16 k/q/v promoted to FP32"},
+            "boundary": {"ms_per_step": round(ms_bnd, 3), "tok_per_s": round(tok / (ms_bnd / 1e3), 1),
+                         "path": "reference fused_cuda.fused_diagonal_bayesian on FP32 inputs + backward"},
+            "parity_vs_oracle_rel_l2": parity, "parity_chains": int(idx.numel()),
+            "extension_load_s": round(build_s, 1), "arch_list": os.environ.get("TORCH_CUDA_ARCH_LIST"),
+            "steps": steps, "warmup": warmup, "data": "synthetic"}
+
+
 def _peak_hbm() -> float:
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -304,11 +453,13 @@ def _peak_hbm() -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", choices=("2", "4", "envelope", "mixer"), required=True)
+    ap.add_argument("--config", choices=("2", "4", "envelope", "envelope-profile", "mixer", "refcuda"),
+                    required=True)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()
-    fn = {"2": config2, "4": config4, "envelope": envelope, "mixer": mixer}[args.config]
+    fn = {"2": config2, "4": config4, "envelope": envelope, "envelope-profile": envelope_profile, "mixer": mixer,
+          "refcuda": refcuda}[args.config]
     print(json.dumps(fn(args.steps, max(3, args.warmup))), flush=True)
 
 

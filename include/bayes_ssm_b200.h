@@ -241,8 +241,9 @@ int bssm_d2_backward_chunked_noinitial_fixed(
  *     static size is rejected with BSSM_ERR_WORKSPACE and a message.
  *   - Nothing is allocated or freed (no cudaMalloc / cudaFree).
  *   - The first call on a device looks up the array's device address with
- *     cudaGetSymbolAddress (with that device current); make that first call
- *     before any stream capture on that device.
+ *     cudaGetSymbolAddress (with that device current) and caches it under the
+ *     current CUDA context; make that first call before any stream capture on
+ *     that device.  A new context (after a device reset) gets a new lookup.
  *   - All calls on a device share the one array and it keeps the last call's
  *     contents; nothing in it needs to start at zero.  Calls that overlap on
  *     the GPU (concurrent streams, or several host threads on one device)

@@ -281,3 +281,8 @@ def test_api_validation_errors_on_gpu(dtype):
         call(p=poked("p", float("nan")))
     with pytest.raises(ValueError, match="^observation_variances must be strictly positive$"):
         call(r=poked("r", 0.0))
+    # a value check that precedes a host-side check wins, as in the reference
+    with pytest.raises(ValueError, match="^keys must contain only finite values$"):
+        call(k=poked("k", float("nan")), r=base["r"][:, :5])
+    with pytest.raises(ValueError, match="^observation_variances must be scalar or have shape"):
+        call(r=base["r"][:, :5])
