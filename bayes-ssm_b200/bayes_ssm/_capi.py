@@ -19,7 +19,7 @@ BSSM_F32 = 0
 BSSM_BF16 = 1
 BSSM_F16 = 2
 CHECK_NONFINITE, CHECK_NOT_POSITIVE, CHECK_NEGATIVE = 1, 2, 4
-SUPPORTED = ((1, 8), (2, 8), (4, 8), (8, 8))
+SUPPORTED = ((1, 8), (2, 8), (4, 8), (8, 8), (64, 64))
 
 _LIB: Optional[ctypes.CDLL] = None
 _LOAD_ERROR: Optional[BaseException] = None
@@ -212,7 +212,7 @@ def wait_probe(limit, stream) -> None:
     check(load().bssm_debug_wait_probe(int(limit), stream), "bssm_debug_wait_probe")
 
 
-FAMILIES = {0: None, 1: "chain", 2: "staged", 3: "v1"}
+FAMILIES = {0: None, 1: "chain", 2: "staged", 3: "v1", 4: "tile64"}
 
 
 def last_family() -> str | None:

@@ -516,7 +516,7 @@ def bayesian_layer(
         and (diagonal is not None or identity_dynamics)
     )
     if kernel_path:
-        kernel_dtype = torch.bfloat16 if all_bf16 else torch.float32
+        kernel_dtype = torch.bfloat16 if all_bf16 and d != 64 else torch.float32
         src = (raw_keys, raw_values, raw_queries) if all_bf16 else (keys, values, queries)
         return _fused_path(
             *src, diagonal, process_variances, observation_variances,

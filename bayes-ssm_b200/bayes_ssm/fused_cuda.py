@@ -212,6 +212,8 @@ def fused_diagonal_bayesian(
         decay = ones.expand(n, t, d) if decay is None else decay
         process = ones.expand(n, t) if process is None else process
         observation = ones.expand(n, t) if observation is None else observation
+    if d == 64 and keys.dtype != f32:  # the (64, 64) kernels read float32 projections only
+        keys, values, queries = keys.to(f32), values.to(f32), queries.to(f32)
     keys = _aligned(keys.contiguous())
     values = _aligned(values.contiguous())
     queries = _aligned(queries.contiguous())

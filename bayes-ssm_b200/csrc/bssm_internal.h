@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <string>
+#include <type_traits>
 
 #include "bayes_ssm_b200.h"
 #include "bssm_common.cuh"
@@ -186,6 +187,10 @@ int staged_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a
 // T, chunk length multiples of kReplaySpan.  The backward needs the forward's
 // replay states whenever a chunk is longer than kReplaySpan tokens.
 template <typename TIn> bool chain_eligible(int d, long n, long t, int chunks, bool forward);
+// Key dim 64 x value dim 64, float32 (bssm_d64.cu): one CTA per chain.
+int d64_forward(int fixed, const FwdArgs<float> &a, cudaStream_t st);
+int d64_backward(int fixed, bool dyn, bool init, const BwdArgs<float> &a, cudaStream_t st);
+size_t d64_workspace_bytes(long n, long t, int chunks);
 template <typename TIn> int chain_forward(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st);
 template <typename TIn>
 int chain_backward(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st);

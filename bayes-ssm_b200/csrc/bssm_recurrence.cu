@@ -743,6 +743,7 @@ size_t workspace_bytes_t(long n, long t, int chunks) {
 }
 
 inline size_t workspace_bytes(int d, int m, long n, long t, int chunks) {
+    if (d == 64 && m == 64) return d64_workspace_bytes(n, t, chunks);
     if (m != 8) return 0;
     switch (d) {
         case 1: return workspace_bytes_t<1, 8>(n, t, chunks);
@@ -753,10 +754,13 @@ inline size_t workspace_bytes(int d, int m, long n, long t, int chunks) {
     return 0;
 }
 
-inline bool supported(int d, int m) { return m == 8 && (d == 1 || d == 2 || d == 4 || d == 8); }
+inline bool supported(int d, int m) {
+    return (m == 8 && (d == 1 || d == 2 || d == 4 || d == 8)) || (d == 64 && m == 64);
+}
 
 inline size_t replay_bytes(int d, int m, long n, long t, int chunks) {
     if (n <= 0 || t <= 0 || chunks <= 0) return 0;
+    if (d == 64) return 0;  // the D64 backward recomputes each chunk into the workspace
     return static_cast<size_t>(replay_floats(n, t, chunks, d, m)) * sizeof(float);
 }
 
@@ -769,7 +773,7 @@ inline size_t replay_bytes(int d, int m, long n, long t, int chunks) {
 // Default: chain for large batches, staged below that, v1 where neither
 // supports the shape.  BSSM_KERNELS=chain|staged|v1 forces a family (the
 // tests run every family against the oracle).
-enum Family { kAuto = 0, kChain = 1, kStaged = 2, kV1 = 3 };
+enum Family { kAuto = 0, kChain = 1, kStaged = 2, kV1 = 3, kTile64 = 4 };
 constexpr long kChainMinChains = 4096;
 
 // Read at every call (a getenv per launch), so one process can switch.
@@ -798,6 +802,12 @@ thread_local int g_last_family = 0;
 
 template <typename TIn>
 int forward_dispatch(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
+    if constexpr (std::is_same_v<TIn, float>) {
+        if (d == 64) {
+            g_last_family = kTile64;
+            return d64_forward(fixed, a, st);
+        }
+    }
     const Family f = pick_family<TIn>(d, a.n, a.t, a.chunks, true, true);
     g_last_family = f;
     if (f == kChain) return chain_forward<TIn>(d, fixed, a, st);
@@ -813,6 +823,12 @@ int forward_dispatch(int d, int fixed, const FwdArgs<TIn> &a, cudaStream_t st) {
 
 template <typename TIn>
 int backward_dispatch(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> &a, cudaStream_t st) {
+    if constexpr (std::is_same_v<TIn, float>) {
+        if (d == 64) {
+            g_last_family = kTile64;
+            return d64_backward(fixed, dyn, init, a, st);
+        }
+    }
     const bool chain_ok = a.rs != nullptr || replay_slots_per_chunk(a.t, a.chunks) == 0;
     const Family f = pick_family<TIn>(d, a.n, a.t, a.chunks, chain_ok, false);
     g_last_family = (f == kStaged && a.t == 0) ? kV1 : f;
@@ -834,9 +850,11 @@ int backward_dispatch(int d, int fixed, bool dyn, bool init, const BwdArgs<TIn> 
 int validate_common(int d, int m, int io_dtype, long n, long t, int chunks, double floor_) {
     if (!supported(d, m))
         return fail(BSSM_ERR_UNSUPPORTED, "(key_dim, value_dim) = (%d, %d) has no kernel; supported: "
-                    "(1,8), (2,8), (4,8), (8,8)", d, m);
+                    "(1,8), (2,8), (4,8), (8,8), (64,64)", d, m);
     if (io_dtype != BSSM_F32 && io_dtype != BSSM_BF16)
         return fail(BSSM_ERR_UNSUPPORTED, "io_dtype %d", io_dtype);
+    if (d == 64 && io_dtype != BSSM_F32)
+        return fail(BSSM_ERR_UNSUPPORTED, "(64, 64) takes float32 keys/values/queries only");
     if (n < 0 || t < 0) return fail(BSSM_ERR_INVALID, "negative size n=%ld t=%ld", n, t);
     if (chunks <= 0) return fail(BSSM_ERR_INVALID, "chunks must be positive (got %d)", chunks);
     if (!(floor_ > 0.0) || floor_ != floor_ || floor_ > 3.0e38)
@@ -1060,7 +1078,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
 }
 
 // ---- reference-named float32 wrappers ---------------------------------------
-#define BSSM_DEFINE_DIM(DN)                                                                        \
+#define BSSM_DEFINE_DIM(DN, MN)                                                                        \
     int bssm_d##DN##_forward_chunked(const float *keys, const float *values, const float *queries,   \
                                      const float *decay, const float *process,                     \
                                      const float *observation, const float *mean0,                 \
@@ -1068,7 +1086,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                                      float *cov_final, float *boundary_mean, float *boundary_cov,  \
                                      long n, long t, int chunks, double denominator_floor,         \
                                      void *stream) {                                               \
-        return bssm_forward_chunked_ex(DN, 8, BSSM_F32, 0, keys, values, queries, decay, process,  \
+        return bssm_forward_chunked_ex(DN, MN, BSSM_F32, 0, keys, values, queries, decay, process,  \
                                        observation, mean0, cov0, out, mean_final, cov_final,       \
                                        boundary_mean, boundary_cov, nullptr, 0, n, t, chunks,      \
                                        denominator_floor, stream);                                 \
@@ -1081,7 +1099,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                                            float *boundary_mean, float *boundary_cov, long n,      \
                                            long t, int chunks, double denominator_floor,           \
                                            void *stream) {                                         \
-        return bssm_forward_chunked_ex(DN, 8, BSSM_F32, 1, keys, values, queries, decay, process,  \
+        return bssm_forward_chunked_ex(DN, MN, BSSM_F32, 1, keys, values, queries, decay, process,  \
                                        observation, mean0, cov0, out, mean_final, cov_final,       \
                                        boundary_mean, boundary_cov, nullptr, 0, n, t, chunks,      \
                                        denominator_floor, stream);                                 \
@@ -1095,7 +1113,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         float *grad_observation, float *grad_mean0, float *grad_cov0, void *workspace,             \
         size_t workspace_bytes, long n, long t, int chunks, double denominator_floor,              \
         void *stream) {                                                                            \
-        return bssm_backward_chunked_ex(DN, 8, BSSM_F32, 0, 1, 1, keys, values, queries, decay,    \
+        return bssm_backward_chunked_ex(DN, MN, BSSM_F32, 0, 1, 1, keys, values, queries, decay,    \
                                         process, observation, mean0, cov0, boundary_mean,          \
                                         boundary_cov, nullptr, 0, grad_out, grad_mean_final,       \
                                         grad_cov_final,                                            \
@@ -1111,7 +1129,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,               \
         float *grad_values, float *grad_queries, void *workspace, size_t workspace_bytes, long n,  \
         long t, int chunks, double denominator_floor, void *stream) {                              \
-        return bssm_backward_chunked_ex(DN, 8, BSSM_F32, 0, 0, 0, keys, values, queries, decay,    \
+        return bssm_backward_chunked_ex(DN, MN, BSSM_F32, 0, 0, 0, keys, values, queries, decay,    \
                                         process, observation, mean0, cov0, boundary_mean,          \
                                         boundary_cov, nullptr, 0, grad_out, grad_mean_final,       \
                                         grad_cov_final,                                            \
@@ -1128,7 +1146,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         float *grad_observation, float *grad_mean0, float *grad_cov0, void *workspace,             \
         size_t workspace_bytes, long n, long t, int chunks, double denominator_floor,              \
         void *stream) {                                                                            \
-        return bssm_backward_chunked_ex(DN, 8, BSSM_F32, 1, 1, 1, keys, values, queries, decay,    \
+        return bssm_backward_chunked_ex(DN, MN, BSSM_F32, 1, 1, 1, keys, values, queries, decay,    \
                                         process, observation, mean0, cov0, boundary_mean,          \
                                         boundary_cov, nullptr, 0, grad_out, grad_mean_final,       \
                                         grad_cov_final,                                            \
@@ -1144,7 +1162,7 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
         const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,               \
         float *grad_values, float *grad_queries, void *workspace, size_t workspace_bytes, long n,  \
         long t, int chunks, double denominator_floor, void *stream) {                              \
-        return bssm_backward_chunked_ex(DN, 8, BSSM_F32, 1, 0, 0, keys, values, queries, decay,    \
+        return bssm_backward_chunked_ex(DN, MN, BSSM_F32, 1, 0, 0, keys, values, queries, decay,    \
                                         process, observation, mean0, cov0, boundary_mean,          \
                                         boundary_cov, nullptr, 0, grad_out, grad_mean_final,       \
                                         grad_cov_final,                                            \
@@ -1153,10 +1171,11 @@ int bssm_backward_chunked_ex(int key_dim, int value_dim, int io_dtype, int fixed
                                         t, chunks, denominator_floor, stream);                     \
     }
 
-BSSM_DEFINE_DIM(1)
-BSSM_DEFINE_DIM(2)
-BSSM_DEFINE_DIM(4)
-BSSM_DEFINE_DIM(8)
+BSSM_DEFINE_DIM(1, 8)
+BSSM_DEFINE_DIM(2, 8)
+BSSM_DEFINE_DIM(4, 8)
+BSSM_DEFINE_DIM(8, 8)
+BSSM_DEFINE_DIM(64, 64)
 
 int bssm_d2_backward_chunked_noinitial(
     const float *keys, const float *values, const float *queries, const float *decay,

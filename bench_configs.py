@@ -310,6 +310,80 @@ def mixer(steps: int, warmup: int) -> dict:
             "results": res, "steps": max(3, steps // 2), "warmup": warmup, "data": "synthetic"}
 
 
+def d64(steps: int, warmup: int) -> dict:
+    """Key dim 64 x value dim 64 (the reference trainer's layer at 8 heads of
+    width 64): B256 T512 H8 -> 2,048 chains, chunk 64, FP32 inputs, forward +
+    backward with all dynamics gradients of a readout loss, through the C ABI;
+    8 chains checked against the FP64 oracle."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+    from bayes_ssm import _capi
+    from oracle import oracle
+    b, t, h, d, m, chunk, floor = 256, 512, 8, 64, 64, 64, 1e-6
+    n = b * h
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(64)
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=g, device=dev)
+
+    kk = F.normalize(rn(n, t, d), dim=-1)
+    qq = F.normalize(rn(n, t, d), dim=-1)
+    vv = rn(n, t, m) / math.sqrt(m)
+    aa = torch.sigmoid(2.0 + rn(n, t, d))
+    pp = F.softplus(-4.0 + rn(n, t))
+    rr = F.softplus(rn(n, t)) + 1e-4
+    gy = rn(n, t, m) / math.sqrt(m)
+    nb = (t + chunk - 1) // chunk
+    f32 = dict(device=dev, dtype=torch.float32)
+    out = torch.empty(n, t, m, **f32)
+    mt, pt = torch.empty(n, d, m, **f32), torch.empty(n, d, d, **f32)
+    bm, bc = torch.empty(n, nb + 1, d, m, **f32), torch.empty(n, nb + 1, d, d, **f32)
+    gk, gq, gv = torch.empty_like(kk), torch.empty_like(qq), torch.empty_like(vv)
+    gd, gp, gr = torch.empty(n, t, d, **f32), torch.empty(n, t, **f32), torch.empty(n, t, **f32)
+    wsb = _capi.workspace_bytes(d, m, n, t, chunk)
+    ws = torch.empty(max(wsb, 1), device=dev, dtype=torch.uint8)
+    sp = torch.cuda.current_stream().cuda_stream
+    io = _capi.BSSM_F32
+
+    def fwd():
+        _capi.forward_chunked(d, m, io, False, kk, vv, qq, aa, pp, rr, None, None, out, mt, pt, bm, bc, n, t, chunk,
+                              floor, sp)
+
+    def bwd():
+        _capi.backward_chunked(d, m, io, False, True, False, kk, vv, qq, aa, pp, rr, None, None, bm, bc, gy, None,
+                               None, gk, gv, gq, gd, gp, gr, None, None, ws, wsb, n, t, chunk, floor, sp)
+
+    ms_f = _time(fwd, steps, warmup)
+    ms_b = _time(bwd, steps, warmup)
+    _capi.stream_status(sp)
+    idx = torch.tensor([0, 1, n // 2, n - 1, 100, 777, 1500, 2000], device=dev)
+
+    def np64(x):
+        return x.index_select(0, idx).double().cpu().numpy()
+
+    arrs = [np64(x) for x in (kk, vv, qq, aa, pp, rr)]
+    ry, _, _ = oracle.forward(*arrs, None, None, floor=floor)
+    rg = oracle.backward(*arrs, None, None, np64(gy), None, None, floor=floor)
+
+    def rel(x, want):
+        return float(np.linalg.norm(np64(x) - want) / np.linalg.norm(want))
+
+    parity = {"y": rel(out, ry)}
+    for name, gr_ in zip("kvqapr", (gk, gv, gq, gd, gp, gr)):
+        parity["grad_" + name] = rel(gr_, rg[name])
+    chain_steps = n * t
+    flops = chain_steps * (26 * d * d + 34 * d * m + 30 * d + 3 * m + 2)
+    ms = ms_f + ms_b
+    return {"config": "d64", "workload": "D64 M64, B256 T512 H8 -> 2,048 chains, chunk 64, FP32, fwd + bwd "
+            "(all dynamics gradients, readout loss)", "metric": "tok/s/GPU", "unit": "tok/s",
+            "value": round(b * t / (ms / 1e3), 1), "ms_per_step": round(ms, 4), "forward_ms": round(ms_f, 4),
+            "backward_ms": round(ms_b, 4), "step_tflops": round(flops / (ms / 1e3) / 1e12, 2),
+            "workspace_bytes": wsb, "parity_vs_oracle_rel_l2": parity, "parity_chains": int(idx.numel()),
+            "family": _capi.last_family(), "steps": steps, "warmup": warmup, "data": "synthetic"}
+
+
 def envelope_profile(steps: int, warmup: int) -> dict:
     """The prologue kernels alone at an eighth of config 3's mixer shape
     (B32 T512, 64 heads, key_dim 8, head_dim 8, BF16 projection, FP32
@@ -346,14 +420,20 @@ def envelope_profile(steps: int, warmup: int) -> dict:
             "case)", "launches": 2 * steps, "timed": False}
 
 
-def refcuda(steps: int, warmup: int) -> dict:
-    """The reference's CUDA path at config 3 on this GPU (see the module doc)."""
+def refcuda64(steps: int, warmup: int) -> dict:
+    """The reference's D64 kernels at the ``--config d64`` workload."""
+    return refcuda(steps, warmup, key_dim=64)
+
+
+def refcuda(steps: int, warmup: int, key_dim: int = 8) -> dict:
+    """The reference's CUDA path at config 3 on this GPU (see the module doc);
+    ``key_dim=64`` runs the D64 M64 workload of ``--config d64`` instead."""
     import os
     ref = ROOT / "baseline" / "_ref"
     if not (ref / "bayes_ssm" / "fused_cuda.py").exists():
         return {"config": "refcuda", "unavailable": "baseline/_ref holds no reference install"}
     os.environ.setdefault("TORCH_EXTENSIONS_DIR", str(ref / "_ext"))
-    os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"  # B200 (sm_100a); the prebuilt extension matches it
     sys.path[:] = [p for p in sys.path if not p.endswith("bayes-ssm_b200")]
     sys.path.insert(0, str(ref))
     import time
@@ -367,7 +447,10 @@ def refcuda(steps: int, warmup: int) -> dict:
     assert str(ref) in ref_pkg.__file__, ref_pkg.__file__
     from oracle import oracle
 
-    b, t, h, d, m, chunk, floor = 256, 512, 64, 8, 8, 64, 1e-6
+    if key_dim == 64:
+        b, t, h, d, m, chunk, floor = 256, 512, 8, 64, 64, 64, 1e-6
+    else:
+        b, t, h, d, m, chunk, floor = 256, 512, 64, 8, 8, 64, 1e-6
     n = b * h
     dev = torch.device("cuda")
     t0 = time.perf_counter()
@@ -431,8 +514,10 @@ def refcuda(steps: int, warmup: int) -> dict:
     ms_api = _time(api_step, steps, warmup)
     ms_bnd = _time(boundary_step, steps, warmup)
     tok = b * t
-    return {"config": "refcuda", "workload": "reference CUDA kernels (catid/bayes-ssm, unmodified, JIT-built for "
-            "sm_100) at config 3: B256 T512 H64 D8 M8, chunk 64, fwd + bwd, readout loss gradient",
+    return {"config": "refcuda" if key_dim == 8 else "refcuda64",
+            "workload": "reference CUDA kernels (catid/bayes-ssm, unmodified, JIT-built for sm_100) at "
+            + ("config 3: B256 T512 H64 D8 M8" if key_dim == 8 else "B256 T512 H8 D64 M64")
+            + ", chunk 64, fwd + bwd, readout loss gradient",
             "metric": "tok/s/GPU", "unit": "tok/s",
             "api": {"ms_per_step": round(ms_api, 3), "tok_per_s": round(tok / (ms_api / 1e3), 1),
                     "path": "reference bayesian_layer(optimized=True) + backward, BF16 k/q/v promoted to FP32"},
@@ -453,13 +538,13 @@ def _peak_hbm() -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", choices=("2", "4", "envelope", "envelope-profile", "mixer", "refcuda"),
-                    required=True)
+    ap.add_argument("--config", choices=("2", "4", "d64", "envelope", "envelope-profile", "mixer", "refcuda",
+                                         "refcuda64"), required=True)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()
-    fn = {"2": config2, "4": config4, "envelope": envelope, "envelope-profile": envelope_profile, "mixer": mixer,
-          "refcuda": refcuda}[args.config]
+    fn = {"2": config2, "4": config4, "d64": d64, "envelope": envelope, "envelope-profile": envelope_profile,
+          "mixer": mixer, "refcuda": refcuda, "refcuda64": refcuda64}[args.config]
     print(json.dumps(fn(args.steps, max(3, args.warmup))), flush=True)
 
 

@@ -13,10 +13,12 @@
  *   observation [N,T]; mean0 [N,D,M]; cov0 [N,D,D];
  *   out [N,T,M]; mean_final [N,D,M]; cov_final [N,D,D];
  *   boundary_mean [N,NB+1,D,M]; boundary_cov [N,NB+1,D,D], NB = ceil(T/chunks).
- * Supported (D, M): (1,8), (2,8), (4,8), (8,8).
+ * Supported (D, M): (1,8), (2,8), (4,8), (8,8) and (64,64).
  * io_dtype selects the element type of keys/values/queries and of their
- * gradients: BSSM_F32 or BSSM_BF16.  Everything else is float32; the mean,
- * covariance and every reduction are float32.
+ * gradients: BSSM_F32 or BSSM_BF16 ((64,64): BSSM_F32 only, as in the
+ * reference).  Everything else is float32; the mean, covariance and every
+ * reduction are float32.  (64,64) needs no replay states (its backward
+ * recomputes each chunk into the workspace, bssm_backward_workspace_bytes).
  *
  * Pointer alignment: every tensor pointer of the recurrence entry points must
  * be 16-byte aligned (any fresh CUDA allocation is); BSSM_ERR_ALIGNMENT
@@ -143,8 +145,10 @@ int bssm_assoc_scan_ex(int key_dim, int value_dim, const float *keys, const floa
 
 /* ---------------------------------------------------------------------
  * Reference-named float32 entry points, one set per key dimension
- * (M = 8).  Same arguments as the reference's pybind functions, with the
- * output buffers and the backward workspace supplied by the caller.
+ * (M = 8; M = 64 for the D = 64 set).  Same arguments as the reference's
+ * pybind functions, with the output buffers and the backward workspace
+ * supplied by the caller.  The D = 64 set replaces the exports of
+ * bayes_ssm/persistent_bayes_chunked.cu:436.
  * ------------------------------------------------------------------- */
 #define BSSM_DECLARE_DIM(DN)                                                                     \
     /* forward_chunked: persistent_bayes_chunked_d8.cu:530 and its D4/D2/D1 twins */            \
@@ -205,6 +209,7 @@ BSSM_DECLARE_DIM(1)
 BSSM_DECLARE_DIM(2)
 BSSM_DECLARE_DIM(4)
 BSSM_DECLARE_DIM(8)
+BSSM_DECLARE_DIM(64)
 
 /* backward_chunked_noinitial[_fixed] (6 gradients: k, v, q, decay, process,
  * observation): persistent_bayes_chunked_d2m8.cu:576-600. */
@@ -405,7 +410,8 @@ long bssm_debug_fma_probe_flops(int blocks, int iters);
 
 /*
  * Kernel family that served the calling thread's last forward or backward
- * call: 1 thread-per-chain, 2 staged, 3 per-lane; 0 before any call.  The
+ * call: 1 thread-per-chain, 2 staged, 3 per-lane, 4 the (64,64) tile
+ * kernels; 0 before any call.  The
  * library picks by shape and batch size; the environment variable
  * BSSM_KERNELS=chain|staged|v1, read at every call, forces a family where it
  * supports the shape.
