@@ -18,7 +18,7 @@ INCLUDE = PKG_ROOT.parent / "include"
 LIB_DIR = PKG_ROOT / "lib"
 LIB = LIB_DIR / "libbayes_ssm_b200.so"
 SOURCES = ["bssm_recurrence.cu", "bssm_staged.cu", "bssm_chain.cu", "bssm_assoc_scan.cu", "bssm_check.cu",
-           "bssm_envelope.cu", "bssm_d64.cu"]
+           "bssm_envelope.cu", "bssm_d64.cu", "bssm_rotation.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

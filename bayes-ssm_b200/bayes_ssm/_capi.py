@@ -58,6 +58,9 @@ _SIGNATURES = {
     "bssm_envelope_epilogue": ([_vp, _i, _vp, _i, _l, _vp, ctypes.c_float, _l, _l, _i, _i, _vp, _vp], _i),
     "bssm_envelope_epilogue_backward": ([_vp, _i, _vp, _i, _l, _vp, ctypes.c_float, _l, _l, _i, _i, _vp, _vp, _vp,
                                          _l, _vp, _vp, _l, _vp], _i),
+    "bssm_rotation_workspace_bytes": ([_i, _i, _l, _l, _i], _sz),
+    "bssm_rotation_forward_chunked": ([_i, _i] + [_vp] * 14 + [_l, _l, _i, _d, _vp], _i),
+    "bssm_rotation_backward_chunked": ([_i, _i, _i] + [_vp] * 22 + [_sz, _l, _l, _i, _d, _vp], _i),
     "bssm_debug_wait_timeouts": ([], ctypes.c_uint),
     "bssm_stream_status": ([_vp], _i),
     "bssm_debug_wait_probe": ([_i, _vp], _i),
@@ -145,6 +148,30 @@ def assoc_scan(key_dim, value_dim, keys, values, queries, observation, mean0, co
                                 ptr(observation), ptr(mean0), ptr(cov0), ptr(out), ptr(mean_final),
                                 ptr(cov_final), ptr(status), n, t, float(floor), stream)
     check(rc, "bssm_assoc_scan_ex")
+
+
+def rotation_workspace_bytes(key_dim, value_dim, n, t, chunks) -> int:
+    return int(load().bssm_rotation_workspace_bytes(key_dim, value_dim, n, t, chunks))
+
+
+def rotation_forward(key_dim, value_dim, keys, values, queries, cosines, sines, process, observation, mean0, cov0,
+                     out, mean_final, cov_final, bmean, bcov, n, t, chunks, floor, stream) -> None:
+    rc = load().bssm_rotation_forward_chunked(
+        key_dim, value_dim, ptr(keys), ptr(values), ptr(queries), ptr(cosines), ptr(sines), ptr(process),
+        ptr(observation), ptr(mean0), ptr(cov0), ptr(out), ptr(mean_final), ptr(cov_final), ptr(bmean), ptr(bcov),
+        n, t, chunks, float(floor), stream)
+    check(rc, "bssm_rotation_forward_chunked")
+
+
+def rotation_backward(key_dim, value_dim, need_initial, keys, values, queries, cosines, sines, process,
+                      observation, bmean, bcov, gy, gmf, gcf, gk, gv, gq, gcos, gsin, gproc, gobs, gm0, gc0,
+                      workspace, workspace_nbytes, n, t, chunks, floor, stream) -> None:
+    rc = load().bssm_rotation_backward_chunked(
+        key_dim, value_dim, int(need_initial), ptr(keys), ptr(values), ptr(queries), ptr(cosines), ptr(sines),
+        ptr(process), ptr(observation), ptr(bmean), ptr(bcov), ptr(gy), ptr(gmf), ptr(gcf), ptr(gk), ptr(gv),
+        ptr(gq), ptr(gcos), ptr(gsin), ptr(gproc), ptr(gobs), ptr(gm0), ptr(gc0), ptr(workspace), workspace_nbytes,
+        n, t, chunks, float(floor), stream)
+    check(rc, "bssm_rotation_backward_chunked")
 
 
 def backward_chunked_noalloc(key_dim, value_dim, io_dtype, fixed, need_dynamics, need_initial, keys,

@@ -246,6 +246,27 @@ def _dense_recurrence(keys: Tensor, values: Tensor, queries: Tensor, transitions
     return torch.stack(outputs, dim=-2), mean, covariance
 
 
+def _rotation_path(keys, values, queries, cosines, sines, process_variances, observation_variances, mean,
+                   covariance, *, batch_shape, t, d, m, chunk_length, denominator_floor, pending_checks=None):
+    """Flatten the batch to chains and run the rotation kernels."""
+    from .rotation_cuda import rotation_bayesian
+
+    n = 1
+    for s_ in batch_shape:
+        n *= int(s_)
+    j = d // 2
+
+    def chains(x, tail):
+        return x.expand(*batch_shape, *tail).reshape(n, *tail).float()
+
+    y, mt, pt = rotation_bayesian(
+        chains(keys, (t, d)), chains(values, (t, m)), chains(queries, (t, d)), chains(cosines, (t, j)),
+        chains(sines, (t, j)), chains(process_variances, (t, j)), chains(observation_variances, (t,)),
+        None if mean is None else chains(mean, (d, m)), None if covariance is None else chains(covariance, (d, d)),
+        chunk_length=chunk_length, denominator_floor=denominator_floor, _pending_checks=pending_checks)
+    return (y.reshape(*batch_shape, t, m), mt.reshape(*batch_shape, d, m), pt.reshape(*batch_shape, d, d))
+
+
 def _default_mean(mean, batch_shape, d, m, device, dtype):
     return torch.zeros(*batch_shape, d, m, device=device, dtype=dtype) if mean is None else mean
 
@@ -505,6 +526,21 @@ def bayesian_layer(
             chunk_length = t
 
     from .fused_cuda import kernel_supports
+    from .rotation_cuda import SUPPORTED as ROTATION_SUPPORTED
+
+    if (rotation and optimized and device.type == "cuda" and (d, m) in ROTATION_SUPPORTED
+            and dtype in (torch.float32, torch.bfloat16)):
+        # the reference's radius handling and make_rotation_dynamics' own
+        # operations, so autograd reaches the radii and angles the same way
+        radius = rotation_radii.clamp_min(torch.finfo(dtype).tiny)
+        radius = torch.where(radius <= 1.0, radius, torch.ones_like(radius))
+        raw = torch.log(radius).exp()
+        rho = torch.where(raw <= 1.0, raw, torch.ones_like(raw))
+        return _rotation_path(keys, values, queries, rho * rotation_angles.cos(), rho * rotation_angles.sin(),
+                              process_variances, observation_variances, mean if user_mean else None,
+                              covariance if user_cov else None, batch_shape=batch_shape, t=t, d=d, m=m,
+                              chunk_length=chunk_length, denominator_floor=float(denominator_floor),
+                              pending_checks=chk)
 
     kernel_path = (
         optimized

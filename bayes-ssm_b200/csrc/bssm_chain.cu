@@ -57,7 +57,9 @@ constexpr int kSmemMax = 227 * 1024;
 // backward's two replay loops fully took it from 0.867 to 0.824 ms; fully
 // unrolled adjoint loops were slower (0.965 ms; 1.18 ms together with the
 // replays), 2-way neutral; the forward's loops were neutral at 2 and slower
-// at 4 (0.432 -> 0.472 ms).
+// at 4 (0.432 -> 0.472 ms).  Also neutral (within 0.5 %): loading the
+// covariance warp's tile rows before its exchange wait, splitting its
+// gain-adjoint sum into two chains, and the replay update in packed pairs.
 #ifndef BSSM_SPLIT_UNROLL_FWD
 #define BSSM_SPLIT_UNROLL_FWD 1
 #endif
@@ -1803,8 +1805,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                 rd.decay(tau, a);
                 gains(tile, tau, u);
                 const float p = sel4v(p4, tau), bt = sel4v(b4, tau), beta = fabsf(bt);
-                float gb = xv[3 * D];
                 float Ru[D], trR = 0.f;
+                float gb = xv[3 * D];
 #pragma unroll
                 for (int i = 0; i < D; ++i) {
                     float acc = 0.f;

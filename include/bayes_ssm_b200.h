@@ -270,6 +270,37 @@ int bssm_backward_chunked_noalloc(int key_dim, int value_dim, int io_dtype, int 
                                   void *stream);
 
 /*
+ * Rotation dynamics (replaces the dense path of bayes_ssm/bayesian_layer.py:
+ * 254-340 for rotation_radii / rotation_angles: the reference has no kernel
+ * for it).  Transition A = blockdiag(A_m), A_m = [[c_m, -s_m], [s_m, c_m]]
+ * per key pair m, given as cosines[n,t,m] = rho cos(theta) and
+ * sines[n,t,m] = rho sin(theta); process noise blockdiag(diag(q_m, 0)) with
+ * process[n,t,m] = q_m (>= 0); observation [n,t].  Float32 throughout;
+ * (key_dim, value_dim) in {(2,8), (4,8), (8,8)}.  Layouts, boundary states,
+ * floor and NULL initial-state conventions as bssm_forward_chunked_ex.  The
+ * backward recomputes each chunk into `workspace`
+ * (bssm_rotation_workspace_bytes) and writes the gradients of keys, values,
+ * queries, cosines, sines, process and observation (and of the initial
+ * state when need_initial != 0; the covariance's is symmetric).
+ */
+size_t bssm_rotation_workspace_bytes(int key_dim, int value_dim, long n, long t, int chunks);
+int bssm_rotation_forward_chunked(int key_dim, int value_dim, const float *keys, const float *values,
+                                  const float *queries, const float *cosines, const float *sines,
+                                  const float *process, const float *observation, const float *mean0,
+                                  const float *cov0, float *out, float *mean_final, float *cov_final,
+                                  float *boundary_mean, float *boundary_cov, long n, long t, int chunks,
+                                  double denominator_floor, void *stream);
+int bssm_rotation_backward_chunked(int key_dim, int value_dim, int need_initial, const float *keys,
+                                   const float *values, const float *queries, const float *cosines,
+                                   const float *sines, const float *process, const float *observation,
+                                   const float *boundary_mean, const float *boundary_cov, const float *grad_out,
+                                   const float *grad_mean_final, const float *grad_cov_final, float *grad_keys,
+                                   float *grad_values, float *grad_queries, float *grad_cosines,
+                                   float *grad_sines, float *grad_process, float *grad_observation,
+                                   float *grad_mean0, float *grad_cov0, void *workspace, size_t workspace_bytes,
+                                   long n, long t, int chunks, double denominator_floor, void *stream);
+
+/*
  * Input checks of bayesian_layer in one pass (replaces the torch.isfinite(x)
  * .all() and x.min() validation of bayes_ssm/bayesian_layer.py:105-128).
  *

@@ -17,6 +17,9 @@ Sources exercised (paths within the reference project):
   fixed-dynamics (0.97 / 0.1 / 1.0) core.
 * ``bayes_ssm/replay_ssm.py:155`` ``associative_static_bayesian`` -- the
   information-form scan, and its observation-variance rejection (:243-248).
+* ``bayes_ssm/bayesian_layer.py:254-340`` -- rotation dynamics (damped 2-D
+  rotations per key pair, per-pair process noise), through the dense path
+  (``--rotation-only`` regenerates just those fixtures).
 """
 from __future__ import annotations
 
@@ -168,8 +171,59 @@ def assoc_case(name: str, *, seed: int, n: int, t: int, d: int, m: int, init: st
     print(name, "assoc", tuple(y.shape))
 
 
+def rotation_case(name: str, *, seed: int, n: int, t: int, d: int, m: int, chunk: int, init: str,
+                  loss: str) -> None:
+    """``bayesian_layer(..., rotation_radii=, rotation_angles=, optimized=False)``:
+    the reference's rotation dynamics (bayesian_layer.py:254-340 with
+    make_rotation_dynamics / make_rotation_process_covariances)."""
+    g = torch.Generator().manual_seed(seed)
+    j = d // 2
+    k = F.normalize(torch.randn(n, t, d, generator=g), dim=-1)
+    q = F.normalize(torch.randn(n, t, d, generator=g), dim=-1)
+    v = torch.randn(n, t, m, generator=g) / math.sqrt(m)
+    radii = 0.8 + 0.19 * torch.rand(n, t, j, generator=g)
+    angles = 0.5 * torch.randn(n, t, j, generator=g)
+    p = F.softplus(-3.0 + torch.randn(n, t, j, generator=g))
+    r = F.softplus(torch.randn(n, t, generator=g)) + 1e-2
+    if init == "random":
+        m0 = torch.randn(n, d, m, generator=g) * 0.3
+        p0 = spd(g, n, d)
+    else:
+        m0 = torch.zeros(n, d, m)
+        p0 = torch.eye(d).expand(n, d, d).clone()
+    ins = {key: f32(val).requires_grad_() for key, val in
+           dict(k=k, v=v, q=q, radii=radii, angles=angles, p=p, r=r, M0=m0, P0=p0).items()}
+    y, mt, pt = bayesian_layer(
+        ins["k"], ins["v"], ins["q"], rotation_radii=ins["radii"], rotation_angles=ins["angles"],
+        process_variances=ins["p"], observation_variances=ins["r"], initial_mean=ins["M0"],
+        initial_covariance=ins["P0"], chunk_length=chunk, optimized=False)
+    if loss == "all":
+        total = y.square().mean() + mt.square().mean() + pt.square().mean()
+    else:
+        total = y.square().sum()
+    names = list(ins)
+    grads = torch.autograd.grad(total, [ins[x] for x in names])
+    arrays = {f"in_{x}": ins[x].detach().numpy() for x in names}
+    arrays.update(out_y=y.detach().numpy(), out_MT=mt.detach().numpy(), out_PT=pt.detach().numpy())
+    arrays.update({f"grad_{x}": gr.numpy() for x, gr in zip(names, grads)})
+    arrays.update(chunk=np.array(chunk), loss_all=np.array(int(loss == "all")))
+    np.savez_compressed(OUT / f"{name}.npz", **arrays)
+    print(name, "rotation", tuple(y.shape))
+
+
+def rotation_cases() -> None:
+    rotation_case("rotation_d2m8_all", seed=500, n=2, t=11, d=2, m=8, chunk=4, init="random", loss="all")
+    rotation_case("rotation_d4m8_all", seed=501, n=2, t=13, d=4, m=8, chunk=5, init="random", loss="all")
+    rotation_case("rotation_d8m8_readout", seed=502, n=2, t=17, d=8, m=8, chunk=8, init="identity",
+                  loss="readout")
+
+
 def main() -> None:
+    import sys
     torch.set_default_dtype(F64)
+    if "--rotation-only" in sys.argv:
+        rotation_cases()
+        return
     dense_case("diag_d4m3_all", seed=44, n=2, t=7, d=4, m=3, chunk=3, dist="unit",
                init="random", loss="all")
     dense_case("diag_d3m2_all", seed=45, n=1, t=6, d=3, m=2, chunk=2, dist="unit",
@@ -187,6 +241,7 @@ def main() -> None:
     assoc_case("assoc_random_init", seed=1, n=2, t=9, d=4, m=3, init="random", dist="softplus")
     assoc_case("assoc_config2_slice", seed=2, n=4, t=64, d=16, m=16, init="identity",
                dist="softplus")
+    rotation_cases()
 
 
 if __name__ == "__main__":

@@ -11,7 +11,7 @@ import pytest
 from conftest import GOLDEN
 from oracle import oracle
 
-DENSE = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("assoc"))
+DENSE = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("assoc", "rotation")))
 ASSOC = sorted(p.stem for p in GOLDEN.glob("assoc*.npz"))
 
 

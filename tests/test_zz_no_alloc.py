@@ -19,7 +19,7 @@ from harness import assert_parity, capi_backward, capi_forward, io_code, make_in
 pytestmark = pytest.mark.gpu
 
 
-def _noalloc(inp, fwd, gy, *, chunks, n, t, d=8, m=8):
+def _noalloc(inp, fwd, gy, *, chunks, n, t, d=8, m=8, fixed=False):
     from bayes_ssm import _capi
     dev = torch.device("cuda")
     k, v, q = (inp[x].cuda().contiguous() for x in ("k", "v", "q"))
@@ -30,7 +30,7 @@ def _noalloc(inp, fwd, gy, *, chunks, n, t, d=8, m=8):
     gr = torch.empty(n, t, device=dev)
     gm0 = torch.empty(n, d, m, device=dev)
     gc0 = torch.empty(n, d, d, device=dev)
-    _capi.backward_chunked_noalloc(d, m, io_code(k.dtype), False, True, True, k, v, q, a, p, r, None,
+    _capi.backward_chunked_noalloc(d, m, io_code(k.dtype), fixed, True, True, k, v, q, a, p, r, None,
                                    None, fwd["bm"], fwd["bc"], gy.cuda(), None, None, gk, gv, gq, gd,
                                    gp, gr, gm0, gc0, n, t, chunks, 1e-6,
                                    torch.cuda.current_stream().cuda_stream)
@@ -50,6 +50,28 @@ def test_noalloc_backward_matches_workspace_backward_twice():
         got = _noalloc(inp, fwd, gy, chunks=chunks, n=n, t=t)
         for key in want:
             assert_parity(got[key], want[key].float().cpu().numpy(), what=f"noalloc grad {key}")
+
+
+@pytest.mark.parametrize("d,m,n", [(1, 8, 24), (2, 8, 24), (4, 8, 24), (8, 8, 24), (64, 64, 3)])
+@pytest.mark.parametrize("dtype", (torch.float32, torch.bfloat16))
+@pytest.mark.parametrize("fixed", (False, True))
+def test_noalloc_every_shape_family_and_dynamics(d, m, n, dtype, fixed):
+    """Every key dimension (each with its own scratch layout), FP32 and BF16
+    projections and fixed dynamics, two calls in a row; chunk 64 so the
+    scratch is used."""
+    from bayes_ssm import _capi
+    if d == 64 and dtype == torch.bfloat16:
+        pytest.skip("(64, 64) takes float32 projections only")
+    t, chunks = 70, 64
+    assert _capi.workspace_bytes(d, m, n, t, chunks) > 0
+    gy = torch.randn(n, t, m, generator=torch.Generator().manual_seed(7))
+    for seed in (3, 4):
+        inp = make_inputs(n, t, d, m, seed=seed, io_dtype=dtype)
+        fwd = capi_forward(inp, chunks=chunks, fixed=fixed, replay_states=False)
+        want = capi_backward(inp, fwd, gy, None, None, chunks=chunks, fixed=fixed)
+        got = _noalloc(inp, fwd, gy, chunks=chunks, n=n, t=t, d=d, m=m, fixed=fixed)
+        for key in want:
+            assert_parity(got[key], want[key].float().cpu().numpy(), what=f"noalloc d{d} grad {key}")
 
 
 def test_noalloc_backward_rejects_problems_larger_than_the_scratch():
