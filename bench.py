@@ -518,8 +518,8 @@ def main() -> None:
         key = f"{args.config}:{wl.dominant.split(' ')[0]}"
         rec, rec_src = _captured_traffic(key)
         traffic = None
-        if rec is not None and n == wl.shard(world):
-            traffic = rec["dram_bytes_per_full_launch"]
+        if rec is not None:  # captured for all B*H chains; traffic grows with the chains
+            traffic = int(rec["dram_bytes_per_full_launch"] * n / wl.N)
         binding = "fp32" if bwd_tflops / fp32 >= bwd_gbs / hbm_peak else "hbm"
         roofline = {
             "kernel": wl.dominant,
