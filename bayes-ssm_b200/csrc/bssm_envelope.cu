@@ -61,13 +61,13 @@ constexpr int kThreads = 256;
 #ifndef BSSM_ENV_BWD_UNROLL
 #define BSSM_ENV_BWD_UNROLL 1
 #endif
-#ifndef BSSM_ENV_BWD_PREFETCH
-#define BSSM_ENV_BWD_PREFETCH 0
-#endif
 // CTAs per SM the compiler sizes registers for (launch-bounds minimum): the
 // walks are bound by load latency, so occupancy beats registers here
 // (backward 2.61 -> 1.63 ms, forward 0.89 -> 0.72 ms on one box against 1 / 1;
-// 5 / 6 spilled more and was slower).
+// 5 / 6 spilled more and was slower; 3 in the backward: 1.92 ms).  Issuing
+// the backward walk's loads one token ahead (double-buffered in registers)
+// was neutral with FP32 outputs (1.617 against 1.628 ms) and slower with
+// BF16 ones (1.71 against 1.65 ms).
 #ifndef BSSM_ENV_FWD_MINB
 #define BSSM_ENV_FWD_MINB 5
 #endif
@@ -413,68 +413,13 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
         ldx(hi - 2, x1);
         ldx(hi - 3, x2);
     }
-#if BSSM_ENV_BWD_PREFETCH
-    // The walk's loads for token t - 1 are issued before token t is computed,
-    // so their latency overlaps the arithmetic instead of following it:
-    // conv channels need x[t - 3] and the recurrence-input gradient at t, the
-    // auxiliary channels x[t] and their variance / decay gradients at t.
-    auto fetch = [&](long t, float *xo, float *go) {
-#pragma unroll
-        for (int j = 0; j < CW; ++j) go[j] = 0.f;
-        if (conv) {
-            ldx(t - 3, xo);
-            if (gsrc != nullptr) {
-                if (hm.ng == 1 || ch.kind == kV) {
-                    ldn<OUT_BF, CW>(gsrc, (chain * s.t + t) * grow + ch.within, go);
-                } else {
-                    ld_heads<OUT_BF, CW>(gsrc, chain, t, s.t, s.d, go);
-                }
-            }
-        } else if (t < t1 && (ch.kind == kDecay || ch.kind == kNoise)) {
-            ldx(t, xo);
-            if (ch.kind == kDecay) {
-                if (a.gdecay != nullptr) {
-                    if (hm.ng == 1) {
-                        ldn<false, CW>(a.gdecay, (chain * s.t + t) * s.d + ch.within, go);
-                    } else {
-                        ld_heads<false, CW>(a.gdecay, chain, t, s.t, s.d, go);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < CW / 2; ++i) {
-                    go[2 * i] = a.gprocess != nullptr ? __ldg(a.gprocess + (chain + i) * s.t + t) : 0.f;
-                    go[2 * i + 1] = a.gobservation != nullptr ? __ldg(a.gobservation + (chain + i) * s.t + t) : 0.f;
-                }
-            }
-        }
-    };
-    float xa[CW], ga[CW];
-#pragma unroll
-    for (int j = 0; j < CW; ++j) xa[j] = ga[j] = 0.f;
-    if (hi > t0) fetch(hi - 1, xa, ga);
-#endif
 #pragma unroll (kBwdUnroll)
     for (long t = hi - 1; t >= t0; --t) {
         float gc[CW], g[CW], o[CW], ds[CW];
 #pragma unroll
         for (int j = 0; j < CW; ++j) gc[j] = g[j] = o[j] = ds[j] = 0.f;
-#if BSSM_ENV_BWD_PREFETCH
-        float xcur[CW], gcur[CW];
-#pragma unroll
-        for (int j = 0; j < CW; ++j) {
-            xcur[j] = xa[j];
-            gcur[j] = ga[j];
-        }
-        if (t - 1 >= t0) fetch(t - 1, xa, ga);
-#endif
         if (conv) {
-#if BSSM_ENV_BWD_PREFETCH
-#pragma unroll
-            for (int j = 0; j < CW; ++j) x3[j] = xcur[j];
-#else
             ldx(t - 3, x3);
-#endif
 #pragma unroll
             for (int j = 0; j < CW; ++j) {
                 const float c = fmaf(w[3][j], x0[j], fmaf(w[2][j], x1[j], fmaf(w[1][j], x2[j], w[0][j] * x3[j])));
@@ -482,10 +427,6 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
                 o[j] = c * sg;
                 ds[j] = sg * fmaf(c, 1.f - sg, 1.f);  // silu'
             }
-#if BSSM_ENV_BWD_PREFETCH
-#pragma unroll
-            for (int j = 0; j < CW; ++j) g[j] = gcur[j];
-#else
             if (gsrc != nullptr) {
                 if (hm.ng == 1 || ch.kind == kV) {
                     ldn<OUT_BF, CW>(gsrc, (chain * s.t + t) * grow + ch.within, g);
@@ -493,7 +434,6 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
                     ld_heads<OUT_BF, CW>(gsrc, chain, t, s.t, s.d, g);
                 }
             }
-#endif
         }
         // q, k: y = s / max(|s|, eps); dy/ds = (I - y y^T) / |s| above eps, I / eps below
         if (hm.ng == 1) {
@@ -546,18 +486,9 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
                 stn<IN_BF, CW>(a.gx, (row0 + t) * a.gx_stride + c0, gx);
             } else if (ch.kind == kDecay || ch.kind == kNoise) {
                 float xv[CW], gz[CW];
-#if BSSM_ENV_BWD_PREFETCH
-#pragma unroll
-                for (int j = 0; j < CW; ++j) xv[j] = xcur[j];
-#else
                 ldx(t, xv);
-#endif
                 if (ch.kind == kDecay) {
                     float gd[CW];
-#if BSSM_ENV_BWD_PREFETCH
-#pragma unroll
-                    for (int j = 0; j < CW; ++j) gd[j] = gcur[j];
-#else
 #pragma unroll
                     for (int j = 0; j < CW; ++j) gd[j] = 0.f;
                     if (a.gdecay != nullptr) {
@@ -567,7 +498,6 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
                             ld_heads<false, CW>(a.gdecay, chain, t, s.t, s.d, gd);
                         }
                     }
-#endif
 #pragma unroll
                     for (int j = 0; j < CW; ++j) {
                         // d/dz 1 / (1 + e^z) = -decay (1 - decay)
@@ -577,12 +507,8 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
                 } else {
 #pragma unroll
                     for (int i = 0; i < CW / 2; ++i) {
-#if BSSM_ENV_BWD_PREFETCH
-                        const float gpv = gcur[2 * i], gov = gcur[2 * i + 1];
-#else
                         const float gpv = a.gprocess != nullptr ? __ldg(a.gprocess + (chain + i) * s.t + t) : 0.f;
                         const float gov = a.gobservation != nullptr ? __ldg(a.gobservation + (chain + i) * s.t + t) : 0.f;
-#endif
                         gz[2 * i] = gpv * softplus_grad(xv[2 * i] + bias[2 * i]);
                         gz[2 * i + 1] = gov * softplus_grad(xv[2 * i + 1] + bias[2 * i + 1]);
                     }
