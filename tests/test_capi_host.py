@@ -121,3 +121,24 @@ def test_misaligned_pointer_rejected_before_launch(lib):
     ptrs[0] += 4  # keys: misaligned
     rc = lib.bssm_forward_chunked_ex(8, 8, 0, 0, *ptrs, None, 0, 2, 16, 8, 1e-6, None)
     assert rc == 3 and b"16-byte" in lib.bssm_last_error()
+
+
+def test_d64_and_rotation_host_checks_without_gpu(lib):
+    from bayes_ssm import _capi
+    _capi.load()
+    # (64, 64): float32 only; no replay states; the workspace holds 64 KB per
+    # saved 2-token sub-chunk state and chain
+    fwd_nulls = [None] * 13 + [None, 0]
+    rc = lib.bssm_forward_chunked_ex(64, 64, 1, 0, *fwd_nulls, 1, 1, 1, 1e-6, None)
+    assert rc == 2 and b"float32" in lib.bssm_last_error()
+    assert lib.bssm_replay_states_bytes(64, 64, 4, 512, 64) == 0
+    assert lib.bssm_backward_workspace_bytes(64, 64, 3, 512, 64) == 3 * 31 * 2 * 16 * 256 * 4
+    # rotation: (2|4|8, 8) only, workspace (D + M) floats per lane and saved state
+    assert lib.bssm_rotation_workspace_bytes(8, 8, 10, 512, 64) == 10 * 15 * 8 * 16 * 4
+    assert lib.bssm_rotation_workspace_bytes(1, 8, 10, 512, 64) == 0
+    rc = lib.bssm_rotation_forward_chunked(1, 8, *([None] * 14), 1, 1, 1, 1e-6, None)
+    assert rc == 2 and b"rotation" in lib.bssm_last_error()
+    rc = lib.bssm_rotation_forward_chunked(8, 8, *([None] * 14), 1, 4, 4, 1e-6, None)
+    assert rc == 1 and b"null" in lib.bssm_last_error()
+    rc = lib.bssm_rotation_backward_chunked(8, 8, 0, *([None] * 22), 0, 1, 4, 0, 1e-6, None)
+    assert rc == 1 and b"chunks" in lib.bssm_last_error()
