@@ -79,6 +79,13 @@ constexpr int kUnrollMean = BSSM_SPLIT_UNROLL_MEAN;      // backward_split mean 
 
 constexpr int al128(int x) { return (x + 127) / 128 * 128; }
 constexpr int al1024(int x) { return (x + 1023) / 1024 * 1024; }
+// Start of a region of line boxes whose lines span `span` bytes: swizzled
+// lines (32 bytes and up) need the swizzle atom's 1024-byte alignment;
+// 16-byte lines are not swizzled and need only the TMA's 128 bytes.
+constexpr int al_line(int x, int span) { return span == 16 ? al128(x) : al1024(x); }
+// Shared memory one CTA may take when two share an SM (228 KB per SM, 1 KB
+// reserved per CTA).
+constexpr int kSmemTwoPerSm = (228 * 1024 - 2 * 1024) / 2;
 
 // N consecutive floats from 16-byte aligned shared memory.
 template <int N>
@@ -411,10 +418,13 @@ struct Tile {
     static constexpr int rbK = D * static_cast<int>(sizeof(TIn)), rbV = M * static_cast<int>(sizeof(TIn));
     static constexpr int szK = kS * 32 * rbK, szV = kS * 32 * rbV, szA = FIXED ? 0 : kS * 32 * D * 4;
     static constexpr int szP = FIXED ? 0 : 32 * kS * 4, szG = BWD ? kS * 32 * M * 4 : 0;
-    // line regions, each 1024-byte aligned for the swizzle, then the
-    // [chain][tau] noise rows
-    static constexpr int oK = 0, oQ = al1024(oK + szK), oV = al1024(oQ + szK), oA = al1024(oV + szV);
-    static constexpr int oG = al1024(oA + szA), oP = al1024(oG + szG), oR = oP + szP;
+    // line regions, aligned for their swizzle, then the [chain][tau] noise
+    // rows; the tile itself spans whole KB so every warp's tile starts
+    // 1024-byte aligned
+    static constexpr int spK = kS * rbK, spV = kS * rbV, spA = kS * D * 4, spG = kS * M * 4;
+    static constexpr int oK = 0, oQ = al_line(oK + szK, spK), oV = al_line(oQ + szK, spV);
+    static constexpr int oA = al_line(oV + szV, spA), oG = al_line(oA + szA, spG), oP = al128(oG + szG);
+    static constexpr int oR = oP + szP;
     static constexpr int kBytes = al1024(oR + szP);
     static constexpr int kTx = 2 * szK + szV + szA + 2 * szP;  // bytes the token maps deliver, without gy
 };
@@ -599,7 +609,12 @@ struct FwdGeo {
     static constexpr int kFixed = kWarps * kYB + 1024 + kWarps * 4 * 8;
     static constexpr int kFit = (kSmemMax - kFixed) / kPerStage;
     static constexpr bool kFits = kFit >= 2;  // else the shape goes to another family
-    static constexpr int kStages = kFit < 2 ? 2 : (kFit < 4 ? kFit : 4);
+    // Two CTAs per SM when two or more stages still fit in half the SM's
+    // shared memory (small rows: at D2 a lone CTA left three warps of every
+    // four sub-partition slots empty and ran 65,536 chains in four waves),
+    // else up to four stages in one CTA.
+    static constexpr int kFitTwo = (kSmemTwoPerSm - kFixed - kWarps * 4 * 8 - 1024) / kPerStage;
+    static constexpr int kStages = kFitTwo >= 2 ? (kFitTwo < 4 ? kFitTwo : 4) : (kFit < 2 ? 2 : (kFit < 4 ? kFit : 4));
     static constexpr int oY = 0;                            // [warp][kYB]
     static constexpr int oT = oY + kWarps * kYB;            // [stage][warp][tile]
     static constexpr int oBar = oT + kStages * kPerStage;   // [warp][stage]
@@ -1156,8 +1171,8 @@ struct BwdGeo {
     // a warp's gradient rows of one sub-chunk: keys, values, queries, decay
     // as line boxes (whole KB each); process, observation [chain][tau]
     static constexpr int rbK = Tl::rbK, rbV = Tl::rbV;
-    static constexpr int gK = 0, gV = al1024(gK + kS * 32 * rbK), gQ = al1024(gV + kS * 32 * rbV);
-    static constexpr int gA = al1024(gQ + kS * 32 * rbK), gP = al1024(gA + kS * 32 * D * 4);
+    static constexpr int gK = 0, gV = al_line(gK + kS * 32 * rbK, Tl::spV), gQ = al_line(gV + kS * 32 * rbV, Tl::spK);
+    static constexpr int gA = al_line(gQ + kS * 32 * rbK, Tl::spA), gP = al128(gA + kS * 32 * D * 4);
     static constexpr int gR = gP + 32 * kS * 4, kOB = al1024(gR + 32 * kS * 4);
     static constexpr int kPerStage = kWarps * Tl::kBytes;
     static constexpr int oT = 0;                              // [stage][warp][tile]
