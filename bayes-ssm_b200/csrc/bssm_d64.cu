@@ -345,8 +345,15 @@ struct BwdSmem {
     float trp[kSub][16];                 // partial traces of the symmetric covariance adjoint
 };
 
+// Two CTAs per SM (registers capped at 128, a few bytes spilled in three of
+// the eight instantiations): the backward is bound by its barriers, so a second
+// chain per SM helps (B256 T512 H8: 24.9 -> 19.8 ms against one CTA at 189
+// registers).
+#ifndef BSSM_D64_BWD_MINB
+#define BSSM_D64_BWD_MINB 2
+#endif
 template <bool FIXED, bool NEED_DYN, bool NEED_INIT>
-__global__ void __launch_bounds__(kThreads, 1) d64_backward(const BwdArgs<float> A) {
+__global__ void __launch_bounds__(kThreads, BSSM_D64_BWD_MINB) d64_backward(const BwdArgs<float> A) {
     extern __shared__ __align__(16) char smem_raw[];
     BwdSmem &sm = *reinterpret_cast<BwdSmem *>(smem_raw);
     const long chain = blockIdx.x;
