@@ -43,9 +43,8 @@ constexpr int kThreads = 256;
 // Tokens per span (one thread walks one span) and the widest channel group,
 // per direction, as measured at the config-3 mixer shape (B256 T512 H64 D8):
 // forward 4 channels over 64 tokens (0.71 ms; 2 over 128: 0.87 ms; 8 over
-// 32: 1.27 ms), backward 2 over 128 without unrolling the walk (1.92 ms;
-// 4 over 64: 2.0-3.4 ms; unrolled by 2 or 4: 2.65 ms).  Both kernels are
-// bound by instruction issue and load latency, not DRAM.
+// 32: 1.27 ms), backward 2 over 128 (before its load ring: 1.92 ms; 4 over
+// 64: 2.0-3.4 ms; the walk unrolled by 2 or 4: 2.65 ms).
 #ifndef BSSM_ENV_FWD_SPAN
 #define BSSM_ENV_FWD_SPAN 64
 #endif
@@ -55,29 +54,47 @@ constexpr int kThreads = 256;
 #ifndef BSSM_ENV_FWD_CW
 #define BSSM_ENV_FWD_CW 4
 #endif
+// Tokens of loads each walk keeps in flight per thread (powers of two; per
+// token and thread the forward's ring holds 16 bytes of shared memory, the
+// backward's 2 x 8).
+#ifndef BSSM_ENV_FWD_RING
+#define BSSM_ENV_FWD_RING 8
+#endif
+#ifndef BSSM_ENV_BWD_RING
+#define BSSM_ENV_BWD_RING 8
+#endif
+#ifndef BSSM_ENV_BWD_RING4  // the backward's ring with four channels per thread
+#define BSSM_ENV_BWD_RING4 4
+#endif
+// Channels per thread in the backward where the shape allows four (2: always two).
 #ifndef BSSM_ENV_BWD_CW
-#define BSSM_ENV_BWD_CW 2
+#define BSSM_ENV_BWD_CW 4
 #endif
-#ifndef BSSM_ENV_BWD_UNROLL
-#define BSSM_ENV_BWD_UNROLL 1
-#endif
-// CTAs per SM the compiler sizes registers for (launch-bounds minimum): the
-// walks are bound by load latency, so occupancy beats registers here
-// (backward 2.61 -> 1.63 ms, forward 0.89 -> 0.72 ms on one box against 1 / 1;
-// 5 / 6 spilled more and was slower; 3 in the backward: 1.92 ms).  Issuing
-// the backward walk's loads one token ahead (double-buffered in registers)
-// was neutral with FP32 outputs (1.617 against 1.628 ms) and slower with
-// BF16 ones (1.71 against 1.65 ms).
+// CTAs per SM the compiler sizes registers for (launch-bounds minimum; the
+// backward's with two and with four channels per thread).  Before the load
+// rings the walks were bound by load latency and occupancy won (5 / 4:
+// forward 0.72 ms, backward 1.63 ms, against 0.89 / 2.61 ms at 1 / 1; issuing
+// the backward's loads one token ahead in registers was neutral).  With the
+// rings (8 tokens; 4 times the same) neither spills at 3 / 3 / 2: forward
+// 0.44 ms (0.49 at 4), backward 0.97 ms with four channels per thread (1.35 at
+// 3 CTAs, which spills) and 1.01 ms with two.
 #ifndef BSSM_ENV_FWD_MINB
-#define BSSM_ENV_FWD_MINB 5
+#define BSSM_ENV_FWD_MINB 3
 #endif
 #ifndef BSSM_ENV_BWD_MINB
-#define BSSM_ENV_BWD_MINB 4
+#define BSSM_ENV_BWD_MINB 3
+#endif
+#ifndef BSSM_ENV_BWD_MINB4
+#define BSSM_ENV_BWD_MINB4 2
 #endif
 constexpr int kFwdSpan = BSSM_ENV_FWD_SPAN, kBwdSpan = BSSM_ENV_BWD_SPAN;
-constexpr int kFwdCW = BSSM_ENV_FWD_CW, kBwdCW = BSSM_ENV_BWD_CW;
+constexpr int kFwdCW = BSSM_ENV_FWD_CW;
+constexpr int kFwdRing = BSSM_ENV_FWD_RING, kRing = BSSM_ENV_BWD_RING, kRing4 = BSSM_ENV_BWD_RING4;
+constexpr int kBwdCW = BSSM_ENV_BWD_CW;
+static_assert(kRing4 >= 1 && (kRing4 & (kRing4 - 1)) == 0, "ring of a power of two tokens");
+static_assert(kFwdRing >= 1 && (kFwdRing & (kFwdRing - 1)) == 0, "ring of a power of two tokens");
+static_assert(kRing >= 1 && (kRing & (kRing - 1)) == 0, "ring of a power of two tokens");
 constexpr int kRowGroups = 64;  // first-pass row groups of the gradient sums
-constexpr int kBwdUnroll = BSSM_ENV_BWD_UNROLL;
 constexpr float kNormEps = 1e-12f;  // F.normalize's default
 constexpr float kNoiseFloor = 1e-4f;
 
@@ -220,6 +237,18 @@ __device__ __forceinline__ float lane_sum(float v, int lanes) {
     for (int off = 1; off < lanes; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
     return v;
 }
+// The same with the lane count fixed at compile time (L > 0) or read at run
+// time (L = 0).
+template <int L>
+__device__ __forceinline__ float lane_sum_n(float v, int lanes) {
+    if constexpr (L == 0) {
+        return lane_sum(v, lanes);
+    } else {
+#pragma unroll
+        for (int off = 1; off < L; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        return v;
+    }
+}
 
 // How a thread's CW channels map onto heads of D (q, k, decay): one head
 // spread over D / CW lanes (D >= CW), or CW / D whole heads (D < CW).
@@ -234,6 +263,57 @@ __device__ __forceinline__ HeadMap head_map(int d) {
     return d >= CW ? HeadMap{CW, 1, d / CW, 31 - __clz(CW)} : HeadMap{d, CW / d, 1, 31 - __clz(d)};
 }
 
+// Work of one warp: 32 consecutive channel groups of one (batch row, token
+// span).  Warps, not CTAs, tile the (row, span) pairs, so a pair whose groups
+// are not a multiple of the CTA's 256 leaves no partly-empty CTA behind.
+struct Work {
+    long bb;
+    int span, grp;
+    bool live;
+};
+template <int CW>
+__device__ __forceinline__ Work work_of(const Shape &s) {
+    const int wpr = ((s.conv_channels() + s.aux_channels()) / CW + 31) / 32;  // warps per (row, span)
+    const long gw = static_cast<long>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+    const long row = gw / wpr;
+    const int wi = static_cast<int>(gw - row * wpr);
+    return {row / s.tsplit, static_cast<int>(row % s.tsplit), wi * 32 + static_cast<int>(threadIdx.x & 31),
+            row < s.b * s.tsplit};
+}
+
+// Per-thread load rings.  Both walks stream their per-token loads a few
+// tokens ahead through shared memory (cp.async, zero-filled where a token or
+// a gradient is absent), so each warp keeps several tokens of loads in
+// flight instead of one.  Each thread reads back only its own copies, so a
+// ring needs no barrier: cp.async.wait_group orders them.
+__device__ __forceinline__ uint32_t shared_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+template <int G>
+__device__ __forceinline__ void cp_async_zfill(uint32_t dst, const void *src, bool on) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;\n" ::"r"(dst), "l"(src), "n"(G), "r"(on ? G : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// N elements (BF16 or FP32) from the front of a ring slot, as floats.
+template <bool BF, int N, class W>
+__device__ __forceinline__ void unpack(const W &raw, float *v) {
+    const unsigned *u = reinterpret_cast<const unsigned *>(&raw);
+    static_assert(sizeof(W) >= N * (BF ? 2 : 4), "slot too small");
+#pragma unroll
+    for (int i = 0; i < (BF ? N / 2 : N); ++i) {
+        if constexpr (BF) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(u + i));
+            v[2 * i] = f.x, v[2 * i + 1] = f.y;
+        } else {
+            v[i] = __uint_as_float(u[i]);
+        }
+    }
+}
+
 struct ProArgs {
     const void *x;
     const float *w;     // [C][4]
@@ -245,12 +325,17 @@ struct ProArgs {
 
 // Thread = CW adjacent channels of one stream (every stream and head row
 // boundary falls on a multiple of CW), walking one token span.
-template <bool IN_BF, bool OUT_BF, int CW>
+// L > 0: every q / k head spans exactly L lanes (key dim L * CW), fixed at
+// compile time; L = 0: read from the shape, heads of fewer than CW channels
+// included.
+template <bool IN_BF, bool OUT_BF, int CW, int L>
 __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(const Shape s, const ProArgs a) {
-    const int grp = static_cast<int>(blockIdx.x) * kThreads + threadIdx.x;
-    const long bb = blockIdx.z;
+    const Work wk = work_of<CW>(s);
+    if (!wk.live) return;  // past the last (batch row, span): the whole warp (no block barriers here)
+    const int grp = wk.grp;
+    const long bb = wk.bb;
     const long span = (s.t + s.tsplit - 1) / s.tsplit;
-    const long t0 = static_cast<long>(blockIdx.y) * span;
+    const long t0 = wk.span * span;
     const long t1 = t0 + span < s.t ? t0 + span : s.t;
     const int c0 = CW * grp;
     const Chan ch = c0 < s.conv_channels() + s.aux_channels() ? classify(s, c0 / 2) : Chan{kIdle, 0, 0};
@@ -283,11 +368,28 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
         if (t0 - 2 >= 0) ldn<IN_BF, CW>(a.x, (row0 + t0 - 2) * s.in_stride + c0, xm2);
         if (t0 - 1 >= 0) ldn<IN_BF, CW>(a.x, (row0 + t0 - 1) * s.in_stride + c0, xm1);
     }
-#pragma unroll 4
-    for (long t = t0; t < t1; ++t) {
+    // ring of the next kFwdRing tokens' projection elements (step k = token t0 + k)
+    constexpr int XS = CW * (IN_BF ? 2 : 4);
+    static_assert(XS <= 16, "one cp.async per token");
+    __shared__ uint4 ring[kFwdRing][kThreads];
+    const char *const xb = static_cast<const char *>(a.x);
+    const long xstep = s.in_stride * (XS / CW);
+    const char *const xrow = xb + row0 * xstep + c0 * static_cast<long>(XS / CW);
+    const int steps = static_cast<int>(t1 - t0);
+    const char *xp = xrow + t0 * xstep;  // the next token to issue
+    auto issue = [&](int k) {
+        const bool on = k < steps && ch.kind != kIdle;
+        cp_async_zfill<XS>(shared_addr(&ring[k & (kFwdRing - 1)][threadIdx.x]), on ? xp : xb, on);
+        xp += xstep;
+        cp_async_commit_group();
+    };
 #pragma unroll
-        for (int j = 0; j < CW; ++j) x[j] = 0.f;
-        if (ch.kind != kIdle) ldn<IN_BF, CW>(a.x, (row0 + t) * s.in_stride + c0, x);
+    for (int k = 0; k < kFwdRing; ++k) issue(k);
+#pragma unroll 4
+    for (int k = 0; k < steps; ++k) {
+        const long t = t0 + k;
+        cp_async_wait_group<kFwdRing - 1>();
+        unpack<IN_BF, CW>(ring[k & (kFwdRing - 1)][threadIdx.x], x);
         float ss[CW];
 #pragma unroll
         for (int j = 0; j < CW; ++j) {
@@ -299,11 +401,11 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
             xm1[j] = x[j];
         }
         const bool qk = ch.kind == kQ || ch.kind == kK;
-        if (hm.ng == 1) {  // one head (part) per thread: reduce across its lanes
+        if (L > 0 || hm.ng == 1) {  // one head (part) per thread: reduce across its lanes
             float tot = 0.f;
 #pragma unroll
             for (int j = 0; j < CW; ++j) tot += ss[j];
-            tot = lane_sum(qk ? tot : 0.f, hm.lanes);
+            tot = lane_sum_n<L>(qk ? tot : 0.f, hm.lanes);
             if (qk) {
                 const float r = inv_norm(tot);
 #pragma unroll
@@ -331,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
             float dcy[CW];
 #pragma unroll
             for (int j = 0; j < CW; ++j) dcy[j] = decay_of(x[j] + bias[j]);
-            if (hm.ng == 1) {
+            if (L > 0 || hm.ng == 1) {
                 stn<false, CW>(a.decay, (chain * s.t + t) * s.d + ch.within, dcy);
             } else {
                 st_heads<false, CW>(a.decay, chain, t, s.t, s.d, dcy);
@@ -343,7 +445,9 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
                 a.observation[(chain + i) * s.t + t] = softplus(x[2 * i + 1] + bias[2 * i + 1]) + kNoiseFloor;
             }
         }
+        issue(k + kFwdRing);  // after the slot's values were used
     }
+    cp_async_wait_group<0>();
 }
 
 struct EnvBwdArgs {
@@ -361,24 +465,38 @@ struct EnvBwdArgs {
 // gx[t] = sum_j w_j gc[t + 3 - j].  The span also recomputes the 3 tokens
 // after it (their gc feeds its last gx) without counting them in the weight
 // gradient, which their own span does.
-template <bool IN_BF, bool OUT_BF, int CW>
-__global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward_kernel(const Shape s,
-                                                                                      const EnvBwdArgs a) {
-    const int grp = static_cast<int>(blockIdx.x) * kThreads + threadIdx.x;
-    const long bb = blockIdx.z;
+//
+// A thread owns CW = 2 or 4 adjacent channels, never more than one q / k head
+// (the host takes CW = 4 only for key dims >= 4), so a head spans d / CW
+// whole lanes; L is that lane count when the host fixes it at compile time
+// (0: read from the shape).  Its ring holds, per token, the projection
+// elements and the incoming gradients of its channels.
+template <bool IN_BF, bool OUT_BF, int CW, int L>
+__global__ void __launch_bounds__(kThreads, CW == 4 ? BSSM_ENV_BWD_MINB4 : BSSM_ENV_BWD_MINB)
+    prologue_backward_kernel(const Shape s, const EnvBwdArgs a) {
+    static_assert(CW == 2 || CW == 4, "two or four channels per thread");
+    constexpr int XS = CW * (IN_BF ? 2 : 4), GS = CW * (OUT_BF ? 2 : 4);  // bytes per token
+    constexpr int R = CW == 2 ? kRing : kRing4;
+    using Slot = typename std::conditional<CW == 2, uint2, uint4>::type;
+    __shared__ Slot ring_x[R][kThreads], ring_g[R][kThreads];
+    const Work wk = work_of<CW>(s);
+    if (!wk.live) return;  // past the last (batch row, span): the whole warp (no block barriers here)
+    const int grp = wk.grp;
+    const long bb = wk.bb;
     const long span = (s.t + s.tsplit - 1) / s.tsplit;
-    const long t0 = static_cast<long>(blockIdx.y) * span;
+    const long t0 = wk.span * span;
     const long t1 = t0 + span < s.t ? t0 + span : s.t;
     const long hi = t1 + 3 < s.t ? t1 + 3 : s.t;
     const int c0 = CW * grp;
     const int C = s.conv_channels();
     const Chan ch = c0 < C + s.aux_channels() ? classify(s, c0 / 2) : Chan{kIdle, 0, 0};
-    const HeadMap hm = head_map<CW>(s.d);
+    const int lanes = L > 0 ? L : s.d / CW;  // lanes per q / k head
     const long row0 = bb * s.t;
     const long chain = bb * s.heads + ch.head;
     const bool conv = ch.kind <= kV;
     const bool qk = ch.kind == kQ || ch.kind == kK;
-    float *const part = a.partial + (bb * s.tsplit + blockIdx.y) * static_cast<long>(s.partial_cols());
+    const bool aux = ch.kind == kDecay || ch.kind == kNoise;
+    float *const part = a.partial + (bb * s.tsplit + wk.span) * static_cast<long>(s.partial_cols());
     float w[4][CW], bias[CW], gw[4][CW], gb[CW];
 #pragma unroll
     for (int j = 0; j < CW; ++j) {
@@ -392,34 +510,94 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
             const float4 wj = *reinterpret_cast<const float4 *>(a.w + (c0 + j) * 4);
             w[0][j] = wj.x, w[1][j] = wj.y, w[2][j] = wj.z, w[3][j] = wj.w;
         }
-    } else if (ch.kind != kIdle && a.bias != nullptr) {
+    } else if (aux && a.bias != nullptr) {
 #pragma unroll
         for (int j = 0; j < CW; ++j) bias[j] = a.bias[c0 - C + j];
     }
-    auto ldx = [&](long t, float *v) {
+    // Byte addresses of these channels at token 0 and per token: the
+    // projection row, and the incoming gradient -- a [B*H, T, .] row for
+    // q / k / v or the decay, or the per-chain variances (gsrc: the process
+    // variance of the first chain, gsrc2: its observation variance; the
+    // second chain's, for CW = 4, sit T floats further on).
+    const char *const xb = static_cast<const char *>(a.x);
+    const long xstep = s.in_stride * (XS / CW);
+    const char *const xrow = xb + row0 * xstep + c0 * static_cast<long>(XS / CW);
+    const char *gsrc = nullptr, *gsrc2 = nullptr;
+    long gstep = 0;
+    if (conv) {
+        gstep = (ch.kind == kV ? s.hd : s.d) * static_cast<long>(GS / CW);
+        gsrc = static_cast<const char *>(ch.kind == kQ ? a.gq : ch.kind == kK ? a.gk : a.gv);
+        if (gsrc) gsrc += chain * s.t * gstep + ch.within * static_cast<long>(GS / CW);
+    } else if (ch.kind == kDecay) {
+        gstep = s.d * 4L;
+        gsrc = reinterpret_cast<const char *>(a.gdecay);
+        if (gsrc) gsrc += chain * s.t * gstep + ch.within * 4L;
+    } else if (ch.kind == kNoise) {
+        gstep = 4;
+        gsrc = reinterpret_cast<const char *>(a.gprocess);
+        gsrc2 = reinterpret_cast<const char *>(a.gobservation);
+        if (gsrc) gsrc += chain * s.t * 4L;
+        if (gsrc2) gsrc2 += chain * s.t * 4L;
+    }
+    const long chain_bytes = s.t * 4L;  // between two chains' variance rows
+    // Step k of the walk is token hi - 1 - k: conv channels need x[t - 3]
+    // (x[t .. t - 2] are in registers), the auxiliary ones x[t] inside the span.
+    const int steps = static_cast<int>(hi - t0);
+    const char *xp = xrow + (conv ? hi - 4 : hi - 1) * xstep;  // step 0's loads; each step moves one token down
+    const char *gq1 = gsrc ? gsrc + (hi - 1) * gstep : nullptr;
+    const char *gq2 = gsrc2 ? gsrc2 + (hi - 1) * gstep : nullptr;
+    auto issue = [&](int k) {
+        const long t = hi - 1 - k;
+        const int slot = k & (R - 1);
+        const bool live = k < steps && ch.kind != kIdle;
+        const bool xon = live && (conv ? t >= 3 : t < t1);
+        cp_async_zfill<XS>(shared_addr(&ring_x[slot][threadIdx.x]), xon ? xp : xb, xon);
+        const bool gon = live && (conv || t < t1);
+        const bool on1 = gon && gq1 != nullptr, on2 = gon && gq2 != nullptr;
+        const uint32_t gdst = shared_addr(&ring_g[slot][threadIdx.x]);
+        if (ch.kind == kNoise) {  // (process, observation) of CW / 2 chains
 #pragma unroll
-        for (int j = 0; j < CW; ++j) v[j] = 0.f;
-        if (t >= 0 && ch.kind != kIdle) ldn<IN_BF, CW>(a.x, (row0 + t) * s.in_stride + c0, v);
+            for (int i = 0; i < CW / 2; ++i) {
+                cp_async_zfill<4>(gdst + 8 * i, on1 ? gq1 + i * chain_bytes : xb, on1);
+                cp_async_zfill<4>(gdst + 8 * i + 4, on2 ? gq2 + i * chain_bytes : xb, on2);
+            }
+        } else if (ch.kind == kDecay) {
+            cp_async_zfill<4 * CW>(gdst, on1 ? gq1 : xb, on1);
+        } else {
+            cp_async_zfill<GS>(gdst, on1 ? gq1 : xb, on1);
+        }
+        xp -= xstep;
+        if (gq1) gq1 -= gstep;
+        if (gq2) gq2 -= gstep;
+        cp_async_commit_group();
     };
-    const void *gsrc = ch.kind == kQ ? a.gq : ch.kind == kK ? a.gk : a.gv;
-    const int grow = ch.kind == kV ? s.hd : s.d;
     // x0 = x[t], x1 = x[t-1], x2 = x[t-2], x3 = x[t-3] (conv channels)
     float x0[CW], x1[CW], x2[CW], x3[CW];
     float gp1[CW], gp2[CW], gp3[CW];  // gc[t+1], gc[t+2], gc[t+3]
 #pragma unroll
     for (int j = 0; j < CW; ++j) x0[j] = x1[j] = x2[j] = x3[j] = gp1[j] = gp2[j] = gp3[j] = 0.f;
+    auto ldx = [&](long t, float *v) {
+        if (t >= 0) ldn<IN_BF, CW>(a.x, (row0 + t) * s.in_stride + c0, v);
+    };
     if (conv && hi > t0) {
         ldx(hi - 1, x0);
         ldx(hi - 2, x1);
         ldx(hi - 3, x2);
     }
-#pragma unroll (kBwdUnroll)
-    for (long t = hi - 1; t >= t0; --t) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) issue(k);
+    for (int k = 0; k < steps; ++k) {
+        const long t = hi - 1 - k;
+        cp_async_wait_group<R - 1>();
+        const int slot = k & (R - 1);
+        const Slot rx = ring_x[slot][threadIdx.x], rg = ring_g[slot][threadIdx.x];
         float gc[CW], g[CW], o[CW], ds[CW];
 #pragma unroll
-        for (int j = 0; j < CW; ++j) gc[j] = g[j] = o[j] = ds[j] = 0.f;
+        for (int j = 0; j < CW; ++j) gc[j] = o[j] = ds[j] = 0.f;
+        unpack<false, CW>(rg, g);  // decay / variance gradients (FP32)
         if (conv) {
-            ldx(t - 3, x3);
+            unpack<IN_BF, CW>(rx, x3);
+            unpack<OUT_BF, CW>(rg, g);
 #pragma unroll
             for (int j = 0; j < CW; ++j) {
                 const float c = fmaf(w[3][j], x0[j], fmaf(w[2][j], x1[j], fmaf(w[1][j], x2[j], w[0][j] * x3[j])));
@@ -427,45 +605,23 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
                 o[j] = c * sg;
                 ds[j] = sg * fmaf(c, 1.f - sg, 1.f);  // silu'
             }
-            if (gsrc != nullptr) {
-                if (hm.ng == 1 || ch.kind == kV) {
-                    ldn<OUT_BF, CW>(gsrc, (chain * s.t + t) * grow + ch.within, g);
-                } else {
-                    ld_heads<OUT_BF, CW>(gsrc, chain, t, s.t, s.d, g);
-                }
-            }
         }
         // q, k: y = s / max(|s|, eps); dy/ds = (I - y y^T) / |s| above eps, I / eps below
-        if (hm.ng == 1) {
+        {
             float ss = 0.f;
 #pragma unroll
             for (int j = 0; j < CW; ++j) ss += o[j] * o[j];
-            ss = lane_sum(qk ? ss : 0.f, hm.lanes);
+            ss = lane_sum_n<L>(qk ? ss : 0.f, lanes);
             const float r = inv_norm(ss);
             const bool above = ss > kNormEps * kNormEps;
             float dot = 0.f;
 #pragma unroll
             for (int j = 0; j < CW; ++j) dot += o[j] * r * g[j];
-            dot = lane_sum(qk ? dot : 0.f, hm.lanes);
+            dot = lane_sum_n<L>(qk ? dot : 0.f, lanes);
             if (qk) {
                 const float dd = above ? dot : 0.f;
 #pragma unroll
                 for (int j = 0; j < CW; ++j) gc[j] = (g[j] - o[j] * r * dd) * r * ds[j];
-            }
-        } else if (qk) {
-            for (int gi = 0; gi < hm.ng; ++gi) {
-                float ss = 0.f, dot = 0.f;
-#pragma unroll
-                for (int j = 0; j < CW; ++j)
-                    if ((j >> hm.shift) == gi) ss += o[j] * o[j];
-                const float r = inv_norm(ss);
-#pragma unroll
-                for (int j = 0; j < CW; ++j)
-                    if ((j >> hm.shift) == gi) dot += o[j] * r * g[j];
-                const float dd = ss > kNormEps * kNormEps ? dot : 0.f;
-#pragma unroll
-                for (int j = 0; j < CW; ++j)
-                    if ((j >> hm.shift) == gi) gc[j] = (g[j] - o[j] * r * dd) * r * ds[j];
             }
         }
         if (ch.kind == kV) {
@@ -484,34 +640,19 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
                     gw[3][j] = fmaf(gc[j], x0[j], gw[3][j]);
                 }
                 stn<IN_BF, CW>(a.gx, (row0 + t) * a.gx_stride + c0, gx);
-            } else if (ch.kind == kDecay || ch.kind == kNoise) {
+            } else if (aux) {
                 float xv[CW], gz[CW];
-                ldx(t, xv);
+                unpack<IN_BF, CW>(rx, xv);
                 if (ch.kind == kDecay) {
-                    float gd[CW];
-#pragma unroll
-                    for (int j = 0; j < CW; ++j) gd[j] = 0.f;
-                    if (a.gdecay != nullptr) {
-                        if (hm.ng == 1) {
-                            ldn<false, CW>(a.gdecay, (chain * s.t + t) * s.d + ch.within, gd);
-                        } else {
-                            ld_heads<false, CW>(a.gdecay, chain, t, s.t, s.d, gd);
-                        }
-                    }
 #pragma unroll
                     for (int j = 0; j < CW; ++j) {
                         // d/dz 1 / (1 + e^z) = -decay (1 - decay)
                         const float dcy = decay_of(xv[j] + bias[j]);
-                        gz[j] = -gd[j] * dcy * (1.f - dcy);
+                        gz[j] = -g[j] * dcy * (1.f - dcy);
                     }
-                } else {
+                } else {  // (process, observation) pairs
 #pragma unroll
-                    for (int i = 0; i < CW / 2; ++i) {
-                        const float gpv = a.gprocess != nullptr ? __ldg(a.gprocess + (chain + i) * s.t + t) : 0.f;
-                        const float gov = a.gobservation != nullptr ? __ldg(a.gobservation + (chain + i) * s.t + t) : 0.f;
-                        gz[2 * i] = gpv * softplus_grad(xv[2 * i] + bias[2 * i]);
-                        gz[2 * i + 1] = gov * softplus_grad(xv[2 * i + 1] + bias[2 * i + 1]);
-                    }
+                    for (int j = 0; j < CW; ++j) gz[j] = g[j] * softplus_grad(xv[j] + bias[j]);
                 }
 #pragma unroll
                 for (int j = 0; j < CW; ++j) gb[j] += gz[j];
@@ -527,12 +668,14 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_BWD_MINB) prologue_backward
             x1[j] = x2[j];
             x2[j] = x3[j];
         }
+        issue(k + R);  // after the slot's values were used
     }
+    cp_async_wait_group<0>();
     if (conv) {
 #pragma unroll
         for (int j = 0; j < CW; ++j)  // [c][4]: 16-byte aligned (rows are multiples of 8 floats)
             *reinterpret_cast<float4 *>(part + (c0 + j) * 4) = make_float4(gw[0][j], gw[1][j], gw[2][j], gw[3][j]);
-    } else if (ch.kind == kDecay || ch.kind == kNoise) {
+    } else if (aux) {
 #pragma unroll
         for (int j = 0; j < CW; ++j) part[4 * C + (c0 - C) + j] = gb[j];
     }
@@ -816,33 +959,56 @@ bool cw_fits(const Shape &s, long other_stride, const void *const *ptrs, int npt
     return true;
 }
 
+// One warp per 32 channel groups of each (batch row, span); see work_of.
+bool too_many_ctas(const Shape &s) {  // two channels per thread launch the most
+    const long wpr = ((s.conv_channels() + s.aux_channels()) / 2 + 31) / 32;
+    return (s.b * s.tsplit * wpr + kThreads / 32 - 1) / (kThreads / 32) > 0x7fffffffL;
+}
 template <int CW>
 dim3 grid_of(const Shape &s) {
-    const int groups = (s.conv_channels() + s.aux_channels()) / CW;
-    return dim3((groups + kThreads - 1) / kThreads, s.tsplit, static_cast<unsigned>(s.b));
+    const long wpr = ((s.conv_channels() + s.aux_channels()) / CW + 31) / 32;
+    const long warps = s.b * s.tsplit * wpr;
+    return dim3(static_cast<unsigned>((warps + kThreads / 32 - 1) / (kThreads / 32)));
 }
 
-template <int CW>
+template <int CW, int L>
 void launch_fwd(const Shape &s, const ProArgs &a, int in_dtype, int out_dtype, cudaStream_t st) {
     const dim3 g = grid_of<CW>(s);
     if (in_dtype == BSSM_BF16) {
-        if (out_dtype == BSSM_BF16) prologue_kernel<true, true, CW><<<g, kThreads, 0, st>>>(s, a);
-        else prologue_kernel<true, false, CW><<<g, kThreads, 0, st>>>(s, a);
+        if (out_dtype == BSSM_BF16) prologue_kernel<true, true, CW, L><<<g, kThreads, 0, st>>>(s, a);
+        else prologue_kernel<true, false, CW, L><<<g, kThreads, 0, st>>>(s, a);
     } else {
-        if (out_dtype == BSSM_BF16) prologue_kernel<false, true, CW><<<g, kThreads, 0, st>>>(s, a);
-        else prologue_kernel<false, false, CW><<<g, kThreads, 0, st>>>(s, a);
+        if (out_dtype == BSSM_BF16) prologue_kernel<false, true, CW, L><<<g, kThreads, 0, st>>>(s, a);
+        else prologue_kernel<false, false, CW, L><<<g, kThreads, 0, st>>>(s, a);
     }
 }
 
-template <int CW>
+template <int CW, int L>
 void launch_bwd(const Shape &s, const EnvBwdArgs &a, int in_dtype, int out_dtype, cudaStream_t st) {
     const dim3 g = grid_of<CW>(s);
     if (in_dtype == BSSM_BF16) {
-        if (out_dtype == BSSM_BF16) prologue_backward_kernel<true, true, CW><<<g, kThreads, 0, st>>>(s, a);
-        else prologue_backward_kernel<true, false, CW><<<g, kThreads, 0, st>>>(s, a);
+        if (out_dtype == BSSM_BF16) prologue_backward_kernel<true, true, CW, L><<<g, kThreads, 0, st>>>(s, a);
+        else prologue_backward_kernel<true, false, CW, L><<<g, kThreads, 0, st>>>(s, a);
     } else {
-        if (out_dtype == BSSM_BF16) prologue_backward_kernel<false, true, CW><<<g, kThreads, 0, st>>>(s, a);
-        else prologue_backward_kernel<false, false, CW><<<g, kThreads, 0, st>>>(s, a);
+        if (out_dtype == BSSM_BF16) prologue_backward_kernel<false, true, CW, L><<<g, kThreads, 0, st>>>(s, a);
+        else prologue_backward_kernel<false, false, CW, L><<<g, kThreads, 0, st>>>(s, a);
+    }
+}
+
+// Four channels per thread where the shape allows it (a thread then never
+// holds more than one q / k head: key dim >= 4), else two; the lanes per head
+// fixed at compile time for the common key dims.
+void dispatch_bwd(const Shape &s, const EnvBwdArgs &a, const void *const *aligned, int nal, int in_dtype,
+                  int out_dtype, cudaStream_t st) {
+    if (kBwdCW >= 4 && s.d >= 4 && cw_fits<4>(s, a.gx_stride, aligned, nal)) {
+        if (s.d == 4) launch_bwd<4, 1>(s, a, in_dtype, out_dtype, st);
+        else if (s.d == 8) launch_bwd<4, 2>(s, a, in_dtype, out_dtype, st);
+        else launch_bwd<4, 0>(s, a, in_dtype, out_dtype, st);
+    } else {
+        if (s.d == 2) launch_bwd<2, 1>(s, a, in_dtype, out_dtype, st);
+        else if (s.d == 4) launch_bwd<2, 2>(s, a, in_dtype, out_dtype, st);
+        else if (s.d == 8) launch_bwd<2, 4>(s, a, in_dtype, out_dtype, st);
+        else launch_bwd<2, 0>(s, a, in_dtype, out_dtype, st);
     }
 }
 
@@ -978,12 +1144,17 @@ int bssm_envelope_prologue(const void *projected, int in_dtype, long batch, long
     if (reinterpret_cast<uintptr_t>(conv_weight) & 15)
         return fail(BSSM_ERR_ALIGNMENT, "envelope prologue: conv_weight must be 16-byte aligned");
     s.tsplit = pick_tsplit(tokens, kFwdSpan);
-    if (s.tsplit > 65535) return fail(BSSM_ERR_INVALID, "envelope: sequence too long (%ld tokens)", tokens);
+    if (s.tsplit > 65535 || too_many_ctas(s))
+        return fail(BSSM_ERR_INVALID, "envelope: sequence too long (%ld tokens)", tokens);
     const ProArgs a{projected, conv_weight, aux_bias, keys, queries, values, decay, process, observation};
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (kFwdCW >= 8 && cw_fits<8>(s, 0, aligned8, 5)) launch_fwd<8>(s, a, in_dtype, out_dtype, st);
-    else if (kFwdCW >= 4 && cw_fits<4>(s, 0, aligned8, 5)) launch_fwd<4>(s, a, in_dtype, out_dtype, st);
-    else launch_fwd<2>(s, a, in_dtype, out_dtype, st);
+    if (kFwdCW >= 4 && cw_fits<4>(s, 0, aligned8, 5)) {
+        if (s.d == 4) launch_fwd<4, 1>(s, a, in_dtype, out_dtype, st);
+        else if (s.d == 8) launch_fwd<4, 2>(s, a, in_dtype, out_dtype, st);
+        else launch_fwd<4, 0>(s, a, in_dtype, out_dtype, st);
+    } else {
+        launch_fwd<2, 0>(s, a, in_dtype, out_dtype, st);
+    }
     return check_launch("envelope prologue");
 }
 
@@ -1012,7 +1183,8 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
     if (!projected || !conv_weight || !grad_projected || !workspace)
         return fail(BSSM_ERR_INVALID, "envelope backward: null pointer");
     s.tsplit = pick_tsplit(tokens, kBwdSpan);
-    if (s.tsplit > 65535) return fail(BSSM_ERR_INVALID, "envelope: sequence too long (%ld tokens)", tokens);
+    if (s.tsplit > 65535 || too_many_ctas(s))
+        return fail(BSSM_ERR_INVALID, "envelope: sequence too long (%ld tokens)", tokens);
     const long prow = batch * s.tsplit;
     const long need = (prow + kRowGroups) * static_cast<long>(pcols);
     if (workspace_floats < need)
@@ -1028,8 +1200,7 @@ int bssm_envelope_prologue_backward(const void *projected, int in_dtype, long ba
     const EnvBwdArgs a{projected, conv_weight, aux_bias, grad_keys, grad_queries, grad_values, grad_decay, grad_process,
                     grad_observation, grad_projected, grad_row_stride, workspace};
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (kBwdCW >= 4 && cw_fits<4>(s, grad_row_stride, aligned8, 6)) launch_bwd<4>(s, a, in_dtype, out_dtype, st);
-    else launch_bwd<2>(s, a, in_dtype, out_dtype, st);
+    dispatch_bwd(s, a, aligned8, 6, in_dtype, out_dtype, st);
     if (int rc = check_launch("envelope prologue backward")) return rc;
     // two passes, each summing rows in order: row groups, then the groups
     const long per = (prow + kRowGroups - 1) / kRowGroups;
