@@ -44,7 +44,7 @@ constexpr int kThreads = 256;
 // per direction, as measured at the config-3 mixer shape (B256 T512 H64 D8):
 // forward 4 channels over 64 tokens (0.71 ms; 2 over 128: 0.87 ms; 8 over
 // 32: 1.27 ms), backward 2 over 128 (before its load ring: 1.92 ms; 4 over
-// 64: 2.0-3.4 ms; the walk unrolled by 2 or 4: 2.65 ms).
+// 64: 2.0-3.4 ms; the walk unrolled by 2 or 4: 2.65 ms, with spills).
 #ifndef BSSM_ENV_FWD_SPAN
 #define BSSM_ENV_FWD_SPAN 64
 #endif
@@ -70,6 +70,12 @@ constexpr int kThreads = 256;
 #ifndef BSSM_ENV_BWD_CW
 #define BSSM_ENV_BWD_CW 4
 #endif
+// Unroll factor of the backward's token walk: the tokens' recomputations are
+// independent, so an unrolled walk overlaps them (4: 0.787 ms, 2: 0.809,
+// 1: 0.824).
+#ifndef BSSM_ENV_BWD_UNROLL
+#define BSSM_ENV_BWD_UNROLL 4
+#endif
 // CTAs per SM the compiler sizes registers for (launch-bounds minimum; the
 // backward's with two and with four channels per thread).  Before the load
 // rings the walks were bound by load latency and occupancy won (5 / 4:
@@ -90,7 +96,7 @@ constexpr int kThreads = 256;
 constexpr int kFwdSpan = BSSM_ENV_FWD_SPAN, kBwdSpan = BSSM_ENV_BWD_SPAN;
 constexpr int kFwdCW = BSSM_ENV_FWD_CW;
 constexpr int kFwdRing = BSSM_ENV_FWD_RING, kRing = BSSM_ENV_BWD_RING, kRing4 = BSSM_ENV_BWD_RING4;
-constexpr int kBwdCW = BSSM_ENV_BWD_CW;
+constexpr int kBwdCW = BSSM_ENV_BWD_CW, kBwdUnroll = BSSM_ENV_BWD_UNROLL;
 static_assert(kRing4 >= 1 && (kRing4 & (kRing4 - 1)) == 0, "ring of a power of two tokens");
 static_assert(kFwdRing >= 1 && (kFwdRing & (kFwdRing - 1)) == 0, "ring of a power of two tokens");
 static_assert(kRing >= 1 && (kRing & (kRing - 1)) == 0, "ring of a power of two tokens");
@@ -385,8 +391,13 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
     };
 #pragma unroll
     for (int k = 0; k < kFwdRing; ++k) issue(k);
+    // element index of this thread's output row at the current token (q / k /
+    // decay rows of d, v rows of hd), and of its chains' variances
+    const long ostep = ch.kind == kV ? s.hd : s.d;
+    long oidx = (chain * s.t + t0) * ostep + ch.within;
+    long nidx = chain * s.t + t0;
 #pragma unroll 4
-    for (int k = 0; k < steps; ++k) {
+    for (int k = 0; k < steps; ++k, oidx += ostep, ++nidx) {
         const long t = t0 + k;
         cp_async_wait_group<kFwdRing - 1>();
         unpack<IN_BF, CW>(ring[k & (kFwdRing - 1)][threadIdx.x], x);
@@ -410,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
                 const float r = inv_norm(tot);
 #pragma unroll
                 for (int j = 0; j < CW; ++j) o[j] *= r;
-                stn<OUT_BF, CW>(ch.kind == kQ ? a.q : a.k, (chain * s.t + t) * s.d + ch.within, o);
+                stn<OUT_BF, CW>(ch.kind == kQ ? a.q : a.k, oidx, o);
             }
         } else if (qk) {  // CW / D whole heads
 #pragma unroll
@@ -428,21 +439,21 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
             st_heads<OUT_BF, CW>(ch.kind == kQ ? a.q : a.k, chain, t, s.t, s.d, o);
         }
         if (ch.kind == kV) {
-            stn<OUT_BF, CW>(a.v, (chain * s.t + t) * s.hd + ch.within, o);
+            stn<OUT_BF, CW>(a.v, oidx, o);
         } else if (ch.kind == kDecay) {
             float dcy[CW];
 #pragma unroll
             for (int j = 0; j < CW; ++j) dcy[j] = decay_of(x[j] + bias[j]);
             if (L > 0 || hm.ng == 1) {
-                stn<false, CW>(a.decay, (chain * s.t + t) * s.d + ch.within, dcy);
+                stn<false, CW>(a.decay, oidx, dcy);
             } else {
                 st_heads<false, CW>(a.decay, chain, t, s.t, s.d, dcy);
             }
         } else if (ch.kind == kNoise) {
 #pragma unroll
             for (int i = 0; i < CW / 2; ++i) {
-                a.process[(chain + i) * s.t + t] = softplus(x[2 * i] + bias[2 * i]) + kNoiseFloor;
-                a.observation[(chain + i) * s.t + t] = softplus(x[2 * i + 1] + bias[2 * i + 1]) + kNoiseFloor;
+                a.process[nidx + i * s.t] = softplus(x[2 * i] + bias[2 * i]) + kNoiseFloor;
+                a.observation[nidx + i * s.t] = softplus(x[2 * i + 1] + bias[2 * i + 1]) + kNoiseFloor;
             }
         }
         issue(k + kFwdRing);  // after the slot's values were used
@@ -586,7 +597,9 @@ __global__ void __launch_bounds__(kThreads, CW == 4 ? BSSM_ENV_BWD_MINB4 : BSSM_
     }
 #pragma unroll
     for (int k = 0; k < R; ++k) issue(k);
-    for (int k = 0; k < steps; ++k) {
+    long gxi = (row0 + hi - 1) * a.gx_stride + c0;  // element of gx at the current token
+#pragma unroll(kBwdUnroll)
+    for (int k = 0; k < steps; ++k, gxi -= a.gx_stride) {
         const long t = hi - 1 - k;
         cp_async_wait_group<R - 1>();
         const int slot = k & (R - 1);
@@ -639,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, CW == 4 ? BSSM_ENV_BWD_MINB4 : BSSM_
                     gw[2][j] = fmaf(gc[j], x1[j], gw[2][j]);
                     gw[3][j] = fmaf(gc[j], x0[j], gw[3][j]);
                 }
-                stn<IN_BF, CW>(a.gx, (row0 + t) * a.gx_stride + c0, gx);
+                stn<IN_BF, CW>(a.gx, gxi, gx);
             } else if (aux) {
                 float xv[CW], gz[CW];
                 unpack<IN_BF, CW>(rx, xv);
@@ -656,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, CW == 4 ? BSSM_ENV_BWD_MINB4 : BSSM_
                 }
 #pragma unroll
                 for (int j = 0; j < CW; ++j) gb[j] += gz[j];
-                stn<IN_BF, CW>(a.gx, (row0 + t) * a.gx_stride + c0, gz);
+                stn<IN_BF, CW>(a.gx, gxi, gz);
             }
         }
 #pragma unroll
