@@ -30,6 +30,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <type_traits>
 
@@ -1081,18 +1082,26 @@ void launch_norm(const void *x, int dt, const float *w, const void *gy, void *ou
 }
 
 // Backward grid: one full wave (resident CTAs per SM x SMs), at most `cap`.
+// The wave is queried once per device and dtype, then cached.
 template <int CPL>
 int norm_wave(int dt, int cap) {
+    constexpr int kMaxDevices = 64;
+    static std::atomic<int> cached[kMaxDevices][2];  // 0: not queried yet
     int dev = 0, sms = 0, per_sm = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return cap;
-    const cudaError_t err =
-        dt == BSSM_BF16
-            ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_backward_kernel<true, CPL>, kThreads, 0)
-            : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_backward_kernel<false, CPL>, kThreads, 0);
-    if (err != cudaSuccess || per_sm <= 0) return cap;
-    const long wave = static_cast<long>(per_sm) * sms;
-    return static_cast<int>(wave < cap ? wave : cap);
+    if (cudaGetDevice(&dev) != cudaSuccess) return cap;
+    const int bf = dt == BSSM_BF16 ? 1 : 0;
+    int wave = dev >= 0 && dev < kMaxDevices ? cached[dev][bf].load(std::memory_order_relaxed) : 0;
+    if (wave == 0) {
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return cap;
+        const cudaError_t err =
+            bf ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_backward_kernel<true, CPL>, kThreads, 0)
+               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_backward_kernel<false, CPL>, kThreads, 0);
+        if (err != cudaSuccess || per_sm <= 0) return cap;
+        const long w = static_cast<long>(per_sm) * sms;
+        wave = static_cast<int>(w < 0x7fffffffL ? w : 0x7fffffffL);
+        if (dev >= 0 && dev < kMaxDevices) cached[dev][bf].store(wave, std::memory_order_relaxed);
+    }
+    return wave < cap ? wave : cap;
 }
 
 int norm_wave_w(int width, int dt, int cap) {

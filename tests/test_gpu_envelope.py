@@ -7,7 +7,7 @@ and the auxiliary bias are compared with torch autograd of
 bfloat16 projections or outputs: rel-L2 <= 4e-3, a few BF16 ulps).  The cases
 cover token spans shorter than the convolution window, span boundaries of the
 kernel's token split, odd head counts (padded partial-sum rows), key_dim 2
-to 16, and the prologue feeding the recurrence end to end.
+to 32, and the prologue feeding the recurrence end to end.
 """
 from __future__ import annotations
 
@@ -34,11 +34,14 @@ def _inputs(b, t, h, d, hd, seed, dtype=torch.float32):
     return x.to(dtype).cuda(), wt.cuda(), bias.cuda()
 
 
-# (B, T, H, D, head_dim): channel-group widths 8/4/2 are picked by divisibility,
-# so these cover one head over several lanes (D >= width), several whole heads
-# per thread (D = 2, 4 below the width), and the 2-channel form
+# (B, T, H, D, head_dim): channel-group widths 4/2 are picked by divisibility
+# (an odd head count forces 2), so these cover one head over several lanes
+# (D >= width), several whole heads per thread (D = 2 below the forward's
+# width), and every compiled lane count: fixed 1/2/4 lanes per head (D = 2, 4,
+# 8 at either width) and the run-time count (D = 16, 32)
 CASES = [(2, 37, 4, 8, 8), (1, 300, 2, 8, 8), (3, 2, 3, 4, 6), (2, 65, 5, 2, 8), (1, 9, 2, 16, 4),
-         (4, 128, 8, 8, 8), (2, 50, 4, 2, 8), (2, 50, 4, 4, 8), (1, 64, 8, 2, 8), (1, 33, 4, 32, 8)]
+         (4, 128, 8, 8, 8), (2, 50, 4, 2, 8), (2, 50, 4, 4, 8), (1, 64, 8, 2, 8), (1, 33, 4, 32, 8),
+         (2, 40, 3, 8, 8), (1, 20, 3, 16, 8)]
 
 
 @pytest.mark.parametrize("shape", CASES)
