@@ -260,6 +260,7 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // (one state, 32 chains).
 struct FwdMaps {
     CUtensorMap k, q, v, a, p, r, y, gu, gb;  // gu, gb: gains and signed gain scales
+    int gains;  // the one-warp forward saves the gains (only the two-warp backward reads them)
 };
 struct BwdMaps {
     CUtensorMap k, q, v, a, p, r, gy, rs, gk, gv, gq, ga, gp, gr, gu, gb;
@@ -719,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_chain(const FwdArgs<TIn> 
             StateQuads<D, M>::put_cov(dst, P);
         }
         char *const yb = ob + G::yY;
-        const bool gains = A.rs != nullptr;
+        const bool gains = A.rs != nullptr && mp.gains != 0;
         float4 p4, r4, b4 = make_float4(0.f, 0.f, 0.f, 0.f);
         rd.noise(p4, r4);
         auto step = [&](int tau) {
@@ -1335,7 +1336,12 @@ __global__ void __launch_bounds__(kThreads, 1) backward_chain(const BwdArgs<TIn>
             float Mm[D][M];
             StateQuads<D, M>::get_mean(state, Mm);
             // every lane has read its start state and is done with the other
-            // stage: fetch the next sub-chunk while this one is processed
+            // stage: fetch the next sub-chunk while this one is processed.
+            // The next start state lands in the same box by TMA (async proxy);
+            // the proxy fence orders this lane's reads of the box before it.
+            // Without it a read still queued could see the next state: at two
+            // CTAs per SM that made the key-dim-2 gradients differ run to run.
+            fence_proxy_async();
             __syncwarp();
             if (!prod.done) {
                 issue_item(prod, static_cast<int>((q + 1) & 1));
@@ -1780,6 +1786,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             const float4 b4 = reinterpret_cast<const float4 *>(tile + G::oB)[lane];
             float P[TRI];
             StateQuads<D, M>::get_cov(state, P);
+            fence_proxy_async();  // these reads before the next state's TMA write (async proxy)
             __syncwarp();
             if (lane == 0) mbar_arrive(sfree);
             if (!nxt.done) issue_checkpoint_part(nxt);  // this warp's part of the row is read
@@ -1941,6 +1948,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             const float4 b4 = reinterpret_cast<const float4 *>(tile + G::oB)[lane];
             float Mm[D][M];
             StateQuads<D, M>::get_mean(state, Mm);
+            fence_proxy_async();  // these reads before the next state's TMA write (async proxy)
             __syncwarp();
             if (lane == 0) mbar_arrive(sfree);
             if (!nxt.done) {
@@ -2137,7 +2145,13 @@ int launch_fwd(const FwdArgs<TIn> &a, cudaStream_t st) {
     if (!FIXED)
         ok = ok && map_tok(&mp.a, a.decay, D, a.n, a.t) && map_rows(&mp.p, a.process, a.t, a.n, kS) &&
              map_rows(&mp.r, a.observation, a.t, a.n, kS);
-    if (a.rs != nullptr) {
+    // The saved gains feed only the two-warp backward (backward_split: key dim
+    // 8, learned dynamics, inputs its tiles fit); every other backward replays
+    // from the saved states and forms the gains itself, so for those shapes
+    // the forward skips the gain stores (12 bytes per chain-step at key dim 2).
+    constexpr bool kGainsRead = D == 8 && !FIXED && SplitGeo<8, 8, TIn>::kFits;
+    mp.gains = kGainsRead ? 1 : 0;
+    if (a.rs != nullptr && kGainsRead) {
         ok = ok && map_tok(&mp.gu, static_cast<const float *>(replay_gains(a.rs, a.n, a.t, a.chunks, D, M)), D,
                            a.n, a.t) &&
              map_rows(&mp.gb, replay_gain_scales(a.rs, a.n, a.t, a.chunks, D, M), a.t, a.n, kS);
