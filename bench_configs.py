@@ -32,6 +32,9 @@ headline, config 3, is ``bench.py``).
 * ``--config envelope-profile``: the prologue kernels alone at an eighth of
   that shape (B32), untimed: the case the prologue's ncu captures run on.
 
+* ``--config d64-profile``: the (64, 64) kernels on 296 chains (B37 T512 H8,
+  one wave at two CTAs per SM), untimed: the case their ncu captures run on.
+
 * ``--config refcuda``: the reference's own CUDA kernels on the same GPU --
   catid/bayes-ssm installed unmodified into ``baseline/_ref`` (``pip install
   --target``), its D8 extension JIT-built by its own loader
@@ -384,6 +387,47 @@ def d64(steps: int, warmup: int) -> dict:
             "family": _capi.last_family(), "steps": steps, "warmup": warmup, "data": "synthetic"}
 
 
+def d64_profile(steps: int, warmup: int) -> dict:
+    """The (64, 64) forward and backward on 296 chains (B37 T512 H8, chunk 64,
+    FP32): ``steps`` forward + backward pairs, untimed -- the small case an ncu
+    capture of ``d64_forward`` / ``d64_backward`` runs on (one wave at two CTAs
+    per SM, as every wave of the full launch)."""
+    import torch
+    import torch.nn.functional as F
+    from bayes_ssm import _capi
+    b, t, h, d, m, chunk, floor = 37, 512, 8, 64, 64, 64, 1e-6
+    n = b * h
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(64)
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=g, device=dev)
+
+    kk, qq = F.normalize(rn(n, t, d), dim=-1), F.normalize(rn(n, t, d), dim=-1)
+    vv, aa = rn(n, t, m) / math.sqrt(m), torch.sigmoid(2.0 + rn(n, t, d))
+    pp, rr = F.softplus(-4.0 + rn(n, t)), F.softplus(rn(n, t)) + 1e-4
+    gy = rn(n, t, m) / math.sqrt(m)
+    nb = (t + chunk - 1) // chunk
+    f32 = dict(device=dev, dtype=torch.float32)
+    out = torch.empty(n, t, m, **f32)
+    mt, pt = torch.empty(n, d, m, **f32), torch.empty(n, d, d, **f32)
+    bm, bc = torch.empty(n, nb + 1, d, m, **f32), torch.empty(n, nb + 1, d, d, **f32)
+    gk, gq, gv = torch.empty_like(kk), torch.empty_like(qq), torch.empty_like(vv)
+    gd, gp, gr = torch.empty(n, t, d, **f32), torch.empty(n, t, **f32), torch.empty(n, t, **f32)
+    wsb = _capi.workspace_bytes(d, m, n, t, chunk)
+    ws = torch.empty(max(wsb, 1), device=dev, dtype=torch.uint8)
+    sp = torch.cuda.current_stream().cuda_stream
+    for _ in range(steps):
+        _capi.forward_chunked(d, m, _capi.BSSM_F32, False, kk, vv, qq, aa, pp, rr, None, None, out, mt, pt, bm, bc,
+                              n, t, chunk, floor, sp)
+        _capi.backward_chunked(d, m, _capi.BSSM_F32, False, True, False, kk, vv, qq, aa, pp, rr, None, None, bm, bc,
+                               gy, None, None, gk, gv, gq, gd, gp, gr, None, None, ws, wsb, n, t, chunk, floor, sp)
+    torch.cuda.synchronize()
+    _capi.stream_status(sp)
+    return {"config": "d64-profile", "workload": "D64 M64 fwd + bwd, B37 T512 H8 = 296 chains (profiling case)",
+            "launches": 2 * steps, "timed": False}
+
+
 def envelope_profile(steps: int, warmup: int) -> dict:
     """The prologue kernels alone at an eighth of config 3's mixer shape
     (B32 T512, 64 heads, key_dim 8, head_dim 8, BF16 projection, FP32
@@ -538,12 +582,13 @@ def _peak_hbm() -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", choices=("2", "4", "d64", "envelope", "envelope-profile", "mixer", "refcuda",
-                                         "refcuda64"), required=True)
+    ap.add_argument("--config", choices=("2", "4", "d64", "d64-profile", "envelope", "envelope-profile", "mixer",
+                                         "refcuda", "refcuda64"), required=True)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()
-    fn = {"2": config2, "4": config4, "d64": d64, "envelope": envelope, "envelope-profile": envelope_profile,
+    fn = {"2": config2, "4": config4, "d64": d64, "d64-profile": d64_profile, "envelope": envelope,
+          "envelope-profile": envelope_profile,
           "mixer": mixer, "refcuda": refcuda, "refcuda64": refcuda64}[args.config]
     print(json.dumps(fn(args.steps, max(3, args.warmup))), flush=True)
 

@@ -104,3 +104,24 @@ def test_d64_api_autograd_and_bf16_promotion():
                                         process_variances=inp["p"].cuda(), observation_variances=inp["r"].cuda(),
                                         chunk_length=8, optimized=True)
     assert torch.equal(yb, yf)
+
+
+def test_d64_full_launch_bit_identical_run_to_run():
+    """2,048 chains (the bench shape's chain count, seven waves at two CTAs per
+    SM), T 128: three forward + backward runs on the same inputs agree bit for
+    bit in every output (a shared-memory race between co-resident CTAs or
+    between a warp's reads and the next copies shows up as differences)."""
+    n, t = 2048, 128
+    inp = make_inputs(n, t, D, M, seed=11, init="random")
+    gy, gmt, gpt = (x.cuda() for x in _grads_out(n, t, 11))
+    first = None
+    for _ in range(3):
+        fwd = capi_forward(inp, chunks=64)
+        got = capi_backward(inp, fwd, gy, gmt, gpt, chunks=64)
+        outs = {"y": fwd["y"], "M_T": fwd["MT"], "P_T": fwd["PT"], **{f"grad {x}": g for x, g in got.items()}}
+        if first is None:
+            first = {x: v.clone() for x, v in outs.items()}
+            continue
+        for x, v in outs.items():
+            assert torch.equal(v, first[x]), f"{x} differs between runs"
+

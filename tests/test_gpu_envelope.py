@@ -221,3 +221,26 @@ def test_rms_norm_matches_torch(width, dtype):
     tol_g = 1e-5 if dtype == torch.float32 else 8e-3
     for a_, b_ in zip(gk, gr):
         assert _rel(a_.float(), b_.float()) <= tol_g
+
+
+def test_prologue_full_shape_bit_identical_run_to_run():
+    """The config-3 mixer shape (B256 T512 H64 D8 head_dim 8, BF16 projection):
+    repeated forward + backward launches on the same inputs agree bit for bit
+    (per-thread load rings, warp-tiled grid, fixed-order gradient sums)."""
+    b, t, h, d, hd = 256, 512, 64, 8, 8
+    x, wt, bias = _inputs(b, t, h, d, hd, seed=5, dtype=torch.bfloat16)
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    first = None
+    for _ in range(3):
+        xk, wk, bk = (z.detach().clone().requires_grad_() for z in (x, wt, bias))
+        got = paper_prologue(xk, wk, bk, heads=h, key_dim=d, head_dim=hd)
+        if first is None:
+            ups = [torch.randn(r_.shape, generator=gen, device="cuda") for r_ in got]
+        grads = torch.autograd.grad(got, (xk, wk, bk), ups)
+        outs = [g_.detach() for g_ in got] + list(grads)
+        if first is None:
+            first = [o.clone() for o in outs]
+            continue
+        for i, (o, f) in enumerate(zip(outs, first)):
+            assert torch.equal(o, f), f"output {i} differs between runs"
+
