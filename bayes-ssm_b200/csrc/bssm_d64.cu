@@ -67,12 +67,69 @@ __device__ __forceinline__ void unpack(const float4 v, float (&o)[4]) {
     o[3] = v.w;
 }
 
-// Sum of 4 values over the 16 lanes of a half-warp (result in every lane).
+// Half-warp sums over the 16 lanes c = 0..15 (lane bits 3..0).  A butterfly
+// on every value would take 4 shuffles per value; these first scatter the
+// values over the lanes (at each of the two top levels a lane keeps half of
+// its values and sends the other half), so each sum is formed once, and the
+// lanes that need every sum gather them back.  Every lane holding a sum holds
+// the same bits, which keeps the covariance tiles exactly symmetric.
+__device__ __forceinline__ float shx(float v, int o) { return __shfl_xor_sync(0xffffffffu, v, o); }
+template <int N>
+__device__ __forceinline__ float pick(const float (&a)[N], int i) {
+    static_assert(N == 4, "four values");
+    return (i & 2) ? ((i & 1) ? a[3] : a[2]) : ((i & 1) ? a[1] : a[0]);
+}
+
+// Sum of value (c >> 2) & 3 of 4 values, in every lane of that group of four
+// lanes (5 shuffles instead of 16).
+__device__ __forceinline__ float hw_scatter4(const float (&x)[4]) {
+    const bool b3 = threadIdx.x & 8, b2 = threadIdx.x & 4;
+    float y[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) y[i] = (b3 ? x[2 + i] : x[i]) + shx(b3 ? x[i] : x[2 + i], 8);
+    float z = (b2 ? y[1] : y[0]) + shx(b2 ? y[0] : y[1], 4);
+    z += shx(z, 2);
+    z += shx(z, 1);
+    return z;
+}
+
+// Sums of 4 values, all of them in every lane (8 shuffles instead of 16).
 __device__ __forceinline__ void hw_sum4(float (&x)[4]) {
+    const bool b3 = threadIdx.x & 8, b2 = threadIdx.x & 4;
+    const float z = hw_scatter4(x), o = shx(z, 4);
+    const float y0 = b2 ? o : z, y1 = b2 ? z : o;  // values 2 b3 and 2 b3 + 1
+    const float p0 = shx(y0, 8), p1 = shx(y1, 8);
+    x[0] = b3 ? p0 : y0;
+    x[1] = b3 ? p1 : y1;
+    x[2] = b3 ? y0 : p0;
+    x[3] = b3 ? y1 : p1;
+}
+
+// Sums of 8 values, all of them in every lane (15 shuffles instead of 32).
+__device__ __forceinline__ void hw_sum8(float (&x)[8]) {
+    const bool b3 = threadIdx.x & 8, b2 = threadIdx.x & 4, b1 = threadIdx.x & 2;
+    float y[4], z[2];
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1)
+    for (int i = 0; i < 4; ++i) y[i] = (b3 ? x[4 + i] : x[i]) + shx(b3 ? x[i] : x[4 + i], 8);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) x[i] += __shfl_xor_sync(0xffffffffu, x[i], o);
+    for (int i = 0; i < 2; ++i) z[i] = (b2 ? y[2 + i] : y[i]) + shx(b2 ? y[i] : y[2 + i], 4);
+    float w = (b1 ? z[1] : z[0]) + shx(b1 ? z[0] : z[1], 2);
+    w += shx(w, 1);  // value 4 b3 + 2 b2 + b1
+    const float w2 = shx(w, 2);
+    z[0] = b1 ? w2 : w;
+    z[1] = b1 ? w : w2;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float o = shx(z[i], 4);
+        y[i] = b2 ? o : z[i];
+        y[2 + i] = b2 ? z[i] : o;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float o = shx(y[i], 8);
+        x[i] = b3 ? o : y[i];
+        x[4 + i] = b3 ? y[i] : o;
+    }
 }
 
 __device__ __forceinline__ float clamp_beta(float s, float floor_) { return 1.0f / (s < floor_ ? floor_ : s); }
@@ -213,13 +270,13 @@ __device__ __forceinline__ void gain_step(const Tiles &st, const TokIn &tk, Xchg
         for (int i = 0; i < 4; ++i) z = fmaf(st.Mt[i][j], w_c[i], z);
         pe[j] = z;
     }
-    hw_sum4(pu);
-    hw_sum4(pe);
+    float pue[8] = {pu[0], pu[1], pu[2], pu[3], pe[0], pe[1], pe[2], pe[3]};
+    hw_sum8(pue);
     const float p = tk.p;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        o.u_r[i] = fmaf(a_r[i], pu[i], p * k_r[i]);
-        o.e_r[i] = v_r[i] - pe[i];
+        o.u_r[i] = fmaf(a_r[i], pue[i], p * k_r[i]);
+        o.e_r[i] = v_r[i] - pue[4 + i];
     }
     if (c == 0) {
         st4(x.u[par] + 4 * r, o.u_r[0], o.u_r[1], o.u_r[2], o.u_r[3]);
@@ -316,8 +373,8 @@ __global__ void __launch_bounds__(kThreads, 2) d64_forward(const FwdArgs<float> 
             for (int i = 0; i < 4; ++i) z = fmaf(st.Mt[i][j], q_c[i], z);
             py[j] = z;
         }
-        hw_sum4(py);
-        if (c == 0) st4(F.out + (chain * T + ti) * M + 4 * r, py[0], py[1], py[2], py[3]);
+        const float yv = hw_scatter4(py);  // y at value column 4r + ((c >> 2) & 3)
+        if ((c & 3) == 0) F.out[(chain * T + ti) * M + 4 * r + ((c >> 2) & 3)] = yv;
         if ((ti + 1) % L == 0 || ti + 1 == T) {
             const long b = (ti + 1 + L - 1) / L;
             store_state_g(st, F.bmean + (chain * (nb + 1) + b) * D * M, F.bcov + (chain * (nb + 1) + b) * D * D, r,
@@ -533,13 +590,15 @@ __global__ void __launch_bounds__(kThreads, BSSM_D64_BWD_MINB) d64_backward(cons
                     for (int j = 0; j < 4; ++j) z = fmaf(R[i][j], u_c[j], z);
                     ru[i] = z;
                 }
-                hw_sum4(ru);
-                if (c == 0) {
-                    st4(sm.ru[par] + 4 * r, ru[0], ru[1], ru[2], ru[3]);
-                    float z = 0.f;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) z = fmaf(u_r[i], ru[i], z);
-                    sm.urup[par][r] = z;
+                {
+                    // (R u) at row 4r + ((c >> 2) & 3) and the half-warp's u . R u
+                    const int ri = (c >> 2) & 3;
+                    const float rv = hw_scatter4(ru);
+                    if ((c & 3) == 0) sm.ru[par][4 * r + ri] = rv;
+                    float uru = pick(u_r, ri) * rv;
+                    uru += shx(uru, 4);
+                    uru += shx(uru, 8);
+                    if (c == 0) sm.urup[par][r] = uru;
                 }
                 if (c == 0) {  // gv = ge at value columns 4r..
                     st4(A.gv + row * M + 4 * r, ge[0], ge[1], ge[2], ge[3]);
@@ -597,29 +656,18 @@ __global__ void __launch_bounds__(kThreads, BSSM_D64_BWD_MINB) d64_backward(cons
                     pgk[i] = zk;
                     pga[i] = za;
                 }
-                hw_sum4(pgk);
-                hw_sum4(pga);
+                // key and decay gradients at row 4r + ((c >> 2) & 3), one lane of each group of four
+                const float gkv = hw_scatter4(pgk), gav = hw_scatter4(pga);
                 if (r == c) sm.trp[x][r] = tr;
+                if ((c & 3) == 0) {
+                    const int ri = (c >> 2) & 3, kr = 4 * r + ri;
+                    A.gk[row * D + kr] = gkv + gs * pick(u_r, ri) - pick(a_r, ri) * sm.fin[2][kr];
+                    if (NEED_DYN) A.ga[row * D + kr] = FIXED ? 0.f : fmaf(2.f, gav, sm.fin[3][kr]);
+                }
                 if (c == 0) {
-                    float gk4[4], ga4[4];
-                    float mg_r[4], gm_r[4], gq4[4];
-                    unpack(ld4(sm.fin[2] + 4 * r), mg_r);
-                    unpack(ld4(sm.fin[3] + 4 * r), gm_r);
+                    float gq4[4];
                     unpack(ld4(sm.fin[0] + 4 * r), gq4);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        gk4[i] = pgk[i] + gs * u_r[i] - a_r[i] * mg_r[i];
-                        ga4[i] = fmaf(2.f, pga[i], gm_r[i]);
-                    }
-                    st4(A.gk + row * D + 4 * r, gk4[0], gk4[1], gk4[2], gk4[3]);
                     st4(A.gq + row * D + 4 * r, gq4[0], gq4[1], gq4[2], gq4[3]);
-                    if (NEED_DYN) {
-                        if (FIXED) {
-                            st4(A.ga + row * D + 4 * r, 0.f, 0.f, 0.f, 0.f);
-                        } else {
-                            st4(A.ga + row * D + 4 * r, ga4[0], ga4[1], ga4[2], ga4[3]);
-                        }
-                    }
                 }
                 if (NEED_DYN && t == 0) A.gr[row] = FIXED ? 0.f : gs;
             }
