@@ -347,6 +347,8 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
     const int c0 = CW * grp;
     const Chan ch = c0 < s.conv_channels() + s.aux_channels() ? classify(s, c0 / 2) : Chan{kIdle, 0, 0};
     const HeadMap hm = head_map<CW>(s.d);
+    // does any lane of this warp hold q / k channels (the head norms run only then)
+    const bool warp_qk = __any_sync(0xffffffffu, ch.kind == kQ || ch.kind == kK);
     const long row0 = bb * s.t;
     const long chain = bb * s.heads + ch.head;
     const bool conv = ch.kind <= kV;
@@ -413,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
             xm1[j] = x[j];
         }
         const bool qk = ch.kind == kQ || ch.kind == kK;
-        if (L > 0 || hm.ng == 1) {  // one head (part) per thread: reduce across its lanes
+        if ((L > 0 || hm.ng == 1) && warp_qk) {  // one head (part) per thread: reduce across its lanes
             float tot = 0.f;
 #pragma unroll
             for (int j = 0; j < CW; ++j) tot += ss[j];
@@ -424,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
                 for (int j = 0; j < CW; ++j) o[j] *= r;
                 stn<OUT_BF, CW>(ch.kind == kQ ? a.q : a.k, oidx, o);
             }
-        } else if (qk) {  // CW / D whole heads
+        } else if (L == 0 && hm.ng > 1 && qk) {  // CW / D whole heads
 #pragma unroll
             for (int gi = 0; gi < CW / 2; ++gi) {
                 if (gi >= hm.ng) break;
@@ -503,6 +505,8 @@ __global__ void __launch_bounds__(kThreads, CW == 4 ? BSSM_ENV_BWD_MINB4 : BSSM_
     const int C = s.conv_channels();
     const Chan ch = c0 < C + s.aux_channels() ? classify(s, c0 / 2) : Chan{kIdle, 0, 0};
     const int lanes = L > 0 ? L : s.d / CW;  // lanes per q / k head
+    // does any lane of this warp hold q / k channels (the head norms run only then)
+    const bool warp_qk = __any_sync(0xffffffffu, ch.kind == kQ || ch.kind == kK);
     const long row0 = bb * s.t;
     const long chain = bb * s.heads + ch.head;
     const bool conv = ch.kind <= kV;
@@ -621,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, CW == 4 ? BSSM_ENV_BWD_MINB4 : BSSM_
             }
         }
         // q, k: y = s / max(|s|, eps); dy/ds = (I - y y^T) / |s| above eps, I / eps below
-        {
+        if (warp_qk) {
             float ss = 0.f;
 #pragma unroll
             for (int j = 0; j < CW; ++j) ss += o[j] * o[j];
