@@ -57,7 +57,9 @@ constexpr int kThreads = 256;
 #endif
 // Tokens of loads each walk keeps in flight per thread (powers of two; per
 // token and thread the forward's ring holds 16 bytes of shared memory, the
-// backward's 2 x 8).
+// backward's 2 x 8).  Where a token's elements fit in 8 bytes (BF16 inputs)
+// the forward's ring holds twice BSSM_ENV_FWD_RING tokens in the same space
+// (16 against 8: 0.412 against 0.419 ms at the config-3 mixer shape).
 #ifndef BSSM_ENV_FWD_RING
 #define BSSM_ENV_FWD_RING 8
 #endif
@@ -377,10 +379,13 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
         if (t0 - 2 >= 0) ldn<IN_BF, CW>(a.x, (row0 + t0 - 2) * s.in_stride + c0, xm2);
         if (t0 - 1 >= 0) ldn<IN_BF, CW>(a.x, (row0 + t0 - 1) * s.in_stride + c0, xm1);
     }
-    // ring of the next kFwdRing tokens' projection elements (step k = token t0 + k)
+    // ring of the next FR tokens' projection elements (step k = token t0 + k)
     constexpr int XS = CW * (IN_BF ? 2 : 4);
     static_assert(XS <= 16, "one cp.async per token");
-    __shared__ uint4 ring[kFwdRing][kThreads];
+    // 8-byte slots hold twice the tokens in the same shared memory
+    using FSlot = typename std::conditional<(XS <= 8), uint2, uint4>::type;
+    constexpr int FR = XS <= 8 ? 2 * kFwdRing : kFwdRing;
+    __shared__ FSlot ring[FR][kThreads];
     const char *const xb = static_cast<const char *>(a.x);
     const long xstep = s.in_stride * (XS / CW);
     const char *const xrow = xb + row0 * xstep + c0 * static_cast<long>(XS / CW);
@@ -388,12 +393,12 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
     const char *xp = xrow + t0 * xstep;  // the next token to issue
     auto issue = [&](int k) {
         const bool on = k < steps && ch.kind != kIdle;
-        cp_async_zfill<XS>(shared_addr(&ring[k & (kFwdRing - 1)][threadIdx.x]), on ? xp : xb, on);
+        cp_async_zfill<XS>(shared_addr(&ring[k & (FR - 1)][threadIdx.x]), on ? xp : xb, on);
         xp += xstep;
         cp_async_commit_group();
     };
 #pragma unroll
-    for (int k = 0; k < kFwdRing; ++k) issue(k);
+    for (int k = 0; k < FR; ++k) issue(k);
     // element index of this thread's output row at the current token (q / k /
     // decay rows of d, v rows of hd), and of its chains' variances
     const long ostep = ch.kind == kV ? s.hd : s.d;
@@ -402,8 +407,8 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
 #pragma unroll 4
     for (int k = 0; k < steps; ++k, oidx += ostep, ++nidx) {
         const long t = t0 + k;
-        cp_async_wait_group<kFwdRing - 1>();
-        unpack<IN_BF, CW>(ring[k & (kFwdRing - 1)][threadIdx.x], x);
+        cp_async_wait_group<FR - 1>();
+        unpack<IN_BF, CW>(ring[k & (FR - 1)][threadIdx.x], x);
         float ss[CW];
 #pragma unroll
         for (int j = 0; j < CW; ++j) {
@@ -459,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
                 a.observation[nidx + i * s.t] = softplus(x[2 * i + 1] + bias[2 * i + 1]) + kNoiseFloor;
             }
         }
-        issue(k + kFwdRing);  // after the slot's values were used
+        issue(k + FR);  // after the slot's values were used
     }
     cp_async_wait_group<0>();
 }
