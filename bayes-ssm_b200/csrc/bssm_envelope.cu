@@ -821,6 +821,178 @@ __global__ void __launch_bounds__(kThreads) epilogue_backward_kernel(const EpiAr
     }
 }
 
+// Tiled readout for head dims 8 and 16, where a (token, head) row of the
+// chain-major reads is only 32 or 64 bytes and the row-per-thread kernels
+// above touch one scattered sector per thread.  A CTA takes 32 heads x (256 /
+// HD) tokens of one batch row: it copies each head's run of tokens (256
+// contiguous elements) into a shared tile, then works the rows in token-major
+// order, so the gate, output and gate-gradient rows of a warp are contiguous
+// too.  The backward writes the read gradient back through the same tile.
+template <int HD>
+struct EpiTile {
+    static constexpr int kT = 256 / HD;        // tokens per tile
+    static constexpr int kH = 32;              // heads per tile
+    static constexpr int kRowF = kT * HD + 4;  // floats per head in shared memory (+4: float4 reads across heads hit distinct banks)
+};
+
+inline long epi_tiles(long b, long t, int heads, int hd) {
+    return b * ((t + 256 / hd - 1) / (256 / hd)) * ((heads + 31) / 32);
+}
+
+template <int HD>
+__device__ __forceinline__ void epi_tile_of(const EpiArgs &a, long &bb, long &t0, int &h0) {
+    constexpr int kT = EpiTile<HD>::kT;
+    const long ht = (a.heads + 31) / 32, tt = (a.t + kT - 1) / kT;
+    long i = blockIdx.x;
+    h0 = static_cast<int>(i % ht) * 32;
+    i /= ht;
+    t0 = (i % tt) * kT;
+    bb = i / tt;
+}
+
+// Four elements per thread and head, 64 threads per head: heads hl, hl + 4, ...
+// Elements past the sequence end or past the last head stay zero in the tile.
+template <bool RBF, int HD>
+__device__ __forceinline__ void epi_load_tile(const EpiArgs &a, long bb, long t0, int h0,
+                                              float (*sm)[EpiTile<HD>::kRowF]) {
+    constexpr int kT = EpiTile<HD>::kT;
+    const int valid = static_cast<int>((a.t - t0 < kT ? a.t - t0 : kT) * HD);
+    const int e = (threadIdx.x & 63) * 4;
+    for (int hl = threadIdx.x >> 6; hl < EpiTile<HD>::kH; hl += kThreads / 64) {
+        const int h = h0 + hl;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (h < a.heads && e < valid) ldn<RBF, 4>(a.read, ((bb * a.heads + h) * a.t + t0) * HD + e, v);
+        *reinterpret_cast<float4 *>(&sm[hl][e]) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+}
+
+template <bool RBF, bool GBF, int HD>
+__global__ void __launch_bounds__(kThreads) epilogue_tile_kernel(const EpiArgs a) {
+    using E = EpiTile<HD>;
+    __shared__ __align__(16) float sm[E::kH][E::kRowF];
+    long bb, t0;
+    int h0;
+    epi_tile_of<HD>(a, bb, t0, h0);
+    epi_load_tile<RBF, HD>(a, bb, t0, h0, sm);
+    __syncthreads();
+    const int hl = threadIdx.x & 31, h = h0 + hl;
+    float w[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) w[i] = __ldg(a.w + i);
+    for (int tl = threadIdx.x >> 5; tl < E::kT; tl += kThreads / 32) {
+        const long t = t0 + tl;
+        if (h >= a.heads || t >= a.t) continue;
+        const long tok = bb * a.t + t;
+        float r[HD], g[HD];
+#pragma unroll
+        for (int i = 0; i < HD; i += 4) {
+            const float4 f = *reinterpret_cast<const float4 *>(&sm[hl][tl * HD + i]);
+            r[i] = f.x, r[i + 1] = f.y, r[i + 2] = f.z, r[i + 3] = f.w;
+        }
+        ldv<GBF, HD>(a.gate, tok * a.gate_stride + static_cast<long>(h) * HD, g);
+        float ms = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD; ++i) {
+            if constexpr (GBF) r[i] = round_bf16(r[i]);  // read.to(x.dtype)
+            ms = fmaf(r[i], r[i], ms);
+        }
+        const float inv = rsqrtf(ms * (1.0f / HD) + a.eps);
+        float o[HD];
+#pragma unroll
+        for (int i = 0; i < HD; ++i) o[i] = r[i] * inv * w[i] * (g[i] * sigmoid(g[i]));
+        stv<GBF, HD>(a.out, tok * static_cast<long>(a.heads) * HD + static_cast<long>(h) * HD, o);
+    }
+}
+
+template <bool RBF, bool GBF, int HD>
+__global__ void __launch_bounds__(kThreads) epilogue_tile_backward_kernel(const EpiArgs a) {
+    using E = EpiTile<HD>;
+    __shared__ __align__(16) float sm[E::kH][E::kRowF];
+    __shared__ float red[kThreads / 32][HD];
+    long bb, t0;
+    int h0;
+    epi_tile_of<HD>(a, bb, t0, h0);
+    epi_load_tile<RBF, HD>(a, bb, t0, h0, sm);
+    __syncthreads();
+    const int hl = threadIdx.x & 31, h = h0 + hl;
+    float w[HD], gw[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) {
+        w[i] = __ldg(a.w + i);
+        gw[i] = 0.f;
+    }
+    for (int tl = threadIdx.x >> 5; tl < E::kT; tl += kThreads / 32) {
+        const long t = t0 + tl;
+        if (h >= a.heads || t >= a.t) continue;
+        const long tok = bb * a.t + t;
+        float r[HD], g[HD], go[HD];
+#pragma unroll
+        for (int i = 0; i < HD; i += 4) {
+            const float4 f = *reinterpret_cast<const float4 *>(&sm[hl][tl * HD + i]);
+            r[i] = f.x, r[i + 1] = f.y, r[i + 2] = f.z, r[i + 3] = f.w;
+        }
+        ldv<GBF, HD>(a.gate, tok * a.gate_stride + static_cast<long>(h) * HD, g);
+        ldv<GBF, HD>(a.out, tok * static_cast<long>(a.heads) * HD + static_cast<long>(h) * HD, go);
+        float ms = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD; ++i) {
+            if constexpr (GBF) r[i] = round_bf16(r[i]);
+            ms = fmaf(r[i], r[i], ms);
+        }
+        const float inv = rsqrtf(ms * (1.0f / HD) + a.eps);
+        float ggt[HD], gr[HD], dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD; ++i) {
+            const float sg = sigmoid(g[i]);
+            const float silu = g[i] * sg, dsilu = sg * fmaf(g[i], 1.f - sg, 1.f);
+            const float n = r[i] * inv;          // normalised, before the weight
+            ggt[i] = go[i] * n * w[i] * dsilu;   // d/dgate
+            const float gy = go[i] * silu;       // d/d(normalised * weight)
+            gw[i] = fmaf(gy, n, gw[i]);
+            gr[i] = w[i] * gy;                   // z = w * gy
+            dot = fmaf(r[i], gr[i], dot);
+        }
+        // d/dr of r * inv: inv * z - r * inv^3 * (r . z) / HD
+        const float c3 = inv * inv * inv * dot * (1.0f / HD);
+#pragma unroll
+        for (int i = 0; i < HD; ++i) gr[i] = inv * gr[i] - r[i] * c3;
+        stv<GBF, HD>(a.ggate, tok * a.ggate_stride + static_cast<long>(h) * HD, ggt);
+#pragma unroll
+        for (int i = 0; i < HD; i += 4)  // this thread's own row of the tile
+            *reinterpret_cast<float4 *>(&sm[hl][tl * HD + i]) = make_float4(gr[i], gr[i + 1], gr[i + 2], gr[i + 3]);
+    }
+    __syncthreads();
+    {  // the read gradient, each head's run of tokens as one contiguous store
+        constexpr int kT = E::kT;
+        const int valid = static_cast<int>((a.t - t0 < kT ? a.t - t0 : kT) * HD);
+        const int e = (threadIdx.x & 63) * 4;
+        for (int hx = threadIdx.x >> 6; hx < E::kH; hx += kThreads / 64) {
+            const int hh = h0 + hx;
+            if (hh < a.heads && e < valid) {
+                const float4 f = *reinterpret_cast<const float4 *>(&sm[hx][e]);
+                const float v[4] = {f.x, f.y, f.z, f.w};
+                stn<RBF, 4>(a.gread, ((bb * a.heads + hh) * a.t + t0) * HD + e, v);
+            }
+        }
+    }
+    // weight gradient: warp sums, then the CTA's warps in order
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < HD; ++i) {
+        float v = gw[i];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) red[warp][i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < HD) {
+        float acc = 0.f;
+#pragma unroll
+        for (int wv = 0; wv < kThreads / 32; ++wv) acc += red[wv][threadIdx.x];
+        a.partial[static_cast<long>(blockIdx.x) * HD + threadIdx.x] = acc;
+    }
+}
+
 // First pass of the many-column sum: CTA (x, y) sums rows [y * per, (y + 1) *
 // per) of its columns into row y of `out` (rows in order).
 __global__ void __launch_bounds__(kThreads) reduce_row_groups_kernel(const float *partial, long rows, int cols,
@@ -1049,14 +1221,25 @@ int epi_check(long batch, long tokens, int heads, int head_dim, int read_dtype, 
     return BSSM_OK;
 }
 
+// CTAs the readout launches for a shape (tiles for head dims 8 and 16, else
+// one CTA per 256 rows); the backward writes one partial-sum row per CTA.
+long epi_ctas(long b, long t, int heads, int hd) {
+    if (hd == 8 || hd == 16) return epi_tiles(b, t, heads, hd);
+    return (b * t * heads + kThreads - 1) / kThreads;
+}
+
 template <int HD>
 void launch_epi(const EpiArgs &a, int rd, int gd, bool backward, cudaStream_t st) {
-    const long rows = a.b * a.t * a.heads;
-    const unsigned grid = static_cast<unsigned>((rows + kThreads - 1) / kThreads);
-#define BSSM_EPI(R, G)                                                                       \
-    do {                                                                                     \
-        if (backward) epilogue_backward_kernel<R, G, HD><<<grid, kThreads, 0, st>>>(a);     \
-        else epilogue_kernel<R, G, HD><<<grid, kThreads, 0, st>>>(a);                       \
+    const unsigned grid = static_cast<unsigned>(epi_ctas(a.b, a.t, a.heads, HD));
+#define BSSM_EPI(R, G)                                                                            \
+    do {                                                                                          \
+        if constexpr (HD == 8 || HD == 16) {                                                      \
+            if (backward) epilogue_tile_backward_kernel<R, G, HD><<<grid, kThreads, 0, st>>>(a); \
+            else epilogue_tile_kernel<R, G, HD><<<grid, kThreads, 0, st>>>(a);                   \
+        } else {                                                                                  \
+            if (backward) epilogue_backward_kernel<R, G, HD><<<grid, kThreads, 0, st>>>(a);      \
+            else epilogue_kernel<R, G, HD><<<grid, kThreads, 0, st>>>(a);                        \
+        }                                                                                         \
     } while (0)
     if (rd == BSSM_BF16) {
         if (gd == BSSM_BF16) BSSM_EPI(true, true);
@@ -1299,8 +1482,11 @@ int bssm_rms_norm_backward(const void *x, int dtype, long rows, int width, const
 }
 
 long bssm_envelope_epilogue_partial_floats(long batch, long tokens, int heads, int head_dim) {
+    // at least one row per CTA of either kernel form
     const long rows = batch * tokens * heads;
-    return (rows + kThreads - 1) / kThreads * head_dim;
+    const long rowwise = (rows + kThreads - 1) / kThreads;
+    const long tiles = head_dim == 8 || head_dim == 16 ? epi_tiles(batch, tokens, heads, head_dim) : 0;
+    return (rowwise > tiles ? rowwise : tiles) * head_dim;
 }
 
 int bssm_envelope_epilogue(const void *read, int read_dtype, const void *gate, int gate_dtype, long gate_row_stride,
@@ -1352,7 +1538,7 @@ int bssm_envelope_epilogue_backward(const void *read, int read_dtype, const void
               grad_read, grad_gate, grad_gate_row_stride, workspace};
     launch_epi_hd(a, head_dim, read_dtype, gate_dtype, true, st);
     if (int rc = check_launch("envelope epilogue backward")) return rc;
-    const long ctas = need / head_dim;
+    const long ctas = epi_ctas(batch, tokens, heads, head_dim);
     reduce_cols_kernel<<<head_dim, kThreads, 0, st>>>(workspace, ctas, head_dim, grad_norm_weight);
     return check_launch("envelope epilogue reduction");
 }

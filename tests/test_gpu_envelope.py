@@ -130,7 +130,10 @@ def test_prologue_feeds_the_recurrence():
 @pytest.mark.parametrize("shape,read_dtype,gate_dtype", [
     ((2, 37, 4, 8), torch.float32, torch.float32), ((3, 64, 64, 8), torch.float32, torch.bfloat16),
     ((1, 19, 2, 16), torch.float32, torch.float32), ((2, 8, 3, 32), torch.bfloat16, torch.bfloat16),
-    ((1, 5, 2, 64), torch.float32, torch.float32)])
+    ((1, 5, 2, 64), torch.float32, torch.float32),
+    # head dims 8 and 16 run in tiles of 32 heads x 256 / hd tokens: BF16 reads,
+    # a head count past one tile and not a multiple of it, ragged token tiles
+    ((2, 45, 40, 8), torch.bfloat16, torch.bfloat16), ((1, 33, 33, 16), torch.bfloat16, torch.float32)])
 def test_read_epilogue_forward_backward(shape, read_dtype, gate_dtype):
     from bayes_ssm.envelope import read_epilogue, read_epilogue_torch
     b, t, h, hd = shape
