@@ -43,7 +43,20 @@ __global__ void check_values_kernel(const T *__restrict__ x, long n, unsigned *f
     if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         const long nvec = n / EC;
         const uint4 *xv = reinterpret_cast<const uint4 *>(x);
-        for (long i = tid; i < nvec; i += nthreads) {
+        // four independent 16-byte loads in flight per thread, then the rest
+        long i = tid;
+        for (; i + 3 * nthreads < nvec; i += 4 * nthreads) {
+            uint4 w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) w[u] = __ldg(xv + i + u * nthreads);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const T *e = reinterpret_cast<const T *>(&w[u]);
+#pragma unroll
+                for (int j = 0; j < EC; ++j) f |= flags_of(widen(e[j]));
+            }
+        }
+        for (; i < nvec; i += nthreads) {
             const uint4 w = __ldg(xv + i);
             const T *e = reinterpret_cast<const T *>(&w);
 #pragma unroll

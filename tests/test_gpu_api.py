@@ -246,6 +246,25 @@ def test_check_values_flags_match_torch(dtype):
 
 
 @pytest.mark.parametrize("dtype", (torch.float32, torch.bfloat16, torch.float16))
+def test_check_values_flags_large_tensor(dtype):
+    """Tensors far larger than one pass of the check kernel's grid, where each
+    thread keeps four loads in flight: a bad value planted early, in the
+    middle, near the end of the four-load loop, in its remainder and in the
+    scalar tail is found (and nothing is flagged without one)."""
+    from bayes_ssm import _capi
+    n = 40_000_003  # not a multiple of a 16-byte vector either
+    x = torch.ones(n, device="cuda", dtype=dtype)
+    assert _capi.check_values([x]) == [0]
+    for pos, val, flag in ((17, float("nan"), _capi.CHECK_NONFINITE), (n // 2, -2.0, _capi.CHECK_NEGATIVE),
+                           (n - 1_000_000, 0.0, _capi.CHECK_NOT_POSITIVE), (n - 40_000, float("inf"), _capi.CHECK_NONFINITE),
+                           (n - 1, -1.0, _capi.CHECK_NEGATIVE)):
+        y = x.clone()
+        y[pos] = val
+        got = _capi.check_values([y])[0]
+        assert got & flag, (pos, val, got)
+
+
+@pytest.mark.parametrize("dtype", (torch.float32, torch.bfloat16, torch.float16))
 def test_api_validation_errors_on_gpu(dtype):
     """CUDA inputs raise the reference's validation errors, first failing
     check first (keys before values, finiteness before sign)."""
