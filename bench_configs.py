@@ -32,6 +32,13 @@ headline, config 3, is ``bench.py``).
 * ``--config envelope-profile``: the prologue kernels alone at an eighth of
   that shape (B32), untimed: the case the prologue's ncu captures run on.
 
+* ``--config rotation``: rotation dynamics (damped 2-D rotations per key pair,
+  per-pair process noise) at config 3's shape (B256 T512 H64 D8 M8, chunk 64,
+  FP32), forward + backward of a readout loss through the public
+  ``bayesian_layer(rotation_radii=, rotation_angles=, optimized=True)``, beside
+  the dense PyTorch path on the same GPU (the reference's only path for these
+  dynamics), with 8 chains checked against that path in FP64 on the CPU.
+
 * ``--config d64-profile``: the (64, 64) kernels on 296 chains (B37 T512 H8,
   one wave at two CTAs per SM), untimed: the case their ncu captures run on.
 
@@ -387,6 +394,65 @@ def d64(steps: int, warmup: int) -> dict:
             "family": _capi.last_family(), "steps": steps, "warmup": warmup, "data": "synthetic"}
 
 
+def rotation(steps: int, warmup: int) -> dict:
+    """Rotation dynamics at config 3's shape through the public API (see the
+    module doc): the kernels, the dense path on the GPU, and parity."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+    import bayes_ssm
+    b, t, h, d, m, chunk = 256, 512, 64, 8, 8, 64
+    n, j = b * h, d // 2
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(8)
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=g, device=dev)
+
+    base = dict(k=F.normalize(rn(n, t, d), dim=-1), v=rn(n, t, m) / math.sqrt(m), q=F.normalize(rn(n, t, d), dim=-1),
+                radii=0.85 + 0.2 * torch.rand(n, t, j, generator=g, device=dev), angles=0.4 * rn(n, t, j),
+                p=F.softplus(-3.0 + rn(n, t, j)), r=F.softplus(rn(n, t)) + 1e-3)
+    gy = rn(n, t, m) / math.sqrt(m)
+
+    def step(inp, optimized, out=None):
+        leaves = {x: v.detach().requires_grad_() for x, v in inp.items()}
+        y, _, _ = bayes_ssm.bayesian_layer(leaves["k"], leaves["v"], leaves["q"], rotation_radii=leaves["radii"],
+                                           rotation_angles=leaves["angles"], process_variances=leaves["p"],
+                                           observation_variances=leaves["r"], chunk_length=chunk,
+                                           optimized=optimized)
+        grads = torch.autograd.grad(y, list(leaves.values()), gy)
+        if out is not None:
+            out["y"] = y.detach()
+            out.update({x: gr_ for x, gr_ in zip(leaves, grads)})
+
+    ms_k = _time(lambda: step(base, True), steps, warmup)
+    ms_dense = _time(lambda: step(base, False), 1, 1)
+    got = {}
+    step(base, True, got)
+    idx = torch.tensor([0, 1, n // 2, n - 1, 77, 4321, 9000, 16000], device=dev)
+    sub = {x: v.index_select(0, idx).double().cpu() for x, v in base.items()}
+    gy_sub = gy.index_select(0, idx).double().cpu()
+    leaves = {x: v.clone().requires_grad_() for x, v in sub.items()}
+    y0, _, _ = bayes_ssm.bayesian_layer(leaves["k"], leaves["v"], leaves["q"], rotation_radii=leaves["radii"],
+                                        rotation_angles=leaves["angles"], process_variances=leaves["p"],
+                                        observation_variances=leaves["r"], chunk_length=chunk, optimized=False)
+    want = dict(zip(leaves, torch.autograd.grad(y0, list(leaves.values()), gy_sub)))
+    want["y"] = y0.detach()
+
+    def rel(x):
+        a = got[x].index_select(0, idx).double().cpu().numpy()
+        e = want[x].numpy()
+        return float(np.linalg.norm(a - e) / np.linalg.norm(e))
+
+    parity = {x: rel(x) for x in ("y", "k", "v", "q", "radii", "angles", "p", "r")}
+    return {"config": "rotation", "workload": "rotation dynamics, B256 T512 H64 D8 M8, chunk 64, FP32, fwd + bwd "
+            "through bayesian_layer(optimized=True), readout gradient given", "metric": "tok/s/GPU", "unit": "tok/s",
+            "value": round(b * t / (ms_k / 1e3), 1), "ms_per_step": round(ms_k, 4),
+            "dense_torch_gpu_ms_per_step": round(ms_dense, 2), "speedup_vs_dense": round(ms_dense / ms_k, 1),
+            "parity_vs_dense_fp64_rel_l2": parity, "parity_chains": int(idx.numel()), "steps": steps,
+            "warmup": warmup, "data": "synthetic"}
+
+
 def d64_profile(steps: int, warmup: int) -> dict:
     """The (64, 64) forward and backward on 296 chains (B37 T512 H8, chunk 64,
     FP32): ``steps`` forward + backward pairs, untimed -- the small case an ncu
@@ -583,13 +649,13 @@ def _peak_hbm() -> float:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", choices=("2", "4", "d64", "d64-profile", "envelope", "envelope-profile", "mixer",
-                                         "refcuda", "refcuda64"), required=True)
+                                         "refcuda", "refcuda64", "rotation"), required=True)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()
     fn = {"2": config2, "4": config4, "d64": d64, "d64-profile": d64_profile, "envelope": envelope,
           "envelope-profile": envelope_profile,
-          "mixer": mixer, "refcuda": refcuda, "refcuda64": refcuda64}[args.config]
+          "mixer": mixer, "refcuda": refcuda, "refcuda64": refcuda64, "rotation": rotation}[args.config]
     print(json.dumps(fn(args.steps, max(3, args.warmup))), flush=True)
 
 
