@@ -34,6 +34,13 @@ namespace rot {
 
 constexpr int kThreads = 128;
 constexpr int kSub = 4;
+// CTAs per SM the backward's registers are sized for.  At config 3's shape
+// (16,384 chains at D8: 1,024 CTAs) four per SM run the launch in two waves
+// where three (166 registers, no spills) took three: 8.00 against 8.36 ms per
+// API step, with 52 bytes spilled; three per SM forced: 8.73 ms.
+#ifndef BSSM_ROT_BWD_MINB
+#define BSSM_ROT_BWD_MINB 4
+#endif
 
 struct Args {
     const float *keys, *values, *queries;  // [N,T,D], [N,T,M], [N,T,D]
@@ -247,7 +254,7 @@ struct Hist {
 };
 
 template <int D, int M, bool NEED_INIT>
-__global__ void __launch_bounds__(kThreads) rot_backward(const Args A) {
+__global__ void __launch_bounds__(kThreads, BSSM_ROT_BWD_MINB) rot_backward(const Args A) {
     constexpr int CPL = M / D, J = D / 2;
     using H = Hist<D, M>;
     __shared__ float hist[kSub * H::kFloats * kThreads];
