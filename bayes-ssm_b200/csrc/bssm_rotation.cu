@@ -41,6 +41,14 @@ constexpr int kSub = 4;
 #ifndef BSSM_ROT_BWD_MINB
 #define BSSM_ROT_BWD_MINB 4
 #endif
+// The forward's launch bounds (by default the block size alone: 96 registers,
+// five CTAs per SM).  Eight or six per SM (64 / 80 registers, with spills) did
+// not help: 7.95-8.18 and 8.11 against 7.97 ms per API step.
+#ifdef BSSM_ROT_FWD_MINB
+#define BSSM_ROT_FWD_BOUNDS __launch_bounds__(kThreads, BSSM_ROT_FWD_MINB)
+#else
+#define BSSM_ROT_FWD_BOUNDS __launch_bounds__(kThreads)
+#endif
 
 struct Args {
     const float *keys, *values, *queries;  // [N,T,D], [N,T,M], [N,T,D]
@@ -208,7 +216,7 @@ __device__ __forceinline__ void store_state(float *mean, float *cov, int own, in
 
 // ---------------------------------------------------------------------------
 template <int D, int M>
-__global__ void __launch_bounds__(kThreads) rot_forward(const Args A) {
+__global__ void BSSM_ROT_FWD_BOUNDS rot_forward(const Args A) {
     constexpr int CPL = M / D;
     const LaneGroup<D> g;
     const long chain = (static_cast<long>(blockIdx.x) * kThreads + threadIdx.x) / D;
