@@ -61,6 +61,8 @@ _SIGNATURES = {
     "bssm_rotation_workspace_bytes": ([_i, _i, _l, _l, _i], _sz),
     "bssm_rotation_forward_chunked": ([_i, _i] + [_vp] * 14 + [_l, _l, _i, _d, _vp], _i),
     "bssm_rotation_backward_chunked": ([_i, _i, _i] + [_vp] * 22 + [_sz, _l, _l, _i, _d, _vp], _i),
+    "bssm_rotation_coefficients": ([_vp, _vp, _l, _vp, _vp, _vp], _i),
+    "bssm_rotation_coefficients_backward": ([_vp, _vp, _vp, _vp, _l, _vp, _vp, _vp], _i),
     "bssm_debug_wait_timeouts": ([], ctypes.c_uint),
     "bssm_stream_status": ([_vp], _i),
     "bssm_debug_wait_probe": ([_i, _vp], _i),
@@ -172,6 +174,17 @@ def rotation_backward(key_dim, value_dim, need_initial, keys, values, queries, c
         ptr(gq), ptr(gcos), ptr(gsin), ptr(gproc), ptr(gobs), ptr(gm0), ptr(gc0), ptr(workspace), workspace_nbytes,
         n, t, chunks, float(floor), stream)
     check(rc, "bssm_rotation_backward_chunked")
+
+
+def rotation_coefficients(radii, angles, cosines, sines, stream) -> None:
+    rc = load().bssm_rotation_coefficients(ptr(radii), ptr(angles), radii.numel(), ptr(cosines), ptr(sines), stream)
+    check(rc, "bssm_rotation_coefficients")
+
+
+def rotation_coefficients_backward(radii, angles, grad_cosines, grad_sines, grad_radii, grad_angles, stream) -> None:
+    rc = load().bssm_rotation_coefficients_backward(ptr(radii), ptr(angles), ptr(grad_cosines), ptr(grad_sines),
+                                                    radii.numel(), ptr(grad_radii), ptr(grad_angles), stream)
+    check(rc, "bssm_rotation_coefficients_backward")
 
 
 def backward_chunked_noalloc(key_dim, value_dim, io_dtype, fixed, need_dynamics, need_initial, keys,

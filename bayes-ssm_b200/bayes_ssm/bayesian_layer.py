@@ -531,12 +531,18 @@ def bayesian_layer(
     if (rotation and optimized and device.type == "cuda" and (d, m) in ROTATION_SUPPORTED
             and dtype in (torch.float32, torch.bfloat16)):
         # the reference's radius handling and make_rotation_dynamics' own
-        # operations, so autograd reaches the radii and angles the same way
-        radius = rotation_radii.clamp_min(torch.finfo(dtype).tiny)
-        radius = torch.where(radius <= 1.0, radius, torch.ones_like(radius))
-        raw = torch.log(radius).exp()
-        rho = torch.where(raw <= 1.0, raw, torch.ones_like(raw))
-        return _rotation_path(keys, values, queries, rho * rotation_angles.cos(), rho * rotation_angles.sin(),
+        # operations, so autograd reaches the radii and angles the same way:
+        # one fused kernel pair for same-shape float32 tensors, else the ops
+        from .rotation_cuda import coefficients_apply, rotation_coefficients
+        if coefficients_apply(rotation_radii, rotation_angles):
+            cosines, sines = rotation_coefficients(rotation_radii, rotation_angles)
+        else:
+            radius = rotation_radii.clamp_min(torch.finfo(dtype).tiny)
+            radius = torch.where(radius <= 1.0, radius, torch.ones_like(radius))
+            raw = torch.log(radius).exp()
+            rho = torch.where(raw <= 1.0, raw, torch.ones_like(raw))
+            cosines, sines = rho * rotation_angles.cos(), rho * rotation_angles.sin()
+        return _rotation_path(keys, values, queries, cosines, sines,
                               process_variances, observation_variances, mean if user_mean else None,
                               covariance if user_cov else None, batch_shape=batch_shape, t=t, d=d, m=m,
                               chunk_length=chunk_length, denominator_floor=float(denominator_floor),

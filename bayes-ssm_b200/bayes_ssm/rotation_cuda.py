@@ -78,6 +78,46 @@ class _RotationFunction(torch.autograd.Function):
                 None)
 
 
+class _CoefficientsFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, radii, angles):
+        cosines, sines = torch.empty_like(radii), torch.empty_like(radii)
+        with torch.cuda.device(radii.device):
+            _capi.rotation_coefficients(radii, angles, cosines, sines, _stream(radii.device))
+        ctx.save_for_backward(radii, angles)
+        ctx.set_materialize_grads(False)
+        return cosines, sines
+
+    @staticmethod
+    def backward(ctx, grad_cosines, grad_sines):
+        radii, angles = ctx.saved_tensors
+        if grad_cosines is None and grad_sines is None:
+            return None, None
+        gc = None if grad_cosines is None else grad_cosines.contiguous()
+        gs = None if grad_sines is None else grad_sines.contiguous()
+        g_radii, g_angles = torch.empty_like(radii), torch.empty_like(angles)
+        with torch.cuda.device(radii.device):
+            _capi.rotation_coefficients_backward(radii, angles, gc, gs, g_radii, g_angles, _stream(radii.device))
+        return g_radii, g_angles
+
+
+def rotation_coefficients(radii: Tensor, angles: Tensor):
+    """``(rho cos(angles), rho sin(angles))`` with the reference's radius
+    handling (``bayesian_layer.py``: radii clamped to [tiny, 1], then
+    ``make_rotation_dynamics``' ``exp(log(radius))`` clipped at 1), in one
+    kernel each way; same-shape contiguous float32 CUDA tensors."""
+    return _CoefficientsFunction.apply(radii, angles)
+
+
+def coefficients_apply(radii, angles) -> bool:
+    """Whether :func:`rotation_coefficients` takes these tensors (else the
+    caller runs the same chain as PyTorch operations)."""
+    return (isinstance(radii, Tensor) and isinstance(angles, Tensor) and radii.is_cuda and angles.is_cuda
+            and radii.device == angles.device and radii.dtype == angles.dtype == torch.float32
+            and radii.shape == angles.shape and radii.is_contiguous() and angles.is_contiguous()
+            and radii.data_ptr() % 4 == 0 and angles.data_ptr() % 4 == 0)
+
+
 def rotation_bayesian(keys: Tensor, values: Tensor, queries: Tensor, cosines: Tensor, sines: Tensor,
                       process: Tensor, observation: Tensor, initial_mean, initial_covariance, *,
                       chunk_length: int, denominator_floor: float, _pending_checks=None):
@@ -99,4 +139,4 @@ def rotation_bayesian(keys: Tensor, values: Tensor, queries: Tensor, cosines: Te
         prep(initial_covariance, (n, d, d)), int(chunk_length), float(denominator_floor), _pending_checks)
 
 
-__all__ = ["rotation_bayesian", "SUPPORTED"]
+__all__ = ["rotation_bayesian", "rotation_coefficients", "SUPPORTED"]

@@ -622,3 +622,101 @@ extern "C" int bssm_rotation_backward_chunked(
     if (t == 0 && !init) return BSSM_OK;
     return bssm::rot::run(key_dim, true, init, a, static_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------------------
+// The rotation coefficients rho cos(theta), rho sin(theta) from the caller's
+// radii and angles, with the reference's radius handling (bayesian_layer.py:
+// the radii clamped below at the smallest normal float and above at 1, then
+// make_rotation_dynamics' exp(log(radius)) clipped at 1), and their backward
+// as the chain of those operations' derivatives.  One pass over the elements
+// each way instead of one per operation.  Products and the division are
+// rounded separately (no contraction), as the separate operations round them.
+// ---------------------------------------------------------------------------
+namespace bssm {
+namespace rot {
+
+constexpr float kTinyRadius = 1.17549435e-38f;  // smallest normal float (torch.finfo(float32).tiny)
+
+__device__ __forceinline__ void radius_chain(float r, float &t2, float &raw, float &rho) {
+    const float t1 = r < kTinyRadius ? kTinyRadius : r;  // clamp_min (NaN passes through)
+    t2 = t1 <= 1.0f ? t1 : 1.0f;
+    raw = expf(logf(t2));
+    rho = raw <= 1.0f ? raw : 1.0f;
+}
+
+__global__ void __launch_bounds__(256) coeff_kernel(const float *__restrict__ radii, const float *__restrict__ angles,
+                                                    long count, float *__restrict__ cosines,
+                                                    float *__restrict__ sines) {
+    for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += static_cast<long>(gridDim.x) * blockDim.x) {
+        float t2, raw, rho;
+        radius_chain(__ldg(radii + i), t2, raw, rho);
+        const float th = __ldg(angles + i);
+        cosines[i] = __fmul_rn(rho, cosf(th));
+        sines[i] = __fmul_rn(rho, sinf(th));
+    }
+}
+
+__global__ void __launch_bounds__(256) coeff_backward_kernel(const float *__restrict__ radii,
+                                                             const float *__restrict__ angles,
+                                                             const float *__restrict__ gcos,
+                                                             const float *__restrict__ gsin, long count,
+                                                             float *__restrict__ gradii,
+                                                             float *__restrict__ gangles) {
+    for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const float r = __ldg(radii + i), th = __ldg(angles + i);
+        float t2, raw, rho;
+        radius_chain(r, t2, raw, rho);
+        const float gc = gcos ? __ldg(gcos + i) : 0.f, gs = gsin ? __ldg(gsin + i) : 0.f;
+        const float c = cosf(th), sn = sinf(th);
+        // c_out = rho * cos(theta), s_out = rho * sin(theta)
+        const float g_rho = __fadd_rn(__fmul_rn(gc, c), __fmul_rn(gs, sn));
+        gangles[i] = __fadd_rn(__fmul_rn(__fmul_rn(gc, rho), -sn), __fmul_rn(__fmul_rn(gs, rho), c));
+        const float g_raw = raw <= 1.0f ? g_rho : 0.f;          // rho = where(raw <= 1, raw, 1)
+        const float g_log = __fmul_rn(g_raw, raw);              // raw = exp(l)
+        const float g_t2 = __fdiv_rn(g_log, t2);                // l = log(t2)
+        const float t1 = r < kTinyRadius ? kTinyRadius : r;
+        const float g_t1 = t1 <= 1.0f ? g_t2 : 0.f;             // t2 = where(t1 <= 1, t1, 1)
+        gradii[i] = r >= kTinyRadius ? g_t1 : 0.f;              // t1 = clamp_min(r, tiny)
+    }
+}
+
+int coeff_grid(long count) {
+    const long blocks = (count + 255) / 256;
+    return static_cast<int>(blocks < 148L * 16 ? (blocks > 0 ? blocks : 1) : 148L * 16);
+}
+
+}  // namespace rot
+}  // namespace bssm
+
+extern "C" int bssm_rotation_coefficients(const float *radii, const float *angles, long count, float *cosines,
+                                          float *sines, void *stream) {
+    using namespace bssm;
+    if (count < 0) return fail(BSSM_ERR_INVALID, "rotation coefficients: negative count");
+    if (count == 0) {
+        g_last_error.clear();
+        return BSSM_OK;
+    }
+    if (!radii || !angles || !cosines || !sines) return fail(BSSM_ERR_INVALID, "rotation coefficients: null pointer");
+    rot::coeff_kernel<<<rot::coeff_grid(count), 256, 0, static_cast<cudaStream_t>(stream)>>>(radii, angles, count,
+                                                                                            cosines, sines);
+    return check_launch("rotation coefficients");
+}
+
+extern "C" int bssm_rotation_coefficients_backward(const float *radii, const float *angles, const float *grad_cosines,
+                                                   const float *grad_sines, long count, float *grad_radii,
+                                                   float *grad_angles, void *stream) {
+    using namespace bssm;
+    if (count < 0) return fail(BSSM_ERR_INVALID, "rotation coefficients backward: negative count");
+    if (count == 0) {
+        g_last_error.clear();
+        return BSSM_OK;
+    }
+    if (!radii || !angles || !grad_radii || !grad_angles)
+        return fail(BSSM_ERR_INVALID, "rotation coefficients backward: null pointer");
+    rot::coeff_backward_kernel<<<rot::coeff_grid(count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        radii, angles, grad_cosines, grad_sines, count, grad_radii, grad_angles);
+    return check_launch("rotation coefficients backward");
+}
+

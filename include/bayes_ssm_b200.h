@@ -283,6 +283,20 @@ int bssm_backward_chunked_noalloc(int key_dim, int value_dim, int io_dtype, int 
  * queries, cosines, sines, process and observation (and of the initial
  * state when need_initial != 0; the covariance's is symmetric).
  */
+/*
+ * The rotation coefficients from the caller's radii and angles: cosines[i] =
+ * rho_i cos(angles[i]), sines[i] = rho_i sin(angles[i]) with rho the
+ * reference's radius handling (bayes_ssm/bayesian_layer.py: rotation_radii
+ * clamped below at the smallest normal float and above at 1, then
+ * make_rotation_dynamics' exp(log(radius)) clipped at 1), in one pass; the
+ * backward gives the radii and angles gradients of that chain (grad_cosines /
+ * grad_sines may be NULL for zero).  Float32, `count` elements, contiguous.
+ */
+int bssm_rotation_coefficients(const float *radii, const float *angles, long count, float *cosines, float *sines,
+                               void *stream);
+int bssm_rotation_coefficients_backward(const float *radii, const float *angles, const float *grad_cosines,
+                                        const float *grad_sines, long count, float *grad_radii, float *grad_angles,
+                                        void *stream);
 size_t bssm_rotation_workspace_bytes(int key_dim, int value_dim, long n, long t, int chunks);
 int bssm_rotation_forward_chunked(int key_dim, int value_dim, const float *keys, const float *values,
                                   const float *queries, const float *cosines, const float *sines,

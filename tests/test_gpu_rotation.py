@@ -88,3 +88,41 @@ def test_rotation_batch_shape_and_bf16_promotion():
                                         process_variances=leaves["p"], observation_variances=leaves["r"],
                                         chunk_length=5, optimized=True)
     assert torch.equal(yb, yf)
+
+
+def test_rotation_coefficients_match_the_reference_chain():
+    """The fused coefficient kernels against the reference's own operations
+    (radii clamped to [tiny, 1], exp(log(radius)) clipped at 1, times cos and
+    sin of the angles): values and both gradients, on radii below tiny, zero,
+    negative, exactly 1, above 1 and ordinary, and angles of any size."""
+    from bayes_ssm.rotation_cuda import coefficients_apply, rotation_coefficients
+    g = torch.Generator().manual_seed(3)
+    radii = 0.2 + 1.0 * torch.rand(4, 300, 4, generator=g)
+    angles = 6.0 * torch.randn(4, 300, 4, generator=g)
+    flat = radii.view(-1)
+    flat[:6] = torch.tensor([0.0, -0.5, 1e-40, 1.0, 1.0000001, 3.0])
+    radii, angles = radii.cuda(), angles.cuda()
+    assert coefficients_apply(radii, angles)
+    up_c = torch.randn(radii.shape, generator=g).cuda()
+    up_s = torch.randn(radii.shape, generator=g).cuda()
+
+    def reference(r, a):
+        radius = r.clamp_min(torch.finfo(torch.float32).tiny)
+        radius = torch.where(radius <= 1.0, radius, torch.ones_like(radius))
+        raw = torch.log(radius).exp()
+        rho = torch.where(raw <= 1.0, raw, torch.ones_like(raw))
+        return rho * a.cos(), rho * a.sin()
+
+    rk, ak = radii.clone().requires_grad_(), angles.clone().requires_grad_()
+    rr, ar = radii.clone().requires_grad_(), angles.clone().requires_grad_()
+    ck, sk = rotation_coefficients(rk, ak)
+    cr, sr = reference(rr, ar)
+    gk = torch.autograd.grad((ck, sk), (rk, ak), (up_c, up_s))
+    gr = torch.autograd.grad((cr, sr), (rr, ar), (up_c, up_s))
+    for name, a_, b_ in (("cos", ck, cr), ("sin", sk, sr), ("grad radii", gk[0], gr[0]), ("grad angles", gk[1], gr[1])):
+        torch.testing.assert_close(a_, b_, rtol=1e-6, atol=1e-7, msg=name)
+    # only the sine gradient given: the cosine's is taken as zero
+    gk1 = torch.autograd.grad(rotation_coefficients(rk, ak)[1], (rk, ak), up_s)
+    gr1 = torch.autograd.grad(reference(rr, ar)[1], (rr, ar), up_s)
+    for a_, b_ in zip(gk1, gr1):
+        torch.testing.assert_close(a_, b_, rtol=1e-6, atol=1e-7)
