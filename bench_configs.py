@@ -39,6 +39,9 @@ headline, config 3, is ``bench.py``).
   the dense PyTorch path on the same GPU (the reference's only path for these
   dynamics), with 8 chains checked against that path in FP64 on the CPU.
 
+* ``--config rotation-profile``: the rotation kernels alone at an eighth of
+  that shape (B32, 2,048 chains), untimed: the case their ncu captures run on.
+
 * ``--config d64-profile``: the (64, 64) kernels on 296 chains (B37 T512 H8,
   one wave at two CTAs per SM), untimed: the case their ncu captures run on.
 
@@ -453,6 +456,47 @@ def rotation(steps: int, warmup: int) -> dict:
             "warmup": warmup, "data": "synthetic"}
 
 
+def rotation_profile(steps: int, warmup: int) -> dict:
+    """The rotation kernels through the C ABI on 2,048 chains (B32 T512 H64 D8
+    M8, chunk 64, FP32): ``steps`` forward + backward pairs, untimed -- the
+    small case an ncu capture of ``rot_forward`` / ``rot_backward`` runs on."""
+    import torch
+    import torch.nn.functional as F
+    from bayes_ssm import _capi
+    b, t, h, d, m, chunk, floor = 32, 512, 64, 8, 8, 64, 1e-6
+    n, j = b * h, d // 2
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(8)
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=g, device=dev)
+
+    k, q, v = F.normalize(rn(n, t, d), dim=-1), F.normalize(rn(n, t, d), dim=-1), rn(n, t, m) / math.sqrt(m)
+    rho = 0.85 + 0.1 * torch.rand(n, t, j, generator=g, device=dev)
+    ang = 0.4 * rn(n, t, j)
+    cs, sn = rho * ang.cos(), rho * ang.sin()
+    pp, rr = F.softplus(-3.0 + rn(n, t, j)), F.softplus(rn(n, t)) + 1e-3
+    gy = rn(n, t, m) / math.sqrt(m)
+    nb = (t + chunk - 1) // chunk
+    f32 = dict(device=dev, dtype=torch.float32)
+    out, mt, pt = torch.empty(n, t, m, **f32), torch.empty(n, d, m, **f32), torch.empty(n, d, d, **f32)
+    bm, bc = torch.empty(n, nb + 1, d, m, **f32), torch.empty(n, nb + 1, d, d, **f32)
+    gk, gv, gq = torch.empty_like(k), torch.empty_like(v), torch.empty_like(q)
+    gc, gs, gp = (torch.empty(n, t, j, **f32) for _ in range(3))
+    gr = torch.empty(n, t, **f32)
+    wsb = _capi.rotation_workspace_bytes(d, m, n, t, chunk)
+    ws = torch.empty(max(wsb, 1), device=dev, dtype=torch.uint8)
+    sp = torch.cuda.current_stream().cuda_stream
+    for _ in range(steps):
+        _capi.rotation_forward(d, m, k, v, q, cs, sn, pp, rr, None, None, out, mt, pt, bm, bc, n, t, chunk, floor, sp)
+        _capi.rotation_backward(d, m, False, k, v, q, cs, sn, pp, rr, bm, bc, gy, None, None, gk, gv, gq, gc, gs,
+                                gp, gr, None, None, ws, wsb, n, t, chunk, floor, sp)
+    torch.cuda.synchronize()
+    _capi.stream_status(sp)
+    return {"config": "rotation-profile", "workload": "rotation fwd + bwd, B32 T512 H64 D8 M8 = 2,048 chains "
+            "(profiling case)", "launches": 2 * steps, "timed": False}
+
+
 def d64_profile(steps: int, warmup: int) -> dict:
     """The (64, 64) forward and backward on 296 chains (B37 T512 H8, chunk 64,
     FP32): ``steps`` forward + backward pairs, untimed -- the small case an ncu
@@ -649,13 +693,14 @@ def _peak_hbm() -> float:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", choices=("2", "4", "d64", "d64-profile", "envelope", "envelope-profile", "mixer",
-                                         "refcuda", "refcuda64", "rotation"), required=True)
+                                         "refcuda", "refcuda64", "rotation", "rotation-profile"), required=True)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()
     fn = {"2": config2, "4": config4, "d64": d64, "d64-profile": d64_profile, "envelope": envelope,
           "envelope-profile": envelope_profile,
-          "mixer": mixer, "refcuda": refcuda, "refcuda64": refcuda64, "rotation": rotation}[args.config]
+          "mixer": mixer, "refcuda": refcuda, "refcuda64": refcuda64, "rotation": rotation,
+          "rotation-profile": rotation_profile}[args.config]
     print(json.dumps(fn(args.steps, max(3, args.warmup))), flush=True)
 
 
