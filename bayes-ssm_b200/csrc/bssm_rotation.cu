@@ -41,9 +41,10 @@ constexpr int kSub = 4;
 #ifndef BSSM_ROT_BWD_MINB
 #define BSSM_ROT_BWD_MINB 4
 #endif
-// The forward's launch bounds (by default the block size alone: 96 registers,
-// five CTAs per SM).  Eight or six per SM (64 / 80 registers, with spills) did
-// not help: 7.95-8.18 and 8.11 against 7.97 ms per API step.
+// The forward's launch bounds (by default the block size alone).  Before its
+// one-token prefetch (96 registers, five CTAs per SM), eight or six per SM (64 /
+// 80 registers, with spills) did not help: 7.95-8.18 and 8.11 against 7.97 ms
+// per API step.  The prefetch (128 registers): 6.66 -> 6.48 ms.
 #ifdef BSSM_ROT_FWD_MINB
 #define BSSM_ROT_FWD_BOUNDS __launch_bounds__(kThreads, BSSM_ROT_FWD_MINB)
 #else
@@ -231,10 +232,12 @@ __global__ void BSSM_ROT_FWD_BOUNDS rot_forward(const Args A) {
     float *bm = A.bmean + chain * (nb + 1) * D * M;
     float *bc = A.bcov + chain * (nb + 1) * D * D;
     store_state<D, M>(bm, bc, own, col0, Mc, P);
+    Tok<D, M> nx;  // the next token's inputs, loaded one token ahead
+    if (T > 0) load_tok<D, M, false>(nx, A, chain * T, col0);
     for (long ti = 0; ti < T; ++ti) {
         const long row = chain * T + ti;
-        Tok<D, M> tk;
-        load_tok<D, M, false>(tk, A, row, col0);
+        const Tok<D, M> tk = nx;
+        if (ti + 1 < T) load_tok<D, M, false>(nx, A, row + 1, col0);
         Step<D, M> o;
         fwd_step<D, M>(g, tk, Mc, P, A.floor, o);
 #pragma unroll
