@@ -244,8 +244,8 @@ struct StepOut {
     float beta, s;
 };
 
-__device__ __forceinline__ void gain_step(const Tiles &st, const TokIn &tk, Xchg &x, int par, int r, int c,
-                                          float floor_, StepOut &o) {
+__device__ __forceinline__ void gain_pre(const Tiles &st, const TokIn &tk, Xchg &x, int par, int r, int c,
+                                         StepOut &o) {
     float k_c[4], a_c[4], k_r[4], a_r[4], v_r[4];
     unpack(ld4(tk.k + 4 * c), k_c);
     unpack(ld4(tk.a + 4 * c), a_c);
@@ -285,13 +285,22 @@ __device__ __forceinline__ void gain_step(const Tiles &st, const TokIn &tk, Xchg
         for (int i = 0; i < 4; ++i) sp = fmaf(k_r[i], o.u_r[i], sp);
         x.spart[par][r] = sp;
     }
-    __syncthreads();
+}
+// The rest once the exchange is visible (after a block barrier).
+__device__ __forceinline__ void gain_post(const TokIn &tk, const Xchg &x, int par, int c, float floor_, StepOut &o) {
     float s = tk.r;
 #pragma unroll
     for (int q = 0; q < 16; ++q) s += x.spart[par][q];
     o.s = s;
     o.beta = clamp_beta(s, floor_);
     unpack(ld4(x.u[par] + 4 * c), o.u_c);
+}
+
+__device__ __forceinline__ void gain_step(const Tiles &st, const TokIn &tk, Xchg &x, int par, int r, int c,
+                                          float floor_, StepOut &o) {
+    gain_pre(st, tk, x, par, r, c, o);
+    __syncthreads();
+    gain_post(tk, x, par, c, floor_, o);
 }
 
 // The state update of one token from its gain (in place).
@@ -343,25 +352,27 @@ __global__ void __launch_bounds__(kThreads, 2) d64_forward(const FwdArgs<float> 
     store_state_g(st, F.bmean + chain * (nb + 1) * D * M, F.bcov + chain * (nb + 1) * D * D, r, c);
 #pragma unroll
     for (int s = 0; s < kStages; ++s) fill_constants<FIXED, false>(ring + s, A);
+    // One block barrier per token: the gain exchange's barrier of token ti also
+    // publishes token ti + 1 (each thread waits for its own copies of it first)
+    // and frees the slot of token ti - 1 for token ti + 2.
     for (long ti = 0; ti < 2 && ti < T; ++ti) {
         stage_token<FIXED, true, false>(ring + ti, A, chain, ti);
         cp_async_commit();
     }
+    cp_async_wait<0>();
+    __syncthreads();  // tokens 0 and 1 visible
     for (long ti = 0; ti < T; ++ti) {
         const int slot = static_cast<int>(ti % kStages);
-        if (ti + 1 < T) {
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();  // token ti visible; every thread is done with slot (ti + 2) % kStages
+        const TokIn &tk = ring[slot];
+        StepOut o;
+        gain_pre(st, tk, x, static_cast<int>(ti & 1), r, c, o);
+        cp_async_wait<0>();  // this thread's copies of token ti + 1
+        __syncthreads();     // exchange and token ti + 1 visible; every thread is done with token ti - 1
         if (ti + 2 < T) {
             stage_token<FIXED, true, false>(ring + (ti + 2) % kStages, A, chain, ti + 2);
             cp_async_commit();
         }
-        const TokIn &tk = ring[slot];
-        StepOut o;
-        gain_step(st, tk, x, static_cast<int>(ti & 1), r, c, F.floor, o);
+        gain_post(tk, x, static_cast<int>(ti & 1), c, F.floor, o);
         update_step(st, tk, o, r, c);
         // readout y = M'^T q over the key rows 4c.. of the tile, then the half-warp
         float q_c[4], py[4];
@@ -456,24 +467,24 @@ __global__ void __launch_bounds__(kThreads, BSSM_D64_BWD_MINB) d64_backward(cons
         if (nsub > 1) {
             load_state_g(st, bmean, bcov, r, c);
             const int upto = (nsub - 1) * kSub;  // tokens to replay
+            // one block barrier per token, as in the forward
             for (int li = 0; li < 2 && li < upto; ++li) {
                 stage_token<FIXED, false, false>(sm.ring + li, A, chain, t0 + li);
                 cp_async_commit();
             }
+            cp_async_wait<0>();
+            __syncthreads();
             for (int li = 0; li < upto; ++li) {
-                if (li + 1 < upto) {
-                    cp_async_wait<1>();
-                } else {
-                    cp_async_wait<0>();
-                }
-                __syncthreads();
+                const TokIn &tk = sm.ring[li % kStages];
+                StepOut o;
+                gain_pre(st, tk, sm.x, li & 1, r, c, o);
+                cp_async_wait<0>();  // this thread's copies of token li + 1
+                __syncthreads();     // exchange and token li + 1 visible; token li - 1 done with
                 if (li + 2 < upto) {
                     stage_token<FIXED, false, false>(sm.ring + (li + 2) % kStages, A, chain, t0 + li + 2);
                     cp_async_commit();
                 }
-                const TokIn &tk = sm.ring[li % kStages];
-                StepOut o;
-                gain_step(st, tk, sm.x, li & 1, r, c, floor_, o);
+                gain_post(tk, sm.x, li & 1, c, floor_, o);
                 update_step(st, tk, o, r, c);
                 if ((li + 1) % kSub == 0) store_state_ws(st, ws + static_cast<long>((li + 1) / kSub - 1) * kStateFloats);
             }
