@@ -37,7 +37,9 @@ constexpr int kSub = 4;
 // CTAs per SM the backward's registers are sized for.  At config 3's shape
 // (16,384 chains at D8: 1,024 CTAs) four per SM run the launch in two waves
 // where three (166 registers, no spills) took three: 8.00 against 8.36 ms per
-// API step, with 52 bytes spilled; three per SM forced: 8.73 ms.
+// API step, with 52 bytes spilled; three per SM forced: 8.73 ms.  Loading the
+// chunk replay's tokens one ahead, as the forward does, was slower here (6.67 ms
+// at four CTAs, spilling more; 6.98 at three, against 6.51).
 #ifndef BSSM_ROT_BWD_MINB
 #define BSSM_ROT_BWD_MINB 4
 #endif
