@@ -921,6 +921,7 @@ __global__ void __launch_bounds__(kThreads) epilogue_tile_backward_kernel(const 
         w[i] = __ldg(a.w + i);
         gw[i] = 0.f;
     }
+#pragma unroll  // later rows' gate and output-gradient loads issue early (forward: no gain, 0.126 vs 0.119 ms)
     for (int tl = threadIdx.x >> 5; tl < E::kT; tl += kThreads / 32) {
         const long t = t0 + tl;
         if (h >= a.heads || t >= a.t) continue;

@@ -29,8 +29,8 @@ headline, config 3, is ``bench.py``).
   with BF16 k/q/v, beside the same layer with the PyTorch op chains for the
   prologue and readout.
 
-* ``--config envelope-profile``: the prologue kernels alone at an eighth of
-  that shape (B32), untimed: the case the prologue's ncu captures run on.
+* ``--config envelope-profile``: the prologue and readout kernels alone at an
+  eighth of that shape (B32), untimed: the case their ncu captures run on.
 
 * ``--config rotation``: rotation dynamics (damped 2-D rotations per key pair,
   per-pair process noise) at config 3's shape (B256 T512 H64 D8 M8, chunk 64,
@@ -569,9 +569,17 @@ def envelope_profile(steps: int, warmup: int) -> dict:
                                 proc, obs, sp)
         _capi.envelope_prologue_backward(x, _capi.BSSM_BF16, b, t, h, d, hd, pch, wt, bias, gk, gq, gv,
                                          _capi.BSSM_F32, gd, gp, go, gx, pch, gw, gb, ws, sp)
+    # the readout at the same shape (FP32 reads, BF16 gate), through the public wrapper
+    from bayes_ssm.envelope import read_epilogue
+    read = torch.randn(n, t, hd, generator=g, device=dev).requires_grad_()
+    gate = torch.randn(b, t, w, generator=g, device=dev).to(torch.bfloat16).requires_grad_()
+    nw = (torch.rand(hd, generator=g, device=dev) + 0.5).requires_grad_()
+    up = torch.randn(b, t, w, generator=g, device=dev).to(torch.bfloat16)
+    for _ in range(steps):
+        torch.autograd.grad(read_epilogue(read, gate, nw, heads=h), (read, gate, nw), up)
     torch.cuda.synchronize()
-    return {"config": "envelope-profile", "workload": "prologue fwd + bwd, B32 T512 H64 D8 head_dim 8 (profiling "
-            "case)", "launches": 2 * steps, "timed": False}
+    return {"config": "envelope-profile", "workload": "prologue and readout fwd + bwd, B32 T512 H64 D8 head_dim 8 "
+            "(profiling case)", "launches": 4 * steps, "timed": False}
 
 
 def refcuda64(steps: int, warmup: int) -> dict:
