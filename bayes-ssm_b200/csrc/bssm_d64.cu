@@ -208,30 +208,28 @@ __device__ __forceinline__ void store_state_g(const Tiles &s, float *mean, float
         st4(mean + (4 * c + i) * M + 4 * r, s.Mt[i][0], s.Mt[i][1], s.Mt[i][2], s.Mt[i][3]);
     }
 }
-// Thread-tile layout of a saved state: float x of thread t at x * 256 + t.
+// Thread-tile layout of a saved state: quad x (rows of P, then of Mt) of
+// thread t at (x * 256 + t) * 4, so a warp moves 512 contiguous bytes per
+// 16-byte access.
 __device__ __forceinline__ void store_state_ws(const Tiles &s, float *ws) {
-    const int t = threadIdx.x;
+    float4 *const w = reinterpret_cast<float4 *>(ws) + threadIdx.x;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            ws[(i * 4 + j) * kThreads + t] = s.P[i][j];
-            ws[(16 + i * 4 + j) * kThreads + t] = s.Mt[i][j];
-        }
+    for (int i = 0; i < 4; ++i) {
+        w[i * kThreads] = make_float4(s.P[i][0], s.P[i][1], s.P[i][2], s.P[i][3]);
+        w[(4 + i) * kThreads] = make_float4(s.Mt[i][0], s.Mt[i][1], s.Mt[i][2], s.Mt[i][3]);
+    }
 }
 __device__ __forceinline__ void load_state_ws(Tiles &s, const float *ws) {
-    const int t = threadIdx.x;
+    const float4 *const w = reinterpret_cast<const float4 *>(ws) + threadIdx.x;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            s.P[i][j] = ws[(i * 4 + j) * kThreads + t];
-            s.Mt[i][j] = ws[(16 + i * 4 + j) * kThreads + t];
-        }
+    for (int i = 0; i < 4; ++i) {
+        unpack(w[i * kThreads], s.P[i]);
+        unpack(w[(4 + i) * kThreads], s.Mt[i]);
+    }
 }
 
 // Exchange buffers of one token (double-buffered by token parity).
-struct Xchg {
+struct __align__(16) Xchg {
     float u[2][D];
     float spart[2][16];
 };
@@ -290,7 +288,10 @@ __device__ __forceinline__ void gain_pre(const Tiles &st, const TokIn &tk, Xchg 
 __device__ __forceinline__ void gain_post(const TokIn &tk, const Xchg &x, int par, int c, float floor_, StepOut &o) {
     float s = tk.r;
 #pragma unroll
-    for (int q = 0; q < 16; ++q) s += x.spart[par][q];
+    for (int q = 0; q < 16; q += 4) {  // in order, four at a time
+        const float4 v = ld4(x.spart[par] + q);
+        s = ((s + v.x) + v.y + v.z) + v.w;
+    }
     o.s = s;
     o.beta = clamp_beta(s, floor_);
     unpack(ld4(x.u[par] + 4 * c), o.u_c);
@@ -403,7 +404,7 @@ struct BwdSmem {
     TokIn tok[kSub];                     // the sub-chunk's inputs
     TokIn ring[kStages];                 // phase-A input ring
     Xchg x;
-    float hist[kSub][2 * kTileFloats][kThreads];  // pre-step tiles, thread-private columns
+    float4 hist[kSub][2 * kTileFloats / 4][kThreads];  // pre-step tile rows, thread-private columns
     float hu[kSub][D], he[kSub][M];      // per-token gain and innovation
     float hbeta[kSub], hs[kSub];
     float red[4][16][D];                 // value-index partial sums: gq, h, M ge, gMbar . M
@@ -507,12 +508,10 @@ __global__ void __launch_bounds__(kThreads, BSSM_D64_BWD_MINB) d64_backward(cons
             for (int x = 0; x < slen; ++x) {
                 const TokIn &tk = sm.tok[x];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        sm.hist[x][i * 4 + j][t] = st.P[i][j];
-                        sm.hist[x][16 + i * 4 + j][t] = st.Mt[i][j];
-                    }
+                for (int i = 0; i < 4; ++i) {
+                    sm.hist[x][i][t] = make_float4(st.P[i][0], st.P[i][1], st.P[i][2], st.P[i][3]);
+                    sm.hist[x][4 + i][t] = make_float4(st.Mt[i][0], st.Mt[i][1], st.Mt[i][2], st.Mt[i][3]);
+                }
                 StepOut o;
                 gain_step(st, tk, sm.x, x & 1, r, c, floor_, o);
                 if (c == 0) {
@@ -533,12 +532,10 @@ __global__ void __launch_bounds__(kThreads, BSSM_D64_BWD_MINB) d64_backward(cons
                 const int par = x & 1;
                 float Pp[4][4], Mp[4][4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        Pp[i][j] = sm.hist[x][i * 4 + j][t];
-                        Mp[i][j] = sm.hist[x][16 + i * 4 + j][t];
-                    }
+                for (int i = 0; i < 4; ++i) {
+                    unpack(sm.hist[x][i][t], Pp[i]);
+                    unpack(sm.hist[x][4 + i][t], Mp[i]);
+                }
                 float k_c[4], a_c[4], q_c[4], k_r[4], a_r[4], gy_r[4], u_c[4], u_r[4], e_r[4];
                 unpack(ld4(tk.k + 4 * c), k_c);
                 unpack(ld4(tk.a + 4 * c), a_c);
