@@ -48,7 +48,7 @@ _SIGNATURES = {
     "bssm_backward_chunked_noalloc": ([_i, _i, _i, _i, _i, _i] + [_vp] * 21 + [_l, _l, _i, _d, _vp], _i),
     "bssm_check_values": ([_vp, _l, _i, _vp, _vp], _i),
     "bssm_envelope_partial_floats": ([_l, _l, _i, _i, _i], _l),
-    "bssm_envelope_prologue": ([_vp, _i, _l, _l, _i, _i, _i, _l] + [_vp] * 5 + [_i] + [_vp] * 4, _i),
+    "bssm_envelope_prologue": ([_vp, _i, _l, _l, _i, _i, _i, _l] + [_vp] * 5 + [_i] + [_vp] * 5, _i),
     "bssm_envelope_prologue_backward": ([_vp, _i, _l, _l, _i, _i, _i, _l] + [_vp] * 5 + [_i] + [_vp] * 4
                                         + [_l, _vp, _vp, _vp, _l, _vp], _i),
     "bssm_envelope_epilogue_partial_floats": ([_l, _l, _i, _i], _l),
@@ -265,10 +265,14 @@ def envelope_partial_floats(batch, tokens, heads, key_dim, head_dim) -> int:
 
 
 def envelope_prologue(projected, in_dtype, batch, tokens, heads, key_dim, head_dim, row_stride, conv_weight,
-                      aux_bias, keys, queries, values, out_dtype, decay, process, observation, stream) -> None:
+                      aux_bias, keys, queries, values, out_dtype, decay, process, observation, stream,
+                      check_flags=None) -> None:
+    """``check_flags``: None, or a zeroed int32 tensor of 6 words that receives
+    the CHECK_* flags of keys, values, queries, decay, process, observation."""
     rc = load().bssm_envelope_prologue(ptr(projected), in_dtype, batch, tokens, heads, key_dim, head_dim,
                                        row_stride, ptr(conv_weight), ptr(aux_bias), ptr(keys), ptr(queries),
-                                       ptr(values), out_dtype, ptr(decay), ptr(process), ptr(observation), stream)
+                                       ptr(values), out_dtype, ptr(decay), ptr(process), ptr(observation),
+                                       ptr(check_flags), stream)
     check(rc, "bssm_envelope_prologue")
 
 

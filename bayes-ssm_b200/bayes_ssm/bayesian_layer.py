@@ -21,6 +21,7 @@ Execution:
 from __future__ import annotations
 
 import math
+import weakref
 from numbers import Real
 from typing import Optional, Tuple
 
@@ -105,6 +106,38 @@ def _device_flags(tensors) -> Optional[list]:
     return _capi.check_values([x.detach() for x in tensors])
 
 
+# Tensors whose value checks a producing kernel already computed while it
+# wrote them (the fused mixer prologue): data pointer -> (weak reference to
+# the producer's output, element count, dtype, version, device flag words,
+# word index).  An entry counts only while that output is alive, unchanged
+# (same version counter) and covers exactly the checked tensor; anything else
+# is checked by the check kernel as usual.
+_PRECHECKED: dict = {}
+
+
+def _register_prechecked(tensors, flags: Tensor) -> None:
+    """Record that ``flags[i]`` (an int32 device tensor) holds the CHECK_*
+    flags of every value of ``tensors[i]``, as ``bssm_check_values`` would
+    report them."""
+    for key in [k for k, e in _PRECHECKED.items() if e[0]() is None]:
+        del _PRECHECKED[key]
+    for i, x in enumerate(tensors):
+        _PRECHECKED[x.data_ptr()] = (weakref.ref(x), x.numel(), x.dtype, x._version, flags, i)
+
+
+def _prechecked_word(x: Tensor):
+    """(flags tensor, index) holding x's check flags, or None."""
+    e = _PRECHECKED.get(x.data_ptr()) if x.is_cuda else None
+    if e is None:
+        return None
+    ref, numel, dtype, version, flags, i = e
+    src = ref()
+    if (src is None or x.numel() != numel or x.dtype != dtype or not x.is_contiguous()
+            or src._version != version or x._version != version):
+        return None
+    return flags, i
+
+
 class _DeviceChecks:
     """The value checks of one ``bayesian_layer`` call, raised in the
     reference's order (bayesian_layer.py:798-985) but run together: checks of
@@ -140,7 +173,7 @@ class _DeviceChecks:
             self.flush()
             self._run_now(x, name, kind)
             return
-        self.items.append((x, name, kind))
+        self.items.append((x, name, kind, _prechecked_word(x)))
 
     @staticmethod
     def _run_now(x: Tensor, name: str, kind: int) -> None:
@@ -153,13 +186,21 @@ class _DeviceChecks:
         items, self.items = self.items, []
         if not items:
             return
-        flags = _device_flags([x for x, _, _ in items])
+        plain = [x for x, _, _, pre in items if pre is None]
+        flags = _device_flags(plain) if plain else []
         if flags is None:
-            for x, name, kind in items:
+            for x, name, kind, _ in items:
                 self._run_now(x, name, kind)
             return
+        if len(plain) < len(items):  # words a producing kernel computed: one read-back per word buffer
+            bufs = {}
+            for _, _, _, p in items:
+                if p is not None and id(p[0]) not in bufs:
+                    bufs[id(p[0])] = p[0].tolist()
+            plain_flags = iter(flags)
+            flags = [bufs[id(p[0])][p[1]] if p is not None else next(plain_flags) for _, _, _, p in items]
         from ._capi import CHECK_NEGATIVE, CHECK_NONFINITE, CHECK_NOT_POSITIVE
-        for (x, name, kind), f in zip(items, flags):
+        for (x, name, kind, _), f in zip(items, flags):
             if f & CHECK_NONFINITE:
                 raise ValueError(f"{name} must contain only finite values")
             if kind == 2 and f & CHECK_NOT_POSITIVE:

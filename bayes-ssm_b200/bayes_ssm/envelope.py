@@ -80,7 +80,7 @@ def _rows(x: Tensor) -> int:
 
 class _PaperPrologue(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, projected, conv_weight, aux_bias, heads, key_dim, head_dim, out_dtype):
+    def forward(ctx, projected, conv_weight, aux_bias, heads, key_dim, head_dim, out_dtype, check_flags):
         b, t, _ = projected.shape
         sw, w, c, aux_w = _widths(heads, key_dim, head_dim)
         dev = projected.device
@@ -97,7 +97,7 @@ class _PaperPrologue(torch.autograd.Function):
         with torch.cuda.device(dev):
             _capi.envelope_prologue(projected, _DTYPES[projected.dtype], b, t, heads, key_dim, head_dim,
                                     _rows(projected), wt, bias, keys, queries, values, _DTYPES[out_dtype], decay,
-                                    process, observation, stream)
+                                    process, observation, stream, check_flags=check_flags)
         ctx.save_for_backward(projected, wt, bias)
         ctx.dims = (heads, key_dim, head_dim, out_dtype, conv_weight.dtype,
                     None if aux_bias is None else aux_bias.dtype, tuple(conv_weight.shape))
@@ -129,7 +129,7 @@ class _PaperPrologue(torch.autograd.Function):
         gw = gw.reshape(w_shape).to(w_dtype)
         if gb is not None:
             gb = gb.to(b_dtype)
-        return gx, gw, gb, None, None, None, None
+        return gx, gw, gb, None, None, None, None, None
 
 
 def paper_prologue(projected: Tensor, conv_weight: Tensor, aux_bias: Optional[Tensor] = None, *, heads: int,
@@ -162,7 +162,15 @@ def paper_prologue(projected: Tensor, conv_weight: Tensor, aux_bias: Optional[Te
     if key_dim < 2 or key_dim > 64 or key_dim & (key_dim - 1) or head_dim % 2:
         raise NotImplementedError("paper_prologue on CUDA needs key_dim a power of two in [2, 64] and an even "
                                   f"head_dim (got {key_dim}, {head_dim}); use paper_prologue_torch")
-    return _PaperPrologue.apply(projected, conv_weight, aux_bias, heads, key_dim, head_dim, out_dtype)
+    # The kernel also computes bayesian_layer's value checks of what it writes
+    # (finite keys, values, queries and decay; nonnegative process and
+    # positive observation variances), so that layer need not read them again.
+    check_flags = torch.zeros(6, device=projected.device, dtype=torch.int32)
+    outs = _PaperPrologue.apply(projected, conv_weight, aux_bias, heads, key_dim, head_dim, out_dtype, check_flags)
+    k, q, v, decay, process, observation = outs
+    from .bayesian_layer import _register_prechecked
+    _register_prechecked((k, v, q, decay, process, observation), check_flags)
+    return outs
 
 
 def read_epilogue_torch(read: Tensor, gate: Tensor, norm_weight: Tensor, *, heads: int,

@@ -330,7 +330,32 @@ struct ProArgs {
     void *k, *q, *v;    // [B*H, T, D] / [B*H, T, HD]
     float *decay;       // [B*H, T, D]
     float *process, *observation;  // [B*H, T]
+    // null, or the check words of keys, values, queries, decay, process and
+    // observation (in that order): the CHECK_* flags of the values written
+    unsigned *flags;
 };
+
+// The input checks of bayesian_layer over the values this kernel writes, as
+// bssm_check_values reports them.  The projection streams and the decay are
+// checked for finiteness only, through an accumulator that fma(v, 0, acc)
+// turns NaN exactly when some v is infinite or NaN (0 * finite is a zero and
+// never overflows); the noise rows get all three flags.
+__device__ __forceinline__ unsigned value_flags(float v) {
+    unsigned f = 0;
+    if (!isfinite(v)) f |= BSSM_CHECK_NONFINITE;
+    if (v <= 0.f) f |= BSSM_CHECK_NOT_POSITIVE;  // NaN compares false
+    if (v < 0.f) f |= BSSM_CHECK_NEGATIVE;
+    return f;
+}
+template <bool OUT_BF, int N>
+__device__ __forceinline__ void nonfinite_acc(float &acc, const float (&v)[N]) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        // the value as stored: a BF16 output can round a finite value to infinity
+        const float x = OUT_BF ? __bfloat162float(__float2bfloat16_rn(v[j])) : v[j];
+        acc = fmaf(x, 0.f, acc);
+    }
+}
 
 // Thread = CW adjacent channels of one stream (every stream and head row
 // boundary falls on a multiple of CW), walking one token span.
@@ -404,6 +429,8 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
     const long ostep = ch.kind == kV ? s.hd : s.d;
     long oidx = (chain * s.t + t0) * ostep + ch.within;
     long nidx = chain * s.t + t0;
+    float nfacc = 0.f;               // NaN once a written q / k / v / decay value is not finite
+    unsigned pflags = 0, rflags = 0;  // of the process and observation values written
 #pragma unroll 4
     for (int k = 0; k < steps; ++k, oidx += ostep, ++nidx) {
         const long t = t0 + k;
@@ -430,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
 #pragma unroll
                 for (int j = 0; j < CW; ++j) o[j] *= r;
                 stn<OUT_BF, CW>(ch.kind == kQ ? a.q : a.k, oidx, o);
+                nonfinite_acc<OUT_BF>(nfacc, o);
             }
         } else if (L == 0 && hm.ng > 1 && qk) {  // CW / D whole heads
 #pragma unroll
@@ -445,9 +473,11 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
                     if ((j >> hm.shift) == gi) o[j] *= r;
             }
             st_heads<OUT_BF, CW>(ch.kind == kQ ? a.q : a.k, chain, t, s.t, s.d, o);
+            nonfinite_acc<OUT_BF>(nfacc, o);
         }
         if (ch.kind == kV) {
             stn<OUT_BF, CW>(a.v, oidx, o);
+            nonfinite_acc<OUT_BF>(nfacc, o);
         } else if (ch.kind == kDecay) {
             float dcy[CW];
 #pragma unroll
@@ -457,16 +487,30 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
             } else {
                 st_heads<false, CW>(a.decay, chain, t, s.t, s.d, dcy);
             }
+            nonfinite_acc<false>(nfacc, dcy);
         } else if (ch.kind == kNoise) {
 #pragma unroll
             for (int i = 0; i < CW / 2; ++i) {
-                a.process[nidx + i * s.t] = softplus(x[2 * i] + bias[2 * i]) + kNoiseFloor;
-                a.observation[nidx + i * s.t] = softplus(x[2 * i + 1] + bias[2 * i + 1]) + kNoiseFloor;
+                const float pv = softplus(x[2 * i] + bias[2 * i]) + kNoiseFloor;
+                const float rv = softplus(x[2 * i + 1] + bias[2 * i + 1]) + kNoiseFloor;
+                a.process[nidx + i * s.t] = pv;
+                a.observation[nidx + i * s.t] = rv;
+                pflags |= value_flags(pv);
+                rflags |= value_flags(rv);
             }
         }
         issue(k + FR);  // after the slot's values were used
     }
     cp_async_wait_group<0>();
+    if (a.flags != nullptr) {  // flags are rare: one atomic per thread that saw one
+        if (ch.kind == kNoise) {
+            if (pflags) atomicOr(a.flags + 4, pflags);
+            if (rflags) atomicOr(a.flags + 5, rflags);
+        } else if (ch.kind != kIdle && nfacc != nfacc) {
+            const int slot = ch.kind == kK ? 0 : ch.kind == kV ? 1 : ch.kind == kQ ? 2 : 3;
+            atomicOr(a.flags + slot, BSSM_CHECK_NONFINITE);
+        }
+    }
 }
 
 struct EnvBwdArgs {
@@ -1343,7 +1387,7 @@ long bssm_envelope_partial_floats(long batch, long tokens, int heads, int key_di
 int bssm_envelope_prologue(const void *projected, int in_dtype, long batch, long tokens, int heads, int key_dim,
                            int head_dim, long row_stride, const float *conv_weight, const float *aux_bias,
                            void *keys, void *queries, void *values, int out_dtype, float *decay, float *process,
-                           float *observation, void *stream) {
+                           float *observation, unsigned *check_flags, void *stream) {
     Shape s{batch, tokens, heads, key_dim, head_dim, row_stride, 1};
     if (int rc = check_shape(s, in_dtype, out_dtype)) return rc;
     if (batch == 0 || tokens == 0) {
@@ -1361,7 +1405,10 @@ int bssm_envelope_prologue(const void *projected, int in_dtype, long batch, long
     s.tsplit = pick_tsplit(tokens, kFwdSpan);
     if (s.tsplit > 65535 || too_many_ctas(s))
         return fail(BSSM_ERR_INVALID, "envelope: sequence too long (%ld tokens)", tokens);
-    const ProArgs a{projected, conv_weight, aux_bias, keys, queries, values, decay, process, observation};
+    if (check_flags != nullptr && (reinterpret_cast<uintptr_t>(check_flags) & 3))
+        return fail(BSSM_ERR_ALIGNMENT, "envelope prologue: check_flags must be 4-byte aligned");
+    const ProArgs a{projected, conv_weight, aux_bias, keys, queries, values, decay, process, observation,
+                    check_flags};
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (kFwdCW >= 4 && cw_fits<4>(s, 0, aligned8, 5)) {
         if (s.d == 4) launch_fwd<4, 1>(s, a, in_dtype, out_dtype, st);

@@ -347,11 +347,17 @@ int bssm_check_values(const void *x, long n, int dtype, unsigned *flags, void *s
  * in out_dtype; decay [batch*heads, tokens, key_dim], process and observation
  * [batch*heads, tokens] in float32.  key_dim must be a power of two in
  * [2, 64] and head_dim even; row_stride even; tensors 8-byte aligned.
+ * check_flags is null or six zeroed words into which the kernel ORs the
+ * BSSM_CHECK_* flags of the keys, values, queries, decay, process and
+ * observation it writes (in that order), as bssm_check_values would report
+ * them -- finiteness only for the first four, all three flags for the noise
+ * rows -- so a caller that validates these outputs (bayesian_layer,
+ * reference bayesian_layer.py:105-128) need not read them again.
  */
 int bssm_envelope_prologue(const void *projected, int in_dtype, long batch, long tokens, int heads, int key_dim,
                            int head_dim, long row_stride, const float *conv_weight, const float *aux_bias,
                            void *keys, void *queries, void *values, int out_dtype, float *decay, float *process,
-                           float *observation, void *stream);
+                           float *observation, unsigned *check_flags, void *stream);
 
 /*
  * Backward of bssm_envelope_prologue.  Gradients of the six outputs (any may

@@ -127,6 +127,78 @@ def test_prologue_feeds_the_recurrence():
     assert _rel(gw1, gw2) <= 1e-4
 
 
+# channel offsets of one value in each stream of the fused projection (B, T, H, D, hd = 2, 40, 4, 8, 8):
+# q, k, v, a decay logit, a process and an observation noise channel
+_PLANTS = (None, 3, 32 + 5, 64 + 7, 96 + 2, 128 + 2, 128 + 5)
+
+
+@pytest.mark.parametrize("out_dtype", (torch.float32, torch.bfloat16))
+@pytest.mark.parametrize("plant", _PLANTS)
+def test_prologue_check_words_match_the_check_kernel(out_dtype, plant):
+    """The flags the prologue computes while writing its outputs equal
+    bssm_check_values' flags on those outputs, for every bit bayesian_layer
+    reads (finiteness of keys, values, queries and decay; all three flags of
+    the variances): healthy inputs, and a NaN planted in each stream."""
+    from bayes_ssm import _capi
+    from bayes_ssm.bayesian_layer import _prechecked_word
+    b, t, h, d, hd = 2, 40, 4, 8, 8
+    x, wt, bias = _inputs(b, t, h, d, hd, seed=23)
+    if plant is not None:
+        x[1, 17, plant] = float("nan")
+    outs = paper_prologue(x, wt, bias, heads=h, key_dim=d, head_dim=hd, out_dtype=out_dtype)
+    k, q, v, dec, p, r = outs
+    order = (k, v, q, dec, p, r)
+    words = []
+    for tensor in order:
+        pw = _prechecked_word(tensor)
+        assert pw is not None
+        words.append(int(pw[0][pw[1]]))
+    ref = _capi.check_values(list(order))
+    masks = [_capi.CHECK_NONFINITE] * 4 + [7, 7]
+    assert [w & m for w, m in zip(words, masks)] == [f & m for f, m in zip(ref, masks)]
+    assert any(words) == (plant is not None)
+
+
+def test_bayesian_layer_uses_the_prologue_check_words(monkeypatch):
+    """bayesian_layer reads the prologue's check words instead of launching the
+    check kernel, raises the reference's error from them, and falls back to
+    the check kernel for an output modified in place after the prologue."""
+    import sys
+
+    import bayes_ssm
+    bl = sys.modules["bayes_ssm.bayesian_layer"]
+    calls = []
+    real = bl._device_flags
+
+    def counting(tensors):
+        calls.append(len(tensors))
+        return real(tensors)
+
+    monkeypatch.setattr(bl, "_device_flags", counting)
+    b, t, h, d, hd = 2, 40, 4, 8, 8
+
+    def layer(k, q, v, dec, p, r):
+        return bayes_ssm.bayesian_layer(k, v, q, transition_diagonals=dec, process_variances=p,
+                                        observation_variances=r, chunk_length=16, optimized=True)
+
+    x, wt, bias = _inputs(b, t, h, d, hd, seed=24)
+    outs = paper_prologue(x, wt, bias, heads=h, key_dim=d, head_dim=hd)
+    y, _, _ = layer(*outs)
+    assert torch.isfinite(y).all() and calls == []
+    x[0, 3, 40] = float("inf")  # a key channel
+    outs = paper_prologue(x, wt, bias, heads=h, key_dim=d, head_dim=hd)
+    with pytest.raises(ValueError, match="keys must contain only finite values"):
+        layer(*outs)
+    assert calls == []
+    x, wt, bias = _inputs(b, t, h, d, hd, seed=24)
+    k, q, v, dec, p, r = paper_prologue(x, wt, bias, heads=h, key_dim=d, head_dim=hd)
+    q[1, 5, 2] = float("nan")  # after the prologue: its words no longer cover q
+    assert bl._prechecked_word(q) is None
+    with pytest.raises(ValueError, match="queries must contain only finite values"):
+        layer(k, q, v, dec, p, r)
+    assert calls == [1]
+
+
 @pytest.mark.parametrize("shape,read_dtype,gate_dtype", [
     ((2, 37, 4, 8), torch.float32, torch.float32), ((3, 64, 64, 8), torch.float32, torch.bfloat16),
     ((1, 19, 2, 16), torch.float32, torch.float32), ((2, 8, 3, 32), torch.bfloat16, torch.bfloat16),
