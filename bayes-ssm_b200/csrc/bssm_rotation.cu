@@ -39,7 +39,9 @@ constexpr int kSub = 4;
 // where three (166 registers, no spills) took three: 8.00 against 8.36 ms per
 // API step, with 52 bytes spilled; three per SM forced: 8.73 ms.  Loading the
 // chunk replay's tokens one ahead, as the forward does, was slower here (6.67 ms
-// at four CTAs, spilling more; 6.98 at three, against 6.51).
+// at four CTAs, spilling more; 6.98 at three, against 6.51), and so was an L2
+// prefetch of each chain's next 4-token block in both kernels (6.66 against
+// 6.52): at four CTAs per SM the loads' latency is not what binds.
 #ifndef BSSM_ROT_BWD_MINB
 #define BSSM_ROT_BWD_MINB 4
 #endif
