@@ -142,3 +142,53 @@ def test_assoc_scan_cuda_requires_cuda_tensors():
     k = torch.randn(1, 4, 2)
     with pytest.raises(ValueError, match="CUDA"):
         bayes_ssm.associative_static_bayesian_cuda(k, torch.randn(1, 4, 2), k)
+
+
+def test_queued_checks_merge_precomputed_words_in_order(monkeypatch):
+    """The queued value checks take a producing kernel's precomputed words for
+    some tensors and the check kernel's flags for the rest, and raise the
+    first failure in the reference's order (host logic; the flag sources are
+    faked on CPU)."""
+    import sys
+
+    bl = sys.modules["bayes_ssm.bayesian_layer"]
+    calls = []
+
+    def fake_device_flags(tensors):
+        calls.append(len(tensors))
+        return [int(x.flatten()[0].item()) for x in tensors]  # each fake tensor carries its flags
+
+    monkeypatch.setattr(bl, "_device_flags", fake_device_flags)
+    words = torch.tensor([0, 0, 1, 0, 0, 0], dtype=torch.int32)  # queries not finite
+
+    def run(entries):
+        chk = bl._DeviceChecks()
+        chk.items = list(entries)
+        chk.flush()
+
+    keys, values = torch.zeros(2), torch.zeros(2)
+    # every item precomputed: no check-kernel call, queries' word raises
+    with pytest.raises(ValueError, match="queries must contain only finite values"):
+        run([(keys, "keys", 0, (words, 0)), (values, "values", 0, (words, 1)), (keys, "queries", 0, (words, 2))])
+    assert calls == []
+    # mixed: a plain tensor earlier in the order fails first
+    bad_obs = torch.tensor([float(bayes_ssm._capi.CHECK_NOT_POSITIVE)])
+    with pytest.raises(ValueError, match="observation_variances must be strictly positive"):
+        run([(keys, "keys", 0, (words, 0)), (bad_obs, "observation_variances", 2, None),
+             (keys, "queries", 0, (words, 2))])
+    assert calls == [1]
+    # a negative-variance word on a kind-1 check
+    words2 = torch.tensor([0, 0, 0, 0, bayes_ssm._capi.CHECK_NEGATIVE, 0], dtype=torch.int32)
+    with pytest.raises(ValueError, match="process_variances must be nonnegative"):
+        run([(keys, "process_variances", 1, (words2, 4)), (torch.zeros(1), "observation_variances", 2, None)])
+    # all clear
+    run([(keys, "keys", 0, (torch.zeros(6, dtype=torch.int32), 0)), (torch.zeros(1), "values", 0, None)])
+
+
+def test_prechecked_registry_ignores_cpu_tensors():
+    import sys
+
+    bl = sys.modules["bayes_ssm.bayesian_layer"]
+    x = torch.zeros(4)
+    bl._register_prechecked((x,), torch.zeros(1, dtype=torch.int32))
+    assert bl._prechecked_word(x) is None  # words only stand for CUDA outputs
