@@ -159,6 +159,33 @@ def test_prologue_check_words_match_the_check_kernel(out_dtype, plant):
     assert any(words) == (plant is not None)
 
 
+@pytest.mark.parametrize("h,d,hd", [(4, 2, 8), (2, 16, 4), (4, 4, 6)])
+def test_prologue_check_words_other_head_layouts(h, d, hd):
+    """The same at the other head layouts of the forward (two heads per thread
+    at key dim 2, a head over several lanes at key dims 4 and 16): a NaN
+    planted in each stream sets that output's word as the check kernel does."""
+    from bayes_ssm import _capi
+    from bayes_ssm.bayesian_layer import _prechecked_word
+    b, t = 2, 24
+    sw, w = h * d, h * hd
+    starts = (0, sw, 2 * sw, 2 * sw + w, 3 * sw + w, 3 * sw + w + 1)  # q, k, v, decay, process, observation
+    masks = [_capi.CHECK_NONFINITE] * 4 + [7, 7]
+    for plant in (None,) + starts:
+        x, wt, bias = _inputs(b, t, h, d, hd, seed=25)
+        if plant is not None:
+            x[0, 9, plant] = float("nan")
+        k, q, v, dec, p, r = paper_prologue(x, wt, bias, heads=h, key_dim=d, head_dim=hd)
+        order = (k, v, q, dec, p, r)
+        words = []
+        for tensor in order:
+            pw = _prechecked_word(tensor)
+            assert pw is not None
+            words.append(int(pw[0][pw[1]]))
+        ref = _capi.check_values(list(order))
+        assert [w_ & m for w_, m in zip(words, masks)] == [f & m for f, m in zip(ref, masks)]
+        assert any(words) == (plant is not None)
+
+
 def test_bayesian_layer_uses_the_prologue_check_words(monkeypatch):
     """bayesian_layer reads the prologue's check words instead of launching the
     check kernel, raises the reference's error from them, and falls back to
