@@ -15,18 +15,12 @@
 #include <cstdint>
 
 #include "bayes_ssm_b200.h"
+#include "bssm_flags.cuh"
 #include "bssm_internal.h"
 
 namespace bssm {
 namespace {
 
-__device__ __forceinline__ unsigned flags_of(float v) {
-    unsigned f = 0;
-    if (!isfinite(v)) f |= BSSM_CHECK_NONFINITE;
-    if (v <= 0.f) f |= BSSM_CHECK_NOT_POSITIVE;  // NaN compares false: it only sets the first flag
-    if (v < 0.f) f |= BSSM_CHECK_NEGATIVE;
-    return f;
-}
 __device__ __forceinline__ float widen(float x) { return x; }
 __device__ __forceinline__ float widen(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ float widen(__half x) { return __half2float(x); }
@@ -53,18 +47,18 @@ __global__ void check_values_kernel(const T *__restrict__ x, long n, unsigned *f
             for (int u = 0; u < 4; ++u) {
                 const T *e = reinterpret_cast<const T *>(&w[u]);
 #pragma unroll
-                for (int j = 0; j < EC; ++j) f |= flags_of(widen(e[j]));
+                for (int j = 0; j < EC; ++j) f |= check_flags_of(widen(e[j]));
             }
         }
         for (; i < nvec; i += nthreads) {
             const uint4 w = __ldg(xv + i);
             const T *e = reinterpret_cast<const T *>(&w);
 #pragma unroll
-            for (int j = 0; j < EC; ++j) f |= flags_of(widen(e[j]));
+            for (int j = 0; j < EC; ++j) f |= check_flags_of(widen(e[j]));
         }
         done = nvec * EC;
     }
-    for (long i = done + tid; i < n; i += nthreads) f |= flags_of(widen(x[i]));
+    for (long i = done + tid; i < n; i += nthreads) f |= check_flags_of(widen(x[i]));
     f = __reduce_or_sync(0xffffffffu, f);
     if ((threadIdx.x & 31) == 0 && f != 0) atomicOr(flags, f);
 }

@@ -35,6 +35,7 @@
 #include <type_traits>
 
 #include "bayes_ssm_b200.h"
+#include "bssm_flags.cuh"
 #include "bssm_internal.h"
 
 namespace bssm {
@@ -339,14 +340,7 @@ struct ProArgs {
 // bssm_check_values reports them.  The projection streams and the decay are
 // checked for finiteness only, through an accumulator that fma(v, 0, acc)
 // turns NaN exactly when some v is infinite or NaN (0 * finite is a zero and
-// never overflows); the noise rows get all three flags.
-__device__ __forceinline__ unsigned value_flags(float v) {
-    unsigned f = 0;
-    if (!isfinite(v)) f |= BSSM_CHECK_NONFINITE;
-    if (v <= 0.f) f |= BSSM_CHECK_NOT_POSITIVE;  // NaN compares false
-    if (v < 0.f) f |= BSSM_CHECK_NEGATIVE;
-    return f;
-}
+// never overflows); the noise rows get all three flags (check_flags_of).
 template <bool OUT_BF, int N>
 __device__ __forceinline__ void nonfinite_acc(float &acc, const float (&v)[N]) {
 #pragma unroll
@@ -495,8 +489,8 @@ __global__ void __launch_bounds__(kThreads, BSSM_ENV_FWD_MINB) prologue_kernel(c
                 const float rv = softplus(x[2 * i + 1] + bias[2 * i + 1]) + kNoiseFloor;
                 a.process[nidx + i * s.t] = pv;
                 a.observation[nidx + i * s.t] = rv;
-                pflags |= value_flags(pv);
-                rflags |= value_flags(rv);
+                pflags |= check_flags_of(pv);
+                rflags |= check_flags_of(rv);
             }
         }
         issue(k + FR);  // after the slot's values were used
